@@ -1,0 +1,132 @@
+/*
+ * bh_q4k.h — C ABI of the B200 (sm_100a) Q4_K x Q8_K decode hot path.
+ *
+ * Drop-in boundary for BurnHard's decode matvecs: dense projections, the LM
+ * head and routed-expert FFNs. Plain C types only; no CUDA or torch types in
+ * any signature (streams travel as void*, i.e. a cudaStream_t; NULL is the
+ * CUDA default stream, as in the CUDA runtime).
+ *
+ * Conventions (follow the reference's C entry points):
+ *  - Every call returns int: 0 on success, a negative errno on failure
+ *    (burnhard_residue_matmul.c:93,122 and sp_crt.c:481-496 use the same
+ *    0 / negative convention). Arguments are validated on the host before
+ *    any launch; an invalid call launches nothing.
+ *  - Pointers are DEVICE pointers unless the parameter name starts with
+ *    host_. Device buffers are caller-allocated and caller-owned
+ *    (burnhard_residue_matmul.h:18-19).
+ *  - Layouts are GGML's: a Q4_K weight matrix of N rows and K columns is
+ *    N rows of K/256 consecutive 144-byte block_q4_K (ggml-common.h:317-328);
+ *    an activation column is K/256 consecutive 292-byte block_q8_K
+ *    (ggml-common.h:360-366); outputs are GGML dst [N, B]: column b holds
+ *    y[b*N .. b*N+N-1]. K must be a multiple of 256, 1 <= B <= 8,
+ *    Q4_K weight pointers 16-byte aligned, Q8_K / fp32 pointers 4-byte aligned.
+ *  - A context is bound to one device and is not re-entrant: one host thread
+ *    at a time per context (the reference's CRT context is single-writer,
+ *    sp_crt_dispatch.h:32-33). Kernels are asynchronous on the given stream.
+ *  - fold selects the fp32 reduction order reproduced bit-for-bit:
+ *    BH_FOLD_X86 = the reference's x86 AVX2 vec_dot (ggml-cpu/arch/x86/
+ *    quants.c:1900-1983), BH_FOLD_GENERIC = its portable vec_dot
+ *    (ggml-cpu/quants.c:645-718). Integer partials are identical for both.
+ */
+#ifndef BH_Q4K_H
+#define BH_Q4K_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BH_OK 0
+#define BH_EIO (-5)
+#define BH_ENOMEM (-12)
+#define BH_ENODEV (-19)
+#define BH_EINVAL (-22)
+#define BH_ETIMEDOUT (-110)
+
+#define BH_FOLD_X86 0
+#define BH_FOLD_GENERIC 1
+
+#define BH_QK 256
+#define BH_Q4K_BLOCK_BYTES 144
+#define BH_Q8K_BLOCK_BYTES 292
+#define BH_MAX_BATCH 8
+
+typedef struct bh_ctx bh_ctx;
+
+/* Library version, (major << 16) | minor. */
+int bh_version(void);
+/* Static text for a status code. */
+const char *bh_strerror(int code);
+
+/* Create / destroy a context on CUDA device `device` (sp_crt_dispatch.h:30-33,
+ * 73-76: one context per engine, created at init, freed at shutdown). */
+int bh_init(int device, bh_ctx **out);
+int bh_free(bh_ctx *ctx);
+/* Synchronize the context's device and report (and optionally clear) the
+ * device-side status word that kernels set when a bounded wait runs out:
+ * 0, or BH_ETIMEDOUT / BH_EINVAL. */
+int bh_device_status(bh_ctx *ctx, int clear);
+
+/* Launch-shape tuning of a context (no effect on results): keys below.
+ * BH_TUNE_CTAS_PER_SM: matvec CTAs per SM, 1..4 (default 1);
+ * BH_TUNE_STAGE_BYTES: upper bound on the bytes of one row's slice in a
+ *   weight pipeline stage, 144..65536 (default 16384: as large as shared
+ *   memory allows with 4 or more stages); BH_TUNE_SMEM_CAP: shared-memory budget of a matvec CTA
+ *   whose staged activations are small, 32768..204800 (default 112640). */
+#define BH_TUNE_CTAS_PER_SM 1
+#define BH_TUNE_STAGE_BYTES 2
+#define BH_TUNE_SMEM_CAP 3
+int bh_tune(bh_ctx *ctx, int key, int value);
+
+/* fp32 activations [B][K] -> B columns of Q8_K, byte-identical to
+ * quantize_row_q8_K_ref (ggml-quants.c:2692-2729); replaces the CPU
+ * backend's from_float step (ggml-cpu.c:1322-1333). All-zero blocks get
+ * d = 0, qs = 0 and bsums = 0. */
+int bh_q8k_quantize(bh_ctx *ctx, const float *x, int64_t K, int B, void *x_q8k, void *stream);
+
+/* y[b*N + r] = W_q4k[r] . x_q8k[b] — the Q4_K x Q8_K matvec, batch 1..8.
+ * Replaces the row loop of ggml_compute_forward_mul_mat (ggml-cpu.c:1151-1234)
+ * over ggml_vec_dot_q4_K_q8_K. partials_opt (may be NULL) receives the exact
+ * integer partials, int32 [B][N][K/256][9]: entries 0..7 are the unscaled
+ * sub-block sums sum(q4*q8) over 32 values, entry 8 is the min term
+ * sum_j min6_j * (bsums[2j] + bsums[2j+1]). */
+int bh_q4k_matvec(bh_ctx *ctx, const void *W_q4k, int64_t N, int64_t K, const void *x_q8k, int B,
+                  float *y, int32_t *partials_opt, int fold, void *stream);
+
+/* Same product from fp32 activations [B][K]: the Q8_K quantization runs in
+ * the matvec kernel's prologue (bit-identical to bh_q8k_quantize followed by
+ * bh_q4k_matvec). This is ggml_mul_mat's contract for a Q4_K src0 and an
+ * f32 src1 (ggml-cpu.c:1241-1439). */
+int bh_q4k_matvec_f32(bh_ctx *ctx, const void *W_q4k, int64_t N, int64_t K, const float *x, int B,
+                      float *y, int fold, void *stream);
+
+/* fp32 weights [N][K] -> Q4_K, byte-identical to quantize_row_q4_K_ref
+ * (ggml-quants.c:1395-1465) evaluated without FMA contraction; the
+ * offline weight-prep step of ggml_quantize_chunk (ggml-quants.c:1564-1576). */
+int bh_q4k_quantize(bh_ctx *ctx, const float *w, int64_t N, int64_t K, void *W_q4k, void *stream);
+
+/* Q4_K -> fp32 [N][K], bit-identical to dequantize_row_q4_K
+ * (ggml-quants.c:1467-1489). */
+int bh_q4k_dequantize(bh_ctx *ctx, const void *W_q4k, int64_t N, int64_t K, float *w, void *stream);
+
+/* Host-buffer form of the matvec, the call a CPU caller of ggml_mul_mat makes:
+ * host_x fp32 [B][K] is copied in, quantized, multiplied by the device-resident
+ * W_q4k, and host_y [B][N] is copied back before returning. Uses scratch
+ * buffers owned by the context. */
+int bh_q4k_mul_mat_host(bh_ctx *ctx, const void *W_q4k, int64_t N, int64_t K, const float *host_x,
+                        int B, float *host_y, int fold);
+
+/* ggml_vec_dot_t-shaped shim (ggml-cpu.h:113) for the type_traits slot of
+ * GGML_TYPE_Q4_K: one row of K = n values, HOST pointers vx (block_q4_K)
+ * and vy (block_q8_K), nrc must be 1. Runs on device 0 through a
+ * process-wide context, x86 fold. Slow (two copies per call); it exists so
+ * the reference's row-level tests can drive the device path unchanged. */
+void bh_ggml_vec_dot_q4_K_q8_K(int n, float *s, size_t bs, const void *vx, size_t bx, const void *vy,
+                               size_t by, int nrc);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BH_Q4K_H */

@@ -1,0 +1,211 @@
+"""ctypes bindings for the test-infrastructure libraries in this folder.
+
+TEST INFRASTRUCTURE ONLY: the parity checker (``Oracle`` -> liboracle.so, the
+CPU restatement of the reference's Q4_K x Q8_K arithmetic) and the compiled
+reference (``Reference`` -> _ref/libq4k_ref.so, the reference's own
+ggml-quants.c / ggml-cpu quants sources). Nothing on the product path imports
+this module; tests/, __graft_entry__.smoke() and bench.py's CPU legs do.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libq4k_ref.so")
+
+QK = 256
+Q4K_BYTES = 144
+Q8K_BYTES = 292
+FOLD_X86 = 0
+FOLD_GENERIC = 1
+
+_f32p = C.POINTER(C.c_float)
+_vp = C.c_void_p
+
+
+def build(ref_root: str | None = None) -> None:
+    """Compile liboracle.so (and _ref when the reference tree is present)."""
+    cmd = ["make", "-s", "-C", HERE, "all"]
+    if ref_root:
+        cmd.append(f"REF_ROOT={ref_root}")
+    subprocess.run(cmd, check=True)
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(_vp)
+
+
+def q4k_row_bytes(k: int) -> int:
+    return k // QK * Q4K_BYTES
+
+
+def q8k_row_bytes(k: int) -> int:
+    return k // QK * Q8K_BYTES
+
+
+class Oracle:
+    """The CPU restatement (q4k_oracle.c)."""
+
+    def __init__(self, path: str = ORACLE_SO):
+        if not os.path.exists(path):
+            build()
+        L = C.CDLL(path)
+        self.lib = L
+        L.bho_fp16_to_fp32.argtypes = [C.c_uint16]
+        L.bho_fp16_to_fp32.restype = C.c_float
+        L.bho_fp32_to_fp16.argtypes = [C.c_float]
+        L.bho_fp32_to_fp16.restype = C.c_uint16
+        L.bho_fill_normal_range.argtypes = [_vp, C.c_int64, C.c_int64, C.c_uint64, C.c_double, C.c_double]
+        L.bho_quantize_q4k.argtypes = [_vp, _vp, C.c_int64, C.c_int64, C.c_int]
+        L.bho_dequantize_row_q4k.argtypes = [_vp, _vp, C.c_int64]
+        L.bho_quantize_row_q8k.argtypes = [_vp, _vp, C.c_int64]
+        L.bho_vec_dot_generic.argtypes = [C.c_int, _vp, _vp]
+        L.bho_vec_dot_generic.restype = C.c_float
+        L.bho_vec_dot_x86.argtypes = [C.c_int, _vp, _vp]
+        L.bho_vec_dot_x86.restype = C.c_float
+        L.bho_matvec.argtypes = [_vp, C.c_int64, C.c_int64, _vp, C.c_int, _vp, C.c_int, C.c_int]
+        L.bho_partials.argtypes = [_vp, C.c_int64, C.c_int64, _vp, C.c_int, _vp]
+        L.bho_argmax.argtypes = [_vp, C.c_int64]
+        L.bho_argmax.restype = C.c_int64
+
+    def normal(self, shape, seed: int, mean: float = 0.0, std: float = 1.0, first: int = 0) -> np.ndarray:
+        out = np.empty(shape, dtype=np.float32)
+        self.lib.bho_fill_normal_range(_ptr(out), first, out.size, seed & (2**64 - 1), mean, std)
+        return out
+
+    def quantize_q4k(self, x: np.ndarray, nthreads: int = 0) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        n, k = x.shape
+        out = np.zeros((n, q4k_row_bytes(k)), dtype=np.uint8)
+        self.lib.bho_quantize_q4k(_ptr(x), _ptr(out), n, k, nthreads or (os.cpu_count() or 1))
+        return out
+
+    def dequantize_q4k(self, w: np.ndarray, k: int) -> np.ndarray:
+        w = np.ascontiguousarray(w, dtype=np.uint8)
+        n = w.size // q4k_row_bytes(k)
+        out = np.empty((n, k), dtype=np.float32)
+        self.lib.bho_dequantize_row_q4k(_ptr(w), _ptr(out), n * k)
+        return out
+
+    def quantize_q8k(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rows = x.reshape(-1, x.shape[-1])
+        k = rows.shape[1]
+        out = np.zeros((rows.shape[0], q8k_row_bytes(k)), dtype=np.uint8)
+        self.lib.bho_quantize_row_q8k(_ptr(rows), _ptr(out), rows.size)
+        return out
+
+    def matvec(self, w: np.ndarray, n: int, k: int, xq: np.ndarray, b: int,
+               fold: int = FOLD_X86, nthreads: int = 0) -> np.ndarray:
+        y = np.empty((b, n), dtype=np.float32)
+        self.lib.bho_matvec(_ptr(np.ascontiguousarray(w)), n, k, _ptr(np.ascontiguousarray(xq)), b,
+                            _ptr(y), fold, nthreads or (os.cpu_count() or 1))
+        return y
+
+    def partials(self, w: np.ndarray, n: int, k: int, xq: np.ndarray, b: int) -> np.ndarray:
+        out = np.empty((b, n, k // QK, 9), dtype=np.int32)
+        self.lib.bho_partials(_ptr(np.ascontiguousarray(w)), n, k, _ptr(np.ascontiguousarray(xq)), b, _ptr(out))
+        return out
+
+    def vec_dot(self, k: int, w_row: np.ndarray, x_row: np.ndarray, fold: int = FOLD_X86) -> float:
+        f = self.lib.bho_vec_dot_generic if fold == FOLD_GENERIC else self.lib.bho_vec_dot_x86
+        return float(f(k, _ptr(np.ascontiguousarray(w_row)), _ptr(np.ascontiguousarray(x_row))))
+
+    def argmax(self, v: np.ndarray) -> int:
+        v = np.ascontiguousarray(v, dtype=np.float32)
+        return int(self.lib.bho_argmax(_ptr(v), v.size))
+
+    def fp32_to_fp16(self, f: float) -> int:
+        return int(self.lib.bho_fp32_to_fp16(f))
+
+    def fp16_to_fp32(self, h: int) -> float:
+        return float(self.lib.bho_fp16_to_fp32(h))
+
+
+class Reference:
+    """The reference's own code, compiled from its tree (oracle/_ref)."""
+
+    def __init__(self, path: str = REF_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} not built (make -C oracle ref)")
+        L = C.CDLL(path)
+        self.lib = L
+        L.ref_has_avx2.restype = C.c_int
+        for name in ("ref_quantize_row_q4k", "ref_quantize_row_q8k", "ref_quantize_row_q8k_ref"):
+            getattr(L, name).argtypes = [_vp, _vp, C.c_int64]
+        L.ref_dequantize_row_q4k.argtypes = [_vp, _vp, C.c_int64]
+        for name in ("ref_vec_dot_generic", "ref_vec_dot_x86"):
+            getattr(L, name).argtypes = [C.c_int, _vp, _vp]
+            getattr(L, name).restype = C.c_float
+        L.ref_pool_create.argtypes = [C.c_int]
+        L.ref_pool_create.restype = _vp
+        L.ref_pool_free.argtypes = [_vp]
+        L.ref_pool_threads.argtypes = [_vp]
+        L.ref_pool_threads.restype = C.c_int
+        L.ref_mul_mat.argtypes = [_vp, _vp, C.c_int64, C.c_int64, _vp, C.c_int, _vp, _vp]
+        self.has_avx2 = bool(L.ref_has_avx2())
+        self._pool = None
+
+    def quantize_q4k(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        n, k = x.shape
+        out = np.zeros((n, q4k_row_bytes(k)), dtype=np.uint8)
+        self.lib.ref_quantize_row_q4k(_ptr(x), _ptr(out), n * k)
+        return out
+
+    def quantize_q8k(self, x: np.ndarray, x86: bool = True) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rows = x.reshape(-1, x.shape[-1])
+        out = np.zeros((rows.shape[0], q8k_row_bytes(rows.shape[1])), dtype=np.uint8)
+        f = self.lib.ref_quantize_row_q8k if x86 else self.lib.ref_quantize_row_q8k_ref
+        f(_ptr(rows), _ptr(out), rows.size)
+        return out
+
+    def dequantize_q4k(self, w: np.ndarray, k: int) -> np.ndarray:
+        w = np.ascontiguousarray(w, dtype=np.uint8)
+        n = w.size // q4k_row_bytes(k)
+        out = np.empty((n, k), dtype=np.float32)
+        self.lib.ref_dequantize_row_q4k(_ptr(w), _ptr(out), n * k)
+        return out
+
+    def matvec_rows(self, w: np.ndarray, n: int, k: int, xq: np.ndarray, b: int, fold: int) -> np.ndarray:
+        """Row-by-row vec_dot, single thread (fold selects generic or AVX2)."""
+        f = self.lib.ref_vec_dot_generic if fold == FOLD_GENERIC else self.lib.ref_vec_dot_x86
+        w = np.ascontiguousarray(w, dtype=np.uint8).reshape(n, -1)
+        xq = np.ascontiguousarray(xq, dtype=np.uint8).reshape(b, -1)
+        y = np.empty((b, n), dtype=np.float32)
+        for c in range(b):
+            xp = _ptr(xq[c])
+            for r in range(n):
+                y[c, r] = f(k, w[r].ctypes.data_as(_vp), xp)
+        return y
+
+    def pool(self, nthreads: int):
+        if self._pool is None or self.lib.ref_pool_threads(self._pool) != nthreads:
+            if self._pool is not None:
+                self.lib.ref_pool_free(self._pool)
+            self._pool = self.lib.ref_pool_create(nthreads)
+        return self._pool
+
+    def mul_mat(self, w: np.ndarray, n: int, k: int, x: np.ndarray, nthreads: int,
+                xq_scratch: np.ndarray | None = None, out: np.ndarray | None = None) -> np.ndarray:
+        """ggml-style threaded mul_mat: fp32 activations [B][K] -> Y [B][N]."""
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, k)
+        b = x.shape[0]
+        if xq_scratch is None:
+            xq_scratch = np.empty(b * q8k_row_bytes(k), dtype=np.uint8)
+        y = out if out is not None else np.empty((b, n), dtype=np.float32)
+        self.lib.ref_mul_mat(self.pool(nthreads), _ptr(w), n, k, _ptr(x), b, _ptr(xq_scratch), _ptr(y))
+        return y
+
+    def __del__(self):
+        try:
+            if self._pool is not None:
+                self.lib.ref_pool_free(self._pool)
+        except Exception:
+            pass

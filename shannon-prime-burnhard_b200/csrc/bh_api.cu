@@ -1,0 +1,304 @@
+// bh_api.cu — the extern "C" boundary (include/bh_q4k.h).
+//
+// Host-side argument validation happens before any launch; an invalid call
+// launches nothing and returns BH_EINVAL. There is no CPU fallback: every
+// compute entry point runs the sm_100a kernels or fails.
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "bh_common.cuh"
+#include "bh_kernels.cuh"
+
+struct bh_ctx {
+    int device = 0;
+    int num_sms = 0;
+    cudaStream_t stream = nullptr;
+    int* d_status = nullptr;
+    // scratch for host-buffer entry points and argmax candidates
+    uint8_t* scratch = nullptr;
+    size_t scratch_bytes = 0;
+    // launch-shape tuning (bh_tune)
+    int ctas_per_sm = 1;
+    int stage_bytes = 16384;
+    int smem_cap_small = 110 * 1024;
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// NULL is the CUDA default stream, exactly as in the CUDA runtime; the
+// context's own stream serves only the host-buffer entry points.
+inline cudaStream_t pick_stream(bh_ctx*, void* stream) { return static_cast<cudaStream_t>(stream); }
+
+int ensure_scratch(bh_ctx* ctx, size_t bytes) {
+    if (ctx->scratch_bytes >= bytes) return BH_OK;
+    if (ctx->scratch) {
+        cudaStreamSynchronize(ctx->stream);
+        cudaFree(ctx->scratch);
+        ctx->scratch = nullptr;
+        ctx->scratch_bytes = 0;
+    }
+    const size_t want = (bytes + (1u << 20) - 1) & ~(size_t)((1u << 20) - 1);
+    if (cudaMalloc(&ctx->scratch, want) != cudaSuccess) {
+        cudaGetLastError();
+        return BH_ENOMEM;
+    }
+    ctx->scratch_bytes = want;
+    return BH_OK;
+}
+
+int check_matvec_args(bh_ctx* ctx, const void* W, int64_t N, int64_t K, const void* x, int B, const float* y,
+                      int fold) {
+    if (!ctx) return BH_EINVAL;
+    if (N < 0 || K < 0 || K % bh::QK != 0 || B < 0 || B > BH_MAX_BATCH) return BH_EINVAL;
+    if (K > (int64_t)1 << 30 || N > (int64_t)1 << 31) return BH_EINVAL;
+    if (fold != BH_FOLD_X86 && fold != BH_FOLD_GENERIC) return BH_EINVAL;
+    if (N == 0 || B == 0) return BH_OK;
+    if (!y || !aligned(y, 4)) return BH_EINVAL;
+    if (K == 0) return BH_OK;
+    if (!W || !aligned(W, 16) || !x || !aligned(x, 4)) return BH_EINVAL;
+    return BH_OK;
+}
+
+// Choose the grid and shared-memory budget for one matvec launch.
+int plan_for(bh_ctx* ctx, bh::MatvecParams& p, int grid_override = 0) {
+    int grid = grid_override > 0 ? grid_override : ctx->num_sms * ctx->ctas_per_sm;
+    if ((int64_t)grid > p.N) grid = (int)p.N;
+    const int act_bytes = p.B * p.nb * bh::ACT_BLOCK_BYTES;
+    // small activation footprints keep a CTA under half the SM's shared
+    // memory so a second CTA (or the next kernel of a decode step) fits
+    const int cap = act_bytes <= 24 * 1024 ? ctx->smem_cap_small : 200 * 1024;
+    const int rc = bh::matvec_plan(p, grid, cap, ctx->stage_bytes);
+    return rc == BH_OK ? grid : rc;
+}
+
+bh::MatvecParams base_params(bh_ctx* ctx, const void* W, int64_t N, int64_t K, int B, float* y) {
+    bh::MatvecParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.w[0] = p.w[1] = p.w[2] = static_cast<const uint8_t*>(W);
+    p.seg_end[0] = p.seg_end[1] = p.seg_end[2] = N;
+    p.N = N;
+    p.K = (int)K;
+    p.nb = (int)(K / bh::QK);
+    p.B = B;
+    p.y = y;
+    p.ldy = N;
+    p.status = ctx->d_status;
+    return p;
+}
+
+int run_matvec(bh_ctx* ctx, bh::MatvecParams& p, int fold, int src, int epi, cudaStream_t s) {
+    const int grid = plan_for(ctx, p);
+    if (grid < 0) return grid;
+    bh::LaunchOpts o;
+    o.stream = s;
+    o.grid = grid;
+    return bh::launch_matvec(p, fold, src, epi, o);
+}
+
+}  // namespace
+
+extern "C" {
+
+int bh_version(void) { return (1 << 16) | 0; }
+
+const char* bh_strerror(int code) {
+    switch (code) {
+        case BH_OK: return "ok";
+        case BH_EIO: return "CUDA launch or runtime failure";
+        case BH_ENOMEM: return "device allocation failed";
+        case BH_ENODEV: return "no such CUDA device";
+        case BH_EINVAL: return "invalid argument";
+        case BH_ETIMEDOUT: return "a bounded device-side wait timed out";
+        default: return "unknown status";
+    }
+}
+
+int bh_init(int device, bh_ctx** out) {
+    if (!out) return BH_EINVAL;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+        cudaGetLastError();
+        return BH_ENODEV;
+    }
+    DeviceGuard g(device);
+    if (!g.ok) return BH_ENODEV;
+    bh_ctx* c = new bh_ctx();
+    c->device = device;
+    cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&c->d_status, sizeof(int)) != cudaSuccess ||
+        cudaMemset(c->d_status, 0, sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
+        if (c->stream) cudaStreamDestroy(c->stream);
+        if (c->d_status) cudaFree(c->d_status);
+        delete c;
+        return BH_ENOMEM;
+    }
+    *out = c;
+    return BH_OK;
+}
+
+int bh_free(bh_ctx* ctx) {
+    if (!ctx) return BH_EINVAL;
+    DeviceGuard g(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    if (ctx->scratch) cudaFree(ctx->scratch);
+    cudaFree(ctx->d_status);
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return BH_OK;
+}
+
+int bh_tune(bh_ctx* ctx, int key, int value) {
+    if (!ctx) return BH_EINVAL;
+    switch (key) {
+        case BH_TUNE_CTAS_PER_SM:
+            if (value < 1 || value > 4) return BH_EINVAL;
+            ctx->ctas_per_sm = value;
+            return BH_OK;
+        case BH_TUNE_STAGE_BYTES:
+            if (value < bh::Q4K_BYTES || value > 65536) return BH_EINVAL;
+            ctx->stage_bytes = value;
+            return BH_OK;
+        case BH_TUNE_SMEM_CAP:
+            if (value < 32 * 1024 || value > 200 * 1024) return BH_EINVAL;
+            ctx->smem_cap_small = value;
+            return BH_OK;
+        default:
+            return BH_EINVAL;
+    }
+}
+
+int bh_device_status(bh_ctx* ctx, int clear) {
+    if (!ctx) return BH_EINVAL;
+    DeviceGuard g(ctx->device);
+    if (cudaDeviceSynchronize() != cudaSuccess) return BH_EIO;
+    int st = 0;
+    if (cudaMemcpy(&st, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return BH_EIO;
+    if (clear && st) cudaMemset(ctx->d_status, 0, sizeof(int));
+    if (st == bh::ST_TIMEOUT) return BH_ETIMEDOUT;
+    if (st != 0) return BH_EINVAL;
+    return BH_OK;
+}
+
+int bh_q8k_quantize(bh_ctx* ctx, const float* x, int64_t K, int B, void* x_q8k, void* stream) {
+    if (!ctx || K < 0 || K % bh::QK != 0 || B < 0) return BH_EINVAL;
+    if (K == 0 || B == 0) return BH_OK;
+    if (!x || !aligned(x, 16) || !x_q8k || !aligned(x_q8k, 4)) return BH_EINVAL;
+    DeviceGuard g(ctx->device);
+    return bh::launch_q8k_quantize(x, K, B, static_cast<uint8_t*>(x_q8k), ctx->d_status,
+                                   pick_stream(ctx, stream));
+}
+
+int bh_q4k_matvec(bh_ctx* ctx, const void* W_q4k, int64_t N, int64_t K, const void* x_q8k, int B, float* y,
+                  int32_t* partials_opt, int fold, void* stream) {
+    int rc = check_matvec_args(ctx, W_q4k, N, K, x_q8k, B, y, fold);
+    if (rc != BH_OK || N == 0 || B == 0) return rc;
+    if (partials_opt && !aligned(partials_opt, 4)) return BH_EINVAL;
+    DeviceGuard g(ctx->device);
+    cudaStream_t s = pick_stream(ctx, stream);
+    if (K == 0) return cudaMemsetAsync(y, 0, sizeof(float) * (size_t)N * B, s) == cudaSuccess ? BH_OK : BH_EIO;
+    bh::MatvecParams p = base_params(ctx, W_q4k, N, K, B, y);
+    p.xq = static_cast<const uint8_t*>(x_q8k);
+    p.partials = partials_opt;
+    return run_matvec(ctx, p, fold, bh::ACT_Q8K, bh::EPI_STORE, s);
+}
+
+int bh_q4k_matvec_f32(bh_ctx* ctx, const void* W_q4k, int64_t N, int64_t K, const float* x, int B, float* y,
+                      int fold, void* stream) {
+    int rc = check_matvec_args(ctx, W_q4k, N, K, x, B, y, fold);
+    if (rc != BH_OK || N == 0 || B == 0) return rc;
+    if (K > 0 && !aligned(x, 16)) return BH_EINVAL;
+    DeviceGuard g(ctx->device);
+    cudaStream_t s = pick_stream(ctx, stream);
+    if (K == 0) return cudaMemsetAsync(y, 0, sizeof(float) * (size_t)N * B, s) == cudaSuccess ? BH_OK : BH_EIO;
+    bh::MatvecParams p = base_params(ctx, W_q4k, N, K, B, y);
+    p.xf = x;
+    return run_matvec(ctx, p, fold, bh::ACT_F32, bh::EPI_STORE, s);
+}
+
+int bh_q4k_quantize(bh_ctx* ctx, const float* w, int64_t N, int64_t K, void* W_q4k, void* stream) {
+    if (!ctx || N < 0 || K < 0 || K % bh::QK != 0) return BH_EINVAL;
+    if (N == 0 || K == 0) return BH_OK;
+    if (!w || !aligned(w, 16) || !W_q4k || !aligned(W_q4k, 4)) return BH_EINVAL;
+    DeviceGuard g(ctx->device);
+    return bh::launch_q4k_quantize(w, N, K, static_cast<uint8_t*>(W_q4k), pick_stream(ctx, stream));
+}
+
+int bh_q4k_dequantize(bh_ctx* ctx, const void* W_q4k, int64_t N, int64_t K, float* w, void* stream) {
+    if (!ctx || N < 0 || K < 0 || K % bh::QK != 0) return BH_EINVAL;
+    if (N == 0 || K == 0) return BH_OK;
+    if (!w || !aligned(w, 16) || !W_q4k || !aligned(W_q4k, 2)) return BH_EINVAL;
+    DeviceGuard g(ctx->device);
+    return bh::launch_q4k_dequantize(static_cast<const uint8_t*>(W_q4k), N, K, w, pick_stream(ctx, stream));
+}
+
+int bh_q4k_mul_mat_host(bh_ctx* ctx, const void* W_q4k, int64_t N, int64_t K, const float* host_x, int B,
+                        float* host_y, int fold) {
+    int rc = check_matvec_args(ctx, W_q4k, N, K, host_x, B, host_y, fold);
+    if (rc != BH_OK || N == 0 || B == 0) return rc;
+    DeviceGuard g(ctx->device);
+    const size_t xb = sizeof(float) * (size_t)B * K, yb = sizeof(float) * (size_t)B * N;
+    const size_t xoff = 0, yoff = (xb + 255) & ~(size_t)255;
+    if ((rc = ensure_scratch(ctx, yoff + yb)) != BH_OK) return rc;
+    float* dx = reinterpret_cast<float*>(ctx->scratch + xoff);
+    float* dy = reinterpret_cast<float*>(ctx->scratch + yoff);
+    cudaStream_t s = ctx->stream;
+    if (K > 0 && cudaMemcpyAsync(dx, host_x, xb, cudaMemcpyHostToDevice, s) != cudaSuccess) return BH_EIO;
+    if (K == 0) {
+        if (cudaMemsetAsync(dy, 0, yb, s) != cudaSuccess) return BH_EIO;
+    } else {
+        bh::MatvecParams p = base_params(ctx, W_q4k, N, K, B, dy);
+        p.xf = dx;
+        if ((rc = run_matvec(ctx, p, fold, bh::ACT_F32, bh::EPI_STORE, s)) != BH_OK) return rc;
+    }
+    if (cudaMemcpyAsync(host_y, dy, yb, cudaMemcpyDeviceToHost, s) != cudaSuccess) return BH_EIO;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return BH_EIO;
+    return BH_OK;
+}
+
+void bh_ggml_vec_dot_q4_K_q8_K(int n, float* s, size_t bs, const void* vx, size_t bx, const void* vy, size_t by,
+                               int nrc) {
+    (void)bs;
+    (void)bx;
+    (void)by;
+    static std::mutex mu;
+    static bh_ctx* gctx = nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!s) return;
+    *s = 0.f;
+    if (nrc != 1 || n < 0 || n % bh::QK != 0 || !vx || !vy) return;
+    if (n == 0) return;
+    if (!gctx && bh_init(0, &gctx) != BH_OK) return;
+    DeviceGuard g(gctx->device);
+    const size_t nb = (size_t)n / bh::QK;
+    const size_t wb = nb * bh::Q4K_BYTES, xb = nb * bh::Q8K_BYTES;
+    const size_t xo = (wb + 255) & ~(size_t)255, yo = (xo + xb + 255) & ~(size_t)255;
+    if (ensure_scratch(gctx, yo + 256) != BH_OK) return;
+    cudaStream_t st = gctx->stream;
+    cudaMemcpyAsync(gctx->scratch, vx, wb, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(gctx->scratch + xo, vy, xb, cudaMemcpyHostToDevice, st);
+    bh::MatvecParams p = base_params(gctx, gctx->scratch, 1, n, 1, reinterpret_cast<float*>(gctx->scratch + yo));
+    p.xq = gctx->scratch + xo;
+    if (run_matvec(gctx, p, BH_FOLD_X86, bh::ACT_Q8K, bh::EPI_STORE, st) != BH_OK) return;
+    cudaMemcpyAsync(s, gctx->scratch + yo, sizeof(float), cudaMemcpyDeviceToHost, st);
+    cudaStreamSynchronize(st);
+}
+
+}  // extern "C"

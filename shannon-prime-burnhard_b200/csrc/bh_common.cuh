@@ -1,0 +1,121 @@
+// bh_common.cuh — shared device helpers for the sm_100a Q4_K kernels.
+//
+// PTX wrappers (mbarrier, 1-D bulk async copy, programmatic dependent
+// launch), the bounded-wait policy, and the exact-rounding helpers that the
+// bit-exact paths rely on. Every kernel file is compiled with -fmad=false,
+// so a*b+c is two roundings unless written as __fmaf_rn.
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/bh_q4k.h"
+
+namespace bh {
+
+constexpr int QK = 256;           // values per super-block
+constexpr int Q4K_BYTES = 144;    // block_q4_K (ggml-common.h:317-328)
+constexpr int Q8K_BYTES = 292;    // block_q8_K (ggml-common.h:360-366)
+
+// Device status word values (mirrors the negative errno codes of the C ABI).
+constexpr int ST_OK = 0;
+constexpr int ST_TIMEOUT = 1;     // a bounded wait ran out
+constexpr int ST_BADARG = 2;      // a device-side argument check failed
+
+// Bounded waits: ~2^31 SM cycles (about a second at B200 clocks).
+constexpr long long WAIT_LIMIT_CYCLES = 1ll << 31;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for the phase with the given parity; false when the bound ran out.
+// try_wait suspends the thread for a while on its own, so the clock is only
+// consulted every 64 polls.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (uint32_t n = 1;; ++n) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((n & 63u) == 0 && clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
+    }
+}
+
+// Order this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy (bulk copy) writes to the same buffer.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 1-D bulk copy global -> shared, completion counted on an mbarrier.
+// dst, src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// Programmatic dependent launch (no-ops when the launch did not opt in).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Named barrier among a subset of warps (id 1.. ; id 0 is __syncthreads).
+__device__ __forceinline__ void named_bar(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ void set_status(int* status, int code) {
+    if (status) atomicCAS(status, ST_OK, code);
+}
+
+// Round to nearest, ties to even, through the 1.5*2^23 bias — the integer
+// rounding of ggml-quants.c:559-563, evaluated with a correctly rounded add.
+__device__ __forceinline__ int round_biased(float v) {
+    const float b = __fadd_rn(v, 12582912.f);
+    return (__float_as_int(b) & 0x007fffff) - 0x00400000;
+}
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+}  // namespace bh

@@ -1,0 +1,69 @@
+// bh_kernels.cuh — host-side launch descriptors shared by the kernel files
+// and the C-ABI layer.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace bh {
+
+// Where the matvec prologue takes its activations from.
+enum ActSrc : int {
+    ACT_Q8K = 0,          // GGML block_q8_K columns
+    ACT_F32 = 1,          // fp32 columns, quantized to Q8_K in the prologue
+    ACT_F32_RMSNORM = 2,  // fp32 h, x = h / sqrt(mean(h^2) + eps) * gamma, then Q8_K
+    ACT_F32_SWIGLU = 3,   // fp32 [gate | up] columns of length 2K, x = silu(gate) * up, then Q8_K
+};
+
+// What the epilogue does with the dot product v of row r, column b.
+enum Epilogue : int {
+    EPI_STORE = 0,   // y[b*ldy + r] = v
+    EPI_ADD = 1,     // y[b*ldy + r] += v   (residual add)
+    EPI_ARGMAX = 2,  // y[b*ldy + r] = v, plus per-CTA (max, first index) candidates
+};
+
+struct MatvecParams {
+    const uint8_t* w[3];   // up to three row segments of one virtual weight matrix
+    int64_t seg_end[3];    // cumulative row ends of the segments; seg_end[2] == N
+    int64_t N;
+    int K, nb, B;
+    const uint8_t* xq;     // ACT_Q8K: B x nb x 292 bytes
+    const float* xf;       // fp32 sources (ACT_F32*)
+    const float* gamma;    // ACT_F32_RMSNORM weights [K]
+    float eps;
+    float* y;
+    int64_t ldy;
+    int32_t* partials;     // optional exact integer partials [B][N][nb][9]
+    float* cand_val;       // EPI_ARGMAX: [gridDim][B] per-CTA maxima
+    int32_t* cand_idx;     // EPI_ARGMAX: [gridDim][B] first index of the maxima
+    int* status;           // device status word
+    // tiling, chosen on the host
+    int rows_per_tile;     // <= 32
+    int kc;                // super-blocks per pipeline stage
+    int row_stride;        // shared-memory bytes per row of a stage
+    int stage_bytes;
+    int stages;
+    int act_off, ring_off, bar_off, smem_bytes;
+};
+
+struct LaunchOpts {
+    cudaStream_t stream = nullptr;
+    bool pdl = false;      // programmatic dependent launch attribute
+    int grid = 0;          // 0 = one CTA per SM (capped by N)
+};
+
+constexpr int MV_WARPS = 8;                 // every warp streams and computes its own rows
+constexpr int MV_THREADS = MV_WARPS * 32;
+constexpr int ACT_BLOCK_BYTES = 304;   // staged Q8_K block: 256 q8 + 16 (d) + 32 (S)
+
+// Fill tiling fields of p for the given grid; returns 0 or a negative errno.
+int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target);
+int launch_matvec(const MatvecParams& p, int fold, int act_src, int epi, const LaunchOpts& o);
+
+int launch_q8k_quantize(const float* x, int64_t K, int B, uint8_t* out, int* status, cudaStream_t s);
+int launch_q4k_quantize(const float* w, int64_t N, int64_t K, uint8_t* out, cudaStream_t s);
+int launch_q4k_dequantize(const uint8_t* w, int64_t N, int64_t K, float* out, cudaStream_t s);
+int launch_argmax_finish(const float* cand_val, const int32_t* cand_idx, int ncand, int B,
+                         int32_t* tok_out, float* val_out, cudaStream_t s, bool pdl);
+
+}  // namespace bh
