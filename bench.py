@@ -1,0 +1,314 @@
+"""Benchmark: Q4_K decode step of a Qwen3-8B-shaped block stack (config 2).
+
+One step = one decode token through 36 layers (fused QKV, attention over 128
+KV positions, O, fused gate|up, down) and the 151936-row LM head with the
+greedy argmax: 4.26 GB of Q4_K weights streamed per token, batch 1.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+value  = algorithmic bytes of all matvecs of the step x ranks / step time
+         (GB/s); tokens/s is reported beside it.
+e2e    = the same metric through bh_stack_decode_host: the embedding comes
+         from pinned host memory and the token is read back every step.
+N > 1  = one process per GPU, each decoding its own sequence with its own
+         copy of the weights (replicas: no data-path collective); the value is
+         the sum over ranks, timed as the slowest rank.
+--impl reference times the reference's own CPU path (ggml quantize_row_q8_K +
+ggml_vec_dot_q4_K_q8_K through oracle/_ref, all host threads) on the same
+weights and the same step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "shannon-prime-burnhard_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+METRIC = "Q4_K matvec achieved HBM GB/s (% of peak) and decode tokens/s at 1/2/4/8 B200"
+SEED = 20261201
+KV_POS = 127            # the token attends over 128 positions
+X_SEED = 777
+
+
+def peaks() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def start_clock_sampler(path: str):
+    cmd = ["nvidia-smi",
+           "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+           "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+           "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+           "--format=csv,noheader,nounits", "-lms", "200"]
+    try:
+        return subprocess.Popen(cmd, stdout=open(path, "w"), stderr=subprocess.DEVNULL)
+    except Exception:
+        return None
+
+
+def stop_clock_sampler(proc, path: str, device: int) -> dict:
+    if proc is None:
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+    proc.terminate()
+    try:
+        proc.wait(timeout=5)
+    except Exception:
+        proc.kill()
+    sm, mx, reasons = [], [], set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for line in open(path):
+        f = [x.strip() for x in line.split(",")]
+        if len(f) < 9 or not f[0].isdigit() or int(f[0]) != device:
+            continue
+        try:
+            sm.append(float(f[1]))
+            mx.append(float(f[2]))
+        except ValueError:
+            continue
+        for n, v in zip(names, f[5:9]):
+            if v.lower() == "active":
+                reasons.add(n)
+    return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+            "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ---------------------------------------------------------------- CPU path
+def cpu_reference_step_fn(st, nthreads: int):
+    """The reference's CPU decode step on host copies of the stack."""
+    import numpy as np
+
+    import oracle as om
+    from cpu_stack import CpuStack, stack_to_cpu
+
+    cfg, w, norms, kc, vc = stack_to_cpu(st)
+    if os.path.exists(om.REF_SO) and om.Reference().has_avx2:
+        ref = om.Reference()
+        scratch = {}
+
+        def mv(wb, n, k, x):
+            key = (n, k)
+            if key not in scratch:
+                scratch[key] = (np.empty(x.shape[0] * om.q8k_row_bytes(k), np.uint8), np.empty((x.shape[0], n), np.float32))
+            xq, y = scratch[key]
+            return ref.mul_mat(wb, n, k, x, nthreads, xq_scratch=xq, out=y).copy()
+
+        kind = "reference"
+    else:
+        o = om.Oracle()
+
+        def mv(wb, n, k, x):
+            return o.matvec(wb, n, k, o.quantize_q8k(x), x.shape[0], om.FOLD_X86, nthreads)
+
+        kind = "port"
+    cpu = CpuStack(cfg, w, norms, kc, vc, mv)
+    return cpu, kind
+
+
+def time_cpu_steps(cpu, x, steps: int, budget_s: float):
+    t0 = time.perf_counter()
+    n = 0
+    while n < steps and (n == 0 or time.perf_counter() - t0 < budget_s):
+        cpu.step(x, KV_POS)
+        n += 1
+    return (time.perf_counter() - t0) / n, n
+
+
+# ---------------------------------------------------------------- main
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=0, help="override n_layer (testing only)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world, rank, local = dist_setup()
+    import numpy as np
+    import torch
+
+    import burnhard as bh
+
+    torch.cuda.set_device(local)
+    nthreads = len(os.sched_getaffinity(0))
+    cfg = bh.default_stack_config()
+    if args.layers:
+        cfg.n_layer = args.layers
+    workload = {"workload": "qwen3-8b-shaped decode block stack (config 2), batch 1",
+                "n_layer": cfg.n_layer, "n_embd": cfg.n_embd, "n_head": cfg.n_head, "n_head_kv": cfg.n_head_kv,
+                "head_dim": cfg.head_dim, "n_ff": cfg.n_ff, "n_vocab": cfg.n_vocab,
+                "kv_positions": KV_POS + 1, "weights": "random-init N(0,0.02) quantized to Q4_K",
+                "l2": "no flush needed: 4.26 GB of weights streamed per step >> 126 MB L2",
+                "parallelism": f"replicas x{world}" if world > 1 else "single GPU"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        ctx = bh.Context(local)
+        st = bh.Stack(ctx, cfg, SEED)
+        st.fill_kv(KV_POS, SEED + 1)
+        st.set_pos(KV_POS)
+        step_bytes = st.info()["step_bytes"]
+        cpu, kind = cpu_reference_step_fn(st, nthreads)
+        x = np.asarray(__import__("oracle").Oracle().normal((cfg.n_embd,), X_SEED, 0.0, 1.0))
+        for _ in range(min(args.warmup, 2)):
+            cpu.step(x, KV_POS)
+        sec, n = time_cpu_steps(cpu, x, args.steps, budget_s=120.0)
+        v = step_bytes / sec / 1e9
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": world,
+            "steps": n, "warmup": min(args.warmup, 2), "ms_per_step": round(sec * 1e3, 3),
+            "tokens_per_s": round(1.0 / sec, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q4_K x q8_K (int8 dot, fp32 fold)", "data": "synthetic",
+            "config": workload,
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": nthreads, "kind": kind,
+                             "sample": f"{n} full decode steps (all 36 layers + LM head) on {nthreads} host threads"},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
+
+    ctx = bh.Context(local)
+    st = bh.Stack(ctx, cfg, SEED)
+    st.fill_kv(KV_POS, SEED + 1)
+    st.set_pos(KV_POS)
+    info = st.info()
+    step_bytes, launches = info["step_bytes"], info["launches"]
+    x_host = np.asarray(__import__("oracle").Oracle().normal((cfg.n_embd,), X_SEED, 0.0, 1.0))
+    x_dev = torch.from_numpy(x_host).cuda()
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.Stream()
+
+    clock_file = os.path.join(tempfile.gettempdir(), f"bh_clocks_{os.getpid()}.csv")
+    sampler = start_clock_sampler(clock_file)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            st.decode(x_dev, tok, stream)
+        stream.synchronize()
+        time.sleep(0.3)
+        barrier(world)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            st.decode(x_dev, tok, stream)
+        e1.record(stream)
+        e1.synchronize()
+        torch.cuda.synchronize()
+        barrier(world)
+    clocks = stop_clock_sampler(sampler, clock_file, local)
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    value = step_bytes * world / (ms / 1e3) / 1e9
+
+    # e2e through the host-buffer entry point (pinned input, token read back)
+    pinned = torch.from_numpy(x_host).pin_memory()
+    for _ in range(3):
+        st.decode_host(pinned)
+    barrier(world)
+    e2e_steps = max(20, args.steps // 4)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        st.decode_host(pinned)
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) / e2e_steps * 1e3, world)
+    e2e_value = step_bytes * world / (e2e_ms / 1e3) / 1e9
+
+    # dominant kernel: the fused gate|up matvec (52% of the step's bytes)
+    op_ms, op_bytes = st.time_op(bh.OP_GATE_UP, reps=3)
+    peak, peak_kind = peaks()
+    achieved = op_bytes / (op_ms / 1e3) / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "gate_up_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            traffic = json.load(open(tpath)).get("dram_bytes_per_launch")
+        except Exception:
+            traffic = None
+    status = ctx.status()
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu, kind = cpu_reference_step_fn(st, nthreads)
+        cpu.step(x_host, KV_POS)  # warm the caches of the CPU path
+        sec, n = time_cpu_steps(cpu, x_host, 50, budget_s=12.0)
+        cpu_baseline = {"value": round(step_bytes / sec / 1e9, 3), "unit": "GB/s", "cores": nthreads, "kind": kind,
+                        "tokens_per_s": round(1.0 / sec, 3),
+                        "sample": f"{n} full decode steps of the same stack (same weights) in ~12 s"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "tokens_per_s": round(world * 1e3 / ms, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "q4_K x q8_K (int8 dot, fp32 fold)", "data": "synthetic", "config": workload,
+            "step_bytes": step_bytes, "frac_of_hbm_peak": round(value / world / peak, 4),
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
+                    "h2d_bytes_per_step": cfg.n_embd * 4, "d2h_bytes_per_step": 4},
+            "roofline": {"bound": "hbm", "kernel": "q4k_matvec (fused gate|up, 24576 x 4096)",
+                         "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "bytes_per_launch": op_bytes, "ms_per_launch": round(op_ms, 5)},
+            "cpu_baseline": cpu_baseline,
+            "gpu_launches": launches * args.steps,
+            "clocks": clocks,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    st.close()
+    ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

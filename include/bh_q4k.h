@@ -70,11 +70,12 @@ int bh_free(bh_ctx *ctx);
 int bh_device_status(bh_ctx *ctx, int clear);
 
 /* Launch-shape tuning of a context (no effect on results): keys below.
- * BH_TUNE_CTAS_PER_SM: matvec CTAs per SM, 1..4 (default 1);
- * BH_TUNE_STAGE_BYTES: upper bound on the bytes of one row's slice in a
- *   weight pipeline stage, 144..65536 (default 16384: as large as shared
- *   memory allows with 4 or more stages); BH_TUNE_SMEM_CAP: shared-memory budget of a matvec CTA
- *   whose staged activations are small, 32768..204800 (default 112640). */
+ * BH_TUNE_CTAS_PER_SM: matvec CTAs per SM when the staged activations are
+ *   small (batch x K/256 x 304 bytes <= 24 KiB), 1..4 (default 2);
+ * BH_TUNE_STAGE_BYTES: bytes of one row's slice in a weight pipeline stage
+ *   (rounded down to whole 144-byte blocks, shrunk until 2 stages fit),
+ *   144..65536 (default 576); BH_TUNE_SMEM_CAP: shared-memory budget of a matvec CTA
+ *   whose staged activations are small, 32768..204800 (default 102400). */
 #define BH_TUNE_CTAS_PER_SM 1
 #define BH_TUNE_STAGE_BYTES 2
 #define BH_TUNE_SMEM_CAP 3
@@ -117,6 +118,94 @@ int bh_q4k_dequantize(bh_ctx *ctx, const void *W_q4k, int64_t N, int64_t K, floa
  * buffers owned by the context. */
 int bh_q4k_mul_mat_host(bh_ctx *ctx, const void *W_q4k, int64_t N, int64_t K, const float *host_x,
                         int B, float *host_y, int fold);
+
+/* LM head with the engine's greedy pick: logits = W_q4k . x for fp32
+ * activations x [B][K] (quantized to Q8_K in the prologue), then
+ * tok_out[b] = the first index of the maximum of column b, exactly
+ * argmax() of desktop/engine/src/engine.cpp:36-43 (strict >, first wins).
+ * logits_opt [B][N] and max_opt [B] may be NULL. The per-CTA argmax
+ * candidates live in a buffer the context allocated at bh_init. */
+int bh_q4k_lmhead_argmax(bh_ctx *ctx, const void *W_q4k, int64_t N, int64_t K, const float *x, int B,
+                         float *logits_opt, int32_t *tok_out, float *max_opt, int fold, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Decode block stack: the caller of the matvec in the reference engine's
+ * per-token step (desktop/engine/src/forward.cpp:2663-2854 build_block_decode,
+ * LM head :3413, argmax engine.cpp:36-43), for one sequence at batch 1, with
+ * random-init (seeded N(0, 0.02)) Q4_K weights generated on the device.
+ * Per layer: RMSNorm -> fused Q|K|V matvec -> q/k RMSNorm, NeoX RoPE, KV
+ * append, GQA softmax attention -> O matvec + residual -> RMSNorm -> fused
+ * gate|up matvec -> SiLU(gate)*up -> down matvec + residual; then RMSNorm ->
+ * LM head -> argmax. The whole step is one CUDA graph.
+ * ------------------------------------------------------------------------ */
+typedef struct bh_stack bh_stack;
+typedef struct bh_stack_config {
+    int n_layer;      /* 36 for the Qwen3-8B shape */
+    int n_embd;       /* 4096 */
+    int n_head;       /* 32 query heads */
+    int n_head_kv;    /* 8 KV heads */
+    int head_dim;     /* 128 */
+    int n_ff;         /* 12288 */
+    int n_vocab;      /* 151936 */
+    int n_ctx;        /* KV cache positions */
+    float rms_eps;    /* 1e-6 */
+    float rope_theta; /* 1e6 */
+} bh_stack_config;
+
+/* tensor ids for bh_stack_tensor */
+#define BH_W_Q 0
+#define BH_W_K 1
+#define BH_W_V 2
+#define BH_W_O 3
+#define BH_W_GATE 4
+#define BH_W_UP 5
+#define BH_W_DOWN 6
+#define BH_W_PER_LAYER 7
+#define BH_W_OUTPUT 7
+#define BH_T_ATTN_NORM 8
+#define BH_T_FFN_NORM 9
+#define BH_T_Q_NORM 10
+#define BH_T_K_NORM 11
+#define BH_T_OUT_NORM 12
+#define BH_T_K_CACHE 13
+#define BH_T_V_CACHE 14
+#define BH_T_LOGITS 15
+#define BH_T_HIDDEN 16
+
+/* The Qwen3-8B-shaped defaults (36 x 4096, 32/8 heads of 128, FFN 12288,
+ * vocab 151936, 128 KV positions). */
+void bh_stack_default_config(bh_stack_config *cfg);
+/* Allocate the stack on ctx's device and generate its weights from seed. */
+int bh_stack_create(bh_ctx *ctx, const bh_stack_config *cfg, uint64_t seed, bh_stack **out);
+int bh_stack_free(bh_stack *st);
+/* Position (0 <= pos < n_ctx) at which the next token is decoded; attention
+ * covers positions 0..pos. */
+int bh_stack_set_pos(bh_stack *st, int pos);
+/* Seeded N(0, 1) K/V history for positions [0, n_pos) of every layer. */
+int bh_stack_fill_kv(bh_stack *st, int n_pos, uint64_t seed);
+/* One decode step from the device embedding x [n_embd]; the next token id
+ * is written to device tok_out. Asynchronous on stream. */
+int bh_stack_decode(bh_stack *st, const float *x, int32_t *tok_out, void *stream);
+/* The same step from host memory: host_x is copied in, the step runs, and
+ * the token is copied back before returning. */
+int bh_stack_decode_host(bh_stack *st, const float *host_x, int32_t *host_tok);
+/* Bytes of all Q4_K weights, algorithmic bytes of one step (weights plus
+ * activations read and outputs written by the matvecs) and kernel launches
+ * per step. */
+int bh_stack_info(bh_stack *st, int64_t *weight_bytes, int64_t *step_bytes, int64_t *launches);
+/* Average device time of one op of the step (CUDA events around reps
+ * eager repetitions over all layers on the stack's stream, the same launch
+ * parameters as inside the step), and its algorithmic bytes per launch.
+ * The state it leaves (hidden, caches) is scratch: reset x / pos after it. */
+#define BH_OP_QKV 0
+#define BH_OP_O 1
+#define BH_OP_GATE_UP 2
+#define BH_OP_DOWN 3
+#define BH_OP_LMHEAD 4
+int bh_stack_time_op(bh_stack *st, int op, int reps, float *avg_ms, int64_t *bytes_per_launch);
+/* Device pointer and shape of one tensor (ids above); Q4_K matrices are
+ * rows x cols in values, the rest fp32. */
+int bh_stack_tensor(bh_stack *st, int layer, int which, void **ptr, int64_t *rows, int64_t *cols);
 
 /* ggml_vec_dot_t-shaped shim (ggml-cpu.h:113) for the type_traits slot of
  * GGML_TYPE_Q4_K: one row of K = n values, HOST pointers vx (block_q4_K)

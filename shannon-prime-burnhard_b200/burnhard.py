@@ -49,6 +49,22 @@ def header_functions(path: str = HEADER) -> list[str]:
     return re.findall(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\**\s*(bh_[A-Za-z0-9_]+)\s*\(", src, flags=re.M)
 
 
+class StackConfig(C.Structure):
+    _fields_ = [("n_layer", C.c_int), ("n_embd", C.c_int), ("n_head", C.c_int), ("n_head_kv", C.c_int),
+                ("head_dim", C.c_int), ("n_ff", C.c_int), ("n_vocab", C.c_int), ("n_ctx", C.c_int),
+                ("rms_eps", C.c_float), ("rope_theta", C.c_float)]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN = range(7)
+W_PER_LAYER = 7
+W_OUTPUT = 7
+OP_QKV, OP_O, OP_GATE_UP, OP_DOWN, OP_LMHEAD = range(5)
+T_ATTN_NORM, T_FFN_NORM, T_Q_NORM, T_K_NORM, T_OUT_NORM, T_K_CACHE, T_V_CACHE, T_LOGITS, T_HIDDEN = range(8, 17)
+
+
 def load(path: str = LIB_PATH) -> C.CDLL:
     if not os.path.exists(path):
         raise ImportError(f"{path} is not built: run `make -C {HERE}` (nvcc, sm_100a)")
@@ -66,6 +82,18 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.bh_q4k_quantize.argtypes = [_vp, _vp, _i64, _i64, _vp, _vp]
     L.bh_q4k_dequantize.argtypes = [_vp, _vp, _i64, _i64, _vp, _vp]
     L.bh_q4k_mul_mat_host.argtypes = [_vp, _vp, _i64, _i64, _vp, C.c_int, _vp, C.c_int]
+    L.bh_q4k_lmhead_argmax.argtypes = [_vp, _vp, _i64, _i64, _vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp]
+    L.bh_stack_default_config.argtypes = [C.POINTER(StackConfig)]
+    L.bh_stack_default_config.restype = None
+    L.bh_stack_create.argtypes = [_vp, C.POINTER(StackConfig), C.c_uint64, C.POINTER(_vp)]
+    L.bh_stack_free.argtypes = [_vp]
+    L.bh_stack_set_pos.argtypes = [_vp, C.c_int]
+    L.bh_stack_fill_kv.argtypes = [_vp, C.c_int, C.c_uint64]
+    L.bh_stack_decode.argtypes = [_vp, _vp, _vp, _vp]
+    L.bh_stack_decode_host.argtypes = [_vp, _vp, _vp]
+    L.bh_stack_info.argtypes = [_vp, C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i64)]
+    L.bh_stack_time_op.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(_i64)]
+    L.bh_stack_tensor.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(_vp), C.POINTER(_i64), C.POINTER(_i64)]
     L.bh_ggml_vec_dot_q4_K_q8_K.argtypes = [C.c_int, _vp, C.c_size_t, _vp, C.c_size_t, _vp, C.c_size_t, C.c_int]
     L.bh_ggml_vec_dot_q4_K_q8_K.restype = None
     return L
@@ -187,3 +215,102 @@ class Context:
         yp = host_y.ctypes.data if hasattr(host_y, "ctypes") else host_y.data_ptr()
         _check(lib.bh_q4k_mul_mat_host(self.h, _dp(w), n, k, xp, b, yp, fold), "bh_q4k_mul_mat_host")
         return host_y
+
+
+def default_stack_config(**overrides) -> StackConfig:
+    cfg = StackConfig()
+    lib.bh_stack_default_config(C.byref(cfg))
+    for k, v in overrides.items():
+        setattr(cfg, k, v)
+    return cfg
+
+
+class Stack:
+    """A decode block stack (bh_stack_*) on a Context's device."""
+
+    def __init__(self, ctx: Context, cfg: StackConfig, seed: int):
+        h = _vp()
+        _check(lib.bh_stack_create(ctx.h, C.byref(cfg), seed & (2**64 - 1), C.byref(h)), "bh_stack_create")
+        self.h = h
+        self.ctx = ctx
+        self.cfg = cfg
+
+    def close(self) -> None:
+        if self.h:
+            lib.bh_stack_free(self.h)
+            self.h = _vp()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_pos(self, pos: int) -> None:
+        _check(lib.bh_stack_set_pos(self.h, pos), "bh_stack_set_pos")
+
+    def fill_kv(self, n_pos: int, seed: int) -> None:
+        _check(lib.bh_stack_fill_kv(self.h, n_pos, seed & (2**64 - 1)), "bh_stack_fill_kv")
+
+    def decode(self, x, tok, stream=None) -> None:
+        _check(lib.bh_stack_decode(self.h, _dp(x), _dp(tok), _stream(stream)), "bh_stack_decode")
+
+    def decode_host(self, host_x) -> int:
+        tok = C.c_int32(0)
+        xp = host_x.ctypes.data if hasattr(host_x, "ctypes") else host_x.data_ptr()
+        _check(lib.bh_stack_decode_host(self.h, xp, C.byref(tok)), "bh_stack_decode_host")
+        return tok.value
+
+    def info(self) -> dict:
+        wb, sb, nl = _i64(), _i64(), _i64()
+        _check(lib.bh_stack_info(self.h, C.byref(wb), C.byref(sb), C.byref(nl)), "bh_stack_info")
+        return {"weight_bytes": wb.value, "step_bytes": sb.value, "launches": nl.value}
+
+    def time_op(self, op: int, reps: int = 5):
+        """(average ms per launch, algorithmic bytes per launch) of one op."""
+        ms, nb = C.c_float(0), _i64()
+        _check(lib.bh_stack_time_op(self.h, op, reps, C.byref(ms), C.byref(nb)), "bh_stack_time_op")
+        return ms.value, nb.value
+
+    def tensor(self, layer: int, which: int):
+        """(device pointer, rows, cols) of one stack tensor."""
+        p, r, c = _vp(), _i64(), _i64()
+        _check(lib.bh_stack_tensor(self.h, layer, which, C.byref(p), C.byref(r), C.byref(c)), "bh_stack_tensor")
+        return p.value, r.value, c.value
+
+    def view(self, layer: int, which: int):
+        """A torch tensor aliasing one stack tensor on the device (uint8 Q4_K
+        bytes, or float32 rows x cols)."""
+        ptr, r, c = self.tensor(layer, which)
+        if which <= W_OUTPUT:
+            return device_view(ptr, r * (c // QK) * Q4K_BYTES, "|u1")
+        return device_view(ptr, r * c, "<f4").view(r, c)
+
+    def to_host(self, layer: int, which: int):
+        import torch
+
+        t = self.view(layer, which)
+        torch.cuda.synchronize()
+        return t.cpu().numpy()
+
+
+def device_view(ptr: int, n: int, typestr: str):
+    """Wrap n elements of device memory at ptr as a torch tensor (no copy)."""
+    import torch
+
+    class _Dev:
+        __cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False), "version": 3}
+
+    return torch.as_tensor(_Dev(), device="cuda")
+
+
+def lmhead_argmax(ctx: Context, w, n: int, k: int, x, logits=None, fold: int = FOLD_X86, stream=None):
+    """Token ids (and maxima) of the greedy pick over W . x; x [B][K] fp32 on the device."""
+    import torch
+
+    b = x.shape[0]
+    tok = torch.empty(b, dtype=torch.int32, device=x.device)
+    mx = torch.empty(b, dtype=torch.float32, device=x.device)
+    _check(lib.bh_q4k_lmhead_argmax(ctx.h, _dp(w), n, k, _dp(x), b, _dp(logits), _dp(tok), _dp(mx), fold,
+                                    _stream(stream)), "bh_q4k_lmhead_argmax")
+    return tok, mx

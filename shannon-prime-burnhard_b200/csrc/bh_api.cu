@@ -3,26 +3,14 @@
 // Host-side argument validation happens before any launch; an invalid call
 // launches nothing and returns BH_EINVAL. There is no CPU fallback: every
 // compute entry point runs the sm_100a kernels or fails.
+#include <climits>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
 
 #include "bh_common.cuh"
+#include "bh_ctx.cuh"
 #include "bh_kernels.cuh"
-
-struct bh_ctx {
-    int device = 0;
-    int num_sms = 0;
-    cudaStream_t stream = nullptr;
-    int* d_status = nullptr;
-    // scratch for host-buffer entry points and argmax candidates
-    uint8_t* scratch = nullptr;
-    size_t scratch_bytes = 0;
-    // launch-shape tuning (bh_tune)
-    int ctas_per_sm = 1;
-    int stage_bytes = 16384;
-    int smem_cap_small = 110 * 1024;
-};
 
 namespace {
 
@@ -74,20 +62,26 @@ int check_matvec_args(bh_ctx* ctx, const void* W, int64_t N, int64_t K, const vo
     return BH_OK;
 }
 
-// Choose the grid and shared-memory budget for one matvec launch.
-int plan_for(bh_ctx* ctx, bh::MatvecParams& p, int grid_override = 0) {
-    int grid = grid_override > 0 ? grid_override : ctx->num_sms * ctx->ctas_per_sm;
-    if ((int64_t)grid > p.N) grid = (int)p.N;
+}  // namespace
+
+namespace bh {
+// Choose the grid and shared-memory budget for one matvec launch. Small
+// staged activations get a half-SM shared-memory budget and two CTAs per SM
+// (16 resident warps hide the dp4a chains' latency); large ones (batch x K)
+// get one CTA per SM with the whole budget.
+int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override) {
     const int act_bytes = p.B * p.nb * bh::ACT_BLOCK_BYTES;
-    // small activation footprints keep a CTA under half the SM's shared
-    // memory so a second CTA (or the next kernel of a decode step) fits
-    const int cap = act_bytes <= 24 * 1024 ? ctx->smem_cap_small : 200 * 1024;
+    const bool small = act_bytes <= ctx->small_act_bytes;
+    const int cps = grid_override > 0 ? 1 : (small ? ctx->ctas_per_sm : 1);
+    int grid = grid_override > 0 ? grid_override : ctx->num_sms * cps;
+    if ((int64_t)grid > p.N) grid = (int)p.N;
+    const int cap = small ? ctx->smem_cap_small : 200 * 1024;
     const int rc = bh::matvec_plan(p, grid, cap, ctx->stage_bytes);
     return rc == BH_OK ? grid : rc;
 }
 
-bh::MatvecParams base_params(bh_ctx* ctx, const void* W, int64_t N, int64_t K, int B, float* y) {
-    bh::MatvecParams p;
+MatvecParams base_params(bh_ctx* ctx, const void* W, int64_t N, int64_t K, int B, float* y) {
+    MatvecParams p;
     std::memset(&p, 0, sizeof(p));
     p.w[0] = p.w[1] = p.w[2] = static_cast<const uint8_t*>(W);
     p.seg_end[0] = p.seg_end[1] = p.seg_end[2] = N;
@@ -101,15 +95,23 @@ bh::MatvecParams base_params(bh_ctx* ctx, const void* W, int64_t N, int64_t K, i
     return p;
 }
 
-int run_matvec(bh_ctx* ctx, bh::MatvecParams& p, int fold, int src, int epi, cudaStream_t s) {
-    const int grid = plan_for(ctx, p);
+int run_matvec(bh_ctx* ctx, MatvecParams& p, int fold, int src, int epi, cudaStream_t s, bool pdl) {
+    const int grid = plan_for(ctx, p, 0);
     if (grid < 0) return grid;
-    bh::LaunchOpts o;
+    LaunchOpts o;
     o.stream = s;
     o.grid = grid;
-    return bh::launch_matvec(p, fold, src, epi, o);
+    o.pdl = pdl;
+    return launch_matvec(p, fold, src, epi, o);
 }
+}  // namespace bh
 
+namespace {
+using bh::base_params;
+using bh::plan_for;
+inline int run_matvec(bh_ctx* ctx, bh::MatvecParams& p, int fold, int src, int epi, cudaStream_t s) {
+    return bh::run_matvec(ctx, p, fold, src, epi, s, false);
+}
 }  // namespace
 
 extern "C" {
@@ -141,12 +143,17 @@ int bh_init(int device, bh_ctx** out) {
     bh_ctx* c = new bh_ctx();
     c->device = device;
     cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
+    const size_t ncand = (size_t)c->num_sms * 4 * BH_MAX_BATCH;
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(&c->d_status, sizeof(int)) != cudaSuccess ||
-        cudaMemset(c->d_status, 0, sizeof(int)) != cudaSuccess) {
+        cudaMemset(c->d_status, 0, sizeof(int)) != cudaSuccess ||
+        cudaMalloc(&c->cand_val, ncand * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&c->cand_idx, ncand * sizeof(int32_t)) != cudaSuccess) {
         cudaGetLastError();
         if (c->stream) cudaStreamDestroy(c->stream);
         if (c->d_status) cudaFree(c->d_status);
+        if (c->cand_val) cudaFree(c->cand_val);
+        if (c->cand_idx) cudaFree(c->cand_idx);
         delete c;
         return BH_ENOMEM;
     }
@@ -159,6 +166,8 @@ int bh_free(bh_ctx* ctx) {
     DeviceGuard g(ctx->device);
     cudaStreamSynchronize(ctx->stream);
     if (ctx->scratch) cudaFree(ctx->scratch);
+    cudaFree(ctx->cand_val);
+    cudaFree(ctx->cand_idx);
     cudaFree(ctx->d_status);
     cudaStreamDestroy(ctx->stream);
     delete ctx;
@@ -247,6 +256,28 @@ int bh_q4k_dequantize(bh_ctx* ctx, const void* W_q4k, int64_t N, int64_t K, floa
     if (!w || !aligned(w, 16) || !W_q4k || !aligned(W_q4k, 2)) return BH_EINVAL;
     DeviceGuard g(ctx->device);
     return bh::launch_q4k_dequantize(static_cast<const uint8_t*>(W_q4k), N, K, w, pick_stream(ctx, stream));
+}
+
+int bh_q4k_lmhead_argmax(bh_ctx* ctx, const void* W_q4k, int64_t N, int64_t K, const float* x, int B,
+                         float* logits_opt, int32_t* tok_out, float* max_opt, int fold, void* stream) {
+    if (!ctx || !tok_out || !aligned(tok_out, 4) || N < 1 || K < bh::QK || B < 1) return BH_EINVAL;
+    if (N > INT32_MAX) return BH_EINVAL;
+    int rc = check_matvec_args(ctx, W_q4k, N, K, x, B, logits_opt ? logits_opt : (const float*)tok_out, fold);
+    if (rc != BH_OK) return rc;
+    if (!aligned(x, 16) || (max_opt && !aligned(max_opt, 4))) return BH_EINVAL;
+    DeviceGuard g(ctx->device);
+    cudaStream_t s = pick_stream(ctx, stream);
+    bh::MatvecParams p = base_params(ctx, W_q4k, N, K, B, logits_opt);
+    p.xf = x;
+    p.cand_val = ctx->cand_val;
+    p.cand_idx = ctx->cand_idx;
+    const int grid = plan_for(ctx, p, 0);
+    if (grid < 0) return grid;
+    bh::LaunchOpts o;
+    o.stream = s;
+    o.grid = grid;
+    if ((rc = bh::launch_matvec(p, fold, bh::ACT_F32, bh::EPI_ARGMAX, o)) != BH_OK) return rc;
+    return bh::launch_argmax_finish(ctx->cand_val, ctx->cand_idx, grid, B, tok_out, max_opt, s, false);
 }
 
 int bh_q4k_mul_mat_host(bh_ctx* ctx, const void* W_q4k, int64_t N, int64_t K, const float* host_x, int B,

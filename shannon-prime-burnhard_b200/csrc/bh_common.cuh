@@ -114,6 +114,12 @@ __device__ __forceinline__ int round_biased(float v) {
     return (__float_as_int(b) & 0x007fffff) - 0x00400000;
 }
 
+// Exact int -> float for |v| < 2^22 without the conversion unit: the
+// integer is placed in the mantissa of 1.5 * 2^23 and the bias subtracted.
+__device__ __forceinline__ float i2f_exact(int v) {
+    return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.f);
+}
+
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }

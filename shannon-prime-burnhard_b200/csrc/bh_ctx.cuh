@@ -1,0 +1,38 @@
+// bh_ctx.cuh — the context object behind the opaque bh_ctx handle, and the
+// internal launch planner shared by the C-ABI entry points.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "bh_kernels.cuh"
+
+struct bh_ctx {
+    int device = 0;
+    int num_sms = 0;
+    cudaStream_t stream = nullptr;
+    int* d_status = nullptr;
+    // scratch for host-buffer entry points and argmax candidates
+    uint8_t* scratch = nullptr;
+    size_t scratch_bytes = 0;
+    // launch-shape tuning (bh_tune)
+    int ctas_per_sm = 2;
+    int stage_bytes = 576;
+    int smem_cap_small = 100 * 1024;
+    int small_act_bytes = 24 * 1024;
+    // argmax candidates of the LM-head entry point: [num_sms * 4][BH_MAX_BATCH]
+    float* cand_val = nullptr;
+    int32_t* cand_idx = nullptr;
+};
+
+
+namespace bh {
+// Grid and shared-memory plan for one matvec launch (fills p's tiling
+// fields); returns the grid size or a negative errno.
+int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override);
+// MatvecParams for a single-segment weight matrix.
+MatvecParams base_params(bh_ctx* ctx, const void* W, int64_t N, int64_t K, int B, float* y);
+// plan_for + launch.
+int run_matvec(bh_ctx* ctx, MatvecParams& p, int fold, int src, int epi, cudaStream_t s, bool pdl);
+}  // namespace bh

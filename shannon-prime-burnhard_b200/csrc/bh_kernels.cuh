@@ -52,8 +52,12 @@ struct LaunchOpts {
     int grid = 0;          // 0 = one CTA per SM (capped by N)
 };
 
-constexpr int MV_WARPS = 8;                 // every warp streams and computes its own rows
+#ifndef BH_MV_WARPS
+#define BH_MV_WARPS 8
+#endif
+constexpr int MV_WARPS = BH_MV_WARPS;       // every warp streams and computes its own rows
 constexpr int MV_THREADS = MV_WARPS * 32;
+constexpr int MV_ROWS = 8;                  // rows of one warp's stage ("oct"); 2 per thread
 constexpr int ACT_BLOCK_BYTES = 304;   // staged Q8_K block: 256 q8 + 16 (d) + 32 (S)
 
 // Fill tiling fields of p for the given grid; returns 0 or a negative errno.

@@ -66,7 +66,7 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
             if (lane < 8) {
                 const uint32_t bw = *reinterpret_cast<const uint32_t*>(src + 260 + 4 * lane);
                 const int s = (int)(int16_t)(bw & 0xffffu) + (int)(int16_t)(bw >> 16);
-                reinterpret_cast<int*>(dst + 272)[lane] = (int)(int16_t)s;
+                reinterpret_cast<int16_t*>(dst + 272)[lane] = (int16_t)s;
             }
         }
         return;
@@ -130,34 +130,67 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
 }
 
 // ---------------------------------------------------------------------------
-// per-super-block work of one lane-thread
+// per-super-block work of one thread (two reference lanes of one row)
 // ---------------------------------------------------------------------------
-struct BlockHdr {
+// Thread t (0..3) of a row owns reference lanes 2t and 2t+1. Row side of
+// one super-block: the two fp16 scales, the packed 6-bit scales/mins, and
+// the low/high-nibble code words of both lanes.
+struct RowBlk {
     float fd, fdm;
-    uint32_t sc03, sc47, mn03, mn47;
+    uint32_t sc03, sc47, mnk;   // mnk: the two mins of min lane k = t in bytes 0..1
+    uint32_t lo[2][4], hi[2][4];
 };
 
-__device__ __forceinline__ BlockHdr load_hdr(const uint8_t* blk) {
+template <int FOLD>
+__device__ __forceinline__ RowBlk decode_row(const uint8_t* blk, int t) {
+    RowBlk r;
     const uint4 h = *reinterpret_cast<const uint4*>(blk);
-    BlockHdr r;
     r.fd = h2f((uint16_t)(h.x & 0xffffu));
     r.fdm = h2f((uint16_t)(h.x >> 16));
     // 6-bit scales/mins, get_scale_min_k4 (ggml-quants.c:818-825) word-wise:
     // j<4: sc = q[j] & 63, mn = q[j+4] & 63;
     // j>=4: sc = (q[j+4] & 15) | (q[j-4] >> 6) << 4, mn = (q[j+4] >> 4) | (q[j] >> 6) << 4
     r.sc03 = h.y & 0x3f3f3f3fu;
-    r.mn03 = h.z & 0x3f3f3f3fu;
     r.sc47 = (h.w & 0x0f0f0f0fu) | ((h.y >> 2) & 0x30303030u);
-    r.mn47 = ((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u);
+    const uint32_t mn = (t & 2) ? (((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u)) : (h.z & 0x3f3f3f3fu);
+    r.mnk = mn >> ((t & 1) * 16);
+    const uint32_t* qs = reinterpret_cast<const uint32_t*>(blk + 16);
+    if (FOLD == BH_FOLD_X86) {
+        // lane m = bytes 4m..4m+3 of each 32-byte group: words 2t, 2t+1
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            const uint2 w = *reinterpret_cast<const uint2*>(qs + 8 * g + 2 * t);
+            r.lo[0][g] = w.x & 0x0f0f0f0fu;
+            r.hi[0][g] = (w.x >> 4) & 0x0f0f0f0fu;
+            r.lo[1][g] = w.y & 0x0f0f0f0fu;
+            r.hi[1][g] = (w.y >> 4) & 0x0f0f0f0fu;
+        }
+    } else {
+        // lane l = group bytes l, l+8, l+16, l+24 (a byte gather); lanes 2t and
+        // 2t+1 sit in the same words k0 = t/2 + {0,2,4,6}, bytes tb and tb+1
+        const int k0 = t >> 1, tb = (2 * t) & 3;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            const uint32_t* gw = qs + 8 * g;
+            const uint32_t w0 = gw[k0], w1 = gw[k0 + 2], w2 = gw[k0 + 4], w3 = gw[k0 + 6];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const uint32_t sel = (uint32_t)((tb + e) | ((tb + e + 4) << 4));
+                const uint32_t tw = __byte_perm(__byte_perm(w0, w1, sel), __byte_perm(w2, w3, sel), 0x5410);
+                r.lo[e][g] = tw & 0x0f0f0f0fu;
+                r.hi[e][g] = (tw >> 4) & 0x0f0f0f0fu;
+            }
+        }
+    }
     return r;
 }
 
-__device__ __forceinline__ int byte_of(uint32_t w, int k) { return (int)((w >> (8 * k)) & 0xffu); }
-
-// Integer lane sum of one row-lane for one staged activation block.
-// lo[g]/hi[g]: this lane's four low/high-nibble codes of 32-byte group g.
-__device__ __forceinline__ int lane_dot(const uint32_t (&lo)[4], const uint32_t (&hi)[4], const BlockHdr& h,
-                                        const int4 a0, const int4 a1, int (&sub)[8], bool want_sub) {
+// One lane's exact integer sum over the super-block:
+// sum_j sc_j * (dot of its 4 codes of sub-block j). Each sub-block dot is a
+// dp4a (|dot| <= 4*15*127, fits int16); two of them are packed and scaled by
+// two 6-bit scales in one dp2a.
+__device__ __forceinline__ int lane_sum(const uint32_t (&lo)[4], const uint32_t (&hi)[4], uint32_t sc03,
+                                        uint32_t sc47, const int4 a0, const int4 a1, int (&sub)[8], bool want_sub) {
     const int d0 = dp4a((int)lo[0], a0.x, 0), d1 = dp4a((int)hi[0], a0.y, 0);
     const int d2 = dp4a((int)lo[1], a0.z, 0), d3 = dp4a((int)hi[1], a0.w, 0);
     const int d4 = dp4a((int)lo[2], a1.x, 0), d5 = dp4a((int)hi[2], a1.y, 0);
@@ -166,105 +199,110 @@ __device__ __forceinline__ int lane_dot(const uint32_t (&lo)[4], const uint32_t 
         sub[0] = d0; sub[1] = d1; sub[2] = d2; sub[3] = d3;
         sub[4] = d4; sub[5] = d5; sub[6] = d6; sub[7] = d7;
     }
-    return byte_of(h.sc03, 0) * d0 + byte_of(h.sc03, 1) * d1 + byte_of(h.sc03, 2) * d2 +
-           byte_of(h.sc03, 3) * d3 + byte_of(h.sc47, 0) * d4 + byte_of(h.sc47, 1) * d5 +
-           byte_of(h.sc47, 2) * d6 + byte_of(h.sc47, 3) * d7;
+    int s = __dp2a_lo((int)__byte_perm((uint32_t)d0, (uint32_t)d1, 0x5410), (int)sc03, 0);
+    s = __dp2a_hi((int)__byte_perm((uint32_t)d2, (uint32_t)d3, 0x5410), (int)sc03, s);
+    s = __dp2a_lo((int)__byte_perm((uint32_t)d4, (uint32_t)d5, 0x5410), (int)sc47, s);
+    return __dp2a_hi((int)__byte_perm((uint32_t)d6, (uint32_t)d7, 0x5410), (int)sc47, s);
 }
 
-__device__ __forceinline__ int min_term(const BlockHdr& h, const int* S, int k0, int k1) {
-    // sum over sub-blocks k in [k0, k1) of min6_k * S[k]
-    int s = 0;
-    for (int k = k0; k < k1; ++k) s += byte_of(k < 4 ? h.mn03 : h.mn47, k & 3) * S[k];
-    return s;
+// One activation column applied to one decoded row block: the reference's
+// per-block fp32 step for this thread's two lanes and its min lane.
+template <int FOLD, bool PART>
+__device__ __forceinline__ void fold_block(const MatvecParams& p, const RowBlk& r, const uint8_t* A, int t,
+                                           int b, int i, int64_t row, bool live, float& acc0, float& acc1,
+                                           float& accm) {
+    const int4 a00 = *reinterpret_cast<const int4*>(A + 64 * t);
+    const int4 a01 = *reinterpret_cast<const int4*>(A + 64 * t + 16);
+    const int4 a10 = *reinterpret_cast<const int4*>(A + 64 * t + 32);
+    const int4 a11 = *reinterpret_cast<const int4*>(A + 64 * t + 48);
+    const float yd = *reinterpret_cast<const float*>(A + 256);
+    int sub0[8], sub1[8];
+    const int l0 = lane_sum(r.lo[0], r.hi[0], r.sc03, r.sc47, a00, a01, sub0, PART);
+    const int l1 = lane_sum(r.lo[1], r.hi[1], r.sc03, r.sc47, a10, a11, sub1, PART);
+    if (FOLD == BH_FOLD_X86) {
+        // acc[m] = fma(y.d * fp16(d), sumi[m], acc[m]);
+        // accm[k] = fma(-y.d * fp16(dmin), min_{2k} S_{2k} + min_{2k+1} S_{2k+1}, accm[k]), k = t
+        const float d = __fmul_rn(yd, r.fd);
+        acc0 = __fmaf_rn(d, i2f_exact(l0), acc0);
+        acc1 = __fmaf_rn(d, i2f_exact(l1), acc1);
+        const int spk = reinterpret_cast<const int*>(A + 272)[t];
+        accm = __fmaf_rn(__fmul_rn(-yd, r.fdm), i2f_exact(__dp2a_lo(spk, (int)r.mnk, 0)), accm);
+    } else {
+        // sums[l] += (fp16(d) * y.d) * aux[l];  sumf -= (fp16(dmin) * y.d) * sumi
+        const float d = __fmul_rn(r.fd, yd);
+        acc0 = __fadd_rn(acc0, __fmul_rn(d, i2f_exact(l0)));
+        acc1 = __fadd_rn(acc1, __fmul_rn(d, i2f_exact(l1)));
+        // sumi = the four threads' min pairs (exact ints) summed in thread 0
+        const int spk = reinterpret_cast<const int*>(A + 272)[t];
+        int mp = __dp2a_lo(spk, (int)r.mnk, 0);
+        mp += __shfl_xor_sync(0xffffffffu, mp, 1);
+        mp += __shfl_xor_sync(0xffffffffu, mp, 2);
+        accm = __fsub_rn(accm, __fmul_rn(__fmul_rn(r.fdm, yd), i2f_exact(mp)));
+    }
+    if (PART) {
+        int mp = __dp2a_lo(reinterpret_cast<const int*>(A + 272)[t], (int)r.mnk, 0);
+        mp += __shfl_xor_sync(0xffffffffu, mp, 1);
+        mp += __shfl_xor_sync(0xffffffffu, mp, 2);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            int v = sub0[j] + sub1[j];
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            sub0[j] = v;
+        }
+        if (live && t == 0) {
+            int32_t* o = p.partials + (((int64_t)b * p.N + row) * p.nb + i) * 9;
+            for (int j = 0; j < 8; ++j) o[j] = sub0[j];
+            o[8] = mp;
+        }
+    }
+}
+
+// Per-row combine in the reference's order, then the epilogue.
+template <int FOLD, int EPI>
+__device__ __forceinline__ void finish_row(const MatvecParams& p, float acc0, float acc1, float accm, int rgrp,
+                                           int t, int b, bool has_row, int64_t row, float& best_v, int& best_i) {
+    const unsigned FULLM = 0xffffffffu;
+    float v;
+    if (FOLD == BH_FOLD_X86) {
+        // hsum_float_8 (arch/x86/quants.c:43-49): ((a4+a0)+(a6+a2)) + ((a5+a1)+(a7+a3));
+        // thread t holds lanes 2t (acc0) and 2t+1 (acc1)
+        const float x0 = __fadd_rn(acc0, __shfl_xor_sync(FULLM, acc0, 2));  // t0: a0+a4, t1: a2+a6
+        const float x1 = __fadd_rn(acc1, __shfl_xor_sync(FULLM, acc1, 2));  // t0: a1+a5, t1: a3+a7
+        const float y0 = __fadd_rn(x0, __shfl_xor_sync(FULLM, x0, 1));
+        const float y1 = __fadd_rn(x1, __shfl_xor_sync(FULLM, x1, 1));
+        const float hs = __fadd_rn(y0, y1);
+        // 4-lane min accumulator, lane k in thread k: (m0+m2) + (m1+m3)
+        const float u = __fadd_rn(accm, __shfl_xor_sync(FULLM, accm, 2));
+        const float hm = __fadd_rn(u, __shfl_xor_sync(FULLM, u, 1));
+        v = __fadd_rn(hs, hm);
+    } else {
+        // sumf (the min chain) += sums[0..7] in order
+        v = accm;
+#pragma unroll
+        for (int l = 0; l < 8; ++l) v = __fadd_rn(v, __shfl_sync(FULLM, (l & 1) ? acc1 : acc0, (rgrp << 2) + (l >> 1)));
+    }
+    if (has_row && t == 0) {
+        float* yp = p.y + (int64_t)b * p.ldy + row;
+        if (EPI == EPI_ADD) *yp = __fadd_rn(*yp, v);
+        else if (EPI != EPI_ARGMAX || p.y) *yp = v;
+        if (EPI == EPI_ARGMAX && v > best_v) { best_v = v; best_i = (int)row; }
+    }
 }
 
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-// One super-block of one row for this lane-thread: integer lane sum, then the
-// reference's fp32 step for every activation column.
-template <int FOLD, int NB, bool PART>
-__device__ __forceinline__ void process_block(const MatvecParams& p, const uint8_t* blk, const uint8_t* act, int i,
-                                              int m, int grp, int64_t row, float (&acc)[NB], float (&accm)[NB]) {
-    const BlockHdr h = load_hdr(blk);
-    const uint32_t* qs = reinterpret_cast<const uint32_t*>(blk + 16);
-    uint32_t lo[4], hi[4];
-    if (FOLD == BH_FOLD_X86) {
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-            const uint32_t w = qs[8 * g + m];
-            lo[g] = w & 0x0f0f0f0fu;
-            hi[g] = (w >> 4) & 0x0f0f0f0fu;
-        }
-    } else {
-        const int k0 = m >> 2, tb = m & 3;
-        const uint32_t sel = (uint32_t)(tb | ((tb + 4) << 4));
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-            const uint32_t* gw = qs + 8 * g;
-            const uint32_t p1 = __byte_perm(gw[k0], gw[k0 + 2], sel);
-            const uint32_t p2 = __byte_perm(gw[k0 + 4], gw[k0 + 6], sel);
-            const uint32_t tw = __byte_perm(p1, p2, 0x5410);
-            lo[g] = tw & 0x0f0f0f0fu;
-            hi[g] = (tw >> 4) & 0x0f0f0f0fu;
-        }
-    }
-#pragma unroll
-    for (int b = 0; b < NB; ++b) {
-        const uint8_t* A = act + (b * p.nb + i) * ACT_BLOCK_BYTES;
-        const int4 a0 = *reinterpret_cast<const int4*>(A + 32 * m);
-        const int4 a1 = *reinterpret_cast<const int4*>(A + 32 * m + 16);
-        const float yd = *reinterpret_cast<const float*>(A + 256);
-        const int* S = reinterpret_cast<const int*>(A + 272);
-        int sub[8];
-        const int li = lane_dot(lo, hi, h, a0, a1, sub, PART);
-        if (FOLD == BH_FOLD_X86) {
-            const float d = __fmul_rn(yd, h.fd);
-            acc[b] = __fmaf_rn(d, (float)li, acc[b]);
-            if (m < 4) {
-                const int prod = min_term(h, S, 2 * m, 2 * m + 2);
-                const float dmin = __fmul_rn(-yd, h.fdm);
-                accm[b] = __fmaf_rn(dmin, (float)prod, accm[b]);
-            }
-        } else {
-            const float d = __fmul_rn(h.fd, yd);
-            acc[b] = __fadd_rn(acc[b], __fmul_rn(d, (float)li));
-            if (m == 0) {
-                const int sumi = min_term(h, S, 0, 8);
-                const float dmin = __fmul_rn(h.fdm, yd);
-                accm[b] = __fsub_rn(accm[b], __fmul_rn(dmin, (float)sumi));
-            }
-        }
-        if (PART) {
-            // group-reduce the eight unscaled sub-block sums
-            const unsigned gm = 0xffu << (8 * grp);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                int v = sub[j];
-                v += __shfl_xor_sync(gm, v, 4);
-                v += __shfl_xor_sync(gm, v, 2);
-                v += __shfl_xor_sync(gm, v, 1);
-                sub[j] = v;
-            }
-            if (m == 0) {
-                int32_t* o = p.partials + (((int64_t)b * p.N + row) * p.nb + i) * 9;
-                for (int j = 0; j < 8; ++j) o[j] = sub[j];
-                o[8] = min_term(h, S, 0, 8);
-            }
-        }
-    }
-}
-
-// Each warp owns whole "quads" of 4 consecutive rows (quad w, w+8, ... of
-// the CTA's row range) and runs its own ring of `stages` stages: a stage is
-// the next kc super-blocks of the quad's 4 rows, one bulk copy per row,
-// issued by lanes 0..3 and counted on the stage's mbarrier. The warp both
-// fills and drains its ring, so there is no cross-warp handshake, and eight
-// warps issue copies in parallel.
+// Each warp owns "octs" of 8 consecutive rows (oct w, w+8, ... of the CTA's
+// row range) and runs its own ring of `stages` stages: a stage is the next kc
+// super-blocks of the oct's 8 rows, one bulk copy per row issued by lanes
+// 0..7 and counted on the stage's mbarrier. Thread (r, t) works row r of the
+// oct as reference lanes 2t and 2t+1 (and min lane t). The warp both fills
+// and drains its ring: no cross-warp handshake, and eight warps issue copies
+// in parallel.
 template <int FOLD, int NB, int SRC, int EPI, bool PART>
 __global__ void __launch_bounds__(MV_THREADS, 1) q4k_matvec_kernel(const MatvecParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ int s_abort;
     __shared__ float s_red[MV_WARPS * 2];
     __shared__ int s_redi[MV_WARPS];
 
@@ -276,13 +314,12 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_matvec_kernel(const MatvecP
     const int64_t r_begin = p.N * blockIdx.x / gridDim.x;
     const int64_t r_end = p.N * (blockIdx.x + 1) / gridDim.x;
     const int nrows = (int)(r_end - r_begin);
-    const int nquads = (nrows + 3) >> 2;
-    const int my_quads = warp < nquads ? (nquads - 1 - warp) / MV_WARPS + 1 : 0;
+    const int nocts = (nrows + MV_ROWS - 1) / MV_ROWS;
+    const int my_octs = warp < nocts ? (nocts - 1 - warp) / MV_WARPS + 1 : 0;
     const int nkc = (p.nb + p.kc - 1) / p.kc;
-    const int total = my_quads * nkc;  // this warp's stage sequence
+    const int total = my_octs * nkc;  // this warp's stage sequence
     const unsigned FULLM = 0xffffffffu;
 
-    if (threadIdx.x == 0) s_abort = 0;
     if (lane == 0) {
         for (int s = 0; s < p.stages; ++s) mbar_init(&full[s], 1);
         fence_mbar_init();
@@ -290,102 +327,89 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_matvec_kernel(const MatvecP
     __syncwarp();
 
     const uint64_t pol = policy_evict_first();
-    auto issue = [&](int q) {
-        const int qd = q / nkc, c = q - qd * nkc;
-        const int r0 = (warp + qd * MV_WARPS) * 4;
-        const int rq = min(4, nrows - r0);
-        const int kl = min(p.kc, p.nb - c * p.kc);
+    // issue cursor: next (oct, chunk, stage) to fill; advanced without divisions
+    int i_od = 0, i_c = 0, i_s = 0, issued = 0;
+    auto issue_next = [&]() {
+        const int r0 = (warp + i_od * MV_WARPS) * MV_ROWS;
+        const int rq = min(MV_ROWS, nrows - r0);
+        const int kl = min(p.kc, p.nb - i_c * p.kc);
         const uint32_t bytes = (uint32_t)kl * Q4K_BYTES;
-        const int s = q % p.stages;
-        if (lane == 0) mbar_arrive_expect_tx(&full[s], bytes * (uint32_t)rq);
+        if (lane == 0) mbar_arrive_expect_tx(&full[i_s], bytes * (uint32_t)rq);
         __syncwarp();
         if (lane < rq) {
-            const uint8_t* src = seg_row(p, r_begin + r0 + lane) + (size_t)c * p.kc * Q4K_BYTES;
-            bulk_g2s(ring + (size_t)s * p.stage_bytes + (size_t)lane * p.row_stride, src, bytes, &full[s], pol);
+            const uint8_t* src = seg_row(p, r_begin + r0 + lane) + (size_t)i_c * p.kc * Q4K_BYTES;
+            bulk_g2s(ring + (size_t)i_s * p.stage_bytes + (size_t)lane * p.row_stride, src, bytes, &full[i_s], pol);
         }
+        ++issued;
+        if (++i_c == nkc) { i_c = 0; ++i_od; }
+        if (++i_s == p.stages) i_s = 0;
     };
     // weights do not depend on the previous kernel: start streaming now
     const int prefill = min(p.stages, total);
-    for (int q = 0; q < prefill; ++q) issue(q);
+    for (int q = 0; q < prefill; ++q) issue_next();
     pdl_trigger();
     pdl_wait();
     stage_activations<FOLD, SRC>(p, act, s_red, threadIdx.x);
     __syncthreads();
 
-    const int grp = lane >> 3;  // row of the quad owned by this thread
-    const int m = lane & 7;     // reference lane owned by this thread
+    const int rgrp = lane >> 2;  // row of the oct worked by this thread
+    const int t = lane & 3;      // owns reference lanes 2t, 2t+1
 
     float best_v[NB];
     int best_i[NB];
 #pragma unroll
     for (int b = 0; b < NB; ++b) { best_v[b] = -INFINITY; best_i[b] = 0x7fffffff; }
 
-    int consumed = 0;
+    int consumed = 0, c_s = 0;
+    uint32_t c_ph = 0;
     bool ok = true;
-    for (int qd = 0; qd < my_quads && ok; ++qd) {
-        const int rin = (warp + qd * MV_WARPS) * 4 + grp;
-        const bool has_row = rin < nrows;
-        const int64_t row = r_begin + rin;
-        float acc[NB], accm[NB];
+    for (int od = 0; od < my_octs && ok; ++od) {
+        const int rin = (warp + od * MV_WARPS) * MV_ROWS + rgrp;
+        const bool live = rin < nrows;
+        float acc0[NB], acc1[NB], accm[NB];
 #pragma unroll
-        for (int b = 0; b < NB; ++b) { acc[b] = 0.f; accm[b] = 0.f; }
+        for (int b = 0; b < NB; ++b) { acc0[b] = 0.f; acc1[b] = 0.f; accm[b] = 0.f; }
 
         for (int c = 0; c < nkc; ++c) {
-            const int q = qd * nkc + c;
-            const int s = q % p.stages;
-            if (!__all_sync(FULLM, mbar_wait_bounded(&full[s], (uint32_t)(q / p.stages) & 1u))) {
+            if (!__all_sync(FULLM, mbar_wait_bounded(&full[c_s], c_ph))) {
                 ok = false;
-                if (lane == 0) { s_abort = 1; set_status(p.status, ST_TIMEOUT); }
+                if (lane == 0) set_status(p.status, ST_TIMEOUT);
                 break;
             }
-            consumed = q + 1;
+            ++consumed;
             const int kl = min(p.kc, p.nb - c * p.kc);
-            if (has_row) {
-                const uint8_t* rowp = ring + (size_t)s * p.stage_bytes + (size_t)grp * p.row_stride;
-                for (int kb = 0; kb < kl; ++kb)
-                    process_block<FOLD, NB, PART>(p, rowp + kb * Q4K_BYTES, act, c * p.kc + kb, m, grp, row, acc, accm);
+            // rows past the end of the range read stale (in-bounds) stage bytes
+            // and are never stored
+            const uint8_t* rowp = ring + (size_t)c_s * p.stage_bytes + (size_t)rgrp * p.row_stride;
+            const uint8_t* actc = act + c * p.kc * ACT_BLOCK_BYTES;
+#pragma unroll 2
+            for (int kb = 0; kb < kl; ++kb) {
+                const RowBlk r = decode_row<FOLD>(rowp + kb * Q4K_BYTES, t);
+#pragma unroll
+                for (int b = 0; b < NB; ++b)
+                    fold_block<FOLD, PART>(p, r, actc + (b * p.nb + kb) * ACT_BLOCK_BYTES, t, b, c * p.kc + kb,
+                                           r_begin + rin, live, acc0[b], acc1[b], accm[b]);
             }
             __syncwarp();
-            if (q + p.stages < total) {
+            if (issued < total) {
                 fence_proxy_async_smem();
-                issue(q + p.stages);
+                issue_next();
             }
+            if (++c_s == p.stages) { c_s = 0; c_ph ^= 1u; }
         }
         if (!ok) break;
-
-        // ---- per-row combine in the reference's order, then the epilogue ----
 #pragma unroll
-        for (int b = 0; b < NB; ++b) {
-            float v;
-            if (FOLD == BH_FOLD_X86) {
-                // hsum_float_8 (arch/x86/quants.c:43-49): ((a4+a0)+(a6+a2)) + ((a5+a1)+(a7+a3))
-                const float t1 = __fadd_rn(acc[b], __shfl_xor_sync(FULLM, acc[b], 4));
-                const float t2 = __fadd_rn(t1, __shfl_xor_sync(FULLM, t1, 2));
-                const float hs = __fadd_rn(t2, __shfl_xor_sync(FULLM, t2, 1));
-                // 4-lane min accumulator: (m0+m2) + (m1+m3)
-                const float u1 = __fadd_rn(accm[b], __shfl_xor_sync(FULLM, accm[b], 2));
-                const float hm = __fadd_rn(u1, __shfl_xor_sync(FULLM, u1, 1));
-                v = __fadd_rn(hs, hm);
-            } else {
-                // sumf (lane 0 holds the min chain) += sums[0..7] in order
-                v = accm[b];
-#pragma unroll
-                for (int l = 0; l < 8; ++l) v = __fadd_rn(v, __shfl_sync(FULLM, acc[b], (grp << 3) + l));
-            }
-            if (has_row && m == 0) {
-                float* yp = p.y + (int64_t)b * p.ldy + row;
-                if (EPI == EPI_ADD) *yp = __fadd_rn(*yp, v);
-                else *yp = v;
-                if (EPI == EPI_ARGMAX) {
-                    if (v > best_v[b]) { best_v[b] = v; best_i[b] = (int)row; }
-                }
-            }
-        }
+        for (int b = 0; b < NB; ++b)
+            finish_row<FOLD, EPI>(p, acc0[b], acc1[b], accm[b], rgrp, t, b, live, r_begin + rin, best_v[b], best_i[b]);
     }
     if (!ok && lane == 0) {
         // nothing of this warp may still be in flight when the CTA exits
-        const int issued = min(total, consumed + p.stages);
-        for (int q = consumed; q < issued; ++q) mbar_wait_bounded(&full[q % p.stages], (uint32_t)(q / p.stages) & 1u);
+        int s = c_s;
+        uint32_t ph = c_ph;
+        for (int q = consumed; q < issued; ++q) {
+            mbar_wait_bounded(&full[s], ph);
+            if (++s == p.stages) { s = 0; ph ^= 1u; }
+        }
     }
 
     if (EPI == EPI_ARGMAX) {
@@ -414,7 +438,6 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_matvec_kernel(const MatvecP
         }
     }
 }
-
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
@@ -433,23 +456,22 @@ int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target) {
         const int words = kc * (Q4K_BYTES / 4);
         const int padw = ((8 - (words % 32)) % 32 + 32) % 32;  // row stride == 8 words (mod 32 banks)
         const int stride = kc * Q4K_BYTES + 4 * padw;
-        const int stage = 4 * stride;
-        const int per_stage_all = MV_WARPS * (stage + 8);
-        int stages = (smem_cap - ring_off - 256) / per_stage_all;
-        if (stages > 8) stages = 8;
-        if (stages >= 4 || kc == 1) {
-            if (stages < 2) return BH_EINVAL;  // activations too large for shared memory
+        const int stage = MV_ROWS * stride;
+        int stages = (smem_cap - ring_off - 256) / (MV_WARPS * (stage + 8));
+        if (stages > 4) stages = 4;
+        if (stages >= 2) {
             p.kc = kc;
             p.row_stride = stride;
             p.stage_bytes = stage;
             p.stages = stages;
-            p.rows_per_tile = 4;
+            p.rows_per_tile = MV_ROWS;
             p.act_off = 0;
             p.ring_off = ring_off;
             p.bar_off = ring_off + MV_WARPS * stages * stage;
             p.smem_bytes = p.bar_off + MV_WARPS * stages * 8;
             return BH_OK;
         }
+        if (kc == 1) return BH_EINVAL;  // activations too large for shared memory
     }
 }
 
@@ -502,6 +524,7 @@ static int launch_fold(const MatvecParams& p, int src, int epi, const LaunchOpts
         case ACT_Q8K * 3 + EPI_ARGMAX: return launch_nb<FOLD, ACT_Q8K, EPI_ARGMAX, false>(p, o, grid);
         case ACT_F32 * 3 + EPI_STORE: return launch_nb<FOLD, ACT_F32, EPI_STORE, false>(p, o, grid);
         case ACT_F32 * 3 + EPI_ADD: return launch_nb<FOLD, ACT_F32, EPI_ADD, false>(p, o, grid);
+        case ACT_F32 * 3 + EPI_ARGMAX: return launch_nb<FOLD, ACT_F32, EPI_ARGMAX, false>(p, o, grid);
         case ACT_F32_RMSNORM * 3 + EPI_STORE: return launch_nb<FOLD, ACT_F32_RMSNORM, EPI_STORE, false>(p, o, grid);
         case ACT_F32_RMSNORM * 3 + EPI_ARGMAX: return launch_nb<FOLD, ACT_F32_RMSNORM, EPI_ARGMAX, false>(p, o, grid);
         case ACT_F32_SWIGLU * 3 + EPI_ADD: return launch_nb<FOLD, ACT_F32_SWIGLU, EPI_ADD, false>(p, o, grid);

@@ -59,7 +59,8 @@ __device__ __forceinline__ Q8Block q8k_quantize_warp(const float (&v)[8], int la
 // Staged activation block (ACT_BLOCK_BYTES = 304):
 //   bytes   0..255 : q8 codes as 64 words, lane-major: word [lane*8 + slot]
 //   bytes 256..259 : d (float)
-//   bytes 272..303 : S[t] = bsums[2t] + bsums[2t+1], t = 0..7 (int32)
+//   bytes 272..287 : S[t] = bsums[2t] + bsums[2t+1], t = 0..7, as int16;
+//                    word k = (S[2k], S[2k+1]) feeds one dp2a with two 6-bit mins
 // Word slot layout per fold (lane = the 8-way split of a row's work):
 //   FOLD_X86 (lane m):     slot 2j   = codes 64j + 4m .. +3       (low-nibble half)
 //                          slot 2j+1 = codes 64j + 32 + 4m .. +3  (high-nibble half)
@@ -101,7 +102,7 @@ __device__ __forceinline__ void stage_codes(uint8_t* blk, const int (&q)[8], int
 __device__ __forceinline__ void stage_scalars(uint8_t* blk, float d, int bsum16, int lane) {
     const int pair = bsum16 + __shfl_xor_sync(0xffffffffu, bsum16, 2);
     if (lane == 0) *reinterpret_cast<float*>(blk + 256) = d;
-    if ((lane & 3) == 0) reinterpret_cast<int*>(blk + 272)[lane >> 2] = (int)(int16_t)pair;
+    if ((lane & 3) == 0) reinterpret_cast<int16_t*>(blk + 272)[lane >> 2] = (int16_t)pair;
 }
 
 }  // namespace bh

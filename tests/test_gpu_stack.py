@@ -1,0 +1,90 @@
+"""GPU: the decode block stack (bh_stack_*) against its CPU restatement.
+
+Every matvec is bit-exact given identical inputs (tested elsewhere); here the
+whole step is compared within a float tolerance, because the glue between
+matvecs (RMSNorm, RoPE, softmax, SiLU) sums in a different order on the CPU.
+The greedy token must equal the first argmax of the device's own logits."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as om
+from cpu_stack import CpuStack, stack_to_cpu
+
+pytestmark = pytest.mark.gpu
+
+SMALL = dict(n_layer=2, n_embd=512, n_head=4, n_head_kv=2, head_dim=128, n_ff=1024, n_vocab=2000, n_ctx=16)
+
+
+def make_stack(bh, ctx, seed=7, **cfg):
+    c = bh.default_stack_config(**{**SMALL, **cfg})
+    return bh.Stack(ctx, c, seed)
+
+
+def oracle_matvec(o):
+    def mv(w, n, k, x):
+        return o.matvec(w, n, k, o.quantize_q8k(x), x.shape[0], om.FOLD_X86)
+    return mv
+
+
+@pytest.mark.parametrize("pos", [0, 5, 15])
+def test_stack_step_matches_cpu(ctx, bh, oracle, pos):
+    import torch
+
+    st = make_stack(bh, ctx)
+    st.fill_kv(pos, 1234)
+    st.set_pos(pos)
+    cfg, w, norms, kc, vc = stack_to_cpu(st)
+    x = oracle.normal((cfg["n_embd"],), 4321 + pos, 0.0, 1.0)
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    st.decode(torch.from_numpy(x).cuda(), tok)
+    torch.cuda.synchronize()
+    logits = st.to_host(-1, bh.T_LOGITS)[0]
+    hidden = st.to_host(-1, bh.T_HIDDEN)[0]
+    t_gpu = int(tok.cpu()[0])
+    assert t_gpu == int(np.nonzero(logits == logits.max())[0][0])
+    cpu = CpuStack(cfg, w, norms, kc, vc, oracle_matvec(oracle))
+    t_cpu, lg_cpu, h_cpu = cpu.step(x, pos)
+    scale = np.abs(h_cpu).max()
+    assert np.abs(hidden - h_cpu).max() <= 2e-3 * scale, np.abs(hidden - h_cpu).max() / scale
+    assert np.abs(logits - lg_cpu).max() <= 2e-3 * np.abs(lg_cpu).max()
+    srt = np.sort(lg_cpu)
+    if srt[-1] - srt[-2] > 1e-2 * np.abs(lg_cpu).max():
+        assert t_gpu == t_cpu
+    # the KV append wrote this token's K/V at pos in every layer
+    for l in range(cfg["n_layer"]):
+        assert np.abs(st.to_host(l, bh.T_V_CACHE)[pos] - cpu.vc[l][pos]).max() <= 2e-3 * np.abs(cpu.vc[l][pos]).max()
+    assert ctx.status() == 0
+
+
+def test_stack_host_path_and_repeatability(ctx, bh, oracle):
+    import torch
+
+    st = make_stack(bh, ctx, seed=11)
+    st.fill_kv(8, 99)
+    st.set_pos(8)
+    x = oracle.normal((SMALL["n_embd"],), 77, 0.0, 1.0)
+    t_host = st.decode_host(x)
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    lg1 = st.to_host(-1, bh.T_LOGITS)[0].copy()
+    st.decode(torch.from_numpy(x).cuda(), tok)
+    torch.cuda.synchronize()
+    lg2 = st.to_host(-1, bh.T_LOGITS)[0]
+    assert int(tok.cpu()[0]) == t_host
+    assert np.array_equal(lg1.view(np.uint32), lg2.view(np.uint32))  # deterministic
+    info = st.info()
+    assert info["launches"] == 5 * SMALL["n_layer"] + 2
+    assert info["weight_bytes"] >= sum(
+        r * (c // 256) * 144 for r, c in [(512, 512), (256, 512), (256, 512), (512, 512), (1024, 512), (1024, 512), (512, 1024)]
+    ) * SMALL["n_layer"]
+
+
+def test_stack_rejects_bad_config(ctx, bh):
+    with pytest.raises(bh.BHError):
+        make_stack(bh, ctx, n_embd=500)
+    with pytest.raises(bh.BHError):
+        make_stack(bh, ctx, n_head=3, n_head_kv=2)
+    st = make_stack(bh, ctx)
+    with pytest.raises(bh.BHError):
+        st.set_pos(SMALL["n_ctx"])
