@@ -79,6 +79,10 @@ int bh_device_status(bh_ctx *ctx, int clear);
 #define BH_TUNE_CTAS_PER_SM 1
 #define BH_TUNE_STAGE_BYTES 2
 #define BH_TUNE_SMEM_CAP 3
+/* BH_TUNE_TPR: threads working one matvec row, 0 = the planner's choice
+ * (8 for narrow matrices at batch <= 2, else 4), or 4 / 8 to force it;
+ * results are identical either way. */
+#define BH_TUNE_TPR 4
 int bh_tune(bh_ctx *ctx, int key, int value);
 
 /* fp32 activations [B][K] -> B columns of Q8_K, byte-identical to

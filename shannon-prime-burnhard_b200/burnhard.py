@@ -26,6 +26,7 @@ BH_OK = 0
 TUNE_CTAS_PER_SM = 1
 TUNE_STAGE_BYTES = 2
 TUNE_SMEM_CAP = 3
+TUNE_TPR = 4
 BH_EIO = -5
 BH_ENOMEM = -12
 BH_ENODEV = -19

@@ -65,18 +65,35 @@ int check_matvec_args(bh_ctx* ctx, const void* W, int64_t N, int64_t K, const vo
 }  // namespace
 
 namespace bh {
-// Choose the grid and shared-memory budget for one matvec launch. Small
-// staged activations get a half-SM shared-memory budget and two CTAs per SM
-// (16 resident warps hide the dp4a chains' latency); large ones (batch x K)
-// get one CTA per SM with the whole budget.
+// Choose the grid, shared-memory budget and threads per row for one matvec
+// launch. Wide matrices (at least one 8-row tile per warp with two CTAs per
+// SM) run two CTAs per SM with half the shared memory each and 4 threads per
+// row. Narrow ones (few rows per CTA) run one CTA per SM with 8 threads per
+// row (4-row tiles): twice the busy warps and half the work per warp step,
+// which is what bounds them.
 int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override) {
-    const int act_bytes = p.B * p.nb * bh::ACT_BLOCK_BYTES;
+    const int act_bytes = p.B * p.nb * ACT_BLOCK_BYTES;
     const bool small = act_bytes <= ctx->small_act_bytes;
-    const int cps = grid_override > 0 ? 1 : (small ? ctx->ctas_per_sm : 1);
-    int grid = grid_override > 0 ? grid_override : ctx->num_sms * cps;
-    if ((int64_t)grid > p.N) grid = (int)p.N;
-    const int cap = small ? ctx->smem_cap_small : 200 * 1024;
-    const int rc = bh::matvec_plan(p, grid, cap, ctx->stage_bytes);
+    int grid, cap, tpr = 4;
+    if (grid_override > 0) {
+        grid = grid_override;
+        cap = 200 * 1024;
+    } else {
+        const int64_t cps_grid = (int64_t)ctx->num_sms * ctx->ctas_per_sm;
+        const int64_t tiles_wide = ((p.N + cps_grid - 1) / cps_grid + MV_ROWS - 1) / MV_ROWS;
+        if (small && tiles_wide >= MV_WARPS) {
+            grid = (int)cps_grid;
+            cap = ctx->smem_cap_small;
+        } else {
+            grid = ctx->num_sms;
+            cap = 200 * 1024;
+            if (p.B <= 2) tpr = 8;
+        }
+    }
+    if (ctx->tpr_force) tpr = (ctx->tpr_force == 8 && p.B <= 2) ? 8 : 4;
+    const int64_t ntile = (p.N + 32 / tpr - 1) / (32 / tpr);  // CTAs own whole tiles
+    if ((int64_t)grid > ntile) grid = (int)ntile;
+    const int rc = matvec_plan(p, grid, cap, ctx->stage_bytes, tpr);
     return rc == BH_OK ? grid : rc;
 }
 
@@ -92,6 +109,9 @@ MatvecParams base_params(bh_ctx* ctx, const void* W, int64_t N, int64_t K, int B
     p.y = y;
     p.ldy = N;
     p.status = ctx->d_status;
+#ifdef BH_TRACE
+    p.trace = ctx->trace;
+#endif
     return p;
 }
 
@@ -109,6 +129,9 @@ int run_matvec(bh_ctx* ctx, MatvecParams& p, int fold, int src, int epi, cudaStr
 namespace {
 using bh::base_params;
 using bh::plan_for;
+using bh::ACT_BLOCK_BYTES;
+using bh::MV_ROWS;
+using bh::MV_WARPS;
 inline int run_matvec(bh_ctx* ctx, bh::MatvecParams& p, int fold, int src, int epi, cudaStream_t s) {
     return bh::run_matvec(ctx, p, fold, src, epi, s, false);
 }
@@ -174,6 +197,15 @@ int bh_free(bh_ctx* ctx) {
     return BH_OK;
 }
 
+#ifdef BH_TRACE
+// Timeline probe target (trace builds only; not part of the public header).
+int bh_trace_buffer(bh_ctx* ctx, void* dev_buf) {
+    if (!ctx) return BH_EINVAL;
+    ctx->trace = static_cast<int64_t*>(dev_buf);
+    return BH_OK;
+}
+#endif
+
 int bh_tune(bh_ctx* ctx, int key, int value) {
     if (!ctx) return BH_EINVAL;
     switch (key) {
@@ -184,6 +216,10 @@ int bh_tune(bh_ctx* ctx, int key, int value) {
         case BH_TUNE_STAGE_BYTES:
             if (value < bh::Q4K_BYTES || value > 65536) return BH_EINVAL;
             ctx->stage_bytes = value;
+            return BH_OK;
+        case BH_TUNE_TPR:
+            if (value != 0 && value != 4 && value != 8) return BH_EINVAL;
+            ctx->tpr_force = value;
             return BH_OK;
         case BH_TUNE_SMEM_CAP:
             if (value < 32 * 1024 || value > 200 * 1024) return BH_EINVAL;

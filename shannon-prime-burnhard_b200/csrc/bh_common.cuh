@@ -7,6 +7,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -85,6 +86,19 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
             smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// 2-D tensor copy global -> shared (cp.async.bulk.tensor, tile mode): the
+// box at element coordinates (x, y) of the tensor map lands densely at dst;
+// out-of-range elements are zero-filled. x * element size must be a multiple
+// of 16 bytes.
+__device__ __forceinline__ void tensor_g2s_2d(void* dst, const CUtensorMap* tmap, int x, int y, uint64_t* bar,
+                                              uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
 

@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace bh {
@@ -23,6 +24,9 @@ enum Epilogue : int {
 };
 
 struct MatvecParams {
+    // one 2-D tensor map per weight segment: 8-byte elements, rows of
+    // nb*144 bytes, box = (row_stride/8) x MV_ROWS (filled in by the planner)
+    CUtensorMap tmap[3];
     const uint8_t* w[3];   // up to three row segments of one virtual weight matrix
     int64_t seg_end[3];    // cumulative row ends of the segments; seg_end[2] == N
     int64_t N;
@@ -37,8 +41,10 @@ struct MatvecParams {
     float* cand_val;       // EPI_ARGMAX: [gridDim][B] per-CTA maxima
     int32_t* cand_idx;     // EPI_ARGMAX: [gridDim][B] first index of the maxima
     int* status;           // device status word
+    int64_t* trace;        // timeline probe (builds with BH_TRACE only; else unused)
     // tiling, chosen on the host
-    int rows_per_tile;     // <= 32
+    int rows_per_tile;     // rows of one warp stage: 32 / tpr
+    int tpr;               // threads per row: 4 or 8
     int kc;                // super-blocks per pipeline stage
     int row_stride;        // shared-memory bytes per row of a stage
     int stage_bytes;
@@ -57,11 +63,11 @@ struct LaunchOpts {
 #endif
 constexpr int MV_WARPS = BH_MV_WARPS;       // every warp streams and computes its own rows
 constexpr int MV_THREADS = MV_WARPS * 32;
-constexpr int MV_ROWS = 8;                  // rows of one warp's stage ("oct"); 2 per thread
+constexpr int MV_ROWS = 8;                  // largest tile (rows of one warp stage); segment boundaries align to it
 constexpr int ACT_BLOCK_BYTES = 304;   // staged Q8_K block: 256 q8 + 16 (d) + 32 (S)
 
 // Fill tiling fields of p for the given grid; returns 0 or a negative errno.
-int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target);
+int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int tpr);
 int launch_matvec(const MatvecParams& p, int fold, int act_src, int epi, const LaunchOpts& o);
 
 int launch_q8k_quantize(const float* x, int64_t K, int B, uint8_t* out, int* status, cudaStream_t s);

@@ -99,80 +99,144 @@ __device__ __forceinline__ float block_max(float v, float* red) {
     return t;
 }
 
-__global__ void __launch_bounds__(256) attn_decode_kernel(const AttnParams a) {
+// One CTA of ATTN_THREADS per query head (head_dim 128: lane l of a warp
+// holds dims 4l..4l+3 of a row). Positions are dealt round-robin to the
+// warps; each warp reads whole K / V rows with one coalesced 512-byte load,
+// several rows in flight, and the per-warp partial outputs are combined in
+// warp order.
+constexpr int ATTN_THREADS = 256;
+constexpr int ATTN_WARPS = ATTN_THREADS / 32;
+constexpr int ATTN_HD = 128;
+
+__global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnParams a) {
     extern __shared__ float s_scores[];  // [n_ctx]
-    __shared__ float sq[256], sk[256], sv[256], red[8];
+    __shared__ float sq[ATTN_HD], sk[ATTN_HD], sv[ATTN_HD], red[ATTN_WARPS];
+    __shared__ float4 s_part[ATTN_WARPS][ATTN_HD / 4];
     pdl_trigger();
     pdl_wait();
-    const int h = blockIdx.x, d = threadIdx.x, HD = a.head_dim, half = HD / 2;
+    const int h = blockIdx.x, tid = threadIdx.x, HD = ATTN_HD, half = HD / 2;
     const int group = a.n_head / a.n_head_kv, g = h / group;
     const int q_dim = a.n_head * HD, kv_dim = a.n_head_kv * HD;
     const int pos = *a.pos;
+    const int lane = tid & 31, w = tid >> 5;
+    const int64_t row_stride = (int64_t)a.n_head_kv * HD;
+    const float* kbase = a.kc + (int64_t)g * HD;
+    const float* vbase = a.vc + (int64_t)g * HD;
 
-    float q = a.qkv[h * HD + d];
-    float k = a.qkv[q_dim + g * HD + d];
-    const float v = a.qkv[q_dim + kv_dim + g * HD + d];
-    // per-head RMSNorm of q and k (Qwen3 q_norm / k_norm)
+    // this head's q, k, v (threads 0..HD-1), per-head RMSNorm, NeoX RoPE
+    float q = 0.f, k = 0.f, v = 0.f;
+    if (tid < HD) {
+        q = a.qkv[h * HD + tid];
+        k = a.qkv[q_dim + g * HD + tid];
+        v = a.qkv[q_dim + kv_dim + g * HD + tid];
+    }
     const float sq_q = block_sum(__fmul_rn(q, q), red);
     const float sq_k = block_sum(__fmul_rn(k, k), red);
     const float rq = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq_q, (float)HD), a.eps)));
     const float rk = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq_k, (float)HD), a.eps)));
-    q = __fmul_rn(__fmul_rn(q, rq), a.q_norm[d]);
-    k = __fmul_rn(__fmul_rn(k, rk), a.k_norm[d]);
-    // NeoX rotary embedding: pairs (j, j + half), angle = pos * theta^(-2j/HD)
-    sq[d] = q;
-    sk[d] = k;
-    sv[d] = v;
-    __syncthreads();
-    const int j = d < half ? d : d - half;
-    const float inv_freq = (float)exp(-(2.0 * j / HD) * log((double)a.theta));
-    const float ang = (float)pos * inv_freq;
-    float sn, cs;
-    sincosf(ang, &sn, &cs);
-    float qr, kr;
-    if (d < half) {
-        qr = __fsub_rn(__fmul_rn(q, cs), __fmul_rn(sq[d + half], sn));
-        kr = __fsub_rn(__fmul_rn(k, cs), __fmul_rn(sk[d + half], sn));
-    } else {
-        qr = __fadd_rn(__fmul_rn(q, cs), __fmul_rn(sq[d - half], sn));
-        kr = __fadd_rn(__fmul_rn(k, cs), __fmul_rn(sk[d - half], sn));
+    if (tid < HD) {
+        q = __fmul_rn(__fmul_rn(q, rq), a.q_norm[tid]);
+        k = __fmul_rn(__fmul_rn(k, rk), a.k_norm[tid]);
+        sq[tid] = q;
+        sk[tid] = k;
+        sv[tid] = v;
     }
     __syncthreads();
-    sq[d] = qr;
-    sk[d] = kr;
-    if (h % group == 0) {
-        a.kc[((int64_t)pos * a.n_head_kv + g) * HD + d] = kr;
-        a.vc[((int64_t)pos * a.n_head_kv + g) * HD + d] = v;
+    float qr = 0.f, kr = 0.f;
+    if (tid < HD) {
+        const int j = tid < half ? tid : tid - half;
+        const float inv_freq = (float)exp(-(2.0 * j / HD) * log((double)a.theta));
+        const float ang = (float)pos * inv_freq;
+        float sn, cs;
+        sincosf(ang, &sn, &cs);
+        if (tid < half) {
+            qr = __fsub_rn(__fmul_rn(q, cs), __fmul_rn(sq[tid + half], sn));
+            kr = __fsub_rn(__fmul_rn(k, cs), __fmul_rn(sk[tid + half], sn));
+        } else {
+            qr = __fadd_rn(__fmul_rn(q, cs), __fmul_rn(sq[tid - half], sn));
+            kr = __fadd_rn(__fmul_rn(k, cs), __fmul_rn(sk[tid - half], sn));
+        }
     }
     __syncthreads();
-    // scores: warp w takes positions w, w + nwarps, ...; lanes stride the dims
-    const int lane = d & 31, w = d >> 5, nw = blockDim.x >> 5;
+    if (tid < HD) {
+        sq[tid] = qr;
+        sk[tid] = kr;
+        if (h % group == 0) {
+            a.kc[(int64_t)pos * row_stride + g * HD + tid] = kr;
+            a.vc[(int64_t)pos * row_stride + g * HD + tid] = v;
+        }
+    }
+    __syncthreads();
+    // scores: warp w takes positions w, w + ATTN_WARPS, ...; this token's own
+    // K comes from shared memory
+    const float4 q4 = reinterpret_cast<const float4*>(sq)[lane];
     const float scale = __fdiv_rn(1.f, __fsqrt_rn((float)HD));
-    for (int t = w; t <= pos; t += nw) {
-        const float* kt = (t == pos) ? sk : a.kc + ((int64_t)t * a.n_head_kv + g) * HD;
-        float dot = 0.f;
-        for (int e = lane; e < HD; e += 32) dot = __fadd_rn(dot, __fmul_rn(sq[e], kt[e]));
+    constexpr int U = 4;
+    for (int t0 = w; t0 <= pos; t0 += ATTN_WARPS * U) {
+        float4 kv[U];
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) dot = __fadd_rn(dot, __shfl_xor_sync(0xffffffffu, dot, off));
-        if (lane == 0) s_scores[t] = __fmul_rn(dot, scale);
+        for (int u = 0; u < U; ++u) {
+            const int t = t0 + u * ATTN_WARPS;
+            kv[u] = t > pos ? make_float4(0.f, 0.f, 0.f, 0.f)
+                    : (t == pos ? reinterpret_cast<const float4*>(sk)[lane]
+                                : reinterpret_cast<const float4*>(kbase + (int64_t)t * row_stride)[lane]);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int t = t0 + u * ATTN_WARPS;
+            float dot = __fadd_rn(__fadd_rn(__fmul_rn(q4.x, kv[u].x), __fmul_rn(q4.y, kv[u].y)),
+                                  __fadd_rn(__fmul_rn(q4.z, kv[u].z), __fmul_rn(q4.w, kv[u].w)));
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) dot = __fadd_rn(dot, __shfl_xor_sync(0xffffffffu, dot, off));
+            if (lane == 0 && t <= pos) s_scores[t] = __fmul_rn(dot, scale);
+        }
     }
     __syncthreads();
     float mx = -INFINITY;
-    for (int t = d; t <= pos; t += blockDim.x) mx = fmaxf(mx, s_scores[t]);
+    for (int t = tid; t <= pos; t += ATTN_THREADS) mx = fmaxf(mx, s_scores[t]);
     mx = block_max(mx, red);
     float se = 0.f;
-    for (int t = d; t <= pos; t += blockDim.x) {
+    for (int t = tid; t <= pos; t += ATTN_THREADS) {
         const float e = expf(__fsub_rn(s_scores[t], mx));
         s_scores[t] = e;
         se = __fadd_rn(se, e);
     }
-    se = block_sum(se, red);  // (contains the barrier that publishes s_scores)
-    float o = 0.f;
-    for (int t = 0; t <= pos; ++t) {
-        const float vt = (t == pos) ? sv[d] : a.vc[((int64_t)t * a.n_head_kv + g) * HD + d];
-        o = __fadd_rn(o, __fmul_rn(s_scores[t], vt));
+    se = block_sum(se, red);  // (its barrier publishes s_scores)
+    // weighted V: warp w accumulates its positions for dims 4*lane..4*lane+3
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int t0 = w; t0 <= pos; t0 += ATTN_WARPS * U) {
+        float4 vv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int t = t0 + u * ATTN_WARPS;
+            vv[u] = t > pos ? make_float4(0.f, 0.f, 0.f, 0.f)
+                    : (t == pos ? reinterpret_cast<const float4*>(sv)[lane]
+                                : reinterpret_cast<const float4*>(vbase + (int64_t)t * row_stride)[lane]);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int t = t0 + u * ATTN_WARPS;
+            const float p = t <= pos ? s_scores[t] : 0.f;
+            o.x = __fadd_rn(o.x, __fmul_rn(p, vv[u].x));
+            o.y = __fadd_rn(o.y, __fmul_rn(p, vv[u].y));
+            o.z = __fadd_rn(o.z, __fmul_rn(p, vv[u].z));
+            o.w = __fadd_rn(o.w, __fmul_rn(p, vv[u].w));
+        }
     }
-    a.out[h * HD + d] = __fdiv_rn(o, se);
+    s_part[w][lane] = o;
+    __syncthreads();
+    if (tid < HD / 4) {
+        float4 r = s_part[0][tid];
+        for (int i = 1; i < ATTN_WARPS; ++i) {
+            const float4 pi = s_part[i][tid];
+            r.x = __fadd_rn(r.x, pi.x);
+            r.y = __fadd_rn(r.y, pi.y);
+            r.z = __fadd_rn(r.z, pi.z);
+            r.w = __fadd_rn(r.w, pi.w);
+        }
+        float4 res = make_float4(__fdiv_rn(r.x, se), __fdiv_rn(r.y, se), __fdiv_rn(r.z, se), __fdiv_rn(r.w, se));
+        reinterpret_cast<float4*>(a.out + h * HD)[tid] = res;
+    }
 }
 
 }  // namespace bh
@@ -210,7 +274,7 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 int check_cfg(const bh_stack_config* c) {
     if (!c) return BH_EINVAL;
     if (c->n_layer < 1 || c->n_embd < 256 || c->n_embd % 256 || c->n_ff < 256 || c->n_ff % 256) return BH_EINVAL;
-    if (c->head_dim < 64 || c->head_dim > 256 || c->head_dim % 64) return BH_EINVAL;
+    if (c->head_dim != bh::ATTN_HD) return BH_EINVAL;  // the attention kernel is written for 128
     if (c->n_head < 1 || c->n_head_kv < 1 || c->n_head % c->n_head_kv) return BH_EINVAL;
     if ((c->n_head * c->head_dim) % 256 || c->n_vocab < 1 || c->n_ctx < 1 || c->n_ctx > 8192) return BH_EINVAL;
     return BH_OK;
@@ -286,7 +350,7 @@ int enqueue_step(bh_stack* st) {
         {
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3((unsigned)c.n_head);
-            cfg.blockDim = dim3((unsigned)c.head_dim);
+            cfg.blockDim = dim3((unsigned)bh::ATTN_THREADS);
             cfg.dynamicSmemBytes = sizeof(float) * (size_t)c.n_ctx;
             cfg.stream = st->stream;
             cudaLaunchAttribute at[1];

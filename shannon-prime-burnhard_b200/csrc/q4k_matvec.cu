@@ -28,11 +28,30 @@
 
 namespace bh {
 
-__device__ __forceinline__ const uint8_t* seg_row(const MatvecParams& p, int64_t row) {
-    const int64_t rowb = (int64_t)p.nb * Q4K_BYTES;
-    if (row < p.seg_end[0]) return p.w[0] + row * rowb;
-    if (row < p.seg_end[1]) return p.w[1] + (row - p.seg_end[0]) * rowb;
-    return p.w[2] + (row - p.seg_end[1]) * rowb;
+// Timeline probe: with BH_TRACE defined, lane 0 of every warp records the
+// global timer (ns) at a few points of the kernel into p.trace.
+#ifdef BH_TRACE
+#define BH_TRACE_AT(k)                                                                                  \
+    do {                                                                                                \
+        if (p.trace && (threadIdx.x & 31) == 0) {                                                        \
+            uint64_t t_;                                                                                \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                      \
+            p.trace[((int64_t)blockIdx.x * MV_WARPS + (threadIdx.x >> 5)) * 8 + (k)] = (int64_t)t_;     \
+        }                                                                                               \
+    } while (0)
+#else
+#define BH_TRACE_AT(k) \
+    do {               \
+    } while (0)
+#endif
+
+// Segment holding virtual row `row` (segment boundaries are multiples of 8,
+// so an oct never straddles two) and the row's index within it.
+__device__ __forceinline__ int seg_of(const MatvecParams& p, int64_t row, int64_t& local) {
+    if (row < p.seg_end[0]) { local = row; return 0; }
+    if (row < p.seg_end[1]) { local = row - p.seg_end[0]; return 1; }
+    local = row - p.seg_end[1];
+    return 2;
 }
 
 // ---------------------------------------------------------------------------
@@ -42,31 +61,49 @@ template <int FOLD, int SRC>
 __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* red, int ctid) {
     const int warp = ctid >> 5, lane = ctid & 31;
     const int nblk = p.B * p.nb;
+    // Each warp stages blocks warp, warp+W, ...; U blocks at a time with all
+    // their global loads issued before any is used, so the latency of the
+    // (just produced, L2-resident) activations is paid once per U blocks.
+    constexpr int U = 4;
     if (SRC == ACT_Q8K) {
-        for (int blk = warp; blk < nblk; blk += MV_WARPS) {
-            const uint8_t* src = p.xq + (int64_t)blk * Q8K_BYTES;
-            uint8_t* dst = act + blk * ACT_BLOCK_BYTES;
-            const uint32_t* qw = reinterpret_cast<const uint32_t*>(src + 4);
-            if (FOLD == BH_FOLD_X86) {
+        for (int blk0 = warp; blk0 < nblk; blk0 += MV_WARPS * U) {
+            uint32_t w0[U], w1[U], bw[U];
+            float dv[U];
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int wi = 2 * lane + h;
-                    *reinterpret_cast<uint32_t*>(dst + staged_byte_offset<FOLD>(4 * wi)) = qw[wi];
-                }
-            } else {
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int wi = 2 * lane + h;
-                    const uint32_t w = qw[wi];
-#pragma unroll
-                    for (int b = 0; b < 4; ++b) dst[staged_byte_offset<FOLD>(4 * wi + b)] = (uint8_t)(w >> (8 * b));
+            for (int u = 0; u < U; ++u) {
+                const int blk = blk0 + u * MV_WARPS;
+                w0[u] = w1[u] = bw[u] = 0;
+                dv[u] = 0.f;
+                if (blk < nblk) {
+                    const uint8_t* src = p.xq + (int64_t)blk * Q8K_BYTES;
+                    const uint32_t* qw = reinterpret_cast<const uint32_t*>(src + 4);
+                    w0[u] = qw[2 * lane];
+                    w1[u] = qw[2 * lane + 1];
+                    if (lane == 0) dv[u] = *reinterpret_cast<const float*>(src);
+                    if (lane < 8) bw[u] = *reinterpret_cast<const uint32_t*>(src + 260 + 4 * lane);
                 }
             }
-            if (lane == 0) *reinterpret_cast<float*>(dst + 256) = *reinterpret_cast<const float*>(src);
-            if (lane < 8) {
-                const uint32_t bw = *reinterpret_cast<const uint32_t*>(src + 260 + 4 * lane);
-                const int s = (int)(int16_t)(bw & 0xffffu) + (int)(int16_t)(bw >> 16);
-                reinterpret_cast<int16_t*>(dst + 272)[lane] = (int16_t)s;
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int blk = blk0 + u * MV_WARPS;
+                if (blk >= nblk) break;
+                uint8_t* dst = act + blk * ACT_BLOCK_BYTES;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int wi = 2 * lane + h;
+                    const uint32_t w = h ? w1[u] : w0[u];
+                    if (FOLD == BH_FOLD_X86) {
+                        *reinterpret_cast<uint32_t*>(dst + staged_byte_offset<FOLD>(4 * wi)) = w;
+                    } else {
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) dst[staged_byte_offset<FOLD>(4 * wi + b)] = (uint8_t)(w >> (8 * b));
+                    }
+                }
+                if (lane == 0) *reinterpret_cast<float*>(dst + 256) = dv[u];
+                if (lane < 8) {
+                    const int s = (int)(int16_t)(bw[u] & 0xffffu) + (int)(int16_t)(bw[u] >> 16);
+                    reinterpret_cast<int16_t*>(dst + 272)[lane] = (int16_t)s;
+                }
             }
         }
         return;
@@ -78,6 +115,7 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
         for (int b = 0; b < p.B; ++b) {
             const float* h = p.xf + (int64_t)b * p.K;
             float ss = 0.f;
+#pragma unroll 4
             for (int i = ctid; i < p.K; i += MV_WARPS * 32) ss = __fadd_rn(ss, __fmul_rn(h[i], h[i]));
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
@@ -92,58 +130,73 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
             named_bar(1, MV_WARPS * 32);
         }
     }
-    for (int blk = warp; blk < nblk; blk += MV_WARPS) {
-        const int b = blk / p.nb, i = blk - b * p.nb;
-        const int e0 = i * QK + 8 * lane;
-        float v[8];
-        if (SRC == ACT_F32_SWIGLU) {
-            const float* g = p.xf + (int64_t)b * 2 * p.K + e0;
-            const float* u = g + p.K;
-            const float4 g0 = *reinterpret_cast<const float4*>(g), g1 = *reinterpret_cast<const float4*>(g + 4);
-            const float4 u0 = *reinterpret_cast<const float4*>(u), u1 = *reinterpret_cast<const float4*>(u + 4);
-            const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-            const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+    constexpr int UF = 2;
+    for (int blk0 = warp; blk0 < nblk; blk0 += MV_WARPS * UF) {
+        float v[UF][8], aux[UF][8];
 #pragma unroll
-            for (int t = 0; t < 8; ++t) {
-                const float sg = __fdiv_rn(gv[t], __fadd_rn(1.f, expf(-gv[t])));
-                v[t] = __fmul_rn(sg, uv[t]);
-            }
-        } else {
-            const float* x = p.xf + (int64_t)b * p.K + e0;
-            const float4 a0 = *reinterpret_cast<const float4*>(x), a1 = *reinterpret_cast<const float4*>(x + 4);
-            v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w;
-            v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
-            if (SRC == ACT_F32_RMSNORM) {
-                const float sc = s_scale[b];
-                const float4 c0 = *reinterpret_cast<const float4*>(p.gamma + e0);
-                const float4 c1 = *reinterpret_cast<const float4*>(p.gamma + e0 + 4);
-                const float gm[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+        for (int u = 0; u < UF; ++u) {
+            const int blk = blk0 + u * MV_WARPS;
+            const int b = blk / p.nb, i = blk - b * p.nb;
+            const int e0 = i * QK + 8 * lane;
 #pragma unroll
-                for (int t = 0; t < 8; ++t) v[t] = __fmul_rn(__fmul_rn(v[t], sc), gm[t]);
+            for (int t = 0; t < 8; ++t) { v[u][t] = 0.f; aux[u][t] = 0.f; }
+            if (blk < nblk) {
+                const float* x = SRC == ACT_F32_SWIGLU ? p.xf + (int64_t)b * 2 * p.K + e0 : p.xf + (int64_t)b * p.K + e0;
+                const float4 a0 = *reinterpret_cast<const float4*>(x), a1 = *reinterpret_cast<const float4*>(x + 4);
+                v[u][0] = a0.x; v[u][1] = a0.y; v[u][2] = a0.z; v[u][3] = a0.w;
+                v[u][4] = a1.x; v[u][5] = a1.y; v[u][6] = a1.z; v[u][7] = a1.w;
+                if (SRC == ACT_F32_SWIGLU || SRC == ACT_F32_RMSNORM) {
+                    const float* y = SRC == ACT_F32_SWIGLU ? x + p.K : p.gamma + e0;
+                    const float4 c0 = *reinterpret_cast<const float4*>(y), c1 = *reinterpret_cast<const float4*>(y + 4);
+                    aux[u][0] = c0.x; aux[u][1] = c0.y; aux[u][2] = c0.z; aux[u][3] = c0.w;
+                    aux[u][4] = c1.x; aux[u][5] = c1.y; aux[u][6] = c1.z; aux[u][7] = c1.w;
+                }
             }
         }
-        const Q8Block qb = q8k_quantize_warp(v, lane);
-        uint8_t* dst = act + blk * ACT_BLOCK_BYTES;
-        stage_codes<FOLD>(dst, qb.q, lane);
-        stage_scalars(dst, qb.d, qb.bsum16, lane);
+#pragma unroll
+        for (int u = 0; u < UF; ++u) {
+            const int blk = blk0 + u * MV_WARPS;
+            if (blk >= nblk) break;  // warp-uniform
+            const int b = blk / p.nb;
+            float x[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                if (SRC == ACT_F32_SWIGLU) {
+                    // silu(gate) * up
+                    const float g = v[u][t];
+                    x[t] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), aux[u][t]);
+                } else if (SRC == ACT_F32_RMSNORM) {
+                    x[t] = __fmul_rn(__fmul_rn(v[u][t], s_scale[b]), aux[u][t]);
+                } else {
+                    x[t] = v[u][t];
+                }
+            }
+            const Q8Block qb = q8k_quantize_warp(x, lane);
+            uint8_t* dst = act + blk * ACT_BLOCK_BYTES;
+            stage_codes<FOLD>(dst, qb.q, lane);
+            stage_scalars(dst, qb.d, qb.bsum16, lane);
+        }
     }
 }
 
 // ---------------------------------------------------------------------------
-// per-super-block work of one thread (two reference lanes of one row)
+// per-super-block work of one thread
 // ---------------------------------------------------------------------------
-// Thread t (0..3) of a row owns reference lanes 2t and 2t+1. Row side of
-// one super-block: the two fp16 scales, the packed 6-bit scales/mins, and
-// the low/high-nibble code words of both lanes.
+// TPR threads work one row (TPR = 4: thread t owns reference lanes 2t, 2t+1;
+// TPR = 8: thread t owns lane t); every thread also computes min lane t & 3
+// (threads 4..7 of a TPR = 8 row repeat 0..3 and are not summed).
+template <int TPR>
 struct RowBlk {
+    static constexpr int L = 8 / TPR;  // reference lanes per thread
     float fd, fdm;
-    uint32_t sc03, sc47, mnk;   // mnk: the two mins of min lane k = t in bytes 0..1
-    uint32_t lo[2][4], hi[2][4];
+    uint32_t sc03, sc47, mnk;          // mnk: the two mins of min lane t & 3 in bytes 0..1
+    uint32_t lo[L][4], hi[L][4];
 };
 
-template <int FOLD>
-__device__ __forceinline__ RowBlk decode_row(const uint8_t* blk, int t) {
-    RowBlk r;
+template <int FOLD, int TPR>
+__device__ __forceinline__ RowBlk<TPR> decode_row(const uint8_t* blk, int t) {
+    constexpr int L = RowBlk<TPR>::L;
+    RowBlk<TPR> r;
     const uint4 h = *reinterpret_cast<const uint4*>(blk);
     r.fd = h2f((uint16_t)(h.x & 0xffffu));
     r.fdm = h2f((uint16_t)(h.x >> 16));
@@ -152,29 +205,38 @@ __device__ __forceinline__ RowBlk decode_row(const uint8_t* blk, int t) {
     // j>=4: sc = (q[j+4] & 15) | (q[j-4] >> 6) << 4, mn = (q[j+4] >> 4) | (q[j] >> 6) << 4
     r.sc03 = h.y & 0x3f3f3f3fu;
     r.sc47 = (h.w & 0x0f0f0f0fu) | ((h.y >> 2) & 0x30303030u);
-    const uint32_t mn = (t & 2) ? (((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u)) : (h.z & 0x3f3f3f3fu);
-    r.mnk = mn >> ((t & 1) * 16);
+    const int k = t & 3;
+    const uint32_t mn = (k & 2) ? (((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u)) : (h.z & 0x3f3f3f3fu);
+    r.mnk = mn >> ((k & 1) * 16);
     const uint32_t* qs = reinterpret_cast<const uint32_t*>(blk + 16);
     if (FOLD == BH_FOLD_X86) {
-        // lane m = bytes 4m..4m+3 of each 32-byte group: words 2t, 2t+1
+        // lane m = bytes 4m..4m+3 of each 32-byte group: word m
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-            const uint2 w = *reinterpret_cast<const uint2*>(qs + 8 * g + 2 * t);
-            r.lo[0][g] = w.x & 0x0f0f0f0fu;
-            r.hi[0][g] = (w.x >> 4) & 0x0f0f0f0fu;
-            r.lo[1][g] = w.y & 0x0f0f0f0fu;
-            r.hi[1][g] = (w.y >> 4) & 0x0f0f0f0fu;
+            uint32_t w[L];
+            if (L == 2) {
+                const uint2 w2 = *reinterpret_cast<const uint2*>(qs + 8 * g + 2 * t);
+                w[0] = w2.x;
+                w[L - 1] = w2.y;
+            } else {
+                w[0] = qs[8 * g + t];
+            }
+#pragma unroll
+            for (int e = 0; e < L; ++e) {
+                r.lo[e][g] = w[e] & 0x0f0f0f0fu;
+                r.hi[e][g] = (w[e] >> 4) & 0x0f0f0f0fu;
+            }
         }
     } else {
-        // lane l = group bytes l, l+8, l+16, l+24 (a byte gather); lanes 2t and
-        // 2t+1 sit in the same words k0 = t/2 + {0,2,4,6}, bytes tb and tb+1
-        const int k0 = t >> 1, tb = (2 * t) & 3;
+        // lane l = group bytes l, l+8, l+16, l+24: a byte gather from words
+        // l/4 + {0,2,4,6} (the lanes of one thread share those words)
+        const int l0 = t * L, k0 = l0 >> 2, tb = l0 & 3;
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
             const uint32_t* gw = qs + 8 * g;
             const uint32_t w0 = gw[k0], w1 = gw[k0 + 2], w2 = gw[k0 + 4], w3 = gw[k0 + 6];
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
+            for (int e = 0; e < L; ++e) {
                 const uint32_t sel = (uint32_t)((tb + e) | ((tb + e + 4) << 4));
                 const uint32_t tw = __byte_perm(__byte_perm(w0, w1, sel), __byte_perm(w2, w3, sel), 0x5410);
                 r.lo[e][g] = tw & 0x0f0f0f0fu;
@@ -205,82 +267,98 @@ __device__ __forceinline__ int lane_sum(const uint32_t (&lo)[4], const uint32_t 
     return __dp2a_hi((int)__byte_perm((uint32_t)d6, (uint32_t)d7, 0x5410), (int)sc47, s);
 }
 
+// Sum over the 4 min lanes held by threads t & 3 = 0..3 of a row (exact ints).
+template <int TPR>
+__device__ __forceinline__ int sum_min_lanes(int v) {
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    return v + __shfl_xor_sync(0xffffffffu, v, 2);
+}
+
 // One activation column applied to one decoded row block: the reference's
-// per-block fp32 step for this thread's two lanes and its min lane.
-template <int FOLD, bool PART>
-__device__ __forceinline__ void fold_block(const MatvecParams& p, const RowBlk& r, const uint8_t* A, int t,
-                                           int b, int i, int64_t row, bool live, float& acc0, float& acc1,
+// per-block fp32 step for this thread's lanes and its min lane.
+template <int FOLD, bool PART, int TPR>
+__device__ __forceinline__ void fold_block(const MatvecParams& p, const RowBlk<TPR>& r, const uint8_t* A, int t,
+                                           int b, int i, int64_t row, bool live, float (&acc)[8 / TPR],
                                            float& accm) {
-    const int4 a00 = *reinterpret_cast<const int4*>(A + 64 * t);
-    const int4 a01 = *reinterpret_cast<const int4*>(A + 64 * t + 16);
-    const int4 a10 = *reinterpret_cast<const int4*>(A + 64 * t + 32);
-    const int4 a11 = *reinterpret_cast<const int4*>(A + 64 * t + 48);
+    constexpr int L = RowBlk<TPR>::L;
     const float yd = *reinterpret_cast<const float*>(A + 256);
-    int sub0[8], sub1[8];
-    const int l0 = lane_sum(r.lo[0], r.hi[0], r.sc03, r.sc47, a00, a01, sub0, PART);
-    const int l1 = lane_sum(r.lo[1], r.hi[1], r.sc03, r.sc47, a10, a11, sub1, PART);
+    const int spk = reinterpret_cast<const int*>(A + 272)[t & 3];
+    int li[L];
+    int sub[L][8];
+#pragma unroll
+    for (int e = 0; e < L; ++e) {
+        const int4 a0 = *reinterpret_cast<const int4*>(A + 32 * (t * L + e));
+        const int4 a1 = *reinterpret_cast<const int4*>(A + 32 * (t * L + e) + 16);
+        li[e] = lane_sum(r.lo[e], r.hi[e], r.sc03, r.sc47, a0, a1, sub[e], PART);
+    }
+    const int mp = __dp2a_lo(spk, (int)r.mnk, 0);
     if (FOLD == BH_FOLD_X86) {
         // acc[m] = fma(y.d * fp16(d), sumi[m], acc[m]);
-        // accm[k] = fma(-y.d * fp16(dmin), min_{2k} S_{2k} + min_{2k+1} S_{2k+1}, accm[k]), k = t
+        // accm[k] = fma(-y.d * fp16(dmin), min_{2k} S_{2k} + min_{2k+1} S_{2k+1}, accm[k])
         const float d = __fmul_rn(yd, r.fd);
-        acc0 = __fmaf_rn(d, i2f_exact(l0), acc0);
-        acc1 = __fmaf_rn(d, i2f_exact(l1), acc1);
-        const int spk = reinterpret_cast<const int*>(A + 272)[t];
-        accm = __fmaf_rn(__fmul_rn(-yd, r.fdm), i2f_exact(__dp2a_lo(spk, (int)r.mnk, 0)), accm);
+#pragma unroll
+        for (int e = 0; e < L; ++e) acc[e] = __fmaf_rn(d, i2f_exact(li[e]), acc[e]);
+        accm = __fmaf_rn(__fmul_rn(-yd, r.fdm), i2f_exact(mp), accm);
     } else {
         // sums[l] += (fp16(d) * y.d) * aux[l];  sumf -= (fp16(dmin) * y.d) * sumi
         const float d = __fmul_rn(r.fd, yd);
-        acc0 = __fadd_rn(acc0, __fmul_rn(d, i2f_exact(l0)));
-        acc1 = __fadd_rn(acc1, __fmul_rn(d, i2f_exact(l1)));
-        // sumi = the four threads' min pairs (exact ints) summed in thread 0
-        const int spk = reinterpret_cast<const int*>(A + 272)[t];
-        int mp = __dp2a_lo(spk, (int)r.mnk, 0);
-        mp += __shfl_xor_sync(0xffffffffu, mp, 1);
-        mp += __shfl_xor_sync(0xffffffffu, mp, 2);
-        accm = __fsub_rn(accm, __fmul_rn(__fmul_rn(r.fdm, yd), i2f_exact(mp)));
+#pragma unroll
+        for (int e = 0; e < L; ++e) acc[e] = __fadd_rn(acc[e], __fmul_rn(d, i2f_exact(li[e])));
+        const int sumi = sum_min_lanes<TPR>(mp);
+        accm = __fsub_rn(accm, __fmul_rn(__fmul_rn(r.fdm, yd), i2f_exact(sumi)));
     }
     if (PART) {
-        int mp = __dp2a_lo(reinterpret_cast<const int*>(A + 272)[t], (int)r.mnk, 0);
-        mp += __shfl_xor_sync(0xffffffffu, mp, 1);
-        mp += __shfl_xor_sync(0xffffffffu, mp, 2);
+        const int msum = sum_min_lanes<TPR>(mp);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            int v = sub0[j] + sub1[j];
-            v += __shfl_xor_sync(0xffffffffu, v, 1);
-            v += __shfl_xor_sync(0xffffffffu, v, 2);
-            sub0[j] = v;
+            int v = 0;
+#pragma unroll
+            for (int e = 0; e < L; ++e) v += sub[e][j];
+#pragma unroll
+            for (int off = 1; off < TPR; off <<= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            sub[0][j] = v;
         }
         if (live && t == 0) {
             int32_t* o = p.partials + (((int64_t)b * p.N + row) * p.nb + i) * 9;
-            for (int j = 0; j < 8; ++j) o[j] = sub0[j];
-            o[8] = mp;
+            for (int j = 0; j < 8; ++j) o[j] = sub[0][j];
+            o[8] = msum;
         }
     }
 }
 
 // Per-row combine in the reference's order, then the epilogue.
-template <int FOLD, int EPI>
-__device__ __forceinline__ void finish_row(const MatvecParams& p, float acc0, float acc1, float accm, int rgrp,
+template <int FOLD, int EPI, int TPR>
+__device__ __forceinline__ void finish_row(const MatvecParams& p, const float (&acc)[8 / TPR], float accm, int rgrp,
                                            int t, int b, bool has_row, int64_t row, float& best_v, int& best_i) {
     const unsigned FULLM = 0xffffffffu;
     float v;
     if (FOLD == BH_FOLD_X86) {
-        // hsum_float_8 (arch/x86/quants.c:43-49): ((a4+a0)+(a6+a2)) + ((a5+a1)+(a7+a3));
-        // thread t holds lanes 2t (acc0) and 2t+1 (acc1)
-        const float x0 = __fadd_rn(acc0, __shfl_xor_sync(FULLM, acc0, 2));  // t0: a0+a4, t1: a2+a6
-        const float x1 = __fadd_rn(acc1, __shfl_xor_sync(FULLM, acc1, 2));  // t0: a1+a5, t1: a3+a7
-        const float y0 = __fadd_rn(x0, __shfl_xor_sync(FULLM, x0, 1));
-        const float y1 = __fadd_rn(x1, __shfl_xor_sync(FULLM, x1, 1));
-        const float hs = __fadd_rn(y0, y1);
+        // hsum_float_8 (arch/x86/quants.c:43-49): ((a4+a0)+(a6+a2)) + ((a5+a1)+(a7+a3))
+        float hs;
+        if (TPR == 4) {
+            // thread t holds lanes 2t (acc[0]) and 2t+1 (acc[1])
+            const float x0 = __fadd_rn(acc[0], __shfl_xor_sync(FULLM, acc[0], 2));  // t0: a0+a4, t1: a2+a6
+            const float x1 = __fadd_rn(acc[8 / TPR - 1], __shfl_xor_sync(FULLM, acc[8 / TPR - 1], 2));
+            const float y0 = __fadd_rn(x0, __shfl_xor_sync(FULLM, x0, 1));
+            const float y1 = __fadd_rn(x1, __shfl_xor_sync(FULLM, x1, 1));
+            hs = __fadd_rn(y0, y1);
+        } else {
+            // thread t holds lane t
+            const float t1 = __fadd_rn(acc[0], __shfl_xor_sync(FULLM, acc[0], 4));  // t0: a0+a4
+            const float t2 = __fadd_rn(t1, __shfl_xor_sync(FULLM, t1, 2));          // t0: (a0+a4)+(a2+a6)
+            hs = __fadd_rn(t2, __shfl_xor_sync(FULLM, t2, 1));
+        }
         // 4-lane min accumulator, lane k in thread k: (m0+m2) + (m1+m3)
         const float u = __fadd_rn(accm, __shfl_xor_sync(FULLM, accm, 2));
         const float hm = __fadd_rn(u, __shfl_xor_sync(FULLM, u, 1));
         v = __fadd_rn(hs, hm);
     } else {
         // sumf (the min chain) += sums[0..7] in order
+        constexpr int L = 8 / TPR;
         v = accm;
 #pragma unroll
-        for (int l = 0; l < 8; ++l) v = __fadd_rn(v, __shfl_sync(FULLM, (l & 1) ? acc1 : acc0, (rgrp << 2) + (l >> 1)));
+        for (int l = 0; l < 8; ++l)
+            v = __fadd_rn(v, __shfl_sync(FULLM, acc[l % L], rgrp * TPR + l / L));
     }
     if (has_row && t == 0) {
         float* yp = p.y + (int64_t)b * p.ldy + row;
@@ -293,31 +371,38 @@ __device__ __forceinline__ void finish_row(const MatvecParams& p, float acc0, fl
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-// Each warp owns "octs" of 8 consecutive rows (oct w, w+8, ... of the CTA's
-// row range) and runs its own ring of `stages` stages: a stage is the next kc
-// super-blocks of the oct's 8 rows, one bulk copy per row issued by lanes
-// 0..7 and counted on the stage's mbarrier. Thread (r, t) works row r of the
-// oct as reference lanes 2t and 2t+1 (and min lane t). The warp both fills
-// and drains its ring: no cross-warp handshake, and eight warps issue copies
-// in parallel.
-template <int FOLD, int NB, int SRC, int EPI, bool PART>
-__global__ void __launch_bounds__(MV_THREADS, 1) q4k_matvec_kernel(const MatvecParams p) {
+// Work is dealt in tiles of R = 32 / TPR consecutive rows of the CTA's
+// range: warp w takes tiles w, w+8, ... and streams them through its own
+// ring of `stages` stages. A stage is the next kc super-blocks of the
+// tile's R rows, one 2-D tensor copy (box = R rows x row_stride bytes,
+// rows padded so reads are bank-conflict free) issued by lane 0 and counted
+// on the stage's mbarrier; the warp both fills and drains its ring (no
+// cross-warp handshake). Thread (r, t) works row r of the tile; its fp32
+// fold runs in registers as the blocks stream by.
+template <int FOLD, int NB, int SRC, int EPI, bool PART, int TPR>
+__global__ void __launch_bounds__(MV_THREADS, 1) q4k_matvec_kernel(const __grid_constant__ MatvecParams p) {
+    constexpr int R = 32 / TPR;
+    constexpr int L = 8 / TPR;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float s_red[MV_WARPS * 2];
     __shared__ int s_redi[MV_WARPS];
+    BH_TRACE_AT(0);
 
     uint8_t* act = smem + p.act_off;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint8_t* ring = smem + p.ring_off + (size_t)warp * p.stages * p.stage_bytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off) + warp * p.stages;
 
-    const int64_t r_begin = p.N * blockIdx.x / gridDim.x;
-    const int64_t r_end = p.N * (blockIdx.x + 1) / gridDim.x;
+    // CTA ranges are whole tiles of the virtual matrix
+    const int64_t ntile_all = (p.N + R - 1) / R;
+    const int64_t r_begin = R * (ntile_all * blockIdx.x / gridDim.x);
+    const int64_t r_end_t = R * (ntile_all * (blockIdx.x + 1) / gridDim.x);
+    const int64_t r_end = r_end_t < p.N ? r_end_t : p.N;
     const int nrows = (int)(r_end - r_begin);
-    const int nocts = (nrows + MV_ROWS - 1) / MV_ROWS;
-    const int my_octs = warp < nocts ? (nocts - 1 - warp) / MV_WARPS + 1 : 0;
+    const int ntiles = (nrows + R - 1) / R;
+    const int my_tiles = warp < ntiles ? (ntiles - 1 - warp) / MV_WARPS + 1 : 0;
     const int nkc = (p.nb + p.kc - 1) / p.kc;
-    const int total = my_octs * nkc;  // this warp's stage sequence
+    const int total = my_tiles * nkc;
     const unsigned FULLM = 0xffffffffu;
 
     if (lane == 0) {
@@ -327,33 +412,35 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_matvec_kernel(const MatvecP
     __syncwarp();
 
     const uint64_t pol = policy_evict_first();
-    // issue cursor: next (oct, chunk, stage) to fill; advanced without divisions
-    int i_od = 0, i_c = 0, i_s = 0, issued = 0;
+    // issue cursor: (tile, chunk, stage), advanced without divisions; one
+    // tensor-map box per stage (bytes past a row's end and rows past the
+    // matrix are zero-filled and never used)
+    int i_j = 0, i_c = 0, i_s = 0, issued = 0;
     auto issue_next = [&]() {
-        const int r0 = (warp + i_od * MV_WARPS) * MV_ROWS;
-        const int rq = min(MV_ROWS, nrows - r0);
-        const int kl = min(p.kc, p.nb - i_c * p.kc);
-        const uint32_t bytes = (uint32_t)kl * Q4K_BYTES;
-        if (lane == 0) mbar_arrive_expect_tx(&full[i_s], bytes * (uint32_t)rq);
-        __syncwarp();
-        if (lane < rq) {
-            const uint8_t* src = seg_row(p, r_begin + r0 + lane) + (size_t)i_c * p.kc * Q4K_BYTES;
-            bulk_g2s(ring + (size_t)i_s * p.stage_bytes + (size_t)lane * p.row_stride, src, bytes, &full[i_s], pol);
+        if (lane == 0) {
+            int64_t local;
+            const int sg = seg_of(p, r_begin + (int64_t)(warp + i_j * MV_WARPS) * R, local);
+            mbar_arrive_expect_tx(&full[i_s], (uint32_t)p.stage_bytes);
+            tensor_g2s_2d(ring + (size_t)i_s * p.stage_bytes, &p.tmap[sg], i_c * p.kc * (Q4K_BYTES / 8), (int)local,
+                          &full[i_s], pol);
         }
+        __syncwarp();
         ++issued;
-        if (++i_c == nkc) { i_c = 0; ++i_od; }
+        if (++i_c == nkc) { i_c = 0; ++i_j; }
         if (++i_s == p.stages) i_s = 0;
     };
     // weights do not depend on the previous kernel: start streaming now
     const int prefill = min(p.stages, total);
     for (int q = 0; q < prefill; ++q) issue_next();
+    BH_TRACE_AT(1);
     pdl_trigger();
     pdl_wait();
     stage_activations<FOLD, SRC>(p, act, s_red, threadIdx.x);
     __syncthreads();
+    BH_TRACE_AT(2);
 
-    const int rgrp = lane >> 2;  // row of the oct worked by this thread
-    const int t = lane & 3;      // owns reference lanes 2t, 2t+1
+    const int rgrp = lane / TPR;  // row of the tile worked by this thread
+    const int t = lane % TPR;
 
     float best_v[NB];
     int best_i[NB];
@@ -363,32 +450,38 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_matvec_kernel(const MatvecP
     int consumed = 0, c_s = 0;
     uint32_t c_ph = 0;
     bool ok = true;
-    for (int od = 0; od < my_octs && ok; ++od) {
-        const int rin = (warp + od * MV_WARPS) * MV_ROWS + rgrp;
+    for (int j = 0; j < my_tiles && ok; ++j) {
+        const int rin = (warp + j * MV_WARPS) * R + rgrp;
         const bool live = rin < nrows;
-        float acc0[NB], acc1[NB], accm[NB];
+        float acc[NB][L], accm[NB];
 #pragma unroll
-        for (int b = 0; b < NB; ++b) { acc0[b] = 0.f; acc1[b] = 0.f; accm[b] = 0.f; }
-
+        for (int b = 0; b < NB; ++b) {
+#pragma unroll
+            for (int e = 0; e < L; ++e) acc[b][e] = 0.f;
+            accm[b] = 0.f;
+        }
         for (int c = 0; c < nkc; ++c) {
             if (!__all_sync(FULLM, mbar_wait_bounded(&full[c_s], c_ph))) {
                 ok = false;
                 if (lane == 0) set_status(p.status, ST_TIMEOUT);
                 break;
             }
+#ifdef BH_TRACE
+            if (consumed == 0) BH_TRACE_AT(3);
+#endif
             ++consumed;
-            const int kl = min(p.kc, p.nb - c * p.kc);
-            // rows past the end of the range read stale (in-bounds) stage bytes
-            // and are never stored
+            const int sbc = c * p.kc;
+            const int kl = min(p.kc, p.nb - sbc);
+            // rows past the end of the range read zero-filled stage bytes and are never stored
             const uint8_t* rowp = ring + (size_t)c_s * p.stage_bytes + (size_t)rgrp * p.row_stride;
-            const uint8_t* actc = act + c * p.kc * ACT_BLOCK_BYTES;
+            const uint8_t* actc = act + sbc * ACT_BLOCK_BYTES;
 #pragma unroll 2
             for (int kb = 0; kb < kl; ++kb) {
-                const RowBlk r = decode_row<FOLD>(rowp + kb * Q4K_BYTES, t);
+                const RowBlk<TPR> r = decode_row<FOLD, TPR>(rowp + kb * Q4K_BYTES, t);
 #pragma unroll
                 for (int b = 0; b < NB; ++b)
-                    fold_block<FOLD, PART>(p, r, actc + (b * p.nb + kb) * ACT_BLOCK_BYTES, t, b, c * p.kc + kb,
-                                           r_begin + rin, live, acc0[b], acc1[b], accm[b]);
+                    fold_block<FOLD, PART, TPR>(p, r, actc + (b * p.nb + kb) * ACT_BLOCK_BYTES, t, b, sbc + kb,
+                                                r_begin + rin, live, acc[b], accm[b]);
             }
             __syncwarp();
             if (issued < total) {
@@ -398,10 +491,12 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_matvec_kernel(const MatvecP
             if (++c_s == p.stages) { c_s = 0; c_ph ^= 1u; }
         }
         if (!ok) break;
+        BH_TRACE_AT(4);
 #pragma unroll
         for (int b = 0; b < NB; ++b)
-            finish_row<FOLD, EPI>(p, acc0[b], acc1[b], accm[b], rgrp, t, b, live, r_begin + rin, best_v[b], best_i[b]);
+            finish_row<FOLD, EPI, TPR>(p, acc[b], accm[b], rgrp, t, b, live, r_begin + rin, best_v[b], best_i[b]);
     }
+    BH_TRACE_AT(6);
     if (!ok && lane == 0) {
         // nothing of this warp may still be in flight when the CTA exits
         int s = c_s;
@@ -438,46 +533,49 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_matvec_kernel(const MatvecP
         }
     }
 }
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-// Pick kc (super-blocks per row per stage) as large as the shared-memory
-// budget allows with at least 4 stages per warp ring (bulk copies of a few
-// hundred bytes or more keep the copy engine efficient), capped by the
-// per-row copy target.
-int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target) {
-    if (grid < 1) return BH_EINVAL;
+// Plan one launch: R = 32 / tpr rows per stage, kc super-blocks per row per
+// stage (from the copy target, shrunk until 2 stages fit; box rows stay
+// within 2048 bytes), stages <= 4.
+int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int tpr) {
+    if (grid < 1 || (tpr != 4 && tpr != 8)) return BH_EINVAL;
+    const int R = 32 / tpr;
     const int act_bytes = p.B * p.nb * ACT_BLOCK_BYTES;
     const int ring_off = (act_bytes + 127) / 128 * 128;
     int kc = stage_target / Q4K_BYTES;
     if (kc < 1) kc = 1;
+    if (kc > 13) kc = 13;  // box rows of at most 2048 bytes (256 eight-byte elements)
     if (kc > p.nb) kc = p.nb;
-    for (;; --kc) {
+    for (; kc >= 1; --kc) {
         const int words = kc * (Q4K_BYTES / 4);
         const int padw = ((8 - (words % 32)) % 32 + 32) % 32;  // row stride == 8 words (mod 32 banks)
         const int stride = kc * Q4K_BYTES + 4 * padw;
-        const int stage = MV_ROWS * stride;
-        int stages = (smem_cap - ring_off - 256) / (MV_WARPS * (stage + 8));
+        const int stage = R * stride;
+        const int avail = smem_cap - ring_off - 256 - 128;
+        int stages = avail > 0 ? avail / (MV_WARPS * (stage + 8)) : 0;
         if (stages > 4) stages = 4;
-        if (stages >= 2) {
-            p.kc = kc;
-            p.row_stride = stride;
-            p.stage_bytes = stage;
-            p.stages = stages;
-            p.rows_per_tile = MV_ROWS;
-            p.act_off = 0;
-            p.ring_off = ring_off;
-            p.bar_off = ring_off + MV_WARPS * stages * stage;
-            p.smem_bytes = p.bar_off + MV_WARPS * stages * 8;
-            return BH_OK;
-        }
-        if (kc == 1) return BH_EINVAL;  // activations too large for shared memory
+        if (stages < 2) continue;
+        p.kc = kc;
+        p.row_stride = stride;
+        p.stage_bytes = stage;
+        p.stages = stages;
+        p.rows_per_tile = R;
+        p.tpr = tpr;
+        p.act_off = 0;
+        p.ring_off = ring_off;
+        p.bar_off = ring_off + MV_WARPS * stages * stage;
+        p.smem_bytes = p.bar_off + MV_WARPS * stages * 8;
+        return BH_OK;
     }
+    return BH_EINVAL;  // activations too large for shared memory
 }
 
-template <int FOLD, int NB, int SRC, int EPI, bool PART>
+template <int FOLD, int NB, int SRC, int EPI, bool PART, int TPR>
 static int launch_t(const MatvecParams& p, const LaunchOpts& o, int grid) {
-    auto kern = q4k_matvec_kernel<FOLD, NB, SRC, EPI, PART>;
+    auto kern = q4k_matvec_kernel<FOLD, NB, SRC, EPI, PART, TPR>;
     static bool attr_set = false;
     if (!attr_set) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
@@ -499,15 +597,23 @@ static int launch_t(const MatvecParams& p, const LaunchOpts& o, int grid) {
 
 template <int FOLD, int SRC, int EPI, bool PART>
 static int launch_nb(const MatvecParams& p, const LaunchOpts& o, int grid) {
+    if (p.tpr == 8) {
+        // eight threads per row: narrow matrices, batch <= 2
+        switch (p.B) {
+            case 1: return launch_t<FOLD, 1, SRC, EPI, PART, 8>(p, o, grid);
+            case 2: return launch_t<FOLD, 2, SRC, EPI, PART, 8>(p, o, grid);
+            default: return BH_EINVAL;
+        }
+    }
     switch (p.B) {
-        case 1: return launch_t<FOLD, 1, SRC, EPI, PART>(p, o, grid);
-        case 2: return launch_t<FOLD, 2, SRC, EPI, PART>(p, o, grid);
-        case 3: return launch_t<FOLD, 3, SRC, EPI, PART>(p, o, grid);
-        case 4: return launch_t<FOLD, 4, SRC, EPI, PART>(p, o, grid);
-        case 5: return launch_t<FOLD, 5, SRC, EPI, PART>(p, o, grid);
-        case 6: return launch_t<FOLD, 6, SRC, EPI, PART>(p, o, grid);
-        case 7: return launch_t<FOLD, 7, SRC, EPI, PART>(p, o, grid);
-        case 8: return launch_t<FOLD, 8, SRC, EPI, PART>(p, o, grid);
+        case 1: return launch_t<FOLD, 1, SRC, EPI, PART, 4>(p, o, grid);
+        case 2: return launch_t<FOLD, 2, SRC, EPI, PART, 4>(p, o, grid);
+        case 3: return launch_t<FOLD, 3, SRC, EPI, PART, 4>(p, o, grid);
+        case 4: return launch_t<FOLD, 4, SRC, EPI, PART, 4>(p, o, grid);
+        case 5: return launch_t<FOLD, 5, SRC, EPI, PART, 4>(p, o, grid);
+        case 6: return launch_t<FOLD, 6, SRC, EPI, PART, 4>(p, o, grid);
+        case 7: return launch_t<FOLD, 7, SRC, EPI, PART, 4>(p, o, grid);
+        case 8: return launch_t<FOLD, 8, SRC, EPI, PART, 4>(p, o, grid);
         default: return BH_EINVAL;
     }
 }
@@ -532,7 +638,52 @@ static int launch_fold(const MatvecParams& p, int src, int epi, const LaunchOpts
     }
 }
 
-int launch_matvec(const MatvecParams& p, int fold, int act_src, int epi, const LaunchOpts& o) {
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+        cudaGetLastError();
+    }
+    return fn;
+}
+
+// One tensor map per segment: a 2-D array of 8-byte elements, nb*18 wide,
+// segment rows high; the box is the stage slice of one oct.
+static int encode_maps(MatvecParams& p) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return BH_EIO;
+    const int64_t rowbytes = (int64_t)p.nb * Q4K_BYTES;
+    if (p.seg_end[0] < p.N && (p.seg_end[0] % MV_ROWS || p.seg_end[1] % MV_ROWS)) return BH_EINVAL;
+    int64_t prev = 0;
+    for (int sg = 0; sg < 3; ++sg) {
+        const int64_t rows = p.seg_end[sg] - prev;
+        prev = p.seg_end[sg];
+        const cuuint64_t dims[2] = {(cuuint64_t)(rowbytes / 8), (cuuint64_t)(rows > 0 ? rows : 1)};
+        const cuuint64_t strides[1] = {(cuuint64_t)rowbytes};
+        const cuuint32_t box[2] = {(cuuint32_t)(p.row_stride / 8), (cuuint32_t)p.rows_per_tile};
+        const cuuint32_t estr[2] = {1, 1};
+        if (enc(&p.tmap[sg], CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(p.w[sg]), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return BH_EINVAL;
+    }
+    return BH_OK;
+}
+
+int launch_matvec(const MatvecParams& pin, int fold, int act_src, int epi, const LaunchOpts& o) {
+    MatvecParams p = pin;
+    const int rc = encode_maps(p);
+    if (rc != BH_OK) return rc;
     const int grid = o.grid;
     if (fold == BH_FOLD_X86) return launch_fold<BH_FOLD_X86>(p, act_src, epi, o, grid);
     if (fold == BH_FOLD_GENERIC) return launch_fold<BH_FOLD_GENERIC>(p, act_src, epi, o, grid);

@@ -191,3 +191,31 @@ def test_fp16_scale_conversion_matches_oracle(ctx, oracle):
     scales = np.float32(10.0) ** rng.uniform(-9, 3, 256).astype(np.float32)
     w = (oracle.normal((256, 256), 9, 0.0, 1.0) * scales[:, None]).astype(np.float32)
     assert np.array_equal(host(ctx.q4k_quantize(dev(w))), oracle.quantize_q4k(w).reshape(-1))
+
+
+@pytest.mark.parametrize("tpr", [4, 8])
+@pytest.mark.parametrize("n,k,b", [(4096, 4096, 1), (4096, 12288, 2), (1000, 768, 1), (33, 2048, 2), (151936 // 16, 4096, 1)])
+def test_forced_threads_per_row_bit_exact(ctx, bh, oracle, tpr, n, k, b):
+    """4 or 8 threads per row (the planner picks by shape) give the same bits."""
+    w = oracle.normal((n, k), 31 + n + k, 0.0, 0.02)
+    wq = oracle.quantize_q4k(w)
+    x = oracle.normal((b, k), 41 + k, 0.0, 1.0)
+    xq = oracle.quantize_q8k(x)
+    ctx.tune(bh.TUNE_TPR, tpr)
+    try:
+        for fold in FOLDS:
+            y = host(ctx.matvec(dev(wq), n, k, dev(xq), b, fold=fold))
+            assert_bits_equal(y, oracle.matvec(wq, n, k, xq, b, fold), f"tpr{tpr} {n}x{k} b{b} fold{fold}")
+            y2 = host(ctx.matvec_f32(dev(wq), n, k, dev(x), fold=fold))
+            assert_bits_equal(y2, oracle.matvec(wq, n, k, xq, b, fold), f"f32 tpr{tpr}")
+            P = torch_zeros_int((b, n, k // 256, 9))
+            ctx.matvec(dev(wq), n, k, dev(xq), b, partials=P, fold=fold)
+            assert np.array_equal(host(P), oracle.partials(wq, n, k, xq, b))
+    finally:
+        ctx.tune(bh.TUNE_TPR, 0)
+
+
+def torch_zeros_int(shape):
+    import torch
+
+    return torch.zeros(shape, dtype=torch.int32, device="cuda")
