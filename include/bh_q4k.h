@@ -132,6 +132,18 @@ int bh_q4k_mul_mat_host(bh_ctx *ctx, const void *W_q4k, int64_t N, int64_t K, co
 int bh_q4k_lmhead_argmax(bh_ctx *ctx, const void *W_q4k, int64_t N, int64_t K, const float *x, int B,
                          float *logits_opt, int32_t *tok_out, float *max_opt, int fold, void *stream);
 
+/* The same greedy LM-head pick for callers that cannot allocate device
+ * memory (and so cannot create a bh_ctx): no context, no allocation. The
+ * per-CTA argmax candidates live in a 32 KiB static device array of the
+ * library (4096 slots; a launch needs grid x B of them, at most 2368 on a
+ * 148-SM B200, larger requests return BH_EINVAL). The first call on a device
+ * looks up that array's address (cudaGetSymbolAddress) and must come before
+ * any stream capture. Calls share the array: calls that overlap on the GPU
+ * race, so serialize them. Runs on the current device. No counterpart in the
+ * reference. */
+int bh_q4k_lmhead_argmax_noalloc(const void *W_q4k, int64_t N, int64_t K, const float *x, int B,
+                                 float *logits_opt, int32_t *tok_out, float *max_opt, int fold, void *stream);
+
 /* ------------------------------------------------------------------------
  * Decode block stack: the caller of the matvec in the reference engine's
  * per-token step (desktop/engine/src/forward.cpp:2663-2854 build_block_decode,

@@ -84,6 +84,7 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.bh_q4k_dequantize.argtypes = [_vp, _vp, _i64, _i64, _vp, _vp]
     L.bh_q4k_mul_mat_host.argtypes = [_vp, _vp, _i64, _i64, _vp, C.c_int, _vp, C.c_int]
     L.bh_q4k_lmhead_argmax.argtypes = [_vp, _vp, _i64, _i64, _vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp]
+    L.bh_q4k_lmhead_argmax_noalloc.argtypes = [_vp, _i64, _i64, _vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp]
     L.bh_stack_default_config.argtypes = [C.POINTER(StackConfig)]
     L.bh_stack_default_config.restype = None
     L.bh_stack_create.argtypes = [_vp, C.POINTER(StackConfig), C.c_uint64, C.POINTER(_vp)]
