@@ -223,6 +223,85 @@ int bh_stack_time_op(bh_stack *st, int op, int reps, float *avg_ms, int64_t *byt
  * rows x cols in values, the rest fp32. */
 int bh_stack_tensor(bh_stack *st, int layer, int which, void **ptr, int64_t *rows, int64_t *cols);
 
+/* ------------------------------------------------------------------------
+ * Routed-expert FFN (MoE): the stock block of desktop/engine/src/forward.cpp
+ * :1001-1118 (ggml_soft_max -> ggml_top_k -> ggml_get_rows -> renormalise,
+ * then three ggml_mul_mat_id + ggml_silu + ggml_mul + weighted sum) and the
+ * BURN_MOE custom op that replaces its expert half (burn_moe_op.h:47-59,
+ * burn_moe_op.cpp:202-372). At most 8 tokens per call, k <= 8 selected
+ * experts per token, n_expert <= 256; n_embd and n_ff multiples of 256.
+ * ------------------------------------------------------------------------ */
+
+/* Router of n_tok tokens from logits [n_tok][n_expert]: probabilities by
+ * soft_max (max subtracted, exp, sum in double of per-8 fp32 partial sums,
+ * scaled by (float)(1/sum)); the k largest in descending order with slots 0
+ * and 1 swapped, as ggml_top_k writes them (ggml-cpu/ops.cpp:8157-8194;
+ * equal probabilities lower index first); their probabilities, divided by
+ * their double sum when norm_topk != 0. selected_out / weights_out are
+ * device [n_tok][k]. exp is evaluated by the library's own Cody-Waite
+ * routine, within 1 ulp of exp (the reference's SIMD exp differs by a few
+ * ulp). */
+int bh_moe_route(bh_ctx *ctx, const float *logits, int n_tok, int n_expert, int k, int norm_topk,
+                 int32_t *selected_out, float *weights_out, void *stream);
+
+/* out[t] = sum over slots s, in order, of w[t][s] * down_e(silu(gate_e . x_t) * (up_e . x_t)),
+ * e = selected[t][s], for cur [n_tok][n_embd] fp32 (each column quantized
+ * to Q8_K; silu(gate) * up quantized again for down), accumulated in double
+ * and rounded once (ggml_mul then ggml_sum_rows). Banks are GGML's bundled
+ * expert tensors in block_q4_K rows: gate_exps / up_exps [n_expert][n_ff][n_embd],
+ * down_exps [n_expert][n_embd][n_ff]. Routing is either given (selected,
+ * weights: device [n_tok][k], BURN_MOE's inputs) or computed from
+ * router_logits [n_tok][n_expert] as bh_moe_route does (then selected and
+ * weights must be NULL; selected_out / weights_out, if non-NULL, receive
+ * it). A token's k experts must be distinct (else the device status
+ * reports BH_EINVAL and out is not written). Every expert chosen by several
+ * tokens is streamed once. One cooperative launch (all CTAs resident, grid
+ * barriers between the gate|up, down and combine phases); scratch buffers
+ * are owned by the context. */
+int bh_q4k_moe(bh_ctx *ctx, const float *cur, int n_tok, const int32_t *selected, const float *weights,
+               const float *router_logits, int norm_topk, const void *gate_exps, const void *up_exps,
+               const void *down_exps, int n_expert, int n_embd, int n_ff, int k, float *out,
+               int32_t *selected_out, float *weights_out, int fold, void *stream);
+
+/* The MoE layer stack of the 30B-A3B shape: per layer h += moe(RMSNorm(h) *
+ * ffn_norm) with router logits seeded N(0, 1) per (layer, token), expert
+ * banks seeded N(0, 0.02) and quantized to Q4_K on the device. One step runs
+ * every layer for n_tok tokens in one CUDA graph (one launch per layer). */
+typedef struct bh_moe_stack bh_moe_stack;
+typedef struct bh_moe_config {
+    int n_layer;   /* 48 */
+    int n_embd;    /* 2048 */
+    int n_ff;      /* 768 */
+    int n_expert;  /* 128 */
+    int k;         /* 8 */
+    int n_tok;     /* tokens per step, 1..8 */
+    float rms_eps; /* 1e-6 */
+} bh_moe_config;
+
+#define BH_MOE_GATE 0
+#define BH_MOE_UP 1
+#define BH_MOE_DOWN 2
+#define BH_MOE_LOGITS 3    /* [n_tok][n_expert] fp32 */
+#define BH_MOE_NORM 4      /* [n_embd] fp32 */
+#define BH_MOE_SELECTED 5  /* [n_tok][k] int32, written by each step */
+#define BH_MOE_WEIGHTS 6   /* [n_tok][k] fp32, written by each step */
+#define BH_MOE_HIDDEN 7    /* [n_tok][n_embd] fp32 (layer == -1) */
+
+void bh_moe_default_config(bh_moe_config *cfg);
+int bh_moe_stack_create(bh_ctx *ctx, const bh_moe_config *cfg, uint64_t seed, bh_moe_stack **out);
+int bh_moe_stack_free(bh_moe_stack *st);
+/* h [n_tok][n_embd] (device) is copied in, all layers run, the result is
+ * written to h_out (device). Asynchronous on stream. */
+int bh_moe_stack_step(bh_moe_stack *st, const float *h, float *h_out, void *stream);
+/* The same step from and to host memory (copies inside the call). */
+int bh_moe_stack_step_host(bh_moe_stack *st, const float *host_h, float *host_h_out);
+/* Bytes of all expert weights, bytes of the experts the last step selected
+ * (distinct experts per layer x bytes per expert, plus the activations the
+ * matvecs read and write), and launches per step. */
+int bh_moe_stack_info(bh_moe_stack *st, int64_t *weight_bytes, int64_t *step_bytes, int64_t *launches);
+/* Device pointer and bytes of one tensor (ids above) of a layer. */
+int bh_moe_stack_tensor(bh_moe_stack *st, int layer, int which, void **ptr, int64_t *bytes);
+
 /* ggml_vec_dot_t-shaped shim (ggml-cpu.h:113) for the type_traits slot of
  * GGML_TYPE_Q4_K: one row of K = n values, HOST pointers vx (block_q4_K)
  * and vy (block_q8_K), nrc must be 1. Runs on device 0 through a

@@ -72,6 +72,12 @@ class Oracle:
         L.bho_partials.argtypes = [_vp, C.c_int64, C.c_int64, _vp, C.c_int, _vp]
         L.bho_argmax.argtypes = [_vp, C.c_int64]
         L.bho_argmax.restype = C.c_int64
+        L.bho_expf_n.argtypes = [_vp, C.c_int64, _vp]
+        L.bho_silu_n.argtypes = [_vp, C.c_int64, _vp]
+        L.bho_rmsnorm.argtypes = [_vp, _vp, C.c_int, C.c_float, _vp]
+        L.bho_moe_route.argtypes = [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp]
+        L.bho_moe_ffn.argtypes = [_vp, C.c_int, _vp, _vp, C.c_int, _vp, _vp, _vp, C.c_int, C.c_int,
+                                  _vp, _vp, _vp, C.c_int, C.c_int]
 
     def normal(self, shape, seed: int, mean: float = 0.0, std: float = 1.0, first: int = 0) -> np.ndarray:
         out = np.empty(shape, dtype=np.float32)
@@ -123,6 +129,53 @@ class Oracle:
     def fp32_to_fp16(self, f: float) -> int:
         return int(self.lib.bho_fp32_to_fp16(f))
 
+    # ---- routed-expert FFN glue -------------------------------------------
+    def expf(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.empty_like(x)
+        self.lib.bho_expf_n(_ptr(x), x.size, _ptr(y))
+        return y
+
+    def silu(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.empty_like(x)
+        self.lib.bho_silu_n(_ptr(x), x.size, _ptr(y))
+        return y
+
+    def rmsnorm(self, x: np.ndarray, gamma: np.ndarray | None, eps: float) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rows = x.reshape(-1, x.shape[-1])
+        y = np.empty_like(rows)
+        g = None if gamma is None else np.ascontiguousarray(gamma, dtype=np.float32)
+        for i in range(rows.shape[0]):
+            self.lib.bho_rmsnorm(_ptr(rows[i]), None if g is None else _ptr(g), rows.shape[1], eps, _ptr(y[i]))
+        return y.reshape(x.shape)
+
+    def moe_route(self, logits: np.ndarray, k: int, norm: bool = True):
+        """logits [T, n_expert] -> (ids [T, k] int32, w [T, k] float32)."""
+        logits = np.ascontiguousarray(logits, dtype=np.float32)
+        t, e = logits.shape
+        ids = np.empty((t, k), dtype=np.int32)
+        w = np.empty((t, k), dtype=np.float32)
+        for i in range(t):
+            self.lib.bho_moe_route(_ptr(logits[i]), e, k, int(norm), _ptr(ids[i]), _ptr(w[i]))
+        return ids, w
+
+    def moe_ffn(self, cur: np.ndarray, ids: np.ndarray, w: np.ndarray, gate: np.ndarray, up: np.ndarray,
+                down: np.ndarray, n_embd: int, n_ff: int, fold: int = FOLD_X86, nthreads: int = 0):
+        """cur [T, n_embd] -> (out [T, n_embd], gu [T*k, 2*n_ff], dout [T*k, n_embd])."""
+        cur = np.ascontiguousarray(cur, dtype=np.float32)
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        t, k = ids.shape
+        out = np.empty((t, n_embd), dtype=np.float32)
+        gu = np.empty((t * k, 2 * n_ff), dtype=np.float32)
+        dout = np.empty((t * k, n_embd), dtype=np.float32)
+        self.lib.bho_moe_ffn(_ptr(cur), t, _ptr(ids), _ptr(w), k, _ptr(np.ascontiguousarray(gate)),
+                             _ptr(np.ascontiguousarray(up)), _ptr(np.ascontiguousarray(down)), n_embd, n_ff,
+                             _ptr(out), _ptr(gu), _ptr(dout), fold, nthreads or (os.cpu_count() or 1))
+        return out, gu, dout
+
     def fp16_to_fp32(self, h: int) -> float:
         return float(self.lib.bho_fp16_to_fp32(h))
 
@@ -148,6 +201,8 @@ class Reference:
         L.ref_pool_threads.argtypes = [_vp]
         L.ref_pool_threads.restype = C.c_int
         L.ref_mul_mat.argtypes = [_vp, _vp, C.c_int64, C.c_int64, _vp, C.c_int, _vp, _vp]
+        L.ref_soft_max.argtypes = [_vp, C.c_int, _vp]
+        L.ref_silu.argtypes = [_vp, C.c_int, _vp]
         self.has_avx2 = bool(L.ref_has_avx2())
         self._pool = None
 
@@ -183,6 +238,20 @@ class Reference:
             xp = _ptr(xq[c])
             for r in range(n):
                 y[c, r] = f(k, w[r].ctypes.data_as(_vp), xp)
+        return y
+
+    def soft_max(self, x: np.ndarray) -> np.ndarray:
+        """Row-wise ggml soft_max of x [T, n] through the reference's vec.cpp."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.empty_like(x)
+        for i in range(x.shape[0]):
+            self.lib.ref_soft_max(_ptr(x[i]), x.shape[1], _ptr(y[i]))
+        return y
+
+    def silu(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.empty_like(x)
+        self.lib.ref_silu(_ptr(x), x.size, _ptr(y))
         return y
 
     def pool(self, nthreads: int):

@@ -15,6 +15,7 @@
 
 #include <math.h>
 #include <pthread.h>
+#include <stdlib.h>
 #include <string.h>
 
 /* ------------------------------------------------------------------ */
@@ -507,4 +508,141 @@ int64_t bho_argmax(const float *v, int64_t n) {
     for (int64_t i = 1; i < n; ++i)
         if (v[i] > bv) { bv = v[i]; best = i; }
     return best;
+}
+
+/* ------------------------------------------------------------------ */
+/* routed-expert FFN glue (desktop/engine/src/forward.cpp:1001-1118)   */
+/* ------------------------------------------------------------------ */
+
+/* exp by Cody-Waite reduction and a degree-7 Taylor polynomial; the same
+ * operation sequence as the GPU's exp_cw (csrc/bh_math.cuh), so the two
+ * agree bit for bit. The reference itself uses ggml_v_expf
+ * (ggml-cpu/vec.h:1233-1271) or expf; the difference is a few ulp. */
+float bho_expf(float x) {
+    if (x != x) return x;
+    if (x > 0x1.62e430p+6f) return INFINITY;
+    if (x < -103.972084f) return 0.0f;
+    const float n = rintf(x * 0x1.715476p+0f);
+    float r = fmaf(-n, 0x1.62e400p-1f, x);
+    r = fmaf(-n, 0x1.7f7d1cp-20f, r);
+    float q = 0x1.a01a02p-13f;
+    q = fmaf(q, r, 0x1.6c16c2p-10f);
+    q = fmaf(q, r, 0x1.111112p-7f);
+    q = fmaf(q, r, 0x1.555556p-5f);
+    q = fmaf(q, r, 0x1.555556p-3f);
+    q = fmaf(q, r, 0.5f);
+    q = fmaf(q, r, 1.0f);
+    q = fmaf(q, r, 1.0f);
+    const int ni = (int)n;
+    const int n1 = ni >> 1, n2 = ni - n1;
+    return (q * u2f((uint32_t)(n1 + 127) << 23)) * u2f((uint32_t)(n2 + 127) << 23);
+}
+
+/* ggml_silu_f32 (ggml-cpu/vec.h:1064): x / (1 + exp(-x)) */
+float bho_silu(float x) { return x / (1.0f + bho_expf(-x)); }
+
+void bho_expf_n(const float *x, int64_t n, float *y) { for (int64_t i = 0; i < n; ++i) y[i] = bho_expf(x[i]); }
+void bho_silu_n(const float *x, int64_t n, float *y) { for (int64_t i = 0; i < n; ++i) y[i] = bho_silu(x[i]); }
+
+/* ggml_compute_forward_rms_norm_f32 (ggml-cpu/ops.cpp): sum of the fp32
+ * squares accumulated in double, mean = (float)(sum / n),
+ * scale = 1 / sqrtf(mean + eps), y = x * scale; then the norm weight
+ * (ggml_mul): y * gamma. gamma may be NULL (no weight). */
+void bho_rmsnorm(const float *x, const float *gamma, int n, float eps, float *y) {
+    double sum = 0.0;
+    for (int i = 0; i < n; ++i) sum += (double)(x[i] * x[i]);
+    const float mean = (float)(sum / n);
+    const float scale = 1.0f / sqrtf(mean + eps);
+    for (int i = 0; i < n; ++i) {
+        const float v = x[i] * scale;
+        y[i] = gamma ? v * gamma[i] : v;
+    }
+}
+
+/* Router of one token:
+ *  soft_max (ggml-cpu/ops.cpp:5365-5382 with vec.cpp:547-567, AVX2 branch):
+ *    max; p_i = exp(l_i - max); sum in double of per-8 fp32 partial sums
+ *    ((p4+p0)+(p6+p2)) + ((p5+p1)+(p7+p3)), tail added one by one;
+ *    p_i *= (float)(1.0 / sum)
+ *  top_k (ops.cpp:8157-8194): the k largest p in descending order, then
+ *    slots 0 and 1 swapped. Equal p are taken lower index first (the
+ *    reference's std::partial_sort leaves their order unspecified).
+ *  get_rows + norm_topk_prob (forward.cpp:1032-1046): w_s = p[ids_s];
+ *    w_s /= (float)(sum in double of w over the slots, in slot order). */
+void bho_moe_route(const float *logits, int n_expert, int k, int norm, int32_t *ids, float *w) {
+    float p[1024];
+    float mx = -INFINITY;
+    for (int i = 0; i < n_expert; ++i) mx = logits[i] > mx ? logits[i] : mx;
+    for (int i = 0; i < n_expert; ++i) p[i] = bho_expf(logits[i] - mx);
+    double sum = 0.0;
+    int i = 0;
+    for (; i + 7 < n_expert; i += 8) {
+        const float *v = p + i;
+        const float g = ((v[4] + v[0]) + (v[6] + v[2])) + ((v[5] + v[1]) + (v[7] + v[3]));
+        sum += (double)g;
+    }
+    for (; i < n_expert; ++i) sum += (double)p[i];
+    const float inv = (float)(1.0 / sum);
+    for (i = 0; i < n_expert; ++i) p[i] *= inv;
+    /* selection: rank by (p descending, index ascending) */
+    for (int s = 0; s < k; ++s) {
+        int best = -1;
+        for (int e = 0; e < n_expert; ++e) {
+            int taken = 0;
+            for (int u = 0; u < s; ++u) taken |= ids[u] == e;
+            if (taken) continue;
+            if (best < 0 || p[e] > p[best]) best = e;
+        }
+        ids[s] = best;
+    }
+    if (k > 1) { const int32_t t = ids[0]; ids[0] = ids[1]; ids[1] = t; }
+    for (int s = 0; s < k; ++s) w[s] = p[ids[s]];
+    if (norm) {
+        double ws = 0.0;
+        for (int s = 0; s < k; ++s) ws += (double)w[s];
+        const float wsf = (float)ws;
+        for (int s = 0; s < k; ++s) w[s] = w[s] / wsf;
+    }
+}
+
+/* Stock routed-expert FFN (forward.cpp:1090-1107) for T tokens:
+ *   up_e = W_up[e] . q8k(cur_t),  gate_e = W_gate[e] . q8k(cur_t)   (mul_mat_id)
+ *   par  = silu(gate_e) * up_e                                       (ggml_silu, ggml_mul)
+ *   down = W_down[e] . q8k(par)                                      (mul_mat_id)
+ *   out_t = (float) sum over slots s, in order, of (double)(down_s * w_s)
+ *                                                  (ggml_mul, ggml_sum_rows)
+ * Banks: gate/up [n_expert][n_ff rows][n_embd/256 blocks] and
+ * down [n_expert][n_embd rows][n_ff/256 blocks] of block_q4_K.
+ * gu_opt [T*k][2*n_ff] receives gate | up (before SiLU); dout_opt
+ * [T*k][n_embd] the unweighted expert outputs. */
+void bho_moe_ffn(const float *cur, int T, const int32_t *ids, const float *w, int k,
+                 const void *gate, const void *up, const void *down, int n_embd, int n_ff,
+                 float *out, float *gu_opt, float *dout_opt, int fold, int nthreads) {
+    const int64_t nbe = n_embd / BHO_QK, nbf = n_ff / BHO_QK;
+    const int64_t gsz = (int64_t)n_ff * nbe * BHO_Q4K_BYTES;     /* bytes of one gate/up expert */
+    const int64_t dsz = (int64_t)n_embd * nbf * BHO_Q4K_BYTES;   /* bytes of one down expert */
+    uint8_t *xq = (uint8_t *)malloc((size_t)nbe * BHO_Q8K_BYTES);
+    uint8_t *pq = (uint8_t *)malloc((size_t)nbf * BHO_Q8K_BYTES);
+    float *g = (float *)malloc(sizeof(float) * 2 * (size_t)n_ff);
+    float *par = (float *)malloc(sizeof(float) * (size_t)n_ff);
+    float *d = (float *)malloc(sizeof(float) * (size_t)n_embd);
+    double *acc = (double *)malloc(sizeof(double) * (size_t)n_embd);
+    for (int t = 0; t < T; ++t) {
+        bho_quantize_row_q8k(cur + (int64_t)t * n_embd, xq, n_embd);
+        for (int i = 0; i < n_embd; ++i) acc[i] = 0.0;
+        for (int s = 0; s < k; ++s) {
+            const int e = ids[t * k + s];
+            bho_matvec((const uint8_t *)gate + e * gsz, n_ff, n_embd, xq, 1, g, fold, nthreads);
+            bho_matvec((const uint8_t *)up + e * gsz, n_ff, n_embd, xq, 1, g + n_ff, fold, nthreads);
+            if (gu_opt) memcpy(gu_opt + ((int64_t)t * k + s) * 2 * n_ff, g, sizeof(float) * 2 * (size_t)n_ff);
+            for (int i = 0; i < n_ff; ++i) par[i] = bho_silu(g[i]) * g[n_ff + i];
+            bho_quantize_row_q8k(par, pq, n_ff);
+            bho_matvec((const uint8_t *)down + e * dsz, n_embd, n_ff, pq, 1, d, fold, nthreads);
+            if (dout_opt) memcpy(dout_opt + ((int64_t)t * k + s) * n_embd, d, sizeof(float) * (size_t)n_embd);
+            const float ws = w[t * k + s];
+            for (int i = 0; i < n_embd; ++i) acc[i] += (double)(d[i] * ws);
+        }
+        for (int i = 0; i < n_embd; ++i) out[(int64_t)t * n_embd + i] = (float)acc[i];
+    }
+    free(xq); free(pq); free(g); free(par); free(d); free(acc);
 }

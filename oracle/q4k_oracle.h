@@ -68,6 +68,18 @@ void bho_partials(const void *W, int64_t N, int64_t K, const void *Xq, int B, in
 /* engine.cpp:36-43: first index of the strict maximum */
 int64_t bho_argmax(const float *v, int64_t n);
 
+/* ---- routed-expert FFN glue (forward.cpp:1001-1118), see q4k_oracle.c ---- */
+float bho_expf(float x);   /* Cody-Waite + degree-7 Taylor; identical to the GPU's */
+float bho_silu(float x);   /* x / (1 + exp(-x)) */
+void  bho_expf_n(const float *x, int64_t n, float *y);
+void  bho_silu_n(const float *x, int64_t n, float *y);
+void  bho_rmsnorm(const float *x, const float *gamma, int n, float eps, float *y);
+/* softmax -> top-k (slots 0/1 swapped) -> gather -> renormalise; n_expert <= 1024 */
+void  bho_moe_route(const float *logits, int n_expert, int k, int norm, int32_t *ids, float *w);
+void  bho_moe_ffn(const float *cur, int T, const int32_t *ids, const float *w, int k,
+                  const void *gate, const void *up, const void *down, int n_embd, int n_ff,
+                  float *out, float *gu_opt, float *dout_opt, int fold, int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

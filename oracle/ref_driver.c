@@ -19,6 +19,7 @@
  * vector, 16 otherwise; re-chunked per thread when there are fewer than
  * 4 chunks per thread), each row computed by vec_dot.
  */
+#include <math.h>
 #include <pthread.h>
 #include <stdatomic.h>
 #include <stdint.h>
@@ -195,3 +196,21 @@ void ref_mul_mat(void *vp, const void *W, int64_t N, int64_t K, const float *X, 
 }
 
 int ref_pool_threads(void *vp) { return ((ref_pool *)vp)->nth; }
+
+/* ---- the expert glue through the reference's own vec.cpp ---------------- */
+typedef double ggml_float;
+ggml_float ggml_vec_soft_max_f32(const int n, float *y, const float *x, float max);
+void ggml_vec_silu_f32(const int n, float *y, const float *x);
+
+/* One row of ggml_compute_forward_soft_max_f32 (ggml-cpu/ops.cpp:5365-5382)
+ * with scale 1 and no mask or sinks. */
+void ref_soft_max(const float *x, int n, float *y) {
+    float mx = -INFINITY;
+    for (int i = 0; i < n; ++i) mx = x[i] > mx ? x[i] : mx;   /* ggml_vec_max_f32 */
+    ggml_float sum = ggml_vec_soft_max_f32(n, y, x, mx);
+    sum = 1.0 / sum;
+    const float v = (float)sum;                                /* ggml_vec_scale_f32's float argument */
+    for (int i = 0; i < n; ++i) y[i] *= v;
+}
+
+void ref_silu(const float *x, int n, float *y) { ggml_vec_silu_f32(n, y, x); }

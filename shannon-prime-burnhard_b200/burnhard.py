@@ -59,6 +59,16 @@ class StackConfig(C.Structure):
         return {name: getattr(self, name) for name, _ in self._fields_}
 
 
+class MoeConfig(C.Structure):
+    _fields_ = [("n_layer", C.c_int), ("n_embd", C.c_int), ("n_ff", C.c_int), ("n_expert", C.c_int),
+                ("k", C.c_int), ("n_tok", C.c_int), ("rms_eps", C.c_float)]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+MOE_GATE, MOE_UP, MOE_DOWN, MOE_LOGITS, MOE_NORM, MOE_SELECTED, MOE_WEIGHTS, MOE_HIDDEN = range(8)
+
 W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN = range(7)
 W_PER_LAYER = 7
 W_OUTPUT = 7
@@ -96,6 +106,17 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.bh_stack_info.argtypes = [_vp, C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i64)]
     L.bh_stack_time_op.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(_i64)]
     L.bh_stack_tensor.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(_vp), C.POINTER(_i64), C.POINTER(_i64)]
+    L.bh_moe_route.argtypes = [_vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp]
+    L.bh_q4k_moe.argtypes = [_vp, _vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int,
+                             C.c_int, _vp, _vp, _vp, C.c_int, _vp]
+    L.bh_moe_default_config.argtypes = [C.POINTER(MoeConfig)]
+    L.bh_moe_default_config.restype = None
+    L.bh_moe_stack_create.argtypes = [_vp, C.POINTER(MoeConfig), C.c_uint64, C.POINTER(_vp)]
+    L.bh_moe_stack_free.argtypes = [_vp]
+    L.bh_moe_stack_step.argtypes = [_vp, _vp, _vp, _vp]
+    L.bh_moe_stack_step_host.argtypes = [_vp, _vp, _vp]
+    L.bh_moe_stack_info.argtypes = [_vp, C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i64)]
+    L.bh_moe_stack_tensor.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(_vp), C.POINTER(_i64)]
     L.bh_ggml_vec_dot_q4_K_q8_K.argtypes = [C.c_int, _vp, C.c_size_t, _vp, C.c_size_t, _vp, C.c_size_t, C.c_int]
     L.bh_ggml_vec_dot_q4_K_q8_K.restype = None
     return L
@@ -316,3 +337,101 @@ def lmhead_argmax(ctx: Context, w, n: int, k: int, x, logits=None, fold: int = F
     _check(lib.bh_q4k_lmhead_argmax(ctx.h, _dp(w), n, k, _dp(x), b, _dp(logits), _dp(tok), _dp(mx), fold,
                                     _stream(stream)), "bh_q4k_lmhead_argmax")
     return tok, mx
+
+
+# ---------------------------------------------------------------------------
+# routed-expert FFN
+# ---------------------------------------------------------------------------
+def moe_route(ctx: Context, logits, k: int, norm_topk: bool = True, stream=None):
+    """(selected [T, k] int32, weights [T, k] fp32) of router logits [T, n_expert] on the device."""
+    import torch
+
+    t, e = logits.shape
+    ids = torch.empty((t, k), dtype=torch.int32, device=logits.device)
+    w = torch.empty((t, k), dtype=torch.float32, device=logits.device)
+    _check(lib.bh_moe_route(ctx.h, _dp(logits), t, e, k, int(norm_topk), _dp(ids), _dp(w), _stream(stream)),
+           "bh_moe_route")
+    return ids, w
+
+
+def moe(ctx: Context, cur, gate, up, down, n_expert: int, n_ff: int, k: int, selected=None, weights=None,
+        logits=None, norm_topk: bool = True, out=None, fold: int = FOLD_X86, stream=None):
+    """Routed-expert FFN of cur [T, n_embd] (device fp32). Routing is given
+    (selected, weights) or computed from logits; returns (out, selected, weights)."""
+    import torch
+
+    t, n_embd = cur.shape
+    if out is None:
+        out = torch.empty((t, n_embd), dtype=torch.float32, device=cur.device)
+    sel_out = w_out = None
+    if logits is not None:
+        sel_out = torch.empty((t, k), dtype=torch.int32, device=cur.device)
+        w_out = torch.empty((t, k), dtype=torch.float32, device=cur.device)
+    _check(lib.bh_q4k_moe(ctx.h, _dp(cur), t, _dp(selected), _dp(weights), _dp(logits), int(norm_topk), _dp(gate),
+                          _dp(up), _dp(down), n_expert, n_embd, n_ff, k, _dp(out), _dp(sel_out), _dp(w_out), fold,
+                          _stream(stream)), "bh_q4k_moe")
+    if logits is not None:
+        return out, sel_out, w_out
+    return out, selected, weights
+
+
+def default_moe_config(**overrides) -> MoeConfig:
+    cfg = MoeConfig()
+    lib.bh_moe_default_config(C.byref(cfg))
+    for key, v in overrides.items():
+        setattr(cfg, key, v)
+    return cfg
+
+
+class MoeStack:
+    """The MoE layer stack (bh_moe_stack_*) on a Context's device."""
+
+    def __init__(self, ctx: Context, cfg: MoeConfig, seed: int):
+        h = _vp()
+        _check(lib.bh_moe_stack_create(ctx.h, C.byref(cfg), seed & (2**64 - 1), C.byref(h)), "bh_moe_stack_create")
+        self.h = h
+        self.ctx = ctx
+        self.cfg = cfg
+
+    def close(self) -> None:
+        if self.h:
+            lib.bh_moe_stack_free(self.h)
+            self.h = _vp()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def step(self, h_in, h_out, stream=None) -> None:
+        _check(lib.bh_moe_stack_step(self.h, _dp(h_in), _dp(h_out), _stream(stream)), "bh_moe_stack_step")
+
+    def step_host(self, host_h, host_out) -> None:
+        hp = host_h.ctypes.data if hasattr(host_h, "ctypes") else host_h.data_ptr()
+        op = host_out.ctypes.data if hasattr(host_out, "ctypes") else host_out.data_ptr()
+        _check(lib.bh_moe_stack_step_host(self.h, hp, op), "bh_moe_stack_step_host")
+
+    def info(self) -> dict:
+        wb, sb, nl = _i64(), _i64(), _i64()
+        _check(lib.bh_moe_stack_info(self.h, C.byref(wb), C.byref(sb), C.byref(nl)), "bh_moe_stack_info")
+        return {"weight_bytes": wb.value, "step_bytes": sb.value, "launches": nl.value}
+
+    def tensor(self, layer: int, which: int):
+        p, nb = _vp(), _i64()
+        _check(lib.bh_moe_stack_tensor(self.h, layer, which, C.byref(p), C.byref(nb)), "bh_moe_stack_tensor")
+        return p.value, nb.value
+
+    def to_host(self, layer: int, which: int):
+        """A host copy of one tensor (uint8 for the banks, int32 routing ids, else fp32)."""
+        import torch
+
+        ptr, nb = self.tensor(layer, which)
+        if which in (MOE_GATE, MOE_UP, MOE_DOWN):
+            t = device_view(ptr, nb, "|u1")
+        elif which == MOE_SELECTED:
+            t = device_view(ptr, nb // 4, "<i4")
+        else:
+            t = device_view(ptr, nb // 4, "<f4")
+        torch.cuda.synchronize()
+        return t.cpu().numpy()

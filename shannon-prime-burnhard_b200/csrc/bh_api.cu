@@ -189,6 +189,7 @@ int bh_free(bh_ctx* ctx) {
     DeviceGuard g(ctx->device);
     cudaStreamSynchronize(ctx->stream);
     if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->moe_scratch) cudaFree(ctx->moe_scratch);
     cudaFree(ctx->cand_val);
     cudaFree(ctx->cand_idx);
     cudaFree(ctx->d_status);

@@ -26,6 +26,10 @@ struct bh_ctx {
     // argmax candidates of the LM-head entry point: [num_sms * 4][BH_MAX_BATCH]
     float* cand_val = nullptr;
     int32_t* cand_idx = nullptr;
+    // routed-expert FFN scratch: grid-barrier words, gate|up and expert
+    // outputs of every pair, routing
+    uint8_t* moe_scratch = nullptr;
+    size_t moe_scratch_bytes = 0;
 };
 
 
@@ -37,4 +41,8 @@ int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override);
 MatvecParams base_params(bh_ctx* ctx, const void* W, int64_t N, int64_t K, int B, float* y);
 // plan_for + launch.
 int run_matvec(bh_ctx* ctx, MatvecParams& p, int fold, int src, int epi, cudaStream_t s, bool pdl);
+// Plan and launch one routed-expert FFN batch (one cooperative launch; the
+// PDL attribute only when pdl is set). p carries the shapes, routing source,
+// h / gamma, the three banks, the scratch, out and the grid-barrier words.
+int run_moe(bh_ctx* ctx, MoeParams& p, int fold, cudaStream_t s, bool pdl);
 }  // namespace bh

@@ -66,6 +66,54 @@ constexpr int MV_THREADS = MV_WARPS * 32;
 constexpr int MV_ROWS = 8;                  // largest tile (rows of one warp stage); segment boundaries align to it
 constexpr int ACT_BLOCK_BYTES = 304;   // staged Q8_K block: 256 q8 + 16 (d) + 32 (S)
 
+// Routed-expert FFN (the stock MoE block of the reference, gate|up -> SwiGLU
+// -> down -> weighted sum over the top-k slots), one token batch of B <= 8.
+constexpr int MOE_MAX_TOK = 8;
+constexpr int MOE_MAX_K = 8;
+constexpr int MOE_MAX_PAIRS = MOE_MAX_TOK * MOE_MAX_K;
+constexpr int MOE_MAX_EXPERT = 256;
+
+struct MoeParams {
+    CUtensorMap tmap[3];   // gate bank, up bank, down bank (2-D, 8-byte elements)
+    const uint8_t* w[3];
+    int n_expert, n_embd, n_ff, k, B;
+    int norm_topk;         // renormalise the selected weights to sum 1
+    const float* logits;   // [B][n_expert] router logits, or null: routing given in ids_in / w_in
+    const int32_t* ids_in; // [B][k]
+    const float* w_in;     // [B][k]
+    int32_t* ids_out;      // [B][k] routing, written by CTA 0 (may be null)
+    float* w_out;          // [B][k]
+    const float* h;        // [B][n_embd] input
+    const float* gamma;    // RMSNorm weight [n_embd], or null: h is used as is
+    float eps;
+    float* gu;             // [B*k][2*n_ff]: gate | up of pair (token t, slot s) at row t*k + s
+    float* dout;           // [B*k][n_embd]: unweighted expert outputs of each pair
+    float* out;            // [B][n_embd]: the weighted sum (stored, or added when residual)
+    int residual;
+    unsigned int* gbar;    // grid barrier words {count, generation}, zero before first use
+    int* status;
+    int64_t* trace;        // timeline probe (builds with BH_TRACE only; else unused)
+    // tiling, chosen on the host: both phases share one ring of `stages`
+    // slots of slot_bytes per warp
+    int kc_gu, stride_gu, stage_gu;   // gate|up phase (K = n_embd)
+    int kc_dn, stride_dn, stage_dn;   // down phase (K = n_ff)
+    int slot_bytes, stages, act_blocks;
+    int act_off, ring_off, bar_off, smem_bytes;
+};
+
+// Plan the fused MoE layer launch for a shared-memory budget; returns 0 or a
+// negative errno.
+int moe_plan(MoeParams& p, int smem_cap, int stage_target);
+// One routed-expert FFN batch in a single cooperative launch (grid CTAs, all
+// co-resident; o.grid is clamped to what fits).
+int launch_moe(const MoeParams& p, int fold, const LaunchOpts& o);
+// Routing alone (one CTA): logits -> ids_out / w_out.
+int launch_moe_route(const MoeParams& p, const LaunchOpts& o);
+int encode_q4k_map(CUtensorMap* map, const void* base, int64_t rows, int nb, int row_stride, int box_rows);
+// Seeded normal fill (splitmix64 -> Box-Muller in double, the oracle's
+// generator): out[i] = mean + std * z(seed, first + i).
+int fill_normal(float* out, int64_t n, int64_t first, uint64_t seed, double mean, double stddev, cudaStream_t s);
+
 // Fill tiling fields of p for the given grid; returns 0 or a negative errno.
 int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int tpr);
 int launch_matvec(const MatvecParams& p, int fold, int act_src, int epi, const LaunchOpts& o);

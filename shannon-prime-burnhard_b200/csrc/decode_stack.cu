@@ -52,8 +52,7 @@ __global__ void fill_normal_kernel(float* out, int64_t n, int64_t first, uint64_
     out[t] = (float)(mean + stddev * z);
 }
 
-static int fill_normal(float* out, int64_t n, int64_t first, uint64_t seed, double mean, double stddev,
-                       cudaStream_t s) {
+int fill_normal(float* out, int64_t n, int64_t first, uint64_t seed, double mean, double stddev, cudaStream_t s) {
     if (n <= 0) return BH_OK;
     fill_normal_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(out, n, first, seed, mean, stddev);
     return cudaGetLastError() == cudaSuccess ? BH_OK : BH_EIO;

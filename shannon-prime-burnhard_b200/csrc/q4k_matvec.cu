@@ -1,29 +1,21 @@
 // q4k_matvec.cu — the sm_100a Q4_K x Q8_K matvec (batch 1..8).
 //
-// Structure (one CTA of 8 warps per SM, persistent over a contiguous range
-// of rows):
-//  - every warp owns "quads" of 4 consecutive rows and streams them through
-//    its own ring of shared-memory stages with 1-D bulk async copies
-//    (cp.async.bulk, the TMA engine), completion counted on per-stage
-//    mbarriers; one copy per row per stage, rows padded so reads are
-//    bank-conflict free. Eight warps issue copies in parallel (a single
-//    issuing warp caps small-copy throughput far below HBM bandwidth).
-//    Weights do not depend on the previous kernel, so each warp starts
-//    streaming before the programmatic-launch wait.
-//  - all warps stage the activations once (Q8_K input, or fp32
-//    input quantized in the prologue), then each row is worked by 8 threads:
-//    thread "lane" j of the row owns exactly the int32 lane j of the
-//    reference's vec_dot, so its fp32 fold chain stays in registers and the
-//    result is bit-identical to the reference's fold:
-//      FOLD_X86     (ggml-cpu/arch/x86/quants.c:1900-1983): lane m = bytes
-//                   4m..4m+3 of every 32-byte quant group -> a natural word,
-//                   one dp4a per nibble half; acc = fma(d, sumi, acc).
-//      FOLD_GENERIC (ggml-cpu/quants.c:645-718): lane l = positions p % 8 == l,
-//                   a 4x4 byte transpose (prmt) per word; sums += d * aux.
-//    Integer sums are exact (|partial| < 2^24), so only the fp32 order
-//    matters, and it is reproduced operation by operation.
+// Structure (8 warps per CTA, 1 or 2 CTAs per SM, each CTA persistent over a
+// contiguous range of rows):
+//  - every warp owns tiles of 32/TPR consecutive rows and streams them
+//    through its own ring of shared-memory stages: one 2-D tensor copy
+//    (cp.async.bulk.tensor, the TMA engine) per stage, issued by lane 0 and
+//    counted on the stage's mbarrier, rows padded so reads are bank-conflict
+//    free. Eight warps issue copies in parallel; weights do not depend on the
+//    previous kernel, so each warp starts streaming before the programmatic-
+//    launch wait.
+//  - all warps stage the activations once (Q8_K input, or fp32 input
+//    quantized in the prologue, optionally through RMSNorm or SwiGLU), then
+//    TPR threads work each row; the per-block arithmetic (q4k_core.cuh)
+//    reproduces the reference's integer sums and fp32 fold bit for bit.
 #include "bh_common.cuh"
 #include "bh_kernels.cuh"
+#include "q4k_core.cuh"
 #include "q8k_device.cuh"
 
 namespace bh {
@@ -179,187 +171,11 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
     }
 }
 
-// ---------------------------------------------------------------------------
-// per-super-block work of one thread
-// ---------------------------------------------------------------------------
-// TPR threads work one row (TPR = 4: thread t owns reference lanes 2t, 2t+1;
-// TPR = 8: thread t owns lane t); every thread also computes min lane t & 3
-// (threads 4..7 of a TPR = 8 row repeat 0..3 and are not summed).
-template <int TPR>
-struct RowBlk {
-    static constexpr int L = 8 / TPR;  // reference lanes per thread
-    float fd, fdm;
-    uint32_t sc03, sc47, mnk;          // mnk: the two mins of min lane t & 3 in bytes 0..1
-    uint32_t lo[L][4], hi[L][4];
-};
-
-template <int FOLD, int TPR>
-__device__ __forceinline__ RowBlk<TPR> decode_row(const uint8_t* blk, int t) {
-    constexpr int L = RowBlk<TPR>::L;
-    RowBlk<TPR> r;
-    const uint4 h = *reinterpret_cast<const uint4*>(blk);
-    r.fd = h2f((uint16_t)(h.x & 0xffffu));
-    r.fdm = h2f((uint16_t)(h.x >> 16));
-    // 6-bit scales/mins, get_scale_min_k4 (ggml-quants.c:818-825) word-wise:
-    // j<4: sc = q[j] & 63, mn = q[j+4] & 63;
-    // j>=4: sc = (q[j+4] & 15) | (q[j-4] >> 6) << 4, mn = (q[j+4] >> 4) | (q[j] >> 6) << 4
-    r.sc03 = h.y & 0x3f3f3f3fu;
-    r.sc47 = (h.w & 0x0f0f0f0fu) | ((h.y >> 2) & 0x30303030u);
-    const int k = t & 3;
-    const uint32_t mn = (k & 2) ? (((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u)) : (h.z & 0x3f3f3f3fu);
-    r.mnk = mn >> ((k & 1) * 16);
-    const uint32_t* qs = reinterpret_cast<const uint32_t*>(blk + 16);
-    if (FOLD == BH_FOLD_X86) {
-        // lane m = bytes 4m..4m+3 of each 32-byte group: word m
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-            uint32_t w[L];
-            if (L == 2) {
-                const uint2 w2 = *reinterpret_cast<const uint2*>(qs + 8 * g + 2 * t);
-                w[0] = w2.x;
-                w[L - 1] = w2.y;
-            } else {
-                w[0] = qs[8 * g + t];
-            }
-#pragma unroll
-            for (int e = 0; e < L; ++e) {
-                r.lo[e][g] = w[e] & 0x0f0f0f0fu;
-                r.hi[e][g] = (w[e] >> 4) & 0x0f0f0f0fu;
-            }
-        }
-    } else {
-        // lane l = group bytes l, l+8, l+16, l+24: a byte gather from words
-        // l/4 + {0,2,4,6} (the lanes of one thread share those words)
-        const int l0 = t * L, k0 = l0 >> 2, tb = l0 & 3;
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-            const uint32_t* gw = qs + 8 * g;
-            const uint32_t w0 = gw[k0], w1 = gw[k0 + 2], w2 = gw[k0 + 4], w3 = gw[k0 + 6];
-#pragma unroll
-            for (int e = 0; e < L; ++e) {
-                const uint32_t sel = (uint32_t)((tb + e) | ((tb + e + 4) << 4));
-                const uint32_t tw = __byte_perm(__byte_perm(w0, w1, sel), __byte_perm(w2, w3, sel), 0x5410);
-                r.lo[e][g] = tw & 0x0f0f0f0fu;
-                r.hi[e][g] = (tw >> 4) & 0x0f0f0f0fu;
-            }
-        }
-    }
-    return r;
-}
-
-// One lane's exact integer sum over the super-block:
-// sum_j sc_j * (dot of its 4 codes of sub-block j). Each sub-block dot is a
-// dp4a (|dot| <= 4*15*127, fits int16); two of them are packed and scaled by
-// two 6-bit scales in one dp2a.
-__device__ __forceinline__ int lane_sum(const uint32_t (&lo)[4], const uint32_t (&hi)[4], uint32_t sc03,
-                                        uint32_t sc47, const int4 a0, const int4 a1, int (&sub)[8], bool want_sub) {
-    const int d0 = dp4a((int)lo[0], a0.x, 0), d1 = dp4a((int)hi[0], a0.y, 0);
-    const int d2 = dp4a((int)lo[1], a0.z, 0), d3 = dp4a((int)hi[1], a0.w, 0);
-    const int d4 = dp4a((int)lo[2], a1.x, 0), d5 = dp4a((int)hi[2], a1.y, 0);
-    const int d6 = dp4a((int)lo[3], a1.z, 0), d7 = dp4a((int)hi[3], a1.w, 0);
-    if (want_sub) {
-        sub[0] = d0; sub[1] = d1; sub[2] = d2; sub[3] = d3;
-        sub[4] = d4; sub[5] = d5; sub[6] = d6; sub[7] = d7;
-    }
-    int s = __dp2a_lo((int)__byte_perm((uint32_t)d0, (uint32_t)d1, 0x5410), (int)sc03, 0);
-    s = __dp2a_hi((int)__byte_perm((uint32_t)d2, (uint32_t)d3, 0x5410), (int)sc03, s);
-    s = __dp2a_lo((int)__byte_perm((uint32_t)d4, (uint32_t)d5, 0x5410), (int)sc47, s);
-    return __dp2a_hi((int)__byte_perm((uint32_t)d6, (uint32_t)d7, 0x5410), (int)sc47, s);
-}
-
-// Sum over the 4 min lanes held by threads t & 3 = 0..3 of a row (exact ints).
-template <int TPR>
-__device__ __forceinline__ int sum_min_lanes(int v) {
-    v += __shfl_xor_sync(0xffffffffu, v, 1);
-    return v + __shfl_xor_sync(0xffffffffu, v, 2);
-}
-
-// One activation column applied to one decoded row block: the reference's
-// per-block fp32 step for this thread's lanes and its min lane.
-template <int FOLD, bool PART, int TPR>
-__device__ __forceinline__ void fold_block(const MatvecParams& p, const RowBlk<TPR>& r, const uint8_t* A, int t,
-                                           int b, int i, int64_t row, bool live, float (&acc)[8 / TPR],
-                                           float& accm) {
-    constexpr int L = RowBlk<TPR>::L;
-    const float yd = *reinterpret_cast<const float*>(A + 256);
-    const int spk = reinterpret_cast<const int*>(A + 272)[t & 3];
-    int li[L];
-    int sub[L][8];
-#pragma unroll
-    for (int e = 0; e < L; ++e) {
-        const int4 a0 = *reinterpret_cast<const int4*>(A + 32 * (t * L + e));
-        const int4 a1 = *reinterpret_cast<const int4*>(A + 32 * (t * L + e) + 16);
-        li[e] = lane_sum(r.lo[e], r.hi[e], r.sc03, r.sc47, a0, a1, sub[e], PART);
-    }
-    const int mp = __dp2a_lo(spk, (int)r.mnk, 0);
-    if (FOLD == BH_FOLD_X86) {
-        // acc[m] = fma(y.d * fp16(d), sumi[m], acc[m]);
-        // accm[k] = fma(-y.d * fp16(dmin), min_{2k} S_{2k} + min_{2k+1} S_{2k+1}, accm[k])
-        const float d = __fmul_rn(yd, r.fd);
-#pragma unroll
-        for (int e = 0; e < L; ++e) acc[e] = __fmaf_rn(d, i2f_exact(li[e]), acc[e]);
-        accm = __fmaf_rn(__fmul_rn(-yd, r.fdm), i2f_exact(mp), accm);
-    } else {
-        // sums[l] += (fp16(d) * y.d) * aux[l];  sumf -= (fp16(dmin) * y.d) * sumi
-        const float d = __fmul_rn(r.fd, yd);
-#pragma unroll
-        for (int e = 0; e < L; ++e) acc[e] = __fadd_rn(acc[e], __fmul_rn(d, i2f_exact(li[e])));
-        const int sumi = sum_min_lanes<TPR>(mp);
-        accm = __fsub_rn(accm, __fmul_rn(__fmul_rn(r.fdm, yd), i2f_exact(sumi)));
-    }
-    if (PART) {
-        const int msum = sum_min_lanes<TPR>(mp);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            int v = 0;
-#pragma unroll
-            for (int e = 0; e < L; ++e) v += sub[e][j];
-#pragma unroll
-            for (int off = 1; off < TPR; off <<= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-            sub[0][j] = v;
-        }
-        if (live && t == 0) {
-            int32_t* o = p.partials + (((int64_t)b * p.N + row) * p.nb + i) * 9;
-            for (int j = 0; j < 8; ++j) o[j] = sub[0][j];
-            o[8] = msum;
-        }
-    }
-}
-
-// Per-row combine in the reference's order, then the epilogue.
+// Per-row epilogue of the dense kernel.
 template <int FOLD, int EPI, int TPR>
 __device__ __forceinline__ void finish_row(const MatvecParams& p, const float (&acc)[8 / TPR], float accm, int rgrp,
                                            int t, int b, bool has_row, int64_t row, float& best_v, int& best_i) {
-    const unsigned FULLM = 0xffffffffu;
-    float v;
-    if (FOLD == BH_FOLD_X86) {
-        // hsum_float_8 (arch/x86/quants.c:43-49): ((a4+a0)+(a6+a2)) + ((a5+a1)+(a7+a3))
-        float hs;
-        if (TPR == 4) {
-            // thread t holds lanes 2t (acc[0]) and 2t+1 (acc[1])
-            const float x0 = __fadd_rn(acc[0], __shfl_xor_sync(FULLM, acc[0], 2));  // t0: a0+a4, t1: a2+a6
-            const float x1 = __fadd_rn(acc[8 / TPR - 1], __shfl_xor_sync(FULLM, acc[8 / TPR - 1], 2));
-            const float y0 = __fadd_rn(x0, __shfl_xor_sync(FULLM, x0, 1));
-            const float y1 = __fadd_rn(x1, __shfl_xor_sync(FULLM, x1, 1));
-            hs = __fadd_rn(y0, y1);
-        } else {
-            // thread t holds lane t
-            const float t1 = __fadd_rn(acc[0], __shfl_xor_sync(FULLM, acc[0], 4));  // t0: a0+a4
-            const float t2 = __fadd_rn(t1, __shfl_xor_sync(FULLM, t1, 2));          // t0: (a0+a4)+(a2+a6)
-            hs = __fadd_rn(t2, __shfl_xor_sync(FULLM, t2, 1));
-        }
-        // 4-lane min accumulator, lane k in thread k: (m0+m2) + (m1+m3)
-        const float u = __fadd_rn(accm, __shfl_xor_sync(FULLM, accm, 2));
-        const float hm = __fadd_rn(u, __shfl_xor_sync(FULLM, u, 1));
-        v = __fadd_rn(hs, hm);
-    } else {
-        // sumf (the min chain) += sums[0..7] in order
-        constexpr int L = 8 / TPR;
-        v = accm;
-#pragma unroll
-        for (int l = 0; l < 8; ++l)
-            v = __fadd_rn(v, __shfl_sync(FULLM, acc[l % L], rgrp * TPR + l / L));
-    }
+    const float v = row_value<FOLD, TPR>(acc, accm, rgrp);
     if (has_row && t == 0) {
         float* yp = p.y + (int64_t)b * p.ldy + row;
         if (EPI == EPI_ADD) *yp = __fadd_rn(*yp, v);
@@ -480,8 +296,10 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_matvec_kernel(const __grid_
                 const RowBlk<TPR> r = decode_row<FOLD, TPR>(rowp + kb * Q4K_BYTES, t);
 #pragma unroll
                 for (int b = 0; b < NB; ++b)
-                    fold_block<FOLD, PART, TPR>(p, r, actc + (b * p.nb + kb) * ACT_BLOCK_BYTES, t, b, sbc + kb,
-                                                r_begin + rin, live, acc[b], accm[b]);
+                    fold_block<FOLD, PART, TPR>(
+                        r, actc + (b * p.nb + kb) * ACT_BLOCK_BYTES, t,
+                        PART && live ? p.partials + (((int64_t)b * p.N + r_begin + rin) * p.nb + sbc + kb) * 9 : nullptr,
+                        acc[b], accm[b]);
             }
             __syncwarp();
             if (issued < total) {
@@ -657,25 +475,32 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// One tensor map per segment: a 2-D array of 8-byte elements, nb*18 wide,
-// segment rows high; the box is the stage slice of one oct.
-static int encode_maps(MatvecParams& p) {
+// A 2-D tensor map over a Q4_K matrix: 8-byte elements, rows of nb*144
+// bytes, `rows` high; the box is box_rows rows x row_stride bytes.
+int encode_q4k_map(CUtensorMap* map, const void* base, int64_t rows, int nb, int row_stride, int box_rows) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return BH_EIO;
-    const int64_t rowbytes = (int64_t)p.nb * Q4K_BYTES;
+    const int64_t rowbytes = (int64_t)nb * Q4K_BYTES;
+    const cuuint64_t dims[2] = {(cuuint64_t)(rowbytes / 8), (cuuint64_t)(rows > 0 ? rows : 1)};
+    const cuuint64_t strides[1] = {(cuuint64_t)rowbytes};
+    const cuuint32_t box[2] = {(cuuint32_t)(row_stride / 8), (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return BH_EINVAL;
+    return BH_OK;
+}
+
+// One tensor map per segment; the box is the stage slice of one tile.
+static int encode_maps(MatvecParams& p) {
     if (p.seg_end[0] < p.N && (p.seg_end[0] % MV_ROWS || p.seg_end[1] % MV_ROWS)) return BH_EINVAL;
     int64_t prev = 0;
     for (int sg = 0; sg < 3; ++sg) {
         const int64_t rows = p.seg_end[sg] - prev;
         prev = p.seg_end[sg];
-        const cuuint64_t dims[2] = {(cuuint64_t)(rowbytes / 8), (cuuint64_t)(rows > 0 ? rows : 1)};
-        const cuuint64_t strides[1] = {(cuuint64_t)rowbytes};
-        const cuuint32_t box[2] = {(cuuint32_t)(p.row_stride / 8), (cuuint32_t)p.rows_per_tile};
-        const cuuint32_t estr[2] = {1, 1};
-        if (enc(&p.tmap[sg], CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(p.w[sg]), dims, strides, box, estr,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return BH_EINVAL;
+        const int rc = encode_q4k_map(&p.tmap[sg], p.w[sg], rows, p.nb, p.row_stride, p.rows_per_tile);
+        if (rc != BH_OK) return rc;
     }
     return BH_OK;
 }

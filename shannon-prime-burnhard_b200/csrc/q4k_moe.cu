@@ -1,0 +1,734 @@
+// q4k_moe.cu — the routed-expert FFN on sm_100a: top-k routing, the grouped
+// Q4_K x Q8_K matvecs over the selected experts, SwiGLU and the weighted sum.
+//
+// The reference's stock block (desktop/engine/src/forward.cpp:1001-1118):
+//   probs = soft_max(logits); selected = top_k(probs, k); w = probs[selected],
+//   renormalised; up/gate = mul_mat_id(W_up/W_gate, cur); par = silu(gate)*up;
+//   down = mul_mat_id(W_down, par); out = sum over the k slots of w * down.
+// BURN_MOE (burn_moe_op.cpp:202-372) computes the same block from given
+// `selected` / `weights`; both routing sources are supported here.
+//
+// One cooperative launch per batch of B <= 8 tokens, every CTA resident:
+//  1. every CTA routes the batch itself (identical arithmetic, so identical
+//     tables) and at once starts streaming both its gate|up rows and its
+//     down rows of the U distinct selected experts through its warps' rings
+//     (tiles of 8 rows never straddling an expert), so the whole layer's
+//     weights are in flight from the start;
+//  2. the input columns are RMSNorm'd (when a norm weight is given) and
+//     quantized to Q8_K; each gate|up tile computes only the token columns
+//     routed to its expert and writes gate | up of those (token, slot) pairs;
+//  3. grid barrier; the pairs a CTA's down rows serve are quantized from
+//     silu(gate) * up and the down tiles computed from the already-streamed
+//     rows; grid barrier;
+//  4. out = sum over slots, in order, of (double)(w_s * down_s), rounded
+//     once, stored or added to out (the residual stream).
+// Each expert's weights are streamed once per batch however many tokens
+// chose it. Barrier waits are bounded: on expiry the kernel records a
+// timeout in the status word, drains its copies and returns.
+#include <cfloat>
+
+#include "bh_common.cuh"
+#include "bh_kernels.cuh"
+#include "bh_math.cuh"
+#include "q4k_core.cuh"
+#include "q8k_device.cuh"
+
+namespace bh {
+
+namespace {
+
+// Timeline probe: with BH_TRACE defined, lane 0 of every warp records the
+// global timer (ns) at a few points of the kernel into p.trace.
+#ifdef BH_TRACE
+#define MOE_TRACE_AT(k)                                                                                 \
+    do {                                                                                                \
+        if (p.trace && (threadIdx.x & 31) == 0) {                                                        \
+            uint64_t t_;                                                                                \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                      \
+            p.trace[((int64_t)blockIdx.x * MV_WARPS + (threadIdx.x >> 5)) * 8 + (k)] = (int64_t)t_;     \
+        }                                                                                               \
+    } while (0)
+#else
+#define MOE_TRACE_AT(k) \
+    do {                \
+    } while (0)
+#endif
+
+constexpr int MOE_R = 8;   // rows per tile (TPR = 4)
+constexpr int MOE_TPR = 4;
+
+// Routing of one batch, built the same way by every CTA.
+struct MoeTable {
+    int n_unique;
+    int bad;                          // a given expert id out of range, or repeated within a token
+    int32_t ids[MOE_MAX_TOK][MOE_MAX_K];
+    float w[MOE_MAX_TOK][MOE_MAX_K];
+    int16_t expert[MOE_MAX_PAIRS];    // distinct selected experts, ascending
+    int8_t cnt[MOE_MAX_PAIRS];        // token columns of each
+    int8_t col_tok[MOE_MAX_PAIRS][MOE_MAX_TOK];
+    int8_t col_slot[MOE_MAX_PAIRS][MOE_MAX_TOK];
+    uint32_t bits[MOE_MAX_EXPERT / 32];
+    int base[MOE_MAX_EXPERT / 32];
+};
+
+// Shared scratch of the router: probabilities of the batch.
+struct __align__(16) RouteScratch {
+    float p[MOE_MAX_TOK][MOE_MAX_EXPERT];
+    float grp[MOE_MAX_TOK][MOE_MAX_EXPERT / 8];
+};
+
+// soft_max -> top_k -> get_rows -> renormalise, for all B tokens of the batch
+// (ggml-cpu/ops.cpp:5365-5382 with vec.cpp:547-567; ops.cpp:8157-8194;
+// forward.cpp:1032-1046), then the per-expert column lists. All threads of
+// the CTA take part; ends with the table complete and a __syncthreads.
+// Equal probabilities are ranked lower index first (the reference's
+// std::partial_sort leaves their order unspecified). Inputs may have been
+// written by an earlier kernel, so they are read around L1.
+__device__ void moe_route(const MoeParams& p, MoeTable& tb, RouteScratch& rs) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int E = p.n_expert, k = p.k, B = p.B;
+    if (tid == 0) { tb.bad = 0; tb.n_unique = 0; }
+    if (tid < MOE_MAX_EXPERT / 32) tb.bits[tid] = 0;
+    if (tid < MOE_MAX_PAIRS) tb.ids[tid / MOE_MAX_K][tid % MOE_MAX_K] = -1;  // a slot left unset is caught below
+    __syncthreads();
+    if (p.logits) {
+        for (int i = tid; i < B * E; i += MV_THREADS) rs.p[i / E][i % E] = __ldcg(p.logits + i);
+        __syncthreads();
+        if (warp < B) {
+            float* pr = rs.p[warp];
+            float mx = -INFINITY;
+            for (int i = lane; i < E; i += 32) mx = fmaxf(mx, pr[i]);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            for (int i = lane; i < E; i += 32) pr[i] = exp_cw(__fsub_rn(pr[i], mx));
+            __syncwarp();
+            // per-8 fp32 partial sums ((p4+p0)+(p6+p2)) + ((p5+p1)+(p7+p3)), summed in double
+            const int ng = E / 8;
+            for (int g = lane; g < ng; g += 32) {
+                const float* v = pr + 8 * g;
+                rs.grp[warp][g] = __fadd_rn(__fadd_rn(__fadd_rn(v[4], v[0]), __fadd_rn(v[6], v[2])),
+                                            __fadd_rn(__fadd_rn(v[5], v[1]), __fadd_rn(v[7], v[3])));
+            }
+            __syncwarp();
+            float inv = 0.f;
+            if (lane == 0) {
+                double sum = 0.0;
+                for (int g = 0; g < ng; ++g) sum = __dadd_rn(sum, (double)rs.grp[warp][g]);
+                for (int i = 8 * ng; i < E; ++i) sum = __dadd_rn(sum, (double)pr[i]);
+                inv = __double2float_rn(__ddiv_rn(1.0, sum));
+            }
+            inv = __shfl_sync(0xffffffffu, inv, 0);
+            for (int i = lane; i < E; i += 32) pr[i] = __fmul_rn(pr[i], inv);
+        }
+        __syncthreads();
+        // rank of every (token, expert) by (p descending, index ascending);
+        // tpi threads share an item, each scanning every tpi-th group of 4
+        const int items = B * E;
+        int tpi = 1;
+        while (tpi < 32 && items * tpi * 2 <= MV_THREADS) tpi <<= 1;
+        const int per_pass = MV_THREADS / tpi;
+        for (int base = 0; base < items; base += per_pass) {
+            const int it = base + tid / tpi, sub = tid % tpi;
+            const bool valid = it < items;
+            const int b = valid ? it / E : 0, i = valid ? it - b * E : 0;
+            const float* pr = rs.p[b];
+            const float v = pr[i];
+            int rank = 0;
+            if (valid) {
+                if ((E & 3) == 0) {
+                    for (int c = sub; c < E / 4; c += tpi) {
+                        const float4 o = reinterpret_cast<const float4*>(pr)[c];
+                        const int j = 4 * c;
+                        rank += (o.x > v) | ((o.x == v) & (j < i));
+                        rank += (o.y > v) | ((o.y == v) & (j + 1 < i));
+                        rank += (o.z > v) | ((o.z == v) & (j + 2 < i));
+                        rank += (o.w > v) | ((o.w == v) & (j + 3 < i));
+                    }
+                } else {
+                    for (int j = sub; j < E; j += tpi) {
+                        const float o = pr[j];
+                        rank += (o > v) | ((o == v) & (j < i));
+                    }
+                }
+            }
+            for (int off = 1; off < tpi; off <<= 1) rank += __shfl_xor_sync(0xffffffffu, rank, off);
+            if (valid && sub == 0 && rank < k) {
+                const int slot = (k > 1 && rank < 2) ? 1 - rank : rank;  // top_k swaps slots 0 and 1
+                tb.ids[b][slot] = i;
+            }
+        }
+        __syncthreads();
+        if (tid < B) {
+            float ws[MOE_MAX_K];
+            double sum = 0.0;
+            for (int s = 0; s < k; ++s) {
+                ws[s] = rs.p[tid][tb.ids[tid][s]];
+                sum = __dadd_rn(sum, (double)ws[s]);
+            }
+            const float sf = __double2float_rn(sum);
+            for (int s = 0; s < k; ++s) tb.w[tid][s] = p.norm_topk ? __fdiv_rn(ws[s], sf) : ws[s];
+        }
+    } else {
+        for (int i = tid; i < B * k; i += MV_THREADS) {
+            tb.ids[i / k][i % k] = __ldcg(p.ids_in + i);
+            tb.w[i / k][i % k] = __ldcg(p.w_in + i);
+        }
+    }
+    __syncthreads();
+    // distinct experts, ascending: a bitmap, then an exclusive scan of its words
+    if (tid < B * k) {
+        const int e = tb.ids[tid / k][tid % k];
+        if (e < 0 || e >= E) tb.bad = 1;
+        else atomicOr(&tb.bits[e >> 5], 1u << (e & 31));
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = MOE_MAX_EXPERT / 32;
+        const uint32_t word = lane < nw ? tb.bits[lane] : 0u;
+        const int c = __popc(word);
+        int incl = c;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= off) incl += o;
+        }
+        const int base = incl - c;
+        if (lane < nw) {
+            tb.base[lane] = base;
+            uint32_t wv = word;
+            for (int j = 0; wv; ++j) {
+                const int bit = __ffs(wv) - 1;
+                wv &= wv - 1;
+                tb.expert[base + j] = (int16_t)(lane * 32 + bit);
+            }
+        }
+        if (lane == 31) tb.n_unique = incl;
+    }
+    __syncthreads();
+    // column j of pair (t, s) = number of earlier pairs (row-major) on the same expert
+    if (tid < B * k) {
+        const int t = tid / k, s = tid - t * k;
+        const int e = tb.ids[t][s];
+        if (e >= 0 && e < E) {
+            const int u = tb.base[e >> 5] + __popc(tb.bits[e >> 5] & ((1u << (e & 31)) - 1u));
+            int j = 0, n = 0;
+            for (int q = 0; q < B * k; ++q) {
+                const int same = tb.ids[q / k][q % k] == e;
+                j += same & (q < tid);
+                n += same;
+            }
+            if (n > B) tb.bad = 1;  // an expert repeated within one token's selection
+            else {
+                tb.col_tok[u][j] = (int8_t)t;
+                tb.col_slot[u][j] = (int8_t)s;
+                if (j == 0) tb.cnt[u] = (int8_t)n;
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// Gate|up prologue: the B input columns, RMSNorm'd when a weight is given
+// (ggml rms_norm: fp32 squares summed in double, mean = (float)(sum / n),
+// scale = 1 / sqrt(mean + eps), y = (x * scale) * gamma), quantized to Q8_K.
+template <int FOLD>
+__device__ void stage_tokens(const MoeParams& p, uint8_t* act, float* s_scale) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int K = p.n_embd, nb = K / QK;
+    if (p.gamma) {
+        for (int b = warp; b < p.B; b += MV_WARPS) {
+            const float* h = p.h + (int64_t)b * K;
+            double ss = 0.0;
+            for (int i = lane; i < K; i += 32) {
+                const float v = __ldcg(h + i);
+                ss = __dadd_rn(ss, (double)__fmul_rn(v, v));
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+            if (lane == 0) {
+                const float mean = __double2float_rn(__ddiv_rn(ss, (double)K));
+                s_scale[b] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+            }
+        }
+        __syncthreads();
+    }
+    const int nblk = p.B * nb;
+    for (int blk = warp; blk < nblk; blk += MV_WARPS) {
+        const int b = blk / nb, i = blk - b * nb;
+        const int e0 = i * QK + 8 * lane;
+        const float4* x = reinterpret_cast<const float4*>(p.h + (int64_t)b * K + e0);
+        const float4 a0 = __ldcg(x), a1 = __ldcg(x + 1);
+        float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        if (p.gamma) {
+            const float4 g0 = *reinterpret_cast<const float4*>(p.gamma + e0);
+            const float4 g1 = *reinterpret_cast<const float4*>(p.gamma + e0 + 4);
+            const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+            const float sc = s_scale[b];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) v[t] = __fmul_rn(__fmul_rn(v[t], sc), g[t]);
+        }
+        const Q8Block qb = q8k_quantize_warp(v, lane);
+        uint8_t* dst = act + blk * ACT_BLOCK_BYTES;
+        stage_codes<FOLD>(dst, qb.q, lane);
+        stage_scalars(dst, qb.d, qb.bsum16, lane);
+    }
+}
+
+// Down prologue: silu(gate) * up of the pairs of experts u_lo..u_hi (written
+// by other CTAs before the grid barrier, so read around L1), pair q of this
+// CTA staged at act + q * nb blocks.
+template <int FOLD>
+__device__ void stage_pairs(const MoeParams& p, const MoeTable& tb, int u_lo, int u_hi, uint8_t* act,
+                            int* s_qbase) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nb = p.n_ff / QK;
+    if (threadIdx.x == 0) {
+        int q = 0;
+        for (int u = u_lo; u <= u_hi; ++u) { s_qbase[u - u_lo] = q; q += tb.cnt[u]; }
+        s_qbase[u_hi - u_lo + 1] = q;
+    }
+    __syncthreads();
+    const int npairs = s_qbase[u_hi - u_lo + 1];
+    const int nblk = npairs * nb;
+    for (int blk = warp; blk < nblk; blk += MV_WARPS) {
+        const int q = blk / nb, i = blk - q * nb;
+        int u = u_lo;
+        while (u < u_hi && s_qbase[u + 1 - u_lo] <= q) ++u;
+        const int j = q - s_qbase[u - u_lo];
+        const int pair = tb.col_tok[u][j] * p.k + tb.col_slot[u][j];
+        const int e0 = i * QK + 8 * lane;
+        const float4* g = reinterpret_cast<const float4*>(p.gu + (int64_t)pair * 2 * p.n_ff + e0);
+        const float4* up = reinterpret_cast<const float4*>(p.gu + (int64_t)pair * 2 * p.n_ff + p.n_ff + e0);
+        const float4 g0 = __ldcg(g), g1 = __ldcg(g + 1), u0 = __ldcg(up), u1 = __ldcg(up + 1);
+        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+        float v[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) v[t] = __fmul_rn(silu_cw(gv[t]), uv[t]);
+        const Q8Block qb = q8k_quantize_warp(v, lane);
+        uint8_t* dst = act + blk * ACT_BLOCK_BYTES;
+        stage_codes<FOLD>(dst, qb.q, lane);
+        stage_scalars(dst, qb.d, qb.bsum16, lane);
+    }
+}
+
+// Grid-wide barrier of a cooperative launch (every CTA resident). Writes of
+// the CTA before the barrier are visible to every CTA after it. Self-resetting:
+// the last arrival zeroes the count, then advances the generation the others
+// wait on. The wait is bounded; false after a timeout (status recorded).
+__device__ bool grid_barrier(unsigned int* gbar, int* status) {
+    __shared__ int s_ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned int gen;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(gen) : "l"(gbar + 1) : "memory");
+        __threadfence();
+        const unsigned int arrived = atomicAdd(gbar, 1u);
+        int ok = 1;
+        if (arrived == gridDim.x - 1) {
+            atomicExch(gbar, 0u);
+            __threadfence();
+            atomicAdd(gbar + 1, 1u);
+        } else {
+            const long long t0 = clock64();
+            for (;;) {
+                unsigned int g;
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(g) : "l"(gbar + 1) : "memory");
+                if (g != gen) break;
+                if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+                    ok = 0;
+                    set_status(status, ST_TIMEOUT);
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        s_ok = ok;
+    }
+    __syncthreads();
+    return s_ok != 0;
+}
+
+// Tiles of the CTA in one phase: a contiguous range of the phase's 8-row
+// tiles over the U selected experts.
+struct PhaseRange {
+    int t_begin, t_end, te;  // tile range, tiles per expert
+    __device__ int mine(int warp) const {
+        const int n = t_end - t_begin;
+        return warp < n ? (n - 1 - warp) / MV_WARPS + 1 : 0;
+    }
+};
+
+// Work the blocks of one ring slot for this thread's row: TPR threads per
+// row, NB-bounded token columns.
+template <int FOLD, int NB>
+__device__ __forceinline__ void tile_fold(const uint8_t* rowp, int kl, const uint8_t* act_base, int nb,
+                                          const int (&colbase)[NB], int cols, int t, float (&acc)[NB][8 / MOE_TPR],
+                                          float (&accm)[NB], int sbc) {
+#pragma unroll 2
+    for (int kb = 0; kb < kl; ++kb) {
+        const RowBlk<MOE_TPR> r = decode_row<FOLD, MOE_TPR>(rowp + kb * Q4K_BYTES, t);
+#pragma unroll
+        for (int c = 0; c < NB; ++c)
+            if (c < cols)
+                fold_block<FOLD, false, MOE_TPR>(r, act_base + (colbase[c] * nb + sbc + kb) * ACT_BLOCK_BYTES, t,
+                                                 nullptr, acc[c], accm[c]);
+    }
+}
+
+// The fused routed-expert FFN of one batch (see the file comment).
+template <int FOLD, int NB>
+__global__ void __launch_bounds__(MV_THREADS, 1) q4k_moe_kernel(const __grid_constant__ MoeParams p) {
+    constexpr int R = MOE_R, TPR = MOE_TPR, L = 8 / TPR;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ MoeTable tb;
+    __shared__ RouteScratch rs;
+    __shared__ float s_scale[MOE_MAX_TOK];
+    __shared__ int s_qbase[MOE_MAX_PAIRS + 1];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const unsigned FULLM = 0xffffffffu;
+    MOE_TRACE_AT(0);
+    pdl_wait();  // routing inputs and h may come from the previous kernel
+    pdl_trigger();
+    moe_route(p, tb, rs);
+    MOE_TRACE_AT(1);
+    if (tb.bad) {
+        if (threadIdx.x == 0) set_status(p.status, ST_BADARG);
+        return;  // uniform over the grid: every CTA built the same table
+    }
+    if (blockIdx.x == 0 && threadIdx.x < p.B * p.k) {
+        const int t = threadIdx.x / p.k, s = threadIdx.x - t * p.k;
+        if (p.ids_out) p.ids_out[threadIdx.x] = tb.ids[t][s];
+        if (p.w_out) p.w_out[threadIdx.x] = tb.w[t][s];
+    }
+
+    uint8_t* act = smem + p.act_off;
+    uint8_t* ring = smem + p.ring_off + (size_t)warp * p.stages * p.slot_bytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off) + warp * p.stages;
+
+    const int U = tb.n_unique;
+    const int nb_e = p.n_embd / QK, nb_f = p.n_ff / QK;
+    PhaseRange gu, dn;
+    gu.te = 2 * p.n_ff / R;
+    dn.te = p.n_embd / R;
+    gu.t_begin = (int)((int64_t)U * gu.te * blockIdx.x / gridDim.x);
+    gu.t_end = (int)((int64_t)U * gu.te * (blockIdx.x + 1) / gridDim.x);
+    dn.t_begin = (int)((int64_t)U * dn.te * blockIdx.x / gridDim.x);
+    dn.t_end = (int)((int64_t)U * dn.te * (blockIdx.x + 1) / gridDim.x);
+    const int my_gu = gu.mine(warp), my_dn = dn.mine(warp);
+    const int nkc_gu = (nb_e + p.kc_gu - 1) / p.kc_gu, nkc_dn = (nb_f + p.kc_dn - 1) / p.kc_dn;
+    const int total = my_gu * nkc_gu + my_dn * nkc_dn;
+
+    if (lane == 0) {
+        for (int s = 0; s < p.stages; ++s) mbar_init(&full[s], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+
+    // one issue cursor over the warp's gate|up tiles, then its down tiles
+    const uint64_t pol = policy_evict_first();
+    int i_ph = my_gu > 0 ? 0 : 1, i_j = 0, i_c = 0, i_s = 0, issued = 0;
+    auto issue_next = [&]() {
+        if (lane == 0) {
+            int map, row, x;
+            uint32_t bytes;
+            if (i_ph == 0) {
+                const int tile = gu.t_begin + warp + i_j * MV_WARPS;
+                const int u = tile / gu.te, rt = (tile - u * gu.te) * R;
+                map = rt >= p.n_ff;
+                row = tb.expert[u] * p.n_ff + (map ? rt - p.n_ff : rt);
+                x = i_c * p.kc_gu * (Q4K_BYTES / 8);
+                bytes = (uint32_t)p.stage_gu;
+            } else {
+                const int tile = dn.t_begin + warp + i_j * MV_WARPS;
+                const int u = tile / dn.te, rt = (tile - u * dn.te) * R;
+                map = 2;
+                row = tb.expert[u] * p.n_embd + rt;
+                x = i_c * p.kc_dn * (Q4K_BYTES / 8);
+                bytes = (uint32_t)p.stage_dn;
+            }
+            mbar_arrive_expect_tx(&full[i_s], bytes);
+            tensor_g2s_2d(ring + (size_t)i_s * p.slot_bytes, &p.tmap[map], x, row, &full[i_s], pol);
+        }
+        __syncwarp();
+        ++issued;
+        if (++i_c == (i_ph == 0 ? nkc_gu : nkc_dn)) {
+            i_c = 0;
+            if (++i_j == my_gu && i_ph == 0) { i_ph = 1; i_j = 0; }
+        }
+        if (++i_s == p.stages) i_s = 0;
+    };
+    const int prefill = min(p.stages, total);
+    for (int q = 0; q < prefill; ++q) issue_next();
+    MOE_TRACE_AT(2);
+
+    stage_tokens<FOLD>(p, act, s_scale);
+    __syncthreads();
+    MOE_TRACE_AT(3);
+
+    const int rgrp = lane / TPR;
+    const int t = lane % TPR;
+    int consumed = 0, c_s = 0;
+    uint32_t c_ph = 0;
+    bool ok = true;
+    auto wait_slot = [&]() -> bool {
+        if (!__all_sync(FULLM, mbar_wait_bounded(&full[c_s], c_ph))) {
+            if (lane == 0) set_status(p.status, ST_TIMEOUT);
+            return false;
+        }
+#ifdef BH_TRACE
+        if (consumed == 0) MOE_TRACE_AT(4);
+#endif
+        ++consumed;
+        return true;
+    };
+    auto release_slot = [&]() {
+        __syncwarp();
+        if (issued < total) {
+            fence_proxy_async_smem();
+            issue_next();
+        }
+        if (++c_s == p.stages) { c_s = 0; c_ph ^= 1u; }
+    };
+
+    // ---- phase 1: gate | up
+    for (int j = 0; j < my_gu && ok; ++j) {
+        const int tile = gu.t_begin + warp + j * MV_WARPS;
+        const int u = tile / gu.te, rt = (tile - u * gu.te) * R;
+        const int cols = tb.cnt[u];
+        int colbase[NB];
+#pragma unroll
+        for (int c = 0; c < NB; ++c) colbase[c] = tb.col_tok[u][c < cols ? c : 0];
+        float acc[NB][L], accm[NB];
+#pragma unroll
+        for (int c = 0; c < NB; ++c) {
+#pragma unroll
+            for (int e = 0; e < L; ++e) acc[c][e] = 0.f;
+            accm[c] = 0.f;
+        }
+        for (int ci = 0; ci < nkc_gu; ++ci) {
+            if (!(ok = wait_slot())) break;
+            const int sbc = ci * p.kc_gu;
+            tile_fold<FOLD, NB>(ring + (size_t)c_s * p.slot_bytes + (size_t)rgrp * p.stride_gu, min(p.kc_gu, nb_e - sbc),
+                                act, nb_e, colbase, cols, t, acc, accm, sbc);
+            release_slot();
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int c = 0; c < NB; ++c) {
+            if (c < cols) {
+                const float v = row_value<FOLD, TPR>(acc[c], accm[c], rgrp);
+                if (t == 0) {
+                    const int pair = tb.col_tok[u][c] * p.k + tb.col_slot[u][c];
+                    p.gu[(int64_t)pair * 2 * p.n_ff + rt + rgrp] = v;
+                }
+            }
+        }
+    }
+    MOE_TRACE_AT(5);
+    ok = grid_barrier(p.gbar, p.status) && ok;
+
+    // ---- phase 2: down
+    const int u_lo = dn.t_end > dn.t_begin ? dn.t_begin / dn.te : 0;
+    const int u_hi = dn.t_end > dn.t_begin ? (dn.t_end - 1) / dn.te : 0;
+    if (dn.t_end > dn.t_begin && __syncthreads_and(ok)) stage_pairs<FOLD>(p, tb, u_lo, u_hi, act, s_qbase);
+    __syncthreads();
+    MOE_TRACE_AT(6);
+    for (int j = 0; j < my_dn && ok; ++j) {
+        const int tile = dn.t_begin + warp + j * MV_WARPS;
+        const int u = tile / dn.te, rt = (tile - u * dn.te) * R;
+        const int cols = tb.cnt[u];
+        int colbase[NB];
+#pragma unroll
+        for (int c = 0; c < NB; ++c) colbase[c] = s_qbase[u - u_lo] + (c < cols ? c : 0);
+        float acc[NB][L], accm[NB];
+#pragma unroll
+        for (int c = 0; c < NB; ++c) {
+#pragma unroll
+            for (int e = 0; e < L; ++e) acc[c][e] = 0.f;
+            accm[c] = 0.f;
+        }
+        for (int ci = 0; ci < nkc_dn; ++ci) {
+            if (!(ok = wait_slot())) break;
+            const int sbc = ci * p.kc_dn;
+            tile_fold<FOLD, NB>(ring + (size_t)c_s * p.slot_bytes + (size_t)rgrp * p.stride_dn, min(p.kc_dn, nb_f - sbc),
+                                act, nb_f, colbase, cols, t, acc, accm, sbc);
+            release_slot();
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int c = 0; c < NB; ++c) {
+            if (c < cols) {
+                const float v = row_value<FOLD, TPR>(acc[c], accm[c], rgrp);
+                if (t == 0) {
+                    const int pair = tb.col_tok[u][c] * p.k + tb.col_slot[u][c];
+                    p.dout[(int64_t)pair * p.n_embd + rt + rgrp] = v;
+                }
+            }
+        }
+    }
+    if (!ok && lane == 0) {
+        // nothing of this warp may still be in flight when the CTA exits
+        int s = c_s;
+        uint32_t ph = c_ph;
+        for (int q = consumed; q < issued; ++q) {
+            mbar_wait_bounded(&full[s], ph);
+            if (++s == p.stages) { s = 0; ph ^= 1u; }
+        }
+    }
+    MOE_TRACE_AT(7);
+    ok = grid_barrier(p.gbar, p.status) && ok;
+    if (!__syncthreads_and(ok)) return;
+
+    // ---- combine: ggml_mul (fp32 product) then ggml_sum_rows over the slots
+    // (double, in slot order), rounded once; this CTA's slice of the outputs
+    const int n = p.B * p.n_embd;
+    const int per = (n + gridDim.x - 1) / gridDim.x;
+    const int e_end = min(n, (int)(blockIdx.x + 1) * per);
+    for (int idx = blockIdx.x * per + threadIdx.x; idx < e_end; idx += MV_THREADS) {
+        const int tk = idx / p.n_embd, i = idx - tk * p.n_embd;
+        double a = 0.0;
+        for (int s = 0; s < p.k; ++s)
+            a = __dadd_rn(a, (double)__fmul_rn(__ldcg(p.dout + ((int64_t)tk * p.k + s) * p.n_embd + i), tb.w[tk][s]));
+        const float r = __double2float_rn(a);
+        p.out[idx] = p.residual ? __fadd_rn(p.out[idx], r) : r;
+    }
+}
+
+// Routing alone (one CTA): ids / weights of the batch.
+__global__ void __launch_bounds__(MV_THREADS, 1) moe_route_kernel(const __grid_constant__ MoeParams p) {
+    __shared__ MoeTable tb;
+    __shared__ RouteScratch rs;
+    pdl_wait();
+    pdl_trigger();
+    moe_route(p, tb, rs);
+    if (tb.bad) {
+        if (threadIdx.x == 0) set_status(p.status, ST_BADARG);
+        return;
+    }
+    if (threadIdx.x < p.B * p.k) {
+        const int t = threadIdx.x / p.k, s = threadIdx.x - t * p.k;
+        p.ids_out[threadIdx.x] = tb.ids[t][s];
+        p.w_out[threadIdx.x] = tb.w[t][s];
+    }
+}
+
+}  // namespace
+
+// Shared-memory plan: the activation region (B token columns of n_embd, or
+// up to B*k pairs of n_ff, whichever is larger), then per warp `stages` ring
+// slots sized for the larger phase stage, then the mbarriers. kc per phase
+// from the copy target (box rows stay within 2048 bytes).
+int moe_plan(MoeParams& p, int smem_cap, int stage_target) {
+    const int nb_e = p.n_embd / QK, nb_f = p.n_ff / QK;
+    p.act_blocks = max(p.B * nb_e, p.B * p.k * nb_f);
+    const int act_bytes = p.act_blocks * ACT_BLOCK_BYTES;
+    const int ring_off = (act_bytes + 127) / 128 * 128;
+    auto stride_for = [](int kc) {
+        const int words = kc * (Q4K_BYTES / 4);
+        const int padw = ((8 - (words % 32)) % 32 + 32) % 32;  // row stride == 8 words (mod 32 banks)
+        return kc * Q4K_BYTES + 4 * padw;
+    };
+    int kc = stage_target / Q4K_BYTES;
+    if (kc < 1) kc = 1;
+    if (kc > 13) kc = 13;
+    for (; kc >= 1; --kc) {
+        const int kg = min(kc, nb_e), kd = min(kc, nb_f);
+        const int sg = MOE_R * stride_for(kg), sd = MOE_R * stride_for(kd);
+        const int slot = max(sg, sd);
+        const int avail = smem_cap - ring_off - 128;
+        int stages = avail > 0 ? avail / (MV_WARPS * (slot + 8)) : 0;
+        if (stages > 8) stages = 8;
+        if (stages < 2) continue;
+        p.kc_gu = kg;
+        p.stride_gu = stride_for(kg);
+        p.stage_gu = sg;
+        p.kc_dn = kd;
+        p.stride_dn = stride_for(kd);
+        p.stage_dn = sd;
+        p.slot_bytes = slot;
+        p.stages = stages;
+        p.act_off = 0;
+        p.ring_off = ring_off;
+        p.bar_off = ring_off + MV_WARPS * stages * slot;
+        p.smem_bytes = p.bar_off + MV_WARPS * stages * 8;
+        return BH_OK;
+    }
+    return BH_EINVAL;
+}
+
+template <int FOLD, int NB>
+static int launch_moe_t(const MoeParams& p, const LaunchOpts& o) {
+    auto kern = q4k_moe_kernel<FOLD, NB>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
+            return BH_EIO;
+        attr_set = true;
+    }
+    // every CTA must be resident (grid barriers): clamp to what fits
+    int dev = 0, nsm = 0, occ = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, MV_THREADS, (size_t)p.smem_bytes) != cudaSuccess ||
+        occ < 1)
+        return BH_EIO;
+    const int grid = min(o.grid, nsm * occ);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(MV_THREADS);
+    cfg.dynamicSmemBytes = (size_t)p.smem_bytes;
+    cfg.stream = o.stream;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = o.pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, p) == cudaSuccess ? BH_OK : BH_EIO;
+}
+
+template <int FOLD>
+static int launch_moe_nb(const MoeParams& p, const LaunchOpts& o) {
+    // NB bounds the token columns of one expert (at most B)
+    if (p.B <= 1) return launch_moe_t<FOLD, 1>(p, o);
+    if (p.B <= 2) return launch_moe_t<FOLD, 2>(p, o);
+    if (p.B <= 4) return launch_moe_t<FOLD, 4>(p, o);
+    return launch_moe_t<FOLD, 8>(p, o);
+}
+
+int launch_moe(const MoeParams& pin, int fold, const LaunchOpts& o) {
+    if (o.grid < 1 || pin.B < 1 || pin.B > MOE_MAX_TOK || pin.k < 1 || pin.k > MOE_MAX_K ||
+        pin.n_expert < pin.k || pin.n_expert > MOE_MAX_EXPERT || pin.n_ff % QK || pin.n_embd % QK || !pin.gbar ||
+        !pin.out || !pin.gu || !pin.dout)
+        return BH_EINVAL;
+    MoeParams p = pin;
+    const int nb_e = p.n_embd / QK, nb_f = p.n_ff / QK;
+    int rc = encode_q4k_map(&p.tmap[0], p.w[0], (int64_t)p.n_expert * p.n_ff, nb_e, p.stride_gu, MOE_R);
+    if (rc == BH_OK) rc = encode_q4k_map(&p.tmap[1], p.w[1], (int64_t)p.n_expert * p.n_ff, nb_e, p.stride_gu, MOE_R);
+    if (rc == BH_OK) rc = encode_q4k_map(&p.tmap[2], p.w[2], (int64_t)p.n_expert * p.n_embd, nb_f, p.stride_dn, MOE_R);
+    if (rc != BH_OK) return rc;
+    if (fold == BH_FOLD_X86) return launch_moe_nb<BH_FOLD_X86>(p, o);
+    if (fold == BH_FOLD_GENERIC) return launch_moe_nb<BH_FOLD_GENERIC>(p, o);
+    return BH_EINVAL;
+}
+
+int launch_moe_route(const MoeParams& p, const LaunchOpts& o) {
+    if (p.B < 1 || p.B > MOE_MAX_TOK || p.k < 1 || p.k > MOE_MAX_K || p.n_expert < p.k ||
+        p.n_expert > MOE_MAX_EXPERT || !p.logits || !p.ids_out || !p.w_out)
+        return BH_EINVAL;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(MV_THREADS);
+    cfg.stream = o.stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = o.pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, moe_route_kernel, p) == cudaSuccess ? BH_OK : BH_EIO;
+}
+
+}  // namespace bh

@@ -1,0 +1,142 @@
+"""CPU: the routed-expert FFN restatement (oracle) against the reference's own
+code compiled in oracle/_ref (ggml's soft_max, SiLU and Q4_K x Q8_K vec_dot)
+and against the reference's top-k / renormalisation rules
+(desktop/engine/src/forward.cpp:1018-1107, ggml-cpu/ops.cpp:8157-8194)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as om
+
+
+def test_expf_within_one_ulp(oracle):
+    x = np.concatenate([np.linspace(-103.9, 88.7, 400_001, dtype=np.float32),
+                        oracle.normal((200_000,), 5, 0.0, 8.0)]).astype(np.float32)
+    y = oracle.expf(x).astype(np.float64)
+    ref = np.exp(x.astype(np.float64))
+    normal = (ref > 1.2e-38) & (ref < 3.4e38)
+    ulp = np.spacing(ref[normal].astype(np.float32)).astype(np.float64)
+    assert (np.abs(y[normal] - ref[normal]) / ulp).max() <= 1.0
+    assert oracle.expf(np.array([0.0], np.float32))[0] == 1.0
+    specials = oracle.expf(np.array([np.nan, np.inf, -np.inf, 100.0, -200.0], np.float32))
+    assert np.isnan(specials[0]) and specials[1] == np.inf and specials[2] == 0.0
+    assert specials[3] == np.inf and specials[4] == 0.0
+
+
+def test_silu_matches_reference(oracle, reference):
+    x = oracle.normal((200_000,), 3, 0.0, 4.0)
+    a, b = oracle.silu(x), reference.silu(x)
+    rel = np.abs(a - b) / np.maximum(np.abs(b), 1e-30)
+    # ggml_v_silu's own exp differs by a few ulp
+    assert rel.max() < 6e-7
+    assert np.mean(a == b) > 0.5
+
+
+def ref_route(reference, logits, k, norm=True):
+    """Top-k as the reference's ops.cpp writes it, over the reference's own soft_max."""
+    p = reference.soft_max(logits)
+    ids = np.empty((logits.shape[0], k), np.int32)
+    w = np.empty((logits.shape[0], k), np.float32)
+    for t in range(logits.shape[0]):
+        order = np.argsort(-p[t], kind="stable")[:k]
+        if k > 1:
+            order[[0, 1]] = order[[1, 0]]
+        ids[t] = order
+        ww = p[t][order]
+        if norm:
+            ww = ww / np.float32(np.sum(ww.astype(np.float64)))
+        w[t] = ww
+    return ids, w
+
+
+@pytest.mark.parametrize("n_expert,k", [(128, 8), (64, 4), (256, 8), (16, 1), (9, 2)])
+def test_route_matches_reference(oracle, reference, n_expert, k):
+    logits = oracle.normal((32, n_expert), 100 + n_expert + k, 0.0, 1.0)
+    ids, w = oracle.moe_route(logits, k)
+    rids, rw = ref_route(reference, logits, k)
+    assert (ids == rids).all()
+    np.testing.assert_allclose(w, rw, rtol=1e-5, atol=1e-6)
+    assert np.allclose(w.sum(1), 1.0, atol=1e-6)
+
+
+def test_route_ties_take_lower_index(oracle):
+    logits = np.zeros((1, 16), np.float32)
+    logits[0, [3, 9, 12]] = 2.0
+    ids, w = oracle.moe_route(logits, 4)
+    # ranks: 3, 9, 12 (equal, index order), then 0; slots 0 and 1 swapped
+    assert ids[0].tolist() == [9, 3, 12, 0]
+    assert w[0][0] == w[0][1] == w[0][2]
+
+
+def test_route_unnormalised_is_softmax(oracle, reference):
+    logits = oracle.normal((8, 128), 77, 0.0, 1.0)
+    ids, w = oracle.moe_route(logits, 8, norm=False)
+    p = reference.soft_max(logits)
+    for t in range(8):
+        np.testing.assert_allclose(w[t], p[t][ids[t]], rtol=1e-5, atol=1e-7)
+
+
+def test_rmsnorm_restatement(oracle):
+    x = oracle.normal((4, 2048), 9, 0.0, 1.0)
+    g = oracle.normal((2048,), 10, 1.0, 0.02)
+    y = oracle.rmsnorm(x, g, 1e-6)
+    for r in range(4):
+        ss = float(np.sum((x[r] * x[r]).astype(np.float64)))
+        mean = np.float32(ss / 2048)
+        scale = np.float32(1.0) / np.sqrt(np.float32(mean + np.float32(1e-6)))
+        assert (y[r] == (x[r] * scale) * g).all()
+
+
+def small_banks(oracle, n_expert, n_embd, n_ff, seed):
+    gate = oracle.quantize_q4k(oracle.normal((n_expert * n_ff, n_embd), seed, 0.0, 0.02))
+    up = oracle.quantize_q4k(oracle.normal((n_expert * n_ff, n_embd), seed + 1, 0.0, 0.02))
+    down = oracle.quantize_q4k(oracle.normal((n_expert * n_embd, n_ff), seed + 2, 0.0, 0.02))
+    return gate, up, down
+
+
+def test_moe_ffn_internal_consistency(oracle):
+    E, D, F, k, T = 8, 512, 256, 3, 3
+    gate, up, down = small_banks(oracle, E, D, F, 50)
+    cur = oracle.normal((T, D), 60, 0.0, 1.0)
+    ids, w = oracle.moe_route(oracle.normal((T, E), 61), k)
+    out, gu, dout = oracle.moe_ffn(cur, ids, w, gate, up, down, D, F)
+    gb, ub, db = gate.reshape(E, -1), up.reshape(E, -1), down.reshape(E, -1)
+    for t in range(T):
+        xq = oracle.quantize_q8k(cur[t:t + 1])
+        acc = np.zeros(D, np.float64)
+        for s in range(k):
+            e = ids[t, s]
+            g = oracle.matvec(gb[e], F, D, xq, 1)[0]
+            u = oracle.matvec(ub[e], F, D, xq, 1)[0]
+            assert (gu[t * k + s, :F] == g).all() and (gu[t * k + s, F:] == u).all()
+            par = oracle.silu(g) * u
+            d = oracle.matvec(db[e], D, F, oracle.quantize_q8k(par[None]), 1)[0]
+            assert (dout[t * k + s] == d).all()
+            acc += (d * w[t, s]).astype(np.float64)
+        assert (out[t] == acc.astype(np.float32)).all()
+
+
+def test_moe_ffn_vs_reference_kernels(oracle, reference):
+    """The same block composed from the reference's own Q8_K quantizer, x86
+    vec_dot and SiLU: only the SiLU exp differs, so outputs agree to a small
+    tolerance (an occasional Q8_K code of silu(gate)*up flips)."""
+    E, D, F, k, T = 8, 512, 256, 4, 2
+    gate, up, down = small_banks(oracle, E, D, F, 70)
+    cur = oracle.normal((T, D), 80, 0.0, 1.0)
+    ids, w = ref_route(reference, oracle.normal((T, E), 81), k)
+    out, _, _ = oracle.moe_ffn(cur, ids, w, gate, up, down, D, F)
+    gb, ub, db = gate.reshape(E, -1), up.reshape(E, -1), down.reshape(E, -1)
+    for t in range(T):
+        xq = reference.quantize_q8k(cur[t:t + 1])
+        acc = np.zeros(D, np.float64)
+        for s in range(k):
+            e = ids[t, s]
+            g = reference.matvec_rows(gb[e], F, D, xq, 1, om.FOLD_X86)[0]
+            u = reference.matvec_rows(ub[e], F, D, xq, 1, om.FOLD_X86)[0]
+            par = reference.silu(g) * u
+            d = reference.matvec_rows(db[e], D, F, reference.quantize_q8k(par[None]), 1, om.FOLD_X86)[0]
+            acc += (d * w[t, s]).astype(np.float64)
+        ref_out = acc.astype(np.float32)
+        scale = np.abs(ref_out).max()
+        assert np.abs(out[t] - ref_out).max() <= 5e-3 * scale
