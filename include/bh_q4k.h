@@ -266,7 +266,8 @@ int bh_q4k_moe(bh_ctx *ctx, const float *cur, int n_tok, const int32_t *selected
 /* The MoE layer stack of the 30B-A3B shape: per layer h += moe(RMSNorm(h) *
  * ffn_norm) with router logits seeded N(0, 1) per (layer, token), expert
  * banks seeded N(0, 0.02) and quantized to Q4_K on the device. One step runs
- * every layer for n_tok tokens in one CUDA graph (one launch per layer). */
+ * every layer for n_tok tokens, one cooperative launch per layer, captured
+ * in a CUDA graph. */
 typedef struct bh_moe_stack bh_moe_stack;
 typedef struct bh_moe_config {
     int n_layer;   /* 48 */

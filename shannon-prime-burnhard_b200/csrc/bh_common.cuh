@@ -102,6 +102,12 @@ __device__ __forceinline__ void tensor_g2s_2d(void* dst, const CUtensorMap* tmap
         : "memory");
 }
 
+// Fetch a tensor map descriptor (generic address of the kernel parameter) ahead of the
+// first copy that uses it.
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

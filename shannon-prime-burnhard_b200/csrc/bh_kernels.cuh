@@ -90,6 +90,12 @@ struct MoeParams {
     float* dout;           // [B*k][n_embd]: unweighted expert outputs of each pair
     float* out;            // [B][n_embd]: the weighted sum (stored, or added when residual)
     int residual;
+    // layers run by one launch (each reads h after the previous one added
+    // to it; needs residual): per-layer strides of the routing inputs and
+    // outputs, the norm weight, and the banks (the tensor maps cover all
+    // layers: expert e of layer l is bank row block l * n_expert + e)
+    int n_layer;
+    int64_t logits_ls, gamma_ls, route_ls;
     unsigned int* gbar;    // grid barrier words {count, generation}, zero before first use
     int* status;
     int64_t* trace;        // timeline probe (builds with BH_TRACE only; else unused)

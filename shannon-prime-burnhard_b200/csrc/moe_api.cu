@@ -65,6 +65,7 @@ bh::MoeParams moe_base(bh_ctx* ctx, int n_tok, int n_expert, int n_embd, int n_f
     p.n_ff = n_ff;
     p.k = k;
     p.B = n_tok;
+    p.n_layer = 1;
     p.status = ctx->d_status;
 #ifdef BH_TRACE
     p.trace = ctx->trace;
@@ -169,7 +170,7 @@ struct bh_moe_stack {
     bh_ctx* ctx = nullptr;
     bh_moe_config cfg{};
     cudaStream_t stream = nullptr;
-    uint8_t* wbuf = nullptr;    // per layer: gate bank, up bank, down bank
+    uint8_t* wbuf = nullptr;    // gate banks of all layers, then up banks, then down banks
     size_t gate_bytes = 0;      // one gate (or up) bank
     size_t down_bytes = 0;      // one down bank
     float* fbuf = nullptr;      // logits, norm, h, gu, dout, weights
@@ -197,10 +198,14 @@ uint64_t moe_tensor_seed(uint64_t seed, int layer, int which) {
 }
 
 const uint8_t* layer_bank(const bh_moe_stack* st, int l, int which) {
-    const size_t per_layer = 2 * st->gate_bytes + st->down_bytes;
-    return st->wbuf + (size_t)l * per_layer + (size_t)which * st->gate_bytes;
+    const size_t L = (size_t)st->cfg.n_layer;
+    if (which == BH_MOE_DOWN) return st->wbuf + 2 * L * st->gate_bytes + (size_t)l * st->down_bytes;
+    return st->wbuf + ((size_t)which * L + (size_t)l) * st->gate_bytes;
 }
 
+// One cooperative launch per layer (a single launch looping over all layers
+// measured slower: its extra grid barrier per layer costs more than the
+// programmatic-launch boundary it replaces).
 int enqueue_moe_step(bh_moe_stack* st, cudaStream_t s) {
     const bh_moe_config& c = st->cfg;
     for (int l = 0; l < c.n_layer; ++l) {

@@ -48,9 +48,21 @@ namespace {
             p.trace[((int64_t)blockIdx.x * MV_WARPS + (threadIdx.x >> 5)) * 8 + (k)] = (int64_t)t_;     \
         }                                                                                               \
     } while (0)
+// sub-steps of the router, in a second region of the buffer
+#define MOE_TRACE_R(k)                                                                                  \
+    do {                                                                                                \
+        if (p.trace && (threadIdx.x & 31) == 0) {                                                        \
+            uint64_t t_;                                                                                \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                      \
+            p.trace[(4096 + (int64_t)blockIdx.x * MV_WARPS + (threadIdx.x >> 5)) * 8 + (k)] = (int64_t)t_; \
+        }                                                                                               \
+    } while (0)
 #else
 #define MOE_TRACE_AT(k) \
     do {                \
+    } while (0)
+#define MOE_TRACE_R(k) \
+    do {               \
     } while (0)
 #endif
 
@@ -84,16 +96,18 @@ struct __align__(16) RouteScratch {
 // Equal probabilities are ranked lower index first (the reference's
 // std::partial_sort leaves their order unspecified). Inputs may have been
 // written by an earlier kernel, so they are read around L1.
-__device__ void moe_route(const MoeParams& p, MoeTable& tb, RouteScratch& rs) {
+__device__ __forceinline__ void moe_route(const MoeParams& p, const float* logits, MoeTable& tb,
+                                          RouteScratch& rs) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int E = p.n_expert, k = p.k, B = p.B;
     if (tid == 0) { tb.bad = 0; tb.n_unique = 0; }
     if (tid < MOE_MAX_EXPERT / 32) tb.bits[tid] = 0;
     if (tid < MOE_MAX_PAIRS) tb.ids[tid / MOE_MAX_K][tid % MOE_MAX_K] = -1;  // a slot left unset is caught below
     __syncthreads();
-    if (p.logits) {
-        for (int i = tid; i < B * E; i += MV_THREADS) rs.p[i / E][i % E] = __ldcg(p.logits + i);
+    if (logits) {
+        for (int i = tid; i < B * E; i += MV_THREADS) rs.p[i / E][i % E] = __ldcg(logits + i);
         __syncthreads();
+        MOE_TRACE_R(0);
         if (warp < B) {
             float* pr = rs.p[warp];
             float mx = -INFINITY;
@@ -121,6 +135,7 @@ __device__ void moe_route(const MoeParams& p, MoeTable& tb, RouteScratch& rs) {
             for (int i = lane; i < E; i += 32) pr[i] = __fmul_rn(pr[i], inv);
         }
         __syncthreads();
+        MOE_TRACE_R(1);
         // rank of every (token, expert) by (p descending, index ascending);
         // tpi threads share an item, each scanning every tpi-th group of 4
         const int items = B * E;
@@ -144,6 +159,7 @@ __device__ void moe_route(const MoeParams& p, MoeTable& tb, RouteScratch& rs) {
                         rank += (o.z > v) | ((o.z == v) & (j + 2 < i));
                         rank += (o.w > v) | ((o.w == v) & (j + 3 < i));
                     }
+
                 } else {
                     for (int j = sub; j < E; j += tpi) {
                         const float o = pr[j];
@@ -157,7 +173,9 @@ __device__ void moe_route(const MoeParams& p, MoeTable& tb, RouteScratch& rs) {
                 tb.ids[b][slot] = i;
             }
         }
+        MOE_TRACE_R(5);
         __syncthreads();
+        MOE_TRACE_R(2);
         if (tid < B) {
             float ws[MOE_MAX_K];
             double sum = 0.0;
@@ -175,6 +193,7 @@ __device__ void moe_route(const MoeParams& p, MoeTable& tb, RouteScratch& rs) {
         }
     }
     __syncthreads();
+    MOE_TRACE_R(3);
     // distinct experts, ascending: a bitmap, then an exclusive scan of its words
     if (tid < B * k) {
         const int e = tb.ids[tid / k][tid % k];
@@ -205,6 +224,7 @@ __device__ void moe_route(const MoeParams& p, MoeTable& tb, RouteScratch& rs) {
         if (lane == 31) tb.n_unique = incl;
     }
     __syncthreads();
+    MOE_TRACE_R(4);
     // column j of pair (t, s) = number of earlier pairs (row-major) on the same expert
     if (tid < B * k) {
         const int t = tid / k, s = tid - t * k;
@@ -232,10 +252,10 @@ __device__ void moe_route(const MoeParams& p, MoeTable& tb, RouteScratch& rs) {
 // (ggml rms_norm: fp32 squares summed in double, mean = (float)(sum / n),
 // scale = 1 / sqrt(mean + eps), y = (x * scale) * gamma), quantized to Q8_K.
 template <int FOLD>
-__device__ void stage_tokens(const MoeParams& p, uint8_t* act, float* s_scale) {
+__device__ void stage_tokens(const MoeParams& p, const float* gamma, uint8_t* act, float* s_scale) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int K = p.n_embd, nb = K / QK;
-    if (p.gamma) {
+    if (gamma) {
         for (int b = warp; b < p.B; b += MV_WARPS) {
             const float* h = p.h + (int64_t)b * K;
             double ss = 0.0;
@@ -259,9 +279,9 @@ __device__ void stage_tokens(const MoeParams& p, uint8_t* act, float* s_scale) {
         const float4* x = reinterpret_cast<const float4*>(p.h + (int64_t)b * K + e0);
         const float4 a0 = __ldcg(x), a1 = __ldcg(x + 1);
         float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        if (p.gamma) {
-            const float4 g0 = *reinterpret_cast<const float4*>(p.gamma + e0);
-            const float4 g1 = *reinterpret_cast<const float4*>(p.gamma + e0 + 4);
+        if (gamma) {
+            const float4 g0 = *reinterpret_cast<const float4*>(gamma + e0);
+            const float4 g1 = *reinterpret_cast<const float4*>(gamma + e0 + 4);
             const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
             const float sc = s_scale[b];
 #pragma unroll
@@ -340,7 +360,6 @@ __device__ bool grid_barrier(unsigned int* gbar, int* status) {
                     set_status(status, ST_TIMEOUT);
                     break;
                 }
-                __nanosleep(64);
             }
         }
         s_ok = ok;
@@ -388,211 +407,205 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_moe_kernel(const __grid_con
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const unsigned FULLM = 0xffffffffu;
-    MOE_TRACE_AT(0);
+    if (threadIdx.x == 0) {
+        prefetch_tmap(&p.tmap[0]);
+        prefetch_tmap(&p.tmap[1]);
+        prefetch_tmap(&p.tmap[2]);
+    }
     pdl_wait();  // routing inputs and h may come from the previous kernel
     pdl_trigger();
-    moe_route(p, tb, rs);
-    MOE_TRACE_AT(1);
-    if (tb.bad) {
-        if (threadIdx.x == 0) set_status(p.status, ST_BADARG);
-        return;  // uniform over the grid: every CTA built the same table
-    }
-    if (blockIdx.x == 0 && threadIdx.x < p.B * p.k) {
-        const int t = threadIdx.x / p.k, s = threadIdx.x - t * p.k;
-        if (p.ids_out) p.ids_out[threadIdx.x] = tb.ids[t][s];
-        if (p.w_out) p.w_out[threadIdx.x] = tb.w[t][s];
-    }
 
     uint8_t* act = smem + p.act_off;
     uint8_t* ring = smem + p.ring_off + (size_t)warp * p.stages * p.slot_bytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off) + warp * p.stages;
-
-    const int U = tb.n_unique;
-    const int nb_e = p.n_embd / QK, nb_f = p.n_ff / QK;
-    PhaseRange gu, dn;
-    gu.te = 2 * p.n_ff / R;
-    dn.te = p.n_embd / R;
-    gu.t_begin = (int)((int64_t)U * gu.te * blockIdx.x / gridDim.x);
-    gu.t_end = (int)((int64_t)U * gu.te * (blockIdx.x + 1) / gridDim.x);
-    dn.t_begin = (int)((int64_t)U * dn.te * blockIdx.x / gridDim.x);
-    dn.t_end = (int)((int64_t)U * dn.te * (blockIdx.x + 1) / gridDim.x);
-    const int my_gu = gu.mine(warp), my_dn = dn.mine(warp);
-    const int nkc_gu = (nb_e + p.kc_gu - 1) / p.kc_gu, nkc_dn = (nb_f + p.kc_dn - 1) / p.kc_dn;
-    const int total = my_gu * nkc_gu + my_dn * nkc_dn;
-
     if (lane == 0) {
         for (int s = 0; s < p.stages; ++s) mbar_init(&full[s], 1);
         fence_mbar_init();
     }
     __syncwarp();
-
-    // one issue cursor over the warp's gate|up tiles, then its down tiles
     const uint64_t pol = policy_evict_first();
-    int i_ph = my_gu > 0 ? 0 : 1, i_j = 0, i_c = 0, i_s = 0, issued = 0;
-    auto issue_next = [&]() {
-        if (lane == 0) {
-            int map, row, x;
-            uint32_t bytes;
-            if (i_ph == 0) {
-                const int tile = gu.t_begin + warp + i_j * MV_WARPS;
-                const int u = tile / gu.te, rt = (tile - u * gu.te) * R;
-                map = rt >= p.n_ff;
-                row = tb.expert[u] * p.n_ff + (map ? rt - p.n_ff : rt);
-                x = i_c * p.kc_gu * (Q4K_BYTES / 8);
-                bytes = (uint32_t)p.stage_gu;
-            } else {
-                const int tile = dn.t_begin + warp + i_j * MV_WARPS;
-                const int u = tile / dn.te, rt = (tile - u * dn.te) * R;
-                map = 2;
-                row = tb.expert[u] * p.n_embd + rt;
-                x = i_c * p.kc_dn * (Q4K_BYTES / 8);
-                bytes = (uint32_t)p.stage_dn;
-            }
-            mbar_arrive_expect_tx(&full[i_s], bytes);
-            tensor_g2s_2d(ring + (size_t)i_s * p.slot_bytes, &p.tmap[map], x, row, &full[i_s], pol);
-        }
-        __syncwarp();
-        ++issued;
-        if (++i_c == (i_ph == 0 ? nkc_gu : nkc_dn)) {
-            i_c = 0;
-            if (++i_j == my_gu && i_ph == 0) { i_ph = 1; i_j = 0; }
-        }
-        if (++i_s == p.stages) i_s = 0;
-    };
-    const int prefill = min(p.stages, total);
-    for (int q = 0; q < prefill; ++q) issue_next();
-    MOE_TRACE_AT(2);
-
-    stage_tokens<FOLD>(p, act, s_scale);
-    __syncthreads();
-    MOE_TRACE_AT(3);
-
+    const int nb_e = p.n_embd / QK, nb_f = p.n_ff / QK;
+    const int nkc_gu = (nb_e + p.kc_gu - 1) / p.kc_gu, nkc_dn = (nb_f + p.kc_dn - 1) / p.kc_dn;
     const int rgrp = lane / TPR;
     const int t = lane % TPR;
-    int consumed = 0, c_s = 0;
+    // ring cursors run on across layers: every layer consumes all it issues
+    int c_s = 0, i_s = 0;
     uint32_t c_ph = 0;
     bool ok = true;
-    auto wait_slot = [&]() -> bool {
-        if (!__all_sync(FULLM, mbar_wait_bounded(&full[c_s], c_ph))) {
-            if (lane == 0) set_status(p.status, ST_TIMEOUT);
-            return false;
+
+    for (int l = 0; l < p.n_layer; ++l) {
+        MOE_TRACE_AT(0);
+        moe_route(p, p.logits ? p.logits + l * p.logits_ls : nullptr, tb, rs);
+        MOE_TRACE_AT(1);
+        if (tb.bad) {
+            if (threadIdx.x == 0) set_status(p.status, ST_BADARG);
+            return;  // uniform over the grid: every CTA built the same table
         }
+        if (blockIdx.x == 0 && threadIdx.x < p.B * p.k) {
+            const int tk = threadIdx.x / p.k, s = threadIdx.x - tk * p.k;
+            if (p.ids_out) p.ids_out[l * p.route_ls + threadIdx.x] = tb.ids[tk][s];
+            if (p.w_out) p.w_out[l * p.route_ls + threadIdx.x] = tb.w[tk][s];
+        }
+
+        const int U = tb.n_unique;
+        const int ebase = l * p.n_expert;  // bank row blocks of this layer
+        PhaseRange gu, dn;
+        gu.te = 2 * p.n_ff / R;
+        dn.te = p.n_embd / R;
+        gu.t_begin = (int)((int64_t)U * gu.te * blockIdx.x / gridDim.x);
+        gu.t_end = (int)((int64_t)U * gu.te * (blockIdx.x + 1) / gridDim.x);
+        dn.t_begin = (int)((int64_t)U * dn.te * blockIdx.x / gridDim.x);
+        dn.t_end = (int)((int64_t)U * dn.te * (blockIdx.x + 1) / gridDim.x);
+        const int my_gu = gu.mine(warp), my_dn = dn.mine(warp);
+        const int total = my_gu * nkc_gu + my_dn * nkc_dn;
+
+        // one issue cursor over the warp's gate|up tiles, then its down tiles
+        int i_ph = my_gu > 0 ? 0 : 1, i_j = 0, i_c = 0, issued = 0;
+        auto issue_next = [&]() {
+            if (lane == 0) {
+                int map, x;
+                int64_t row;
+                uint32_t bytes;
+                if (i_ph == 0) {
+                    const int tile = gu.t_begin + warp + i_j * MV_WARPS;
+                    const int u = tile / gu.te, rt = (tile - u * gu.te) * R;
+                    map = rt >= p.n_ff;
+                    row = (int64_t)(ebase + tb.expert[u]) * p.n_ff + (map ? rt - p.n_ff : rt);
+                    x = i_c * p.kc_gu * (Q4K_BYTES / 8);
+                    bytes = (uint32_t)p.stage_gu;
+                } else {
+                    const int tile = dn.t_begin + warp + i_j * MV_WARPS;
+                    const int u = tile / dn.te, rt = (tile - u * dn.te) * R;
+                    map = 2;
+                    row = (int64_t)(ebase + tb.expert[u]) * p.n_embd + rt;
+                    x = i_c * p.kc_dn * (Q4K_BYTES / 8);
+                    bytes = (uint32_t)p.stage_dn;
+                }
+                mbar_arrive_expect_tx(&full[i_s], bytes);
+                tensor_g2s_2d(ring + (size_t)i_s * p.slot_bytes, &p.tmap[map], x, (int)row, &full[i_s], pol);
+            }
+            __syncwarp();
+            ++issued;
+            if (++i_c == (i_ph == 0 ? nkc_gu : nkc_dn)) {
+                i_c = 0;
+                if (++i_j == my_gu && i_ph == 0) { i_ph = 1; i_j = 0; }
+            }
+            if (++i_s == p.stages) i_s = 0;
+        };
+        const int prefill = min(p.stages, total);
+        for (int q = 0; q < prefill; ++q) issue_next();
+        MOE_TRACE_AT(2);
+
+        stage_tokens<FOLD>(p, p.gamma ? p.gamma + l * p.gamma_ls : nullptr, act, s_scale);
+        __syncthreads();
+        MOE_TRACE_AT(3);
+
+        int consumed = 0;
+        auto wait_slot = [&]() -> bool {
+            if (!__all_sync(FULLM, mbar_wait_bounded(&full[c_s], c_ph))) {
+                if (lane == 0) set_status(p.status, ST_TIMEOUT);
+                return false;
+            }
 #ifdef BH_TRACE
-        if (consumed == 0) MOE_TRACE_AT(4);
+            if (consumed == 0) MOE_TRACE_AT(4);
 #endif
-        ++consumed;
-        return true;
-    };
-    auto release_slot = [&]() {
-        __syncwarp();
-        if (issued < total) {
-            fence_proxy_async_smem();
-            issue_next();
-        }
-        if (++c_s == p.stages) { c_s = 0; c_ph ^= 1u; }
-    };
+            ++consumed;
+            return true;
+        };
+        auto release_slot = [&]() {
+            __syncwarp();
+            if (issued < total) {
+                fence_proxy_async_smem();
+                issue_next();
+            }
+            if (++c_s == p.stages) { c_s = 0; c_ph ^= 1u; }
+        };
 
-    // ---- phase 1: gate | up
-    for (int j = 0; j < my_gu && ok; ++j) {
-        const int tile = gu.t_begin + warp + j * MV_WARPS;
-        const int u = tile / gu.te, rt = (tile - u * gu.te) * R;
-        const int cols = tb.cnt[u];
-        int colbase[NB];
+        // ---- the two matvec phases share one tile loop (one copy of the
+        // code): phase 0 gate | up over the token columns, then a grid
+        // barrier and the staging of the down columns, phase 1 down over the
+        // (token, slot) pairs
+        const int u_lo = dn.t_end > dn.t_begin ? dn.t_begin / dn.te : 0;
+        const int u_hi = dn.t_end > dn.t_begin ? (dn.t_end - 1) / dn.te : 0;
+        for (int ph = 0; ph < 2; ++ph) {
+            if (ph == 1) {
+                MOE_TRACE_AT(5);
+                ok = grid_barrier(p.gbar, p.status) && ok;
+                if (dn.t_end > dn.t_begin && __syncthreads_and(ok)) stage_pairs<FOLD>(p, tb, u_lo, u_hi, act, s_qbase);
+                __syncthreads();
+                MOE_TRACE_AT(6);
+            }
+            const PhaseRange& pr = ph == 0 ? gu : dn;
+            const int mine = ph == 0 ? my_gu : my_dn;
+            const int kc = ph == 0 ? p.kc_gu : p.kc_dn, stride = ph == 0 ? p.stride_gu : p.stride_dn;
+            const int nb = ph == 0 ? nb_e : nb_f, nkc = ph == 0 ? nkc_gu : nkc_dn;
+            float* const obase = ph == 0 ? p.gu : p.dout;
+            const int64_t ostride = ph == 0 ? 2 * (int64_t)p.n_ff : (int64_t)p.n_embd;
+            for (int j = 0; j < mine && ok; ++j) {
+                const int tile = pr.t_begin + warp + j * MV_WARPS;
+                const int u = tile / pr.te, rt = (tile - u * pr.te) * R;
+                const int cols = tb.cnt[u];
+                int colbase[NB];
 #pragma unroll
-        for (int c = 0; c < NB; ++c) colbase[c] = tb.col_tok[u][c < cols ? c : 0];
-        float acc[NB][L], accm[NB];
+                for (int c = 0; c < NB; ++c) {
+                    const int cc = c < cols ? c : 0;
+                    colbase[c] = ph == 0 ? tb.col_tok[u][cc] : s_qbase[u - u_lo] + cc;
+                }
+                float acc[NB][L], accm[NB];
 #pragma unroll
-        for (int c = 0; c < NB; ++c) {
+                for (int c = 0; c < NB; ++c) {
 #pragma unroll
-            for (int e = 0; e < L; ++e) acc[c][e] = 0.f;
-            accm[c] = 0.f;
-        }
-        for (int ci = 0; ci < nkc_gu; ++ci) {
-            if (!(ok = wait_slot())) break;
-            const int sbc = ci * p.kc_gu;
-            tile_fold<FOLD, NB>(ring + (size_t)c_s * p.slot_bytes + (size_t)rgrp * p.stride_gu, min(p.kc_gu, nb_e - sbc),
-                                act, nb_e, colbase, cols, t, acc, accm, sbc);
-            release_slot();
-        }
-        if (!ok) break;
+                    for (int e = 0; e < L; ++e) acc[c][e] = 0.f;
+                    accm[c] = 0.f;
+                }
+                for (int ci = 0; ci < nkc; ++ci) {
+                    if (!(ok = wait_slot())) break;
+                    const int sbc = ci * kc;
+                    tile_fold<FOLD, NB>(ring + (size_t)c_s * p.slot_bytes + (size_t)rgrp * stride, min(kc, nb - sbc),
+                                        act, nb, colbase, cols, t, acc, accm, sbc);
+                    release_slot();
+                }
+                if (!ok) break;
 #pragma unroll
-        for (int c = 0; c < NB; ++c) {
-            if (c < cols) {
-                const float v = row_value<FOLD, TPR>(acc[c], accm[c], rgrp);
-                if (t == 0) {
-                    const int pair = tb.col_tok[u][c] * p.k + tb.col_slot[u][c];
-                    p.gu[(int64_t)pair * 2 * p.n_ff + rt + rgrp] = v;
+                for (int c = 0; c < NB; ++c) {
+                    if (c < cols) {
+                        const float v = row_value<FOLD, TPR>(acc[c], accm[c], rgrp);
+                        if (t == 0) {
+                            const int pair = tb.col_tok[u][c] * p.k + tb.col_slot[u][c];
+                            obase[(int64_t)pair * ostride + rt + rgrp] = v;
+                        }
+                    }
                 }
             }
         }
-    }
-    MOE_TRACE_AT(5);
-    ok = grid_barrier(p.gbar, p.status) && ok;
-
-    // ---- phase 2: down
-    const int u_lo = dn.t_end > dn.t_begin ? dn.t_begin / dn.te : 0;
-    const int u_hi = dn.t_end > dn.t_begin ? (dn.t_end - 1) / dn.te : 0;
-    if (dn.t_end > dn.t_begin && __syncthreads_and(ok)) stage_pairs<FOLD>(p, tb, u_lo, u_hi, act, s_qbase);
-    __syncthreads();
-    MOE_TRACE_AT(6);
-    for (int j = 0; j < my_dn && ok; ++j) {
-        const int tile = dn.t_begin + warp + j * MV_WARPS;
-        const int u = tile / dn.te, rt = (tile - u * dn.te) * R;
-        const int cols = tb.cnt[u];
-        int colbase[NB];
-#pragma unroll
-        for (int c = 0; c < NB; ++c) colbase[c] = s_qbase[u - u_lo] + (c < cols ? c : 0);
-        float acc[NB][L], accm[NB];
-#pragma unroll
-        for (int c = 0; c < NB; ++c) {
-#pragma unroll
-            for (int e = 0; e < L; ++e) acc[c][e] = 0.f;
-            accm[c] = 0.f;
-        }
-        for (int ci = 0; ci < nkc_dn; ++ci) {
-            if (!(ok = wait_slot())) break;
-            const int sbc = ci * p.kc_dn;
-            tile_fold<FOLD, NB>(ring + (size_t)c_s * p.slot_bytes + (size_t)rgrp * p.stride_dn, min(p.kc_dn, nb_f - sbc),
-                                act, nb_f, colbase, cols, t, acc, accm, sbc);
-            release_slot();
-        }
-        if (!ok) break;
-#pragma unroll
-        for (int c = 0; c < NB; ++c) {
-            if (c < cols) {
-                const float v = row_value<FOLD, TPR>(acc[c], accm[c], rgrp);
-                if (t == 0) {
-                    const int pair = tb.col_tok[u][c] * p.k + tb.col_slot[u][c];
-                    p.dout[(int64_t)pair * p.n_embd + rt + rgrp] = v;
-                }
+        if (!ok && lane == 0) {
+            // nothing of this warp may still be in flight when the CTA exits
+            int s = c_s;
+            uint32_t ph = c_ph;
+            for (int q = consumed; q < issued; ++q) {
+                mbar_wait_bounded(&full[s], ph);
+                if (++s == p.stages) { s = 0; ph ^= 1u; }
             }
         }
-    }
-    if (!ok && lane == 0) {
-        // nothing of this warp may still be in flight when the CTA exits
-        int s = c_s;
-        uint32_t ph = c_ph;
-        for (int q = consumed; q < issued; ++q) {
-            mbar_wait_bounded(&full[s], ph);
-            if (++s == p.stages) { s = 0; ph ^= 1u; }
-        }
-    }
-    MOE_TRACE_AT(7);
-    ok = grid_barrier(p.gbar, p.status) && ok;
-    if (!__syncthreads_and(ok)) return;
+        MOE_TRACE_AT(7);
+        ok = grid_barrier(p.gbar, p.status) && ok;
+        if (!__syncthreads_and(ok)) return;
 
-    // ---- combine: ggml_mul (fp32 product) then ggml_sum_rows over the slots
-    // (double, in slot order), rounded once; this CTA's slice of the outputs
-    const int n = p.B * p.n_embd;
-    const int per = (n + gridDim.x - 1) / gridDim.x;
-    const int e_end = min(n, (int)(blockIdx.x + 1) * per);
-    for (int idx = blockIdx.x * per + threadIdx.x; idx < e_end; idx += MV_THREADS) {
-        const int tk = idx / p.n_embd, i = idx - tk * p.n_embd;
-        double a = 0.0;
-        for (int s = 0; s < p.k; ++s)
-            a = __dadd_rn(a, (double)__fmul_rn(__ldcg(p.dout + ((int64_t)tk * p.k + s) * p.n_embd + i), tb.w[tk][s]));
-        const float r = __double2float_rn(a);
-        p.out[idx] = p.residual ? __fadd_rn(p.out[idx], r) : r;
+        // ---- combine: ggml_mul (fp32 product) then ggml_sum_rows over the
+        // slots (double, in slot order), rounded once; this CTA's slice
+        const int n = p.B * p.n_embd;
+        const int per = (n + gridDim.x - 1) / gridDim.x;
+        const int e_end = min(n, (int)(blockIdx.x + 1) * per);
+        for (int idx = blockIdx.x * per + threadIdx.x; idx < e_end; idx += MV_THREADS) {
+            const int tk = idx / p.n_embd, i = idx - tk * p.n_embd;
+            double a = 0.0;
+            for (int s = 0; s < p.k; ++s)
+                a = __dadd_rn(a, (double)__fmul_rn(__ldcg(p.dout + ((int64_t)tk * p.k + s) * p.n_embd + i), tb.w[tk][s]));
+            const float r = __double2float_rn(a);
+            p.out[idx] = p.residual ? __fadd_rn(p.out[idx], r) : r;
+        }
+        // the next layer's RMSNorm reads every CTA's slice of h
+        if (l + 1 < p.n_layer && !grid_barrier(p.gbar, p.status)) return;
     }
 }
 
@@ -602,7 +615,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) moe_route_kernel(const __grid_c
     __shared__ RouteScratch rs;
     pdl_wait();
     pdl_trigger();
-    moe_route(p, tb, rs);
+    moe_route(p, p.logits, tb, rs);
     if (tb.bad) {
         if (threadIdx.x == 0) set_status(p.status, ST_BADARG);
         return;
@@ -702,13 +715,15 @@ static int launch_moe_nb(const MoeParams& p, const LaunchOpts& o) {
 int launch_moe(const MoeParams& pin, int fold, const LaunchOpts& o) {
     if (o.grid < 1 || pin.B < 1 || pin.B > MOE_MAX_TOK || pin.k < 1 || pin.k > MOE_MAX_K ||
         pin.n_expert < pin.k || pin.n_expert > MOE_MAX_EXPERT || pin.n_ff % QK || pin.n_embd % QK || !pin.gbar ||
-        !pin.out || !pin.gu || !pin.dout)
+        !pin.out || !pin.gu || !pin.dout || pin.n_layer < 1 || (pin.n_layer > 1 && !pin.residual) ||
+        (int64_t)pin.n_layer * pin.n_expert * (pin.n_ff > pin.n_embd ? pin.n_ff : pin.n_embd) >= ((int64_t)1 << 31))
         return BH_EINVAL;
     MoeParams p = pin;
     const int nb_e = p.n_embd / QK, nb_f = p.n_ff / QK;
-    int rc = encode_q4k_map(&p.tmap[0], p.w[0], (int64_t)p.n_expert * p.n_ff, nb_e, p.stride_gu, MOE_R);
-    if (rc == BH_OK) rc = encode_q4k_map(&p.tmap[1], p.w[1], (int64_t)p.n_expert * p.n_ff, nb_e, p.stride_gu, MOE_R);
-    if (rc == BH_OK) rc = encode_q4k_map(&p.tmap[2], p.w[2], (int64_t)p.n_expert * p.n_embd, nb_f, p.stride_dn, MOE_R);
+    const int64_t ne = (int64_t)p.n_layer * p.n_expert;
+    int rc = encode_q4k_map(&p.tmap[0], p.w[0], ne * p.n_ff, nb_e, p.stride_gu, MOE_R);
+    if (rc == BH_OK) rc = encode_q4k_map(&p.tmap[1], p.w[1], ne * p.n_ff, nb_e, p.stride_gu, MOE_R);
+    if (rc == BH_OK) rc = encode_q4k_map(&p.tmap[2], p.w[2], ne * p.n_embd, nb_f, p.stride_dn, MOE_R);
     if (rc != BH_OK) return rc;
     if (fold == BH_FOLD_X86) return launch_moe_nb<BH_FOLD_X86>(p, o);
     if (fold == BH_FOLD_GENERIC) return launch_moe_nb<BH_FOLD_GENERIC>(p, o);
