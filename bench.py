@@ -119,6 +119,96 @@ def barrier(world: int) -> None:
         dist.barrier()
 
 
+# ---------------------------------------------------------- extra configs
+def time_events(fn, reps: int, warm: int = 3) -> float:
+    """Average ms of fn() over reps calls, CUDA events on the current stream."""
+    import torch
+
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def bench_lmhead_tp(bh, ctx, world: int, rank: int, reps: int) -> dict:
+    """Config 5: the 151936 x 4096 Q4_K LM head, rows split over the ranks,
+    all-gather of the fp32 logits (or of the per-rank candidates only) and the
+    identical greedy pick on every rank; batch 1 and 4. Eager launches (host
+    launch cost included); device time as the max over ranks."""
+    import torch
+
+    import sharding
+
+    n, k = 151936, 4096
+    lo, hi = sharding.even_shards(n, world)[rank]
+    g = torch.Generator(device="cuda").manual_seed(SEED + 5)
+    rows = hi - lo
+    w_local = ctx.q4k_quantize(torch.randn((rows, k), generator=g, device="cuda") * 0.02)
+    head = sharding.TPLMHead(ctx, n, k, rank, world, w_local)
+    out = {"workload": "LM head 151936 x 4096 (config 5), rows split over the GPUs", "rows_per_gpu": rows}
+    wbytes = n * (k // 256) * 144
+    for b in (1, 4):
+        x = torch.randn((b, k), generator=g, device="cuda")
+        for mode, gl in (("gather_logits", True), ("gather_candidates", False)):
+            barrier(world)
+            ms = max_over_ranks(time_events(lambda: head.forward(x, gather_logits=gl), reps), world)
+            out[f"b{b}_{mode}"] = {"ms": round(ms, 4), "weight_GBps_all_gpus": round(wbytes / (ms / 1e3) / 1e9, 1)}
+    del w_local, head
+    torch.cuda.empty_cache()
+    return out
+
+
+def bench_moe(bh, ctx, world: int, rank: int, steps: int) -> dict:
+    """Config 4: the 30B-A3B-shaped expert layers (128 experts, 2048 -> 768 ->
+    2048, top-8 of seeded router logits, renormalised). One GPU: the 48-layer
+    stack (one cooperative launch per layer, CUDA graph), 1 and 8 tokens.
+    Several GPUs: one layer expert-parallel (experts split over the ranks,
+    NCCL all-reduce of the expert outputs, slot-order combine), eager."""
+    import torch
+
+    import sharding
+
+    res = {"workload": "MoE 30B-A3B-shaped expert layers (config 4)"}
+    if world == 1:
+        for t in (1, 8):
+            cfg = bh.default_moe_config(n_tok=t)
+            st = bh.MoeStack(ctx, cfg, SEED + 4)
+            h = torch.randn((t, cfg.n_embd), device="cuda")
+            out = torch.empty_like(h)
+            ms = time_events(lambda: st.step(h, out), max(5, steps // 20))
+            info = st.info()
+            res[f"tokens{t}"] = {"layers": cfg.n_layer, "ms_per_step": round(ms, 4),
+                                 "us_per_layer": round(ms * 1e3 / cfg.n_layer, 2),
+                                 "expert_bytes_per_step": info["step_bytes"],
+                                 "GBps": round(info["step_bytes"] / (ms / 1e3) / 1e9, 1),
+                                 "tokens_per_s": round(t * 1e3 / ms, 1)}
+            st.close()
+            del st
+            torch.cuda.empty_cache()
+        return res
+    E, D, F, k = 128, 2048, 768, 8
+    lo, hi = sharding.even_shards(E, world)[rank]
+    g = torch.Generator(device="cuda").manual_seed(SEED + 6)
+    own = {}
+    for name, rows, cols in (("gate", F, D), ("up", F, D), ("down", D, F)):
+        own[name] = ctx.q4k_quantize(torch.randn(((hi - lo) * rows, cols), generator=g, device="cuda") * 0.02)
+    ep = sharding.EPMoE(ctx, E, D, F, k, rank, world, own["gate"], own["up"], own["down"])
+    for t in (1, 8):
+        cur = torch.randn((t, D), device="cuda")
+        lg = torch.randn((t, E), device="cuda")
+        barrier(world)
+        ms = max_over_ranks(time_events(lambda: ep.forward(cur, logits=lg), 20), world)
+        res[f"tokens{t}_one_layer_expert_parallel"] = {"us": round(ms * 1e3, 2)}
+    return res
+
+
 # ---------------------------------------------------------------- CPU path
 def cpu_reference_step_fn(st, nthreads: int):
     """The reference's CPU decode step on host copies of the stack."""
@@ -169,6 +259,7 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=0, help="override n_layer (testing only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the config 4 / config 5 measurements")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -274,6 +365,18 @@ def main() -> None:
             traffic = None
     status = ctx.status()
 
+    # the other configurations of the path, reported beside the headline
+    extra = {}
+    if not args.no_extra:
+        try:
+            extra["lmhead_row_split"] = bench_lmhead_tp(bh, ctx, world, rank, reps=max(20, args.steps // 10))
+        except Exception as e:  # reported, never silently dropped
+            extra["lmhead_row_split"] = {"error": repr(e)}
+        try:
+            extra["moe"] = bench_moe(bh, ctx, world, rank, args.steps)
+        except Exception as e:
+            extra["moe"] = {"error": repr(e)}
+
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu, kind = cpu_reference_step_fn(st, nthreads)
@@ -298,6 +401,7 @@ def main() -> None:
                          "bytes_per_launch": op_bytes, "ms_per_launch": round(op_ms, 5)},
             "cpu_baseline": cpu_baseline,
             "gpu_launches": launches * args.steps,
+            "configs_beside": extra,
             "clocks": clocks,
             "device_status": status,
         }

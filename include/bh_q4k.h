@@ -263,6 +263,27 @@ int bh_q4k_moe(bh_ctx *ctx, const float *cur, int n_tok, const int32_t *selected
                const void *down_exps, int n_expert, int n_embd, int n_ff, int k, float *out,
                int32_t *selected_out, float *weights_out, int fold, void *stream);
 
+/* Expert-parallel share of bh_q4k_moe on one rank: only the pairs (token,
+ * slot) routed to experts [expert_lo, expert_hi) are computed, from banks
+ * holding exactly those experts (gate_own / up_own [expert_hi - expert_lo]
+ * [n_ff][n_embd], down_own [..][n_embd][n_ff]) -- the sub-bank split that
+ * BURN_MOE's pivot makes between its CPU and GPU banks (burn_moe_op.h:40-46).
+ * dout [n_tok*k][n_embd] receives the unweighted expert output of every
+ * owned pair and -0.0 in the rows of the others, so the element-wise sum of
+ * dout over ranks owning disjoint ranges that cover all experts equals the
+ * single-device expert outputs exactly; bh_moe_combine then forms out.
+ * Routing as in bh_q4k_moe (every rank routes identically). */
+int bh_q4k_moe_ep(bh_ctx *ctx, const float *cur, int n_tok, const int32_t *selected, const float *weights,
+                  const float *router_logits, int norm_topk, const void *gate_own, const void *up_own,
+                  const void *down_own, int n_expert, int expert_lo, int expert_hi, int n_embd, int n_ff, int k,
+                  float *dout, int32_t *selected_out, float *weights_out, int fold, void *stream);
+
+/* out[t][i] = (float) sum over slots s, in order, of (double)(dout[t*k+s][i] * weights[t][s])
+ * (ggml_mul then ggml_sum_rows, forward.cpp:1099-1107); with residual != 0
+ * the result is added to out instead. */
+int bh_moe_combine(bh_ctx *ctx, const float *dout, const float *weights, int n_tok, int k, int n_embd, float *out,
+                   int residual, void *stream);
+
 /* The MoE layer stack of the 30B-A3B shape: per layer h += moe(RMSNorm(h) *
  * ffn_norm) with router logits seeded N(0, 1) per (layer, token), expert
  * banks seeded N(0, 0.02) and quantized to Q4_K on the device. One step runs

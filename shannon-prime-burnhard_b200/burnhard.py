@@ -109,6 +109,9 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.bh_moe_route.argtypes = [_vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp]
     L.bh_q4k_moe.argtypes = [_vp, _vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int,
                              C.c_int, _vp, _vp, _vp, C.c_int, _vp]
+    L.bh_q4k_moe_ep.argtypes = [_vp, _vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp, _vp, _vp, C.c_int, C.c_int,
+                                C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp, C.c_int, _vp]
+    L.bh_moe_combine.argtypes = [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp, C.c_int, _vp]
     L.bh_moe_default_config.argtypes = [C.POINTER(MoeConfig)]
     L.bh_moe_default_config.restype = None
     L.bh_moe_stack_create.argtypes = [_vp, C.POINTER(MoeConfig), C.c_uint64, C.POINTER(_vp)]
@@ -373,6 +376,41 @@ def moe(ctx: Context, cur, gate, up, down, n_expert: int, n_ff: int, k: int, sel
     if logits is not None:
         return out, sel_out, w_out
     return out, selected, weights
+
+
+def moe_ep(ctx: Context, cur, gate_own, up_own, down_own, n_expert: int, expert_lo: int, expert_hi: int, n_ff: int,
+           k: int, selected=None, weights=None, logits=None, norm_topk: bool = True, dout=None,
+           fold: int = FOLD_X86, stream=None):
+    """This rank's expert outputs (bh_q4k_moe_ep): dout [T*k, n_embd] holds the
+    owned pairs' outputs and -0.0 elsewhere; returns (dout, selected, weights)."""
+    import torch
+
+    t, n_embd = cur.shape
+    if dout is None:
+        dout = torch.empty((t * k, n_embd), dtype=torch.float32, device=cur.device)
+    sel_out = w_out = None
+    if logits is not None:
+        sel_out = torch.empty((t, k), dtype=torch.int32, device=cur.device)
+        w_out = torch.empty((t, k), dtype=torch.float32, device=cur.device)
+    _check(lib.bh_q4k_moe_ep(ctx.h, _dp(cur), t, _dp(selected), _dp(weights), _dp(logits), int(norm_topk),
+                             _dp(gate_own), _dp(up_own), _dp(down_own), n_expert, expert_lo, expert_hi, n_embd, n_ff,
+                             k, _dp(dout), _dp(sel_out), _dp(w_out), fold, _stream(stream)), "bh_q4k_moe_ep")
+    if logits is not None:
+        return dout, sel_out, w_out
+    return dout, selected, weights
+
+
+def moe_combine(ctx: Context, dout, weights, out=None, residual: bool = False, stream=None):
+    """out [T, n_embd] = sum over slots of weights * dout (bh_moe_combine)."""
+    import torch
+
+    t, k = weights.shape
+    n_embd = dout.shape[1]
+    if out is None:
+        out = torch.empty((t, n_embd), dtype=torch.float32, device=dout.device)
+    _check(lib.bh_moe_combine(ctx.h, _dp(dout), _dp(weights), t, k, n_embd, _dp(out), int(residual),
+                              _stream(stream)), "bh_moe_combine")
+    return out
 
 
 def default_moe_config(**overrides) -> MoeConfig:

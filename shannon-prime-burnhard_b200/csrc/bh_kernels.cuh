@@ -96,6 +96,12 @@ struct MoeParams {
     // layers: expert e of layer l is bank row block l * n_expert + e)
     int n_layer;
     int64_t logits_ls, gamma_ls, route_ls;
+    // expert parallelism: only experts [e_lo, e_hi) are computed, from banks
+    // holding exactly those experts (bank row block = expert - e_lo); with
+    // combine == 0 the launch stops after writing dout (the rows of pairs on
+    // other experts are set to -0.0, so summing the dout of all ranks
+    // reproduces every value exactly) and out is not touched
+    int e_lo, e_hi, combine;
     unsigned int* gbar;    // grid barrier words {count, generation}, zero before first use
     int* status;
     int64_t* trace;        // timeline probe (builds with BH_TRACE only; else unused)
@@ -115,6 +121,9 @@ int moe_plan(MoeParams& p, int smem_cap, int stage_target);
 int launch_moe(const MoeParams& p, int fold, const LaunchOpts& o);
 // Routing alone (one CTA): logits -> ids_out / w_out.
 int launch_moe_route(const MoeParams& p, const LaunchOpts& o);
+// out[t][i] (+)= (float) sum_s (double)(dout[t*k+s][i] * w[t][s])
+int launch_moe_combine(const float* dout, const float* w, int B, int k, int n_embd, float* out, bool residual,
+                       const LaunchOpts& o);
 int encode_q4k_map(CUtensorMap* map, const void* base, int64_t rows, int nb, int row_stride, int box_rows);
 // Seeded normal fill (splitmix64 -> Box-Muller in double, the oracle's
 // generator): out[i] = mean + std * z(seed, first + i).

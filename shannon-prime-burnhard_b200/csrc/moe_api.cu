@@ -66,6 +66,9 @@ bh::MoeParams moe_base(bh_ctx* ctx, int n_tok, int n_expert, int n_embd, int n_f
     p.k = k;
     p.B = n_tok;
     p.n_layer = 1;
+    p.e_lo = 0;
+    p.e_hi = n_expert;
+    p.combine = 1;
     p.status = ctx->d_status;
 #ifdef BH_TRACE
     p.trace = ctx->trace;
@@ -159,6 +162,67 @@ int bh_q4k_moe(bh_ctx* ctx, const float* cur, int n_tok, const int32_t* selected
         p.w_out = weights_out ? weights_out : p.dout + do_f + pairs;
     }
     return bh::run_moe(ctx, p, fold, static_cast<cudaStream_t>(stream), false);
+}
+
+int bh_q4k_moe_ep(bh_ctx* ctx, const float* cur, int n_tok, const int32_t* selected, const float* weights,
+                  const float* router_logits, int norm_topk, const void* gate_own, const void* up_own,
+                  const void* down_own, int n_expert, int expert_lo, int expert_hi, int n_embd, int n_ff, int k,
+                  float* dout, int32_t* selected_out, float* weights_out, int fold, void* stream) {
+    if (!ctx || !cur || !dout || !gate_own || !up_own || !down_own) return BH_EINVAL;
+    if (!moe_shape_ok(n_tok, n_expert, n_embd, n_ff, k)) return BH_EINVAL;
+    if (expert_lo < 0 || expert_hi > n_expert || expert_lo >= expert_hi) return BH_EINVAL;
+    if (fold != BH_FOLD_X86 && fold != BH_FOLD_GENERIC) return BH_EINVAL;
+    const bool given = selected || weights;
+    if (given && (!selected || !weights || router_logits)) return BH_EINVAL;
+    if (!given && !router_logits) return BH_EINVAL;
+    if (!aligned(cur, 16) || !aligned(dout, 4) || !aligned(gate_own, 16) || !aligned(up_own, 16) ||
+        !aligned(down_own, 16))
+        return BH_EINVAL;
+    if ((selected && !aligned(selected, 4)) || (weights && !aligned(weights, 4)) ||
+        (router_logits && !aligned(router_logits, 4)) || (selected_out && !aligned(selected_out, 4)) ||
+        (weights_out && !aligned(weights_out, 4)))
+        return BH_EINVAL;
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return BH_ENODEV;
+    const size_t pairs = (size_t)n_tok * k;
+    const size_t gu_f = pairs * 2 * n_ff;
+    const size_t bytes = 256 + (gu_f + 2 * pairs) * sizeof(float);
+    int rc = ensure_moe_scratch(ctx, bytes);
+    if (rc != BH_OK) return rc;
+    bh::MoeParams p = moe_base(ctx, n_tok, n_expert, n_embd, n_ff, k);
+    p.w[0] = static_cast<const uint8_t*>(gate_own);
+    p.w[1] = static_cast<const uint8_t*>(up_own);
+    p.w[2] = static_cast<const uint8_t*>(down_own);
+    p.e_lo = expert_lo;
+    p.e_hi = expert_hi;
+    p.combine = 0;
+    p.norm_topk = norm_topk ? 1 : 0;
+    p.h = cur;
+    p.gbar = reinterpret_cast<unsigned int*>(ctx->moe_scratch);
+    p.gu = reinterpret_cast<float*>(ctx->moe_scratch + 256);
+    p.dout = dout;
+    if (given) {
+        p.ids_in = selected;
+        p.w_in = weights;
+    } else {
+        p.logits = router_logits;
+        p.ids_out = selected_out ? selected_out : reinterpret_cast<int32_t*>(p.gu + gu_f);
+        p.w_out = weights_out ? weights_out : p.gu + gu_f + pairs;
+    }
+    return bh::run_moe(ctx, p, fold, static_cast<cudaStream_t>(stream), false);
+}
+
+int bh_moe_combine(bh_ctx* ctx, const float* dout, const float* weights, int n_tok, int k, int n_embd, float* out,
+                   int residual, void* stream) {
+    if (!ctx || !dout || !weights || !out || n_tok < 1 || n_tok > bh::MOE_MAX_TOK || k < 1 || k > bh::MOE_MAX_K ||
+        n_embd < 1)
+        return BH_EINVAL;
+    if (!aligned(dout, 4) || !aligned(weights, 4) || !aligned(out, 4)) return BH_EINVAL;
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return BH_ENODEV;
+    bh::LaunchOpts o;
+    o.stream = static_cast<cudaStream_t>(stream);
+    return bh::launch_moe_combine(dout, weights, n_tok, k, n_embd, out, residual != 0, o);
 }
 
 }  // extern "C"

@@ -198,7 +198,7 @@ __device__ __forceinline__ void moe_route(const MoeParams& p, const float* logit
     if (tid < B * k) {
         const int e = tb.ids[tid / k][tid % k];
         if (e < 0 || e >= E) tb.bad = 1;
-        else atomicOr(&tb.bits[e >> 5], 1u << (e & 31));
+        else if (e >= p.e_lo && e < p.e_hi) atomicOr(&tb.bits[e >> 5], 1u << (e & 31));
     }
     __syncthreads();
     if (warp == 0) {
@@ -238,7 +238,7 @@ __device__ __forceinline__ void moe_route(const MoeParams& p, const float* logit
                 n += same;
             }
             if (n > B) tb.bad = 1;  // an expert repeated within one token's selection
-            else {
+            else if (e >= p.e_lo && e < p.e_hi) {
                 tb.col_tok[u][j] = (int8_t)t;
                 tb.col_slot[u][j] = (int8_t)s;
                 if (j == 0) tb.cnt[u] = (int8_t)n;
@@ -447,8 +447,17 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_moe_kernel(const __grid_con
             if (p.w_out) p.w_out[l * p.route_ls + threadIdx.x] = tb.w[tk][s];
         }
 
+        if (!p.combine) {
+            // rows of pairs on other ranks' experts: -0.0, the identity of the cross-rank sum
+            const int np = p.B * p.k * p.n_embd;
+            for (int idx = blockIdx.x * MV_THREADS + threadIdx.x; idx < np; idx += gridDim.x * MV_THREADS) {
+                const int q = idx / p.n_embd;
+                const int e = tb.ids[q / p.k][q % p.k];
+                if (e < p.e_lo || e >= p.e_hi) p.dout[idx] = -0.f;
+            }
+        }
         const int U = tb.n_unique;
-        const int ebase = l * p.n_expert;  // bank row blocks of this layer
+        const int ebase = l * (p.e_hi - p.e_lo);  // bank row blocks of this layer
         PhaseRange gu, dn;
         gu.te = 2 * p.n_ff / R;
         dn.te = p.n_embd / R;
@@ -470,14 +479,14 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_moe_kernel(const __grid_con
                     const int tile = gu.t_begin + warp + i_j * MV_WARPS;
                     const int u = tile / gu.te, rt = (tile - u * gu.te) * R;
                     map = rt >= p.n_ff;
-                    row = (int64_t)(ebase + tb.expert[u]) * p.n_ff + (map ? rt - p.n_ff : rt);
+                    row = (int64_t)(ebase + tb.expert[u] - p.e_lo) * p.n_ff + (map ? rt - p.n_ff : rt);
                     x = i_c * p.kc_gu * (Q4K_BYTES / 8);
                     bytes = (uint32_t)p.stage_gu;
                 } else {
                     const int tile = dn.t_begin + warp + i_j * MV_WARPS;
                     const int u = tile / dn.te, rt = (tile - u * dn.te) * R;
                     map = 2;
-                    row = (int64_t)(ebase + tb.expert[u]) * p.n_embd + rt;
+                    row = (int64_t)(ebase + tb.expert[u] - p.e_lo) * p.n_embd + rt;
                     x = i_c * p.kc_dn * (Q4K_BYTES / 8);
                     bytes = (uint32_t)p.stage_dn;
                 }
@@ -588,6 +597,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_moe_kernel(const __grid_con
             }
         }
         MOE_TRACE_AT(7);
+        if (!p.combine) return;  // the caller sums dout over the ranks, then combines
         ok = grid_barrier(p.gbar, p.status) && ok;
         if (!__syncthreads_and(ok)) return;
 
@@ -625,6 +635,21 @@ __global__ void __launch_bounds__(MV_THREADS, 1) moe_route_kernel(const __grid_c
         p.ids_out[threadIdx.x] = tb.ids[t][s];
         p.w_out[threadIdx.x] = tb.w[t][s];
     }
+}
+
+__global__ void __launch_bounds__(256) moe_combine_kernel(const float* __restrict__ dout, const float* __restrict__ w,
+                                                          int B, int k, int n_embd, float* out, int residual) {
+    pdl_wait();
+    pdl_trigger();
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= B * n_embd) return;
+    const int t = idx / n_embd, i = idx - t * n_embd;
+    // ggml_mul (fp32 product) then ggml_sum_rows over the slots (double, in order)
+    double a = 0.0;
+    for (int s = 0; s < k; ++s)
+        a = __dadd_rn(a, (double)__fmul_rn(__ldcg(dout + ((int64_t)t * k + s) * n_embd + i), __ldcg(w + t * k + s)));
+    const float r = __double2float_rn(a);
+    out[idx] = residual ? __fadd_rn(out[idx], r) : r;
 }
 
 }  // namespace
@@ -715,12 +740,13 @@ static int launch_moe_nb(const MoeParams& p, const LaunchOpts& o) {
 int launch_moe(const MoeParams& pin, int fold, const LaunchOpts& o) {
     if (o.grid < 1 || pin.B < 1 || pin.B > MOE_MAX_TOK || pin.k < 1 || pin.k > MOE_MAX_K ||
         pin.n_expert < pin.k || pin.n_expert > MOE_MAX_EXPERT || pin.n_ff % QK || pin.n_embd % QK || !pin.gbar ||
-        !pin.out || !pin.gu || !pin.dout || pin.n_layer < 1 || (pin.n_layer > 1 && !pin.residual) ||
+        !pin.gu || !pin.dout || pin.n_layer < 1 || (pin.n_layer > 1 && (!pin.residual || !pin.combine)) ||
+        (pin.combine && !pin.out) || pin.e_lo < 0 || pin.e_hi > pin.n_expert || pin.e_lo >= pin.e_hi ||
         (int64_t)pin.n_layer * pin.n_expert * (pin.n_ff > pin.n_embd ? pin.n_ff : pin.n_embd) >= ((int64_t)1 << 31))
         return BH_EINVAL;
     MoeParams p = pin;
     const int nb_e = p.n_embd / QK, nb_f = p.n_ff / QK;
-    const int64_t ne = (int64_t)p.n_layer * p.n_expert;
+    const int64_t ne = (int64_t)p.n_layer * (p.e_hi - p.e_lo);
     int rc = encode_q4k_map(&p.tmap[0], p.w[0], ne * p.n_ff, nb_e, p.stride_gu, MOE_R);
     if (rc == BH_OK) rc = encode_q4k_map(&p.tmap[1], p.w[1], ne * p.n_ff, nb_e, p.stride_gu, MOE_R);
     if (rc == BH_OK) rc = encode_q4k_map(&p.tmap[2], p.w[2], ne * p.n_embd, nb_f, p.stride_dn, MOE_R);
@@ -728,6 +754,24 @@ int launch_moe(const MoeParams& pin, int fold, const LaunchOpts& o) {
     if (fold == BH_FOLD_X86) return launch_moe_nb<BH_FOLD_X86>(p, o);
     if (fold == BH_FOLD_GENERIC) return launch_moe_nb<BH_FOLD_GENERIC>(p, o);
     return BH_EINVAL;
+}
+
+int launch_moe_combine(const float* dout, const float* w, int B, int k, int n_embd, float* out, bool residual,
+                       const LaunchOpts& o) {
+    const int n = B * n_embd;
+    if (n < 1 || k < 1 || !dout || !w || !out) return BH_EINVAL;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((n + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = o.stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = o.pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, moe_combine_kernel, dout, w, B, k, n_embd, out, residual ? 1 : 0) == cudaSuccess
+               ? BH_OK
+               : BH_EIO;
 }
 
 int launch_moe_route(const MoeParams& p, const LaunchOpts& o) {
