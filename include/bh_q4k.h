@@ -83,6 +83,11 @@ int bh_device_status(bh_ctx *ctx, int clear);
  * (8 for narrow matrices at batch <= 2, else 4), or 4 / 8 to force it;
  * results are identical either way. */
 #define BH_TUNE_TPR 4
+/* BH_TUNE_SM_BUDGET: shared memory (bytes) one matvec launch may occupy per
+ * SM, 0 = no limit (default) or 48 KiB..228 KiB; below the SM's capacity the
+ * next launch of a step can become resident early and start streaming its
+ * weights while this one finishes. */
+#define BH_TUNE_SM_BUDGET 5
 int bh_tune(bh_ctx *ctx, int key, int value);
 
 /* fp32 activations [B][K] -> B columns of Q8_K, byte-identical to
@@ -218,6 +223,7 @@ int bh_stack_info(bh_stack *st, int64_t *weight_bytes, int64_t *step_bytes, int6
 #define BH_OP_GATE_UP 2
 #define BH_OP_DOWN 3
 #define BH_OP_LMHEAD 4
+#define BH_OP_ATTN 5
 int bh_stack_time_op(bh_stack *st, int op, int reps, float *avg_ms, int64_t *bytes_per_launch);
 /* Device pointer and shape of one tensor (ids above); Q4_K matrices are
  * rows x cols in values, the rest fp32. */

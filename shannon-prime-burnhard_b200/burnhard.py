@@ -27,6 +27,7 @@ TUNE_CTAS_PER_SM = 1
 TUNE_STAGE_BYTES = 2
 TUNE_SMEM_CAP = 3
 TUNE_TPR = 4
+TUNE_SM_BUDGET = 5
 BH_EIO = -5
 BH_ENOMEM = -12
 BH_ENODEV = -19
@@ -72,7 +73,7 @@ MOE_GATE, MOE_UP, MOE_DOWN, MOE_LOGITS, MOE_NORM, MOE_SELECTED, MOE_WEIGHTS, MOE
 W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN = range(7)
 W_PER_LAYER = 7
 W_OUTPUT = 7
-OP_QKV, OP_O, OP_GATE_UP, OP_DOWN, OP_LMHEAD = range(5)
+OP_QKV, OP_O, OP_GATE_UP, OP_DOWN, OP_LMHEAD, OP_ATTN = range(6)
 T_ATTN_NORM, T_FFN_NORM, T_Q_NORM, T_K_NORM, T_OUT_NORM, T_K_CACHE, T_V_CACHE, T_LOGITS, T_HIDDEN = range(8, 17)
 
 

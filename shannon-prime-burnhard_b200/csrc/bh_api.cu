@@ -90,6 +90,17 @@ int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override) {
             if (p.B <= 2) tpr = 8;
         }
     }
+    if (ctx->sm_budget > 0 && grid_override <= 0) {
+        // leave room on every SM for the next launch's CTAs (programmatic
+        // launch lets them start their weight copies before this one ends)
+        const int per_sm = grid > ctx->num_sms ? (grid + ctx->num_sms - 1) / ctx->num_sms : 1;
+        if (per_sm > 1 && per_sm * cap > ctx->sm_budget) {
+            grid = ctx->num_sms;
+            if (p.B <= 2) tpr = 8;
+        }
+        const int per = grid > ctx->num_sms ? per_sm : 1;
+        if (cap * per > ctx->sm_budget) cap = ctx->sm_budget / per;
+    }
     if (ctx->tpr_force) tpr = (ctx->tpr_force == 8 && p.B <= 2) ? 8 : 4;
     const int64_t ntile = (p.N + 32 / tpr - 1) / (32 / tpr);  // CTAs own whole tiles
     if ((int64_t)grid > ntile) grid = (int)ntile;
@@ -225,6 +236,10 @@ int bh_tune(bh_ctx* ctx, int key, int value) {
         case BH_TUNE_SMEM_CAP:
             if (value < 32 * 1024 || value > 200 * 1024) return BH_EINVAL;
             ctx->smem_cap_small = value;
+            return BH_OK;
+        case BH_TUNE_SM_BUDGET:
+            if (value != 0 && (value < 48 * 1024 || value > 228 * 1024)) return BH_EINVAL;
+            ctx->sm_budget = value;
             return BH_OK;
         default:
             return BH_EINVAL;

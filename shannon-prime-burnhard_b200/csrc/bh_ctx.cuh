@@ -22,6 +22,7 @@ struct bh_ctx {
     int smem_cap_small = 100 * 1024;
     int small_act_bytes = 24 * 1024;
     int tpr_force = 0;  // threads per matvec row: 0 = planner's choice, else 4 or 8
+    int sm_budget = 0;  // shared memory one matvec launch may hold per SM (0 = no limit)
     int64_t* trace = nullptr;  // timeline probe buffer (trace builds only)
     // argmax candidates of the LM-head entry point: [num_sms * 4][BH_MAX_BATCH]
     float* cand_val = nullptr;

@@ -396,7 +396,12 @@ static int launch_t(const MatvecParams& p, const LaunchOpts& o, int grid) {
     auto kern = q4k_matvec_kernel<FOLD, NB, SRC, EPI, PART, TPR>;
     static bool attr_set = false;
     if (!attr_set) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
+        // all kernels of a step ask for the same (largest) shared-memory
+        // carveout, so consecutive launches can share an SM without the SM
+        // having to drain and reconfigure between them
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
+            cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared) != cudaSuccess)
             return BH_EIO;
         attr_set = true;
     }

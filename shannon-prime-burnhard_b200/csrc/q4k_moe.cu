@@ -701,7 +701,9 @@ static int launch_moe_t(const MoeParams& p, const LaunchOpts& o) {
     auto kern = q4k_moe_kernel<FOLD, NB>;
     static bool attr_set = false;
     if (!attr_set) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
+            cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared) != cudaSuccess)
             return BH_EIO;
         attr_set = true;
     }

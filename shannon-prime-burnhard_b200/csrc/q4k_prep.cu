@@ -305,6 +305,14 @@ int launch_argmax_finish(const float* cand_val, const int32_t* cand_idx, int nca
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl ? 1 : 0;
+    static bool attr_set = false;
+    if (!attr_set) {
+        // the same shared-memory carveout as the matvec it follows (no SM reconfiguration between them)
+        if (cudaFuncSetAttribute(argmax_finish_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+            return BH_EIO;
+        attr_set = true;
+    }
     return cudaLaunchKernelEx(&cfg, argmax_finish_kernel, cand_val, cand_idx, ncand, B, tok_out, val_out) ==
                    cudaSuccess
                ? BH_OK
