@@ -21,6 +21,8 @@
 #include <cstring>
 #include <new>
 
+#include <vector>
+
 #include "bh_common.cuh"
 #include "bh_ctx.cuh"
 #include "bh_kernels.cuh"
@@ -67,7 +69,8 @@ struct AttnParams {
     float* vc;               // V cache
     const float* q_norm;     // [head_dim]
     const float* k_norm;     // [head_dim]
-    const int* pos;          // device scalar: position of this token
+    const int* pos;          // device scalar: position of this token (set before the step)
+    const float* rope_inv_freq;  // [head_dim / 2]: theta^(-2j / head_dim)
     float* out;              // [q_dim]
     int n_head, n_head_kv, head_dim, n_ctx;
     float eps, theta;
@@ -100,19 +103,26 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 
 // One CTA of ATTN_THREADS per query head (head_dim 128: lane l of a warp
 // holds dims 4l..4l+3 of a row). Positions are dealt round-robin to the
-// warps; each warp reads whole K / V rows with one coalesced 512-byte load,
-// several rows in flight, and the per-warp partial outputs are combined in
-// warp order.
+// warps, ATTN_U per warp per round; each warp reads whole K / V rows with one
+// coalesced 512-byte load. The K / V history (positions before this token)
+// does not depend on the previous kernel, so the first round's rows are
+// loaded before the programmatic-launch wait and arrive while the QKV
+// projection finishes. Per-warp partial outputs are combined in warp order.
 constexpr int ATTN_THREADS = 256;
 constexpr int ATTN_WARPS = ATTN_THREADS / 32;
 constexpr int ATTN_HD = 128;
+#ifndef BH_ATTN_U
+#define BH_ATTN_U 16
+#endif
+constexpr int ATTN_U = BH_ATTN_U;  // positions per warp per round (16: 128 positions per round)
+
+__device__ __forceinline__ float4 f4_zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
 
 __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnParams a) {
     extern __shared__ float s_scores[];  // [n_ctx]
     __shared__ float sq[ATTN_HD], sk[ATTN_HD], sv[ATTN_HD], red[ATTN_WARPS];
     __shared__ float4 s_part[ATTN_WARPS][ATTN_HD / 4];
-    pdl_trigger();
-    pdl_wait();
+    constexpr int U = ATTN_U;
     const int h = blockIdx.x, tid = threadIdx.x, HD = ATTN_HD, half = HD / 2;
     const int group = a.n_head / a.n_head_kv, g = h / group;
     const int q_dim = a.n_head * HD, kv_dim = a.n_head_kv * HD;
@@ -121,6 +131,23 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnPar
     const int64_t row_stride = (int64_t)a.n_head_kv * HD;
     const float* kbase = a.kc + (int64_t)g * HD;
     const float* vbase = a.vc + (int64_t)g * HD;
+
+    // before the wait: the first round of K / V history rows and the weights
+    float4 kpre[U], vpre[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int t = w + u * ATTN_WARPS;
+        kpre[u] = t < pos ? reinterpret_cast<const float4*>(kbase + (int64_t)t * row_stride)[lane] : f4_zero();
+        vpre[u] = t < pos ? reinterpret_cast<const float4*>(vbase + (int64_t)t * row_stride)[lane] : f4_zero();
+    }
+    float qn = 0.f, kn = 0.f, inv_freq = 0.f;
+    if (tid < HD) {
+        qn = a.q_norm[tid];
+        kn = a.k_norm[tid];
+        inv_freq = a.rope_inv_freq[tid < half ? tid : tid - half];
+    }
+    pdl_trigger();
+    pdl_wait();
 
     // this head's q, k, v (threads 0..HD-1), per-head RMSNorm, NeoX RoPE
     float q = 0.f, k = 0.f, v = 0.f;
@@ -134,8 +161,8 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnPar
     const float rq = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq_q, (float)HD), a.eps)));
     const float rk = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq_k, (float)HD), a.eps)));
     if (tid < HD) {
-        q = __fmul_rn(__fmul_rn(q, rq), a.q_norm[tid]);
-        k = __fmul_rn(__fmul_rn(k, rk), a.k_norm[tid]);
+        q = __fmul_rn(__fmul_rn(q, rq), qn);
+        k = __fmul_rn(__fmul_rn(k, rk), kn);
         sq[tid] = q;
         sk[tid] = k;
         sv[tid] = v;
@@ -143,8 +170,6 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnPar
     __syncthreads();
     float qr = 0.f, kr = 0.f;
     if (tid < HD) {
-        const int j = tid < half ? tid : tid - half;
-        const float inv_freq = (float)exp(-(2.0 * j / HD) * log((double)a.theta));
         const float ang = (float)pos * inv_freq;
         float sn, cs;
         sincosf(ang, &sn, &cs);
@@ -170,15 +195,16 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnPar
     // K comes from shared memory
     const float4 q4 = reinterpret_cast<const float4*>(sq)[lane];
     const float scale = __fdiv_rn(1.f, __fsqrt_rn((float)HD));
-    constexpr int U = 4;
     for (int t0 = w; t0 <= pos; t0 += ATTN_WARPS * U) {
+        const bool first = t0 == w;
         float4 kv[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int t = t0 + u * ATTN_WARPS;
-            kv[u] = t > pos ? make_float4(0.f, 0.f, 0.f, 0.f)
-                    : (t == pos ? reinterpret_cast<const float4*>(sk)[lane]
-                                : reinterpret_cast<const float4*>(kbase + (int64_t)t * row_stride)[lane]);
+            kv[u] = t > pos    ? f4_zero()
+                    : t == pos ? reinterpret_cast<const float4*>(sk)[lane]
+                    : first    ? kpre[u]
+                               : reinterpret_cast<const float4*>(kbase + (int64_t)t * row_stride)[lane];
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -202,15 +228,17 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnPar
     }
     se = block_sum(se, red);  // (its barrier publishes s_scores)
     // weighted V: warp w accumulates its positions for dims 4*lane..4*lane+3
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 o = f4_zero();
     for (int t0 = w; t0 <= pos; t0 += ATTN_WARPS * U) {
+        const bool first = t0 == w;
         float4 vv[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int t = t0 + u * ATTN_WARPS;
-            vv[u] = t > pos ? make_float4(0.f, 0.f, 0.f, 0.f)
-                    : (t == pos ? reinterpret_cast<const float4*>(sv)[lane]
-                                : reinterpret_cast<const float4*>(vbase + (int64_t)t * row_stride)[lane]);
+            vv[u] = t > pos    ? f4_zero()
+                    : t == pos ? reinterpret_cast<const float4*>(sv)[lane]
+                    : first    ? vpre[u]
+                               : reinterpret_cast<const float4*>(vbase + (int64_t)t * row_stride)[lane];
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -256,6 +284,7 @@ struct bh_stack {
     const uint8_t** wq = nullptr;   // [n_layer * BH_W_PER_LAYER] then the LM head
     float* fbuf = nullptr;          // norms, KV caches, activations
     float *attn_norm, *ffn_norm, *q_norm, *k_norm, *out_norm;
+    float* rope_inv_freq;           // [head_dim / 2]
     float *kc, *vc;
     float *x_in, *h, *qkv, *attn, *gu, *logits, *cand_val;
     int32_t *cand_idx, *tok;
@@ -324,6 +353,7 @@ int launch_attn(bh_stack* st, int l, bool pdl) {
     a.n_ctx = c.n_ctx;
     a.eps = c.rms_eps;
     a.theta = c.rope_theta;
+    a.rope_inv_freq = st->rope_inv_freq;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)c.n_head);
     cfg.blockDim = dim3((unsigned)bh::ATTN_THREADS);
@@ -591,7 +621,7 @@ int bh_stack_create(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, bh_s
     const size_t o_kc = take((int64_t)c.n_layer * c.n_ctx * kvd), o_vc = take((int64_t)c.n_layer * c.n_ctx * kvd);
     const size_t o_x = take(c.n_embd), o_h = take(c.n_embd), o_qkv = take(qd + 2 * kvd), o_at = take(qd);
     const size_t o_gu = take(2 * (int64_t)c.n_ff), o_lg = take(c.n_vocab), o_cv = take(cand_max);
-    const size_t o_ci = take(cand_max), o_tk = take(1), o_ps = take(1);
+    const size_t o_ci = take(cand_max), o_tk = take(1), o_ps = take(1), o_rf = take(c.head_dim / 2);
     if (cudaMalloc(&st->fbuf, fl * sizeof(float)) != cudaSuccess ||
         cudaMallocHost(&st->host_tok, sizeof(int32_t)) != cudaSuccess ||
         cudaMallocHost(&st->host_x, sizeof(float) * c.n_embd) != cudaSuccess) {
@@ -607,6 +637,19 @@ int bh_stack_create(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, bh_s
     st->cand_idx = reinterpret_cast<int32_t*>(F + o_ci);
     st->tok = reinterpret_cast<int32_t*>(F + o_tk);
     st->pos = reinterpret_cast<int*>(F + o_ps);
+    st->rope_inv_freq = F + o_rf;
+    {
+        // NeoX RoPE frequencies theta^(-2j / head_dim), evaluated in double once per stack
+        std::vector<float> rf((size_t)c.head_dim / 2);
+        for (int j = 0; j < c.head_dim / 2; ++j)
+            rf[(size_t)j] = (float)std::exp(-(2.0 * j / c.head_dim) * std::log((double)c.rope_theta));
+        if (cudaMemcpyAsync(st->rope_inv_freq, rf.data(), rf.size() * sizeof(float), cudaMemcpyHostToDevice,
+                            st->stream) != cudaSuccess ||
+            cudaStreamSynchronize(st->stream) != cudaSuccess) {
+            bh_stack_free(st);
+            return BH_EIO;
+        }
+    }
     // norm weights ~ 1 + N(0, 0.02)
     if ((rc = bh::fill_normal(st->attn_norm, (int64_t)c.n_layer * c.n_embd, 0, tensor_seed(seed, -1, 1), 1.0, 0.02, st->stream)) ||
         (rc = bh::fill_normal(st->ffn_norm, (int64_t)c.n_layer * c.n_embd, 0, tensor_seed(seed, -1, 2), 1.0, 0.02, st->stream)) ||

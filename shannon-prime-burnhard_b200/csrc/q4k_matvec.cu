@@ -18,6 +18,14 @@
 #include "q4k_core.cuh"
 #include "q8k_device.cuh"
 
+// Super-blocks of one stage worked per unrolled step of a warp (the integer
+// work of consecutive blocks is independent; only the fp32 fold chains them).
+#ifndef BH_KB_UNROLL
+#define BH_KB_UNROLL 2
+#endif
+#define BH_STR_(x) #x
+#define BH_UNROLL(n) _Pragma(BH_STR_(unroll n))
+
 namespace bh {
 
 // Timeline probe: with BH_TRACE defined, lane 0 of every warp records the
@@ -291,7 +299,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_matvec_kernel(const __grid_
             // rows past the end of the range read zero-filled stage bytes and are never stored
             const uint8_t* rowp = ring + (size_t)c_s * p.stage_bytes + (size_t)rgrp * p.row_stride;
             const uint8_t* actc = act + sbc * ACT_BLOCK_BYTES;
-#pragma unroll 2
+BH_UNROLL(BH_KB_UNROLL)
             for (int kb = 0; kb < kl; ++kb) {
                 const RowBlk<TPR> r = decode_row<FOLD, TPR>(rowp + kb * Q4K_BYTES, t);
 #pragma unroll
