@@ -165,6 +165,51 @@ def bench_lmhead_tp(bh, ctx, world: int, rank: int, reps: int) -> dict:
     return out
 
 
+def bench_batch_sweep(bh, ctx) -> dict:
+    """Config 3: the FFN matvecs 12288x4096 and 4096x12288 at batch 1, 2, 4, 8
+    (fp32 activations quantized in the prologue), standalone launch plan.
+    Each timed launch reads a different copy of the weights (the copies
+    together exceed the L2 several times); back-to-back launches in a CUDA
+    graph, CUDA events. GB/s = weight + activation + output bytes / time."""
+    import torch
+
+    out = {"workload": "FFN matvecs 12288x4096 / 4096x12288, batch 1-8 (config 3)"}
+    for n, k in ((12288, 4096), (4096, 12288)):
+        wbytes = n * (k // 256) * 144
+        ncopy = max(8, int(4 * 126e6 // wbytes) + 1)
+        g = torch.Generator(device="cuda").manual_seed(SEED + 3)
+        w0 = ctx.q4k_quantize(torch.randn((n, k), generator=g, device="cuda") * 0.02)
+        ws = [w0] + [w0.clone() for _ in range(ncopy - 1)]
+        for b in (1, 2, 4, 8):
+            x = torch.randn((b, k), generator=g, device="cuda")
+            y = torch.empty((b, n), device="cuda")
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                for i in range(3):
+                    ctx.matvec_f32(ws[i], n, k, x, y=y, stream=s)
+                s.synchronize()
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=s):
+                    for i in range(ncopy):
+                        ctx.matvec_f32(ws[i], n, k, x, y=y, stream=s)
+                gr.replay()
+                s.synchronize()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                for _ in range(5):
+                    gr.replay()
+                e1.record(s)
+                e1.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (5 * ncopy)
+            by = wbytes + b * k * 4 + b * n * 4
+            out[f"{n}x{k}_b{b}"] = {"us": round(us, 2), "GBps": round(by / us / 1e3, 1)}
+            del gr
+        del ws, w0
+        torch.cuda.empty_cache()
+    return out
+
+
 def bench_moe(bh, ctx, world: int, rank: int, steps: int) -> dict:
     """Config 4: the 30B-A3B-shaped expert layers (128 experts, 2048 -> 768 ->
     2048, top-8 of seeded router logits, renormalised). One GPU: the 48-layer
@@ -376,6 +421,10 @@ def main() -> None:
             extra["moe"] = bench_moe(bh, ctx, world, rank, args.steps)
         except Exception as e:
             extra["moe"] = {"error": repr(e)}
+        try:
+            extra["batch_sweep"] = bench_batch_sweep(bh, ctx)
+        except Exception as e:
+            extra["batch_sweep"] = {"error": repr(e)}
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -88,6 +88,9 @@ int bh_device_status(bh_ctx *ctx, int clear);
  * next launch of a step can become resident early and start streaming its
  * weights while this one finishes. */
 #define BH_TUNE_SM_BUDGET 5
+/* BH_TUNE_SMALL_ACT: largest staged activation size (bytes, 0..128 KiB,
+ * default 24 KiB) for which a matvec may run several CTAs per SM. */
+#define BH_TUNE_SMALL_ACT 7
 int bh_tune(bh_ctx *ctx, int key, int value);
 
 /* fp32 activations [B][K] -> B columns of Q8_K, byte-identical to

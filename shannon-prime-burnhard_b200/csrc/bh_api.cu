@@ -237,6 +237,10 @@ int bh_tune(bh_ctx* ctx, int key, int value) {
             if (value < 32 * 1024 || value > 200 * 1024) return BH_EINVAL;
             ctx->smem_cap_small = value;
             return BH_OK;
+        case BH_TUNE_SMALL_ACT:
+            if (value < 0 || value > 128 * 1024) return BH_EINVAL;
+            ctx->small_act_bytes = value;
+            return BH_OK;
         case BH_TUNE_SM_BUDGET:
             if (value != 0 && (value < 48 * 1024 || value > 228 * 1024)) return BH_EINVAL;
             ctx->sm_budget = value;
