@@ -66,38 +66,43 @@ int check_matvec_args(bh_ctx* ctx, const void* W, int64_t N, int64_t K, const vo
 
 namespace bh {
 // Choose the grid, shared-memory budget and threads per row for one matvec
-// launch. Wide matrices (at least one 8-row tile per warp with two CTAs per
-// SM) run two CTAs per SM with half the shared memory each and 4 threads per
-// row. Narrow ones (few rows per CTA) run one CTA per SM with 8 threads per
-// row (4-row tiles): twice the busy warps and half the work per warp step,
-// which is what bounds them.
+// launch.
+//  - Batch 1-2 (16-warp CTAs, whose registers fill an SM): one CTA per SM.
+//    Matrices with fewer than 32 eight-row tiles per CTA (everything but the
+//    LM-head-sized ones) run 8 threads per row, i.e. 4-row tiles: twice the
+//    working warps, each with half the arithmetic per block.
+//  - Larger batches (8-warp CTAs): wide matrices (at least one 8-row tile per
+//    warp with ctas_per_sm CTAs per SM) run that many CTAs per SM, each with
+//    smem_cap_small bytes; narrow ones one CTA per SM.
+// A non-zero sm_budget caps the shared memory one launch holds per SM, so the
+// next programmatic launch finds room to start its weight copies early.
 int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override) {
+    const int W = dense_warps(p.B);
     const int act_bytes = p.B * p.nb * ACT_BLOCK_BYTES;
     const bool small = act_bytes <= ctx->small_act_bytes;
     int grid, cap, tpr = 4;
     if (grid_override > 0) {
         grid = grid_override;
         cap = 200 * 1024;
+    } else if (W == DENSE_MAX_WARPS) {
+        grid = ctx->num_sms;
+        cap = 200 * 1024;
+        const int64_t tiles8 = ((p.N + MV_ROWS - 1) / MV_ROWS + grid - 1) / grid;
+        if (tiles8 < 2 * W) tpr = 8;
     } else {
         const int64_t cps_grid = (int64_t)ctx->num_sms * ctx->ctas_per_sm;
         const int64_t tiles_wide = ((p.N + cps_grid - 1) / cps_grid + MV_ROWS - 1) / MV_ROWS;
-        if (small && tiles_wide >= MV_WARPS) {
+        if (small && tiles_wide >= W) {
             grid = (int)cps_grid;
             cap = ctx->smem_cap_small;
         } else {
             grid = ctx->num_sms;
             cap = 200 * 1024;
-            if (p.B <= 2) tpr = 8;
         }
     }
     if (ctx->sm_budget > 0 && grid_override <= 0) {
-        // leave room on every SM for the next launch's CTAs (programmatic
-        // launch lets them start their weight copies before this one ends)
         const int per_sm = grid > ctx->num_sms ? (grid + ctx->num_sms - 1) / ctx->num_sms : 1;
-        if (per_sm > 1 && per_sm * cap > ctx->sm_budget) {
-            grid = ctx->num_sms;
-            if (p.B <= 2) tpr = 8;
-        }
+        if (per_sm > 1 && per_sm * cap > ctx->sm_budget) grid = ctx->num_sms;
         const int per = grid > ctx->num_sms ? per_sm : 1;
         if (cap * per > ctx->sm_budget) cap = ctx->sm_budget / per;
     }
@@ -142,7 +147,6 @@ using bh::base_params;
 using bh::plan_for;
 using bh::ACT_BLOCK_BYTES;
 using bh::MV_ROWS;
-using bh::MV_WARPS;
 inline int run_matvec(bh_ctx* ctx, bh::MatvecParams& p, int fold, int src, int epi, cudaStream_t s) {
     return bh::run_matvec(ctx, p, fold, src, epi, s, false);
 }

@@ -61,8 +61,14 @@ struct LaunchOpts {
 #ifndef BH_MV_WARPS
 #define BH_MV_WARPS 8
 #endif
-constexpr int MV_WARPS = BH_MV_WARPS;       // every warp streams and computes its own rows
+constexpr int MV_WARPS = BH_MV_WARPS;       // routed-expert kernel: warps per CTA
 constexpr int MV_THREADS = MV_WARPS * 32;
+// Dense matvec: warps per CTA for a batch of B columns. Batch 1-2 runs one
+// CTA of 16 warps per SM (twice the warps to hide each warp's dependent
+// per-block chain; ~100 registers a thread); larger batches hold more
+// accumulators per thread and run 8-warp CTAs.
+constexpr int DENSE_MAX_WARPS = 16;
+__host__ __device__ constexpr int dense_warps(int B) { return B <= 2 ? 16 : 8; }
 constexpr int MV_ROWS = 8;                  // largest tile (rows of one warp stage); segment boundaries align to it
 constexpr int ACT_BLOCK_BYTES = 304;   // staged Q8_K block: 256 q8 + 16 (d) + 32 (S)
 

@@ -570,19 +570,13 @@ int bh_stack_create(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, bh_s
     // The layer matvecs follow one another through programmatic launches; the
     // next one can start its weight copies only if it finds room on the SMs.
     // Unless the caller tuned a per-SM budget on ctx, the step therefore plans
-    // its layer matvecs within 168 KiB of shared memory per SM, 4 threads per
-    // row (8-row tiles) and 1152-byte row slices per stage. With three CTAs
-    // per SM no layer matrix reaches the 8 tiles per CTA the multi-CTA plan
-    // needs, so every layer matvec runs one CTA of 8 warps per SM (measured
-    // best on B200 for this shape: 1.99 ms against 2.36 ms per token with the
-    // standalone plan). The LM head, which nothing follows, keeps ctx's plan.
+    // its layer matvecs within 168 KiB of shared memory per SM with 1152-byte
+    // row slices per stage (one 16-warp CTA per SM; the planner picks the
+    // threads per row). The LM head, which nothing follows, keeps ctx's plan.
     st->plan = *ctx;
     if (ctx->sm_budget == 0) {
         st->plan.sm_budget = 168 * 1024;
-        st->plan.ctas_per_sm = 3;
-        st->plan.smem_cap_small = 56 * 1024;
         st->plan.stage_bytes = 1152;
-        st->plan.tpr_force = 4;
     }
     st->cfg = *cfg;
     const bh_stack_config& c = st->cfg;

@@ -36,7 +36,7 @@ namespace bh {
         if (p.trace && (threadIdx.x & 31) == 0) {                                                        \
             uint64_t t_;                                                                                \
             asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                      \
-            p.trace[((int64_t)blockIdx.x * MV_WARPS + (threadIdx.x >> 5)) * 8 + (k)] = (int64_t)t_;     \
+            p.trace[((int64_t)blockIdx.x * DENSE_MAX_WARPS + (threadIdx.x >> 5)) * 8 + (k)] = (int64_t)t_; \
         }                                                                                               \
     } while (0)
 #else
@@ -57,7 +57,7 @@ __device__ __forceinline__ int seg_of(const MatvecParams& p, int64_t row, int64_
 // ---------------------------------------------------------------------------
 // prologue: activations -> staged Q8_K blocks in shared memory
 // ---------------------------------------------------------------------------
-template <int FOLD, int SRC>
+template <int FOLD, int SRC, int W>
 __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* red, int ctid) {
     const int warp = ctid >> 5, lane = ctid & 31;
     const int nblk = p.B * p.nb;
@@ -66,12 +66,12 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
     // (just produced, L2-resident) activations is paid once per U blocks.
     constexpr int U = 4;
     if (SRC == ACT_Q8K) {
-        for (int blk0 = warp; blk0 < nblk; blk0 += MV_WARPS * U) {
+        for (int blk0 = warp; blk0 < nblk; blk0 += W * U) {
             uint32_t w0[U], w1[U], bw[U];
             float dv[U];
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                const int blk = blk0 + u * MV_WARPS;
+                const int blk = blk0 + u * W;
                 w0[u] = w1[u] = bw[u] = 0;
                 dv[u] = 0.f;
                 if (blk < nblk) {
@@ -85,7 +85,7 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
             }
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                const int blk = blk0 + u * MV_WARPS;
+                const int blk = blk0 + u * W;
                 if (blk >= nblk) break;
                 uint8_t* dst = act + blk * ACT_BLOCK_BYTES;
 #pragma unroll
@@ -108,34 +108,46 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
         }
         return;
     }
-    // fp32 sources
+    // fp32 sources. When every warp's blocks fit one round (nblk <= W*UF, the
+    // decode shapes), all global loads are issued at once and RMSNorm's sum
+    // of squares is taken from the loaded registers: per block (lane sums in
+    // element order, then an xor butterfly), per column (the blocks' sums in
+    // block order, read back by every thread from shared memory). The order is
+    // fixed, so every CTA derives the same scale. Larger batches fall back to
+    // a separate strided pass for the sum of squares.
+    // (UF blocks per warp per round: one round covers the decode step's
+    // K = 4096 RMSNorm / quantize prologues and the K = 12288 SwiGLU one)
+    constexpr int UF = SRC == ACT_F32_SWIGLU ? 3 : 2;
     __shared__ float s_scale[BH_MAX_BATCH];
-    if (SRC == ACT_F32_RMSNORM) {
-        // fixed-order reduction, identical in every CTA
+    const bool one_round = nblk <= W * UF;
+    if (SRC == ACT_F32_RMSNORM && !one_round) {
         for (int b = 0; b < p.B; ++b) {
             const float* h = p.xf + (int64_t)b * p.K;
             float ss = 0.f;
 #pragma unroll 4
-            for (int i = ctid; i < p.K; i += MV_WARPS * 32) ss = __fadd_rn(ss, __fmul_rn(h[i], h[i]));
+            for (int i = ctid; i < p.K; i += W * 32) ss = __fadd_rn(ss, __fmul_rn(h[i], h[i]));
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
             if (lane == 0) red[warp] = ss;
-            named_bar(1, MV_WARPS * 32);
+            named_bar(1, W * 32);
             if (ctid == 0) {
                 float t = 0.f;
-                for (int w = 0; w < MV_WARPS; ++w) t = __fadd_rn(t, red[w]);
+                for (int w = 0; w < W; ++w) t = __fadd_rn(t, red[w]);
                 const float mean = __fdiv_rn(t, (float)p.K);
                 s_scale[b] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
             }
-            named_bar(1, MV_WARPS * 32);
+            named_bar(1, W * 32);
         }
     }
-    constexpr int UF = 2;
-    for (int blk0 = warp; blk0 < nblk; blk0 += MV_WARPS * UF) {
+    // every warp runs the same number of rounds (the RMSNorm path has CTA
+    // barriers inside a round)
+    const int rounds = (nblk + W * UF - 1) / (W * UF);
+    for (int rd = 0; rd < rounds; ++rd) {
+        const int blk0 = warp + rd * W * UF;
         float v[UF][8], aux[UF][8];
 #pragma unroll
         for (int u = 0; u < UF; ++u) {
-            const int blk = blk0 + u * MV_WARPS;
+            const int blk = blk0 + u * W;
             const int b = blk / p.nb, i = blk - b * p.nb;
             const int e0 = i * QK + 8 * lane;
 #pragma unroll
@@ -153,9 +165,30 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
                 }
             }
         }
+        if (SRC == ACT_F32_RMSNORM && one_round) {
+            // red[blk]: sum of squares of block blk (nblk <= W*U entries)
+#pragma unroll
+            for (int u = 0; u < UF; ++u) {
+                const int blk = blk0 + u * W;
+                float ss = 0.f;
+#pragma unroll
+                for (int t = 0; t < 8; ++t) ss = __fadd_rn(ss, __fmul_rn(v[u][t], v[u][t]));
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+                if (lane == 0 && blk < nblk) red[blk] = ss;
+            }
+            named_bar(1, W * 32);
+            if (ctid < p.B) {
+                float t = 0.f;
+                for (int i = 0; i < p.nb; ++i) t = __fadd_rn(t, red[ctid * p.nb + i]);
+                const float mean = __fdiv_rn(t, (float)p.K);
+                s_scale[ctid] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+            }
+            named_bar(1, W * 32);
+        }
 #pragma unroll
         for (int u = 0; u < UF; ++u) {
-            const int blk = blk0 + u * MV_WARPS;
+            const int blk = blk0 + u * W;
             if (blk >= nblk) break;  // warp-uniform
             const int b = blk / p.nb;
             float x[8];
@@ -204,12 +237,13 @@ __device__ __forceinline__ void finish_row(const MatvecParams& p, const float (&
 // cross-warp handshake). Thread (r, t) works row r of the tile; its fp32
 // fold runs in registers as the blocks stream by.
 template <int FOLD, int NB, int SRC, int EPI, bool PART, int TPR>
-__global__ void __launch_bounds__(MV_THREADS, 1) q4k_matvec_kernel(const __grid_constant__ MatvecParams p) {
+__global__ void __launch_bounds__(dense_warps(NB) * 32, 1) q4k_matvec_kernel(const __grid_constant__ MatvecParams p) {
+    constexpr int W = dense_warps(NB);
     constexpr int R = 32 / TPR;
     constexpr int L = 8 / TPR;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float s_red[MV_WARPS * 2];
-    __shared__ int s_redi[MV_WARPS];
+    __shared__ float s_red[DENSE_MAX_WARPS * 4];
+    __shared__ int s_redi[DENSE_MAX_WARPS];
     BH_TRACE_AT(0);
 
     uint8_t* act = smem + p.act_off;
@@ -224,12 +258,14 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_matvec_kernel(const __grid_
     const int64_t r_end = r_end_t < p.N ? r_end_t : p.N;
     const int nrows = (int)(r_end - r_begin);
     const int ntiles = (nrows + R - 1) / R;
-    const int my_tiles = warp < ntiles ? (ntiles - 1 - warp) / MV_WARPS + 1 : 0;
+    const int my_tiles = warp < ntiles ? (ntiles - 1 - warp) / W + 1 : 0;
     const int nkc = (p.nb + p.kc - 1) / p.kc;
     const int total = my_tiles * nkc;
     const unsigned FULLM = 0xffffffffu;
 
-    if (lane == 0) {
+    // (warps without a tile own no ring: the planner sized the rings for the
+    // warps that have one)
+    if (lane == 0 && my_tiles > 0) {
         for (int s = 0; s < p.stages; ++s) mbar_init(&full[s], 1);
         fence_mbar_init();
     }
@@ -243,7 +279,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_matvec_kernel(const __grid_
     auto issue_next = [&]() {
         if (lane == 0) {
             int64_t local;
-            const int sg = seg_of(p, r_begin + (int64_t)(warp + i_j * MV_WARPS) * R, local);
+            const int sg = seg_of(p, r_begin + (int64_t)(warp + i_j * W) * R, local);
             mbar_arrive_expect_tx(&full[i_s], (uint32_t)p.stage_bytes);
             tensor_g2s_2d(ring + (size_t)i_s * p.stage_bytes, &p.tmap[sg], i_c * p.kc * (Q4K_BYTES / 8), (int)local,
                           &full[i_s], pol);
@@ -259,7 +295,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_matvec_kernel(const __grid_
     BH_TRACE_AT(1);
     pdl_trigger();
     pdl_wait();
-    stage_activations<FOLD, SRC>(p, act, s_red, threadIdx.x);
+    stage_activations<FOLD, SRC, W>(p, act, s_red, threadIdx.x);
     __syncthreads();
     BH_TRACE_AT(2);
 
@@ -275,7 +311,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_matvec_kernel(const __grid_
     uint32_t c_ph = 0;
     bool ok = true;
     for (int j = 0; j < my_tiles && ok; ++j) {
-        const int rin = (warp + j * MV_WARPS) * R + rgrp;
+        const int rin = (warp + j * W) * R + rgrp;
         const bool live = rin < nrows;
         float acc[NB][L], accm[NB];
 #pragma unroll
@@ -350,7 +386,7 @@ BH_UNROLL(BH_KB_UNROLL)
             if (threadIdx.x == 0) {
                 float cv = s_red[0];
                 int ci = s_redi[0];
-                for (int w = 1; w < MV_WARPS; ++w)
+                for (int w = 1; w < W; ++w)
                     if (s_red[w] > cv || (s_red[w] == cv && s_redi[w] < ci)) { cv = s_red[w]; ci = s_redi[w]; }
                 p.cand_val[blockIdx.x * p.B + b] = cv;
                 p.cand_idx[blockIdx.x * p.B + b] = ci;
@@ -365,10 +401,16 @@ BH_UNROLL(BH_KB_UNROLL)
 // ---------------------------------------------------------------------------
 // Plan one launch: R = 32 / tpr rows per stage, kc super-blocks per row per
 // stage (from the copy target, shrunk until 2 stages fit; box rows stay
-// within 2048 bytes), stages <= 4.
+// within 2048 bytes), 2-8 stages. Only the warps that own a tile get a ring
+// (a CTA's range is at most ceil(tiles / grid) tiles), so a matrix with few
+// rows per CTA gives its working warps deeper rings, which fill before the
+// programmatic wait.
 int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int tpr) {
     if (grid < 1 || (tpr != 4 && tpr != 8)) return BH_EINVAL;
     const int R = 32 / tpr;
+    const int W = dense_warps(p.B);
+    const int64_t tiles_cta = ((p.N + R - 1) / R + grid - 1) / grid;
+    const int wbusy = tiles_cta < W ? (int)(tiles_cta > 0 ? tiles_cta : 1) : W;
     const int act_bytes = p.B * p.nb * ACT_BLOCK_BYTES;
     const int ring_off = (act_bytes + 127) / 128 * 128;
     int kc = stage_target / Q4K_BYTES;
@@ -380,9 +422,9 @@ int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int t
         const int padw = ((8 - (words % 32)) % 32 + 32) % 32;  // row stride == 8 words (mod 32 banks)
         const int stride = kc * Q4K_BYTES + 4 * padw;
         const int stage = R * stride;
-        const int avail = smem_cap - ring_off - 256 - 128;
-        int stages = avail > 0 ? avail / (MV_WARPS * (stage + 8)) : 0;
-        if (stages > 4) stages = 4;
+        const int avail = smem_cap - ring_off - 512;  // static shared memory of the kernel
+        int stages = avail > 0 ? avail / (wbusy * (stage + 8)) : 0;
+        if (stages > 8) stages = 8;
         if (stages < 2) continue;
         p.kc = kc;
         p.row_stride = stride;
@@ -392,8 +434,8 @@ int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int t
         p.tpr = tpr;
         p.act_off = 0;
         p.ring_off = ring_off;
-        p.bar_off = ring_off + MV_WARPS * stages * stage;
-        p.smem_bytes = p.bar_off + MV_WARPS * stages * 8;
+        p.bar_off = ring_off + wbusy * stages * stage;
+        p.smem_bytes = p.bar_off + wbusy * stages * 8;
         return BH_OK;
     }
     return BH_EINVAL;  // activations too large for shared memory
@@ -415,7 +457,7 @@ static int launch_t(const MatvecParams& p, const LaunchOpts& o, int grid) {
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(MV_THREADS);
+    cfg.blockDim = dim3(dense_warps(NB) * 32);
     cfg.dynamicSmemBytes = (size_t)p.smem_bytes;
     cfg.stream = o.stream;
     cudaLaunchAttribute at[1];
