@@ -91,6 +91,10 @@ int bh_device_status(bh_ctx *ctx, int clear);
 /* BH_TUNE_SMALL_ACT: largest staged activation size (bytes, 0..128 KiB,
  * default 24 KiB) for which a matvec may run several CTAs per SM. */
 #define BH_TUNE_SMALL_ACT 7
+/* BH_TUNE_PREFILL: ring stages per warp a matvec issues before its
+ * programmatic-launch wait, 0..8 (0, the default: the whole ring); the rest
+ * go out right after the activation loads that follow the wait. */
+#define BH_TUNE_PREFILL 8
 int bh_tune(bh_ctx *ctx, int key, int value);
 
 /* fp32 activations [B][K] -> B columns of Q8_K, byte-identical to

@@ -29,6 +29,7 @@ TUNE_SMEM_CAP = 3
 TUNE_TPR = 4
 TUNE_SM_BUDGET = 5
 TUNE_SMALL_ACT = 7
+TUNE_PREFILL = 8
 BH_EIO = -5
 BH_ENOMEM = -12
 BH_ENODEV = -19

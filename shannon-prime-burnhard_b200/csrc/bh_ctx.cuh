@@ -23,6 +23,7 @@ struct bh_ctx {
     int small_act_bytes = 24 * 1024;
     int tpr_force = 0;  // threads per matvec row: 0 = planner's choice, else 4 or 8
     int sm_budget = 0;  // shared memory one matvec launch may hold per SM (0 = no limit)
+    int prefill_stages = 0;  // ring stages per warp a matvec issues before its programmatic wait (0 = all)
     int64_t* trace = nullptr;  // timeline probe buffer (trace builds only)
     // argmax candidates of the LM-head entry point: [num_sms * 4][BH_MAX_BATCH]
     float* cand_val = nullptr;
@@ -37,7 +38,8 @@ struct bh_ctx {
 namespace bh {
 // Grid and shared-memory plan for one matvec launch (fills p's tiling
 // fields); returns the grid size or a negative errno.
-int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override);
+// pairs: the launch uses the gate/up pair epilogue (EPI_SWIGLU).
+int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override, bool pairs = false);
 // MatvecParams for a single-segment weight matrix.
 MatvecParams base_params(bh_ctx* ctx, const void* W, int64_t N, int64_t K, int B, float* y);
 // plan_for + launch.

@@ -13,7 +13,6 @@ enum ActSrc : int {
     ACT_Q8K = 0,          // GGML block_q8_K columns
     ACT_F32 = 1,          // fp32 columns, quantized to Q8_K in the prologue
     ACT_F32_RMSNORM = 2,  // fp32 h, x = h / sqrt(mean(h^2) + eps) * gamma, then Q8_K
-    ACT_F32_SWIGLU = 3,   // fp32 [gate | up] columns of length 2K, x = silu(gate) * up, then Q8_K
 };
 
 // What the epilogue does with the dot product v of row r, column b.
@@ -21,6 +20,12 @@ enum Epilogue : int {
     EPI_STORE = 0,   // y[b*ldy + r] = v
     EPI_ADD = 1,     // y[b*ldy + r] += v   (residual add)
     EPI_ARGMAX = 2,  // y[b*ldy + r] = v, plus per-CTA (max, first index) candidates
+    // Gate/up pairs: segment 0 holds the gate rows, segment 1 the up rows
+    // (N = 2 * n_ff virtual rows). Virtual tile j of R rows is gate rows
+    // [j*R/2, (j+1)*R/2) followed by the same up rows (one copy from each
+    // segment), so one warp has both values of row i:
+    // y[b*ldy + i] = silu(gate_i) * up_i, i < n_ff.
+    EPI_SWIGLU = 3,
 };
 
 struct MatvecParams {
@@ -47,8 +52,11 @@ struct MatvecParams {
     int tpr;               // threads per row: 4 or 8
     int kc;                // super-blocks per pipeline stage
     int row_stride;        // shared-memory bytes per row of a stage
-    int stage_bytes;
+    int stage_bytes;       // shared-memory footprint of one stage (a multiple of 128)
+    int tx_bytes;          // bytes the stage's copies deliver: rows_per_tile * row_stride
+    int half_off;          // EPI_SWIGLU: offset of the up half in a stage (a multiple of 128)
     int stages;
+    int prefill;           // stages per warp issued before the programmatic wait (0 = the whole ring)
     int act_off, ring_off, bar_off, smem_bytes;
 };
 
@@ -136,7 +144,8 @@ int encode_q4k_map(CUtensorMap* map, const void* base, int64_t rows, int nb, int
 int fill_normal(float* out, int64_t n, int64_t first, uint64_t seed, double mean, double stddev, cudaStream_t s);
 
 // Fill tiling fields of p for the given grid; returns 0 or a negative errno.
-int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int tpr);
+// pairs: the launch uses EPI_SWIGLU (two half-tile copies per stage).
+int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int tpr, bool pairs = false);
 int launch_matvec(const MatvecParams& p, int fold, int act_src, int epi, const LaunchOpts& o);
 
 int launch_q8k_quantize(const float* x, int64_t K, int B, uint8_t* out, int* status, cudaStream_t s);

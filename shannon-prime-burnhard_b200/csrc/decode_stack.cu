@@ -74,40 +74,39 @@ struct AttnParams {
     float* out;              // [q_dim]
     int n_head, n_head_kv, head_dim, n_ctx;
     float eps, theta;
+    int64_t* trace;          // timeline probe (builds with BH_TRACE only; else unused)
 };
 
-__device__ __forceinline__ float block_sum(float v, float* red) {
-    // fixed-order reduction: warp butterflies, then warps in order
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
-    const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) red[w] = v;
-    __syncthreads();
-    float t = 0.f;
-    for (int i = 0; i < nw; ++i) t = __fadd_rn(t, red[i]);
-    return t;
-}
-
-__device__ __forceinline__ float block_max(float v, float* red) {
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
-    const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) red[w] = v;
-    __syncthreads();
-    float t = red[0];
-    for (int i = 1; i < nw; ++i) t = fmaxf(t, red[i]);
-    return t;
-}
+#ifdef BH_TRACE
+// lane 0 of every warp records the global timer (ns) at point k
+#define ATTN_TRACE_AT(k)                                                                                    \
+    do {                                                                                                    \
+        if (a.trace && (threadIdx.x & 31) == 0) {                                                           \
+            uint64_t t_;                                                                                    \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                          \
+            a.trace[((int64_t)blockIdx.x * DENSE_MAX_WARPS + (threadIdx.x >> 5)) * 8 + (k)] = (int64_t)t_; \
+        }                                                                                                   \
+    } while (0)
+// each traced launch of a step writes its own region of the buffer
+constexpr int64_t TRACE_LAUNCH = 256 * DENSE_MAX_WARPS * 8;
+#else
+#define ATTN_TRACE_AT(k) \
+    do {                 \
+    } while (0)
+#endif
 
 // One CTA of ATTN_THREADS per query head (head_dim 128: lane l of a warp
-// holds dims 4l..4l+3 of a row). Positions are dealt round-robin to the
-// warps, ATTN_U per warp per round; each warp reads whole K / V rows with one
-// coalesced 512-byte load. The K / V history (positions before this token)
-// does not depend on the previous kernel, so the first round's rows are
-// loaded before the programmatic-launch wait and arrive while the QKV
-// projection finishes. Per-warp partial outputs are combined in warp order.
+// holds dims 4l..4l+3 of a row). Every warp holds the head's q and this
+// token's k and v in registers: the per-head RMSNorm is a warp butterfly and
+// NeoX RoPE pairs dim d with d + 64, i.e. lane l with lane l ^ 16, so no
+// block barrier is needed before the scores. Positions are dealt
+// round-robin to the warps, ATTN_U per warp per round; each warp reads whole
+// K / V rows with one coalesced 512-byte load and keeps its own running
+// softmax (max, sum, weighted V). The K / V history (positions before this
+// token), the norm weights and the rotation angles do not depend on the
+// previous kernel, so the first round's rows, the weights and the
+// sines / cosines are taken before the programmatic-launch wait. The warps'
+// partial results are combined in warp order after one barrier.
 constexpr int ATTN_THREADS = 256;
 constexpr int ATTN_WARPS = ATTN_THREADS / 32;
 constexpr int ATTN_HD = 128;
@@ -118,152 +117,171 @@ constexpr int ATTN_U = BH_ATTN_U;  // positions per warp per round (16: 128 posi
 
 __device__ __forceinline__ float4 f4_zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
 
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+}
+
+__device__ __forceinline__ float sumsq4(float4 v) {
+    return __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
+                     __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w)));
+}
+
+__device__ __forceinline__ float dot4(float4 a, float4 b) {
+    return __fadd_rn(__fadd_rn(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y)),
+                     __fadd_rn(__fmul_rn(a.z, b.z), __fmul_rn(a.w, b.w)));
+}
+
+// x * r * w per component (the per-head RMSNorm)
+__device__ __forceinline__ float4 scale4(float4 x, float r, float4 w) {
+    return make_float4(__fmul_rn(__fmul_rn(x.x, r), w.x), __fmul_rn(__fmul_rn(x.y, r), w.y),
+                       __fmul_rn(__fmul_rn(x.z, r), w.z), __fmul_rn(__fmul_rn(x.w, r), w.w));
+}
+
+// NeoX rotation of the dims this lane holds; p = the partner lane's values
+__device__ __forceinline__ float rot1(float x, float p, float c, float s, bool low) {
+    return low ? __fsub_rn(__fmul_rn(x, c), __fmul_rn(p, s)) : __fadd_rn(__fmul_rn(x, c), __fmul_rn(p, s));
+}
+
+__device__ __forceinline__ float4 rope4(float4 x, const float (&c)[4], const float (&s)[4], bool low) {
+    const float4 p = make_float4(__shfl_xor_sync(0xffffffffu, x.x, 16), __shfl_xor_sync(0xffffffffu, x.y, 16),
+                                 __shfl_xor_sync(0xffffffffu, x.z, 16), __shfl_xor_sync(0xffffffffu, x.w, 16));
+    return make_float4(rot1(x.x, p.x, c[0], s[0], low), rot1(x.y, p.y, c[1], s[1], low),
+                       rot1(x.z, p.z, c[2], s[2], low), rot1(x.w, p.w, c[3], s[3], low));
+}
+
+__device__ __forceinline__ float4 axpy4(float a, float4 x, float4 y) {
+    return make_float4(__fadd_rn(y.x, __fmul_rn(a, x.x)), __fadd_rn(y.y, __fmul_rn(a, x.y)),
+                       __fadd_rn(y.z, __fmul_rn(a, x.z)), __fadd_rn(y.w, __fmul_rn(a, x.w)));
+}
+
+__device__ __forceinline__ float4 mul4(float a, float4 x) {
+    return make_float4(__fmul_rn(a, x.x), __fmul_rn(a, x.y), __fmul_rn(a, x.z), __fmul_rn(a, x.w));
+}
+
+// One round of a warp's positions t0 + u * ATTN_WARPS (u < U): K / V rows of
+// positions before pos in kv / vv, this token's k / v at pos, nothing past it.
+// Scores q.k * scale (a warp butterfly per position); the running max m, sum l
+// and weighted V o are rescaled to the round's maximum, then accumulated.
+template <int U>
+__device__ __forceinline__ void attn_round(const float4 (&kv)[U], const float4 (&vv)[U], int t0, int pos, float4 q,
+                                           float4 k, float4 v, float scale, float& m, float& l, float4& o) {
+    float sc[U];
+    float mr = m;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int t = t0 + u * ATTN_WARPS;
+        const float4 kk = t < pos ? kv[u] : k;  // (past pos: not used)
+        sc[u] = t <= pos ? __fmul_rn(warp_sum(dot4(q, kk)), scale) : -INFINITY;
+        mr = fmaxf(mr, sc[u]);
+    }
+    // mr is finite: position t0 <= pos is in this round
+    const float f = expf(__fsub_rn(m, mr));  // 0 on a warp's first round (m = -inf)
+    l = __fmul_rn(l, f);
+    o = mul4(f, o);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int t = t0 + u * ATTN_WARPS;
+        const float p = expf(__fsub_rn(sc[u], mr));  // 0 past pos
+        l = __fadd_rn(l, p);
+        o = axpy4(p, t < pos ? vv[u] : t == pos ? v : f4_zero(), o);
+    }
+    m = mr;
+}
+
 __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnParams a) {
-    extern __shared__ float s_scores[];  // [n_ctx]
-    __shared__ float sq[ATTN_HD], sk[ATTN_HD], sv[ATTN_HD], red[ATTN_WARPS];
-    __shared__ float4 s_part[ATTN_WARPS][ATTN_HD / 4];
+    __shared__ float s_m[ATTN_WARPS], s_l[ATTN_WARPS];
+    __shared__ float4 s_o[ATTN_WARPS][ATTN_HD / 4];
     constexpr int U = ATTN_U;
-    const int h = blockIdx.x, tid = threadIdx.x, HD = ATTN_HD, half = HD / 2;
+    const int h = blockIdx.x, tid = threadIdx.x, HD = ATTN_HD;
     const int group = a.n_head / a.n_head_kv, g = h / group;
     const int q_dim = a.n_head * HD, kv_dim = a.n_head_kv * HD;
-    const int pos = *a.pos;
     const int lane = tid & 31, w = tid >> 5;
     const int64_t row_stride = (int64_t)a.n_head_kv * HD;
     const float* kbase = a.kc + (int64_t)g * HD;
     const float* vbase = a.vc + (int64_t)g * HD;
+    ATTN_TRACE_AT(0);
 
-    // before the wait: the first round of K / V history rows and the weights
+    // before the wait, nothing that makes the thread wait: loads of the first
+    // round's K / V cache rows (all of them, whatever the position: only
+    // those before pos are used), the norm weights, the rotation frequencies
+    // (lane l: dims 4l..4l+3, frequency index (4l mod 64) + j) and pos
     float4 kpre[U], vpre[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
         const int t = w + u * ATTN_WARPS;
-        kpre[u] = t < pos ? reinterpret_cast<const float4*>(kbase + (int64_t)t * row_stride)[lane] : f4_zero();
-        vpre[u] = t < pos ? reinterpret_cast<const float4*>(vbase + (int64_t)t * row_stride)[lane] : f4_zero();
+        kpre[u] = t < a.n_ctx ? reinterpret_cast<const float4*>(kbase + (int64_t)t * row_stride)[lane] : f4_zero();
+        vpre[u] = t < a.n_ctx ? reinterpret_cast<const float4*>(vbase + (int64_t)t * row_stride)[lane] : f4_zero();
     }
-    float qn = 0.f, kn = 0.f, inv_freq = 0.f;
-    if (tid < HD) {
-        qn = a.q_norm[tid];
-        kn = a.k_norm[tid];
-        inv_freq = a.rope_inv_freq[tid < half ? tid : tid - half];
-    }
+    const float4 qn = reinterpret_cast<const float4*>(a.q_norm)[lane];
+    const float4 kn = reinterpret_cast<const float4*>(a.k_norm)[lane];
+    const float4 fr = reinterpret_cast<const float4*>(a.rope_inv_freq)[lane & 15];
+    const int pos = *a.pos;
     pdl_trigger();
     pdl_wait();
+    ATTN_TRACE_AT(5);
 
-    // this head's q, k, v (threads 0..HD-1), per-head RMSNorm, NeoX RoPE
-    float q = 0.f, k = 0.f, v = 0.f;
-    if (tid < HD) {
-        q = a.qkv[h * HD + tid];
-        k = a.qkv[q_dim + g * HD + tid];
-        v = a.qkv[q_dim + kv_dim + g * HD + tid];
+    // this head's q, this token's k and v (the rotation is computed while
+    // they load); per-head RMSNorm, NeoX RoPE
+    float4 q = reinterpret_cast<const float4*>(a.qkv + (int64_t)h * HD)[lane];
+    float4 k = reinterpret_cast<const float4*>(a.qkv + q_dim + (int64_t)g * HD)[lane];
+    const float4 v = reinterpret_cast<const float4*>(a.qkv + q_dim + kv_dim + (int64_t)g * HD)[lane];
+    float cs[4], sn[4];
+    sincosf(__fmul_rn((float)pos, fr.x), &sn[0], &cs[0]);
+    sincosf(__fmul_rn((float)pos, fr.y), &sn[1], &cs[1]);
+    sincosf(__fmul_rn((float)pos, fr.z), &sn[2], &cs[2]);
+    sincosf(__fmul_rn((float)pos, fr.w), &sn[3], &cs[3]);
+    const float rq = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(warp_sum(sumsq4(q)), (float)HD), a.eps)));
+    const float rk = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(warp_sum(sumsq4(k)), (float)HD), a.eps)));
+    const bool low = lane < 16;
+    q = rope4(scale4(q, rq, qn), cs, sn, low);
+    k = rope4(scale4(k, rk, kn), cs, sn, low);
+    ATTN_TRACE_AT(1);
+    if (h % group == 0 && w == 0) {
+        reinterpret_cast<float4*>(a.kc + (int64_t)pos * row_stride + (int64_t)g * HD)[lane] = k;
+        reinterpret_cast<float4*>(a.vc + (int64_t)pos * row_stride + (int64_t)g * HD)[lane] = v;
     }
-    const float sq_q = block_sum(__fmul_rn(q, q), red);
-    const float sq_k = block_sum(__fmul_rn(k, k), red);
-    const float rq = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq_q, (float)HD), a.eps)));
-    const float rk = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq_k, (float)HD), a.eps)));
-    if (tid < HD) {
-        q = __fmul_rn(__fmul_rn(q, rq), qn);
-        k = __fmul_rn(__fmul_rn(k, rk), kn);
-        sq[tid] = q;
-        sk[tid] = k;
-        sv[tid] = v;
-    }
-    __syncthreads();
-    float qr = 0.f, kr = 0.f;
-    if (tid < HD) {
-        const float ang = (float)pos * inv_freq;
-        float sn, cs;
-        sincosf(ang, &sn, &cs);
-        if (tid < half) {
-            qr = __fsub_rn(__fmul_rn(q, cs), __fmul_rn(sq[tid + half], sn));
-            kr = __fsub_rn(__fmul_rn(k, cs), __fmul_rn(sk[tid + half], sn));
-        } else {
-            qr = __fadd_rn(__fmul_rn(q, cs), __fmul_rn(sq[tid - half], sn));
-            kr = __fadd_rn(__fmul_rn(k, cs), __fmul_rn(sk[tid - half], sn));
-        }
-    }
-    __syncthreads();
-    if (tid < HD) {
-        sq[tid] = qr;
-        sk[tid] = kr;
-        if (h % group == 0) {
-            a.kc[(int64_t)pos * row_stride + g * HD + tid] = kr;
-            a.vc[(int64_t)pos * row_stride + g * HD + tid] = v;
-        }
-    }
-    __syncthreads();
-    // scores: warp w takes positions w, w + ATTN_WARPS, ...; this token's own
-    // K comes from shared memory
-    const float4 q4 = reinterpret_cast<const float4*>(sq)[lane];
+
+    // this warp's positions w, w + ATTN_WARPS, ...: scores, running softmax
+    // (the first round from the rows loaded before the wait)
     const float scale = __fdiv_rn(1.f, __fsqrt_rn((float)HD));
-    for (int t0 = w; t0 <= pos; t0 += ATTN_WARPS * U) {
-        const bool first = t0 == w;
-        float4 kv[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int t = t0 + u * ATTN_WARPS;
-            kv[u] = t > pos    ? f4_zero()
-                    : t == pos ? reinterpret_cast<const float4*>(sk)[lane]
-                    : first    ? kpre[u]
-                               : reinterpret_cast<const float4*>(kbase + (int64_t)t * row_stride)[lane];
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int t = t0 + u * ATTN_WARPS;
-            float dot = __fadd_rn(__fadd_rn(__fmul_rn(q4.x, kv[u].x), __fmul_rn(q4.y, kv[u].y)),
-                                  __fadd_rn(__fmul_rn(q4.z, kv[u].z), __fmul_rn(q4.w, kv[u].w)));
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) dot = __fadd_rn(dot, __shfl_xor_sync(0xffffffffu, dot, off));
-            if (lane == 0 && t <= pos) s_scores[t] = __fmul_rn(dot, scale);
-        }
-    }
-    __syncthreads();
-    float mx = -INFINITY;
-    for (int t = tid; t <= pos; t += ATTN_THREADS) mx = fmaxf(mx, s_scores[t]);
-    mx = block_max(mx, red);
-    float se = 0.f;
-    for (int t = tid; t <= pos; t += ATTN_THREADS) {
-        const float e = expf(__fsub_rn(s_scores[t], mx));
-        s_scores[t] = e;
-        se = __fadd_rn(se, e);
-    }
-    se = block_sum(se, red);  // (its barrier publishes s_scores)
-    // weighted V: warp w accumulates its positions for dims 4*lane..4*lane+3
+    float m = -INFINITY, l = 0.f;
     float4 o = f4_zero();
-    for (int t0 = w; t0 <= pos; t0 += ATTN_WARPS * U) {
-        const bool first = t0 == w;
-        float4 vv[U];
+    if (w <= pos) attn_round<U>(kpre, vpre, w, pos, q, k, v, scale, m, l, o);
+    for (int t0 = w + ATTN_WARPS * U; t0 <= pos; t0 += ATTN_WARPS * U) {
+        float4 kv[U], vv[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int t = t0 + u * ATTN_WARPS;
-            vv[u] = t > pos    ? f4_zero()
-                    : t == pos ? reinterpret_cast<const float4*>(sv)[lane]
-                    : first    ? vpre[u]
-                               : reinterpret_cast<const float4*>(vbase + (int64_t)t * row_stride)[lane];
+            kv[u] = t < pos ? reinterpret_cast<const float4*>(kbase + (int64_t)t * row_stride)[lane] : f4_zero();
+            vv[u] = t < pos ? reinterpret_cast<const float4*>(vbase + (int64_t)t * row_stride)[lane] : f4_zero();
         }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int t = t0 + u * ATTN_WARPS;
-            const float p = t <= pos ? s_scores[t] : 0.f;
-            o.x = __fadd_rn(o.x, __fmul_rn(p, vv[u].x));
-            o.y = __fadd_rn(o.y, __fmul_rn(p, vv[u].y));
-            o.z = __fadd_rn(o.z, __fmul_rn(p, vv[u].z));
-            o.w = __fadd_rn(o.w, __fmul_rn(p, vv[u].w));
-        }
+        attn_round<U>(kv, vv, t0, pos, q, k, v, scale, m, l, o);
     }
-    s_part[w][lane] = o;
+    ATTN_TRACE_AT(2);
+    if (lane == 0) {
+        s_m[w] = m;
+        s_l[w] = l;
+    }
+    s_o[w][lane] = o;
     __syncthreads();
-    if (tid < HD / 4) {
-        float4 r = s_part[0][tid];
-        for (int i = 1; i < ATTN_WARPS; ++i) {
-            const float4 pi = s_part[i][tid];
-            r.x = __fadd_rn(r.x, pi.x);
-            r.y = __fadd_rn(r.y, pi.y);
-            r.z = __fadd_rn(r.z, pi.z);
-            r.w = __fadd_rn(r.w, pi.w);
+    ATTN_TRACE_AT(3);
+    if (w == 0) {
+        // warps in order; a warp without positions has m = -inf and weight 0
+        float mx = s_m[0];
+        for (int i = 1; i < ATTN_WARPS; ++i) mx = fmaxf(mx, s_m[i]);
+        float ls = 0.f;
+        float4 r = f4_zero();
+        for (int i = 0; i < ATTN_WARPS; ++i) {
+            const float f = s_m[i] == -INFINITY ? 0.f : expf(__fsub_rn(s_m[i], mx));
+            ls = __fadd_rn(ls, __fmul_rn(s_l[i], f));
+            r = axpy4(f, s_o[i][lane], r);
         }
-        float4 res = make_float4(__fdiv_rn(r.x, se), __fdiv_rn(r.y, se), __fdiv_rn(r.z, se), __fdiv_rn(r.w, se));
-        reinterpret_cast<float4*>(a.out + h * HD)[tid] = res;
+        const float4 res = make_float4(__fdiv_rn(r.x, ls), __fdiv_rn(r.y, ls), __fdiv_rn(r.z, ls), __fdiv_rn(r.w, ls));
+        reinterpret_cast<float4*>(a.out + (int64_t)h * HD)[lane] = res;
     }
+    ATTN_TRACE_AT(6);
 }
 
 }  // namespace bh
@@ -331,7 +349,26 @@ uint64_t tensor_seed(uint64_t seed, int layer, int which) {
     return z ^ (z >> 27);
 }
 
+// Layer l's gate / up launch: the two matrices as the segments of one row-pair
+// launch; st->gu receives silu(gate) * up (n_ff values).
+bh::MatvecParams gate_up_params(bh_stack* st, int l) {
+    const bh_stack_config& c = st->cfg;
+    const uint8_t* const* W = st->wq + (size_t)l * BH_W_PER_LAYER;
+    bh::MatvecParams p = bh::base_params(st->ctx, W[BH_W_GATE], 2 * (int64_t)c.n_ff, c.n_embd, 1, st->gu);
+    p.w[1] = p.w[2] = W[BH_W_UP];
+    p.seg_end[0] = c.n_ff;
+    p.seg_end[1] = p.seg_end[2] = 2 * (int64_t)c.n_ff;
+    p.ldy = c.n_ff;
+    p.xf = st->h;
+    p.gamma = st->ffn_norm + (size_t)l * c.n_embd;
+    p.eps = c.rms_eps;
+    return p;
+}
+
 int stack_matvec(bh_stack* st, bh::MatvecParams& p, int src, int epi, bool pdl) {
+#ifdef BH_TRACE
+    if (st->ctx->trace) p.trace = st->ctx->trace + st->launches * bh::TRACE_LAUNCH;
+#endif
     return bh::run_matvec(&st->plan, p, BH_FOLD_X86, src, epi, st->stream, pdl);
 }
 
@@ -354,10 +391,14 @@ int launch_attn(bh_stack* st, int l, bool pdl) {
     a.eps = c.rms_eps;
     a.theta = c.rope_theta;
     a.rope_inv_freq = st->rope_inv_freq;
+    a.trace = nullptr;
+#ifdef BH_TRACE
+    if (st->ctx->trace) a.trace = st->ctx->trace + st->launches * bh::TRACE_LAUNCH;
+#endif
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)c.n_head);
     cfg.blockDim = dim3((unsigned)bh::ATTN_THREADS);
-    cfg.dynamicSmemBytes = sizeof(float) * (size_t)c.n_ctx;
+    cfg.dynamicSmemBytes = 0;
     cfg.stream = st->stream;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -385,8 +426,8 @@ int enqueue_step(bh_stack* st) {
         return BH_EIO;
     st->step_bytes = 0;
     st->launches = 0;
-    auto account = [&](const bh::MatvecParams& p, int b_in_bytes) {
-        st->step_bytes += p.N * (int64_t)p.nb * bh::Q4K_BYTES + b_in_bytes + p.N * 4;
+    auto account = [&](const bh::MatvecParams& p, int b_in_bytes, int64_t out_rows) {
+        st->step_bytes += p.N * (int64_t)p.nb * bh::Q4K_BYTES + b_in_bytes + out_rows * 4;
         st->launches += 1;
     };
     for (int l = 0; l < c.n_layer; ++l) {
@@ -402,7 +443,7 @@ int enqueue_step(bh_stack* st) {
         p.gamma = st->attn_norm + (size_t)l * c.n_embd;
         p.eps = c.rms_eps;
         if ((rc = stack_matvec(st, p, bh::ACT_F32_RMSNORM, bh::EPI_STORE, l > 0)) != BH_OK) return rc;
-        account(p, c.n_embd * 4);
+        account(p, c.n_embd * 4, p.N);
         // 2. attention
         if ((rc = launch_attn(st, l, true)) != BH_OK) return rc;
         st->launches += 1;
@@ -410,22 +451,16 @@ int enqueue_step(bh_stack* st) {
         p = bh::base_params(ctx, W[BH_W_O], c.n_embd, qd, 1, st->h);
         p.xf = st->attn;
         if ((rc = stack_matvec(st, p, bh::ACT_F32, bh::EPI_ADD, true)) != BH_OK) return rc;
-        account(p, (int)qd * 4);
-        // 4. gate / up
-        p = bh::base_params(ctx, W[BH_W_GATE], 2 * (int64_t)c.n_ff, c.n_embd, 1, st->gu);
-        p.w[1] = p.w[2] = W[BH_W_UP];
-        p.seg_end[0] = c.n_ff;
-        p.seg_end[1] = p.seg_end[2] = 2 * (int64_t)c.n_ff;
-        p.xf = st->h;
-        p.gamma = st->ffn_norm + (size_t)l * c.n_embd;
-        p.eps = c.rms_eps;
-        if ((rc = stack_matvec(st, p, bh::ACT_F32_RMSNORM, bh::EPI_STORE, true)) != BH_OK) return rc;
-        account(p, c.n_embd * 4);
-        // 5. down, SwiGLU in the prologue, residual add
+        account(p, (int)qd * 4, p.N);
+        // 4. gate / up in row pairs, silu(gate) * up in the epilogue
+        p = gate_up_params(st, l);
+        if ((rc = stack_matvec(st, p, bh::ACT_F32_RMSNORM, bh::EPI_SWIGLU, true)) != BH_OK) return rc;
+        account(p, c.n_embd * 4, c.n_ff);
+        // 5. down, residual add
         p = bh::base_params(ctx, W[BH_W_DOWN], c.n_embd, c.n_ff, 1, st->h);
         p.xf = st->gu;
-        if ((rc = stack_matvec(st, p, bh::ACT_F32_SWIGLU, bh::EPI_ADD, true)) != BH_OK) return rc;
-        account(p, 2 * c.n_ff * 4);
+        if ((rc = stack_matvec(st, p, bh::ACT_F32, bh::EPI_ADD, true)) != BH_OK) return rc;
+        account(p, c.n_ff * 4, p.N);
     }
     // LM head + argmax
     bh::MatvecParams p = bh::base_params(ctx, st->wq[(size_t)c.n_layer * BH_W_PER_LAYER], c.n_vocab, c.n_embd, 1,
@@ -435,6 +470,9 @@ int enqueue_step(bh_stack* st) {
     p.eps = c.rms_eps;
     p.cand_val = st->cand_val;
     p.cand_idx = st->cand_idx;
+#ifdef BH_TRACE
+    if (ctx->trace) p.trace = ctx->trace + st->launches * bh::TRACE_LAUNCH;
+#endif
     const int grid = bh::plan_for(ctx, p, 0);
     if (grid < 0) return grid;
     st->lm_grid = grid;
@@ -443,7 +481,7 @@ int enqueue_step(bh_stack* st) {
     o.grid = grid;
     o.pdl = true;
     if ((rc = bh::launch_matvec(p, BH_FOLD_X86, bh::ACT_F32_RMSNORM, bh::EPI_ARGMAX, o)) != BH_OK) return rc;
-    account(p, c.n_embd * 4);
+    account(p, c.n_embd * 4, p.N);
     if ((rc = bh::launch_argmax_finish(st->cand_val, st->cand_idx, grid, 1, st->tok, nullptr, st->stream, true)) !=
         BH_OK)
         return rc;
@@ -499,19 +537,13 @@ int enqueue_op(bh_stack* st, int op) {
                 rc = stack_matvec(st, p, bh::ACT_F32, bh::EPI_ADD, false);
                 break;
             case BH_OP_GATE_UP:
-                p = bh::base_params(ctx, W[BH_W_GATE], 2 * (int64_t)c.n_ff, c.n_embd, 1, st->gu);
-                p.w[1] = p.w[2] = W[BH_W_UP];
-                p.seg_end[0] = c.n_ff;
-                p.seg_end[1] = p.seg_end[2] = 2 * (int64_t)c.n_ff;
-                p.xf = st->h;
-                p.gamma = st->ffn_norm + (size_t)l * c.n_embd;
-                p.eps = c.rms_eps;
-                rc = stack_matvec(st, p, bh::ACT_F32_RMSNORM, bh::EPI_STORE, false);
+                p = gate_up_params(st, l);
+                rc = stack_matvec(st, p, bh::ACT_F32_RMSNORM, bh::EPI_SWIGLU, false);
                 break;
             case BH_OP_DOWN:
                 p = bh::base_params(ctx, W[BH_W_DOWN], c.n_embd, c.n_ff, 1, st->h);
                 p.xf = st->gu;
-                rc = stack_matvec(st, p, bh::ACT_F32_SWIGLU, bh::EPI_ADD, false);
+                rc = stack_matvec(st, p, bh::ACT_F32, bh::EPI_ADD, false);
                 break;
             default:
                 return BH_EINVAL;
@@ -567,16 +599,18 @@ int bh_stack_create(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, bh_s
     bh_stack* st = new (std::nothrow) bh_stack();
     if (!st) return BH_ENOMEM;
     st->ctx = ctx;
-    // The layer matvecs follow one another through programmatic launches; the
-    // next one can start its weight copies only if it finds room on the SMs.
-    // Unless the caller tuned a per-SM budget on ctx, the step therefore plans
-    // its layer matvecs within 168 KiB of shared memory per SM with 1152-byte
-    // row slices per stage (one 16-warp CTA per SM; the planner picks the
-    // threads per row). The LM head, which nothing follows, keeps ctx's plan.
+    // Launch plan of the layer matvecs, unless the caller tuned a per-SM
+    // budget on ctx: at most 168 KiB of shared memory per SM, 1152-byte row
+    // slices per stage (one 16-warp CTA per SM; the planner picks the threads
+    // per row), and one ring stage per warp issued before the programmatic
+    // wait, the rest right after the activation loads (measured on B200:
+    // 1.74 ms per token against 1.76 with the whole ring before the wait and
+    // 1.79-1.87 with 864- or 576-byte slices). The LM head keeps ctx's plan.
     st->plan = *ctx;
     if (ctx->sm_budget == 0) {
         st->plan.sm_budget = 168 * 1024;
         st->plan.stage_bytes = 1152;
+        st->plan.prefill_stages = 1;
     }
     st->cfg = *cfg;
     const bh_stack_config& c = st->cfg;
@@ -770,7 +804,7 @@ int bh_stack_time_op(bh_stack* st, int op, int reps, float* avg_ms, int64_t* byt
         case BH_OP_QKV: rows = qd + 2 * kvd; k = c.n_embd; xin = (int64_t)c.n_embd * 8; break;
         case BH_OP_O: rows = c.n_embd; k = qd; xin = qd * 4 + (int64_t)c.n_embd * 4; break;
         case BH_OP_GATE_UP: rows = 2 * (int64_t)c.n_ff; k = c.n_embd; xin = (int64_t)c.n_embd * 8; break;
-        case BH_OP_DOWN: rows = c.n_embd; k = c.n_ff; xin = 2 * (int64_t)c.n_ff * 4 + (int64_t)c.n_embd * 4; break;
+        case BH_OP_DOWN: rows = c.n_embd; k = c.n_ff; xin = (int64_t)c.n_ff * 4 + (int64_t)c.n_embd * 4; break;
         case BH_OP_ATTN: break;
         default: rows = c.n_vocab; k = c.n_embd; xin = (int64_t)c.n_embd * 8; break;
     }
@@ -778,7 +812,8 @@ int bh_stack_time_op(bh_stack* st, int op, int reps, float* avg_ms, int64_t* byt
         *bytes_per_launch = op == BH_OP_ATTN
                                 // q, k, v in; K/V of positions 0..pos (fp32) read; the output written
                                 ? (qd + 2 * kvd) * 4 + 2 * (int64_t)c.n_ctx * kvd * 4 + qd * 4
-                                : rows * (k / bh::QK) * bh::Q4K_BYTES + xin + rows * 4;
+                                : rows * (k / bh::QK) * bh::Q4K_BYTES + xin +
+                                      (op == BH_OP_GATE_UP ? (int64_t)c.n_ff : rows) * 4;
     const int per_rep = op == BH_OP_LMHEAD ? 1 : c.n_layer;
     int rc = enqueue_op(st, op);  // warm-up
     if (rc != BH_OK) return rc;

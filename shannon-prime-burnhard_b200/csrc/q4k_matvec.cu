@@ -1,16 +1,16 @@
 // q4k_matvec.cu — the sm_100a Q4_K x Q8_K matvec (batch 1..8).
 //
-// Structure (8 warps per CTA, 1 or 2 CTAs per SM, each CTA persistent over a
-// contiguous range of rows):
+// Structure (16 warps per CTA at batch 1-2, else 8; 1 or 2 CTAs per SM, each
+// CTA persistent over a contiguous range of rows):
 //  - every warp owns tiles of 32/TPR consecutive rows and streams them
 //    through its own ring of shared-memory stages: one 2-D tensor copy
 //    (cp.async.bulk.tensor, the TMA engine) per stage, issued by lane 0 and
 //    counted on the stage's mbarrier, rows padded so reads are bank-conflict
-//    free. Eight warps issue copies in parallel; weights do not depend on the
+//    free. All warps issue copies in parallel; weights do not depend on the
 //    previous kernel, so each warp starts streaming before the programmatic-
 //    launch wait.
 //  - all warps stage the activations once (Q8_K input, or fp32 input
-//    quantized in the prologue, optionally through RMSNorm or SwiGLU), then
+//    quantized in the prologue, optionally through RMSNorm), then
 //    TPR threads work each row; the per-block arithmetic (q4k_core.cuh)
 //    reproduces the reference's integer sums and fp32 fold bit for bit.
 #include "bh_common.cuh"
@@ -57,8 +57,39 @@ __device__ __forceinline__ int seg_of(const MatvecParams& p, int64_t row, int64_
 // ---------------------------------------------------------------------------
 // prologue: activations -> staged Q8_K blocks in shared memory
 // ---------------------------------------------------------------------------
-template <int FOLD, int SRC, int W>
-__device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* red, int ctid) {
+// Blocks per warp per staging round of fp32 sources: with 16 warps one round
+// covers the decode step's prologues at batch 1 (RMSNorm K <= 8192, plain
+// quantize K <= 12288).
+constexpr int STAGE_UF = 2;  // RMSNorm
+template <int SRC>
+__host__ __device__ constexpr int stage_uf() { return SRC == ACT_F32_RMSNORM ? STAGE_UF : 3; }
+
+// RMSNorm weights of this warp's first-round blocks (they do not depend on the
+// previous kernel, so they are loaded before the programmatic wait, ahead of
+// the weight copies).
+template <int W>
+__device__ __forceinline__ void preload_gamma(const MatvecParams& p, float (&gp)[STAGE_UF][8],
+                                              int warp, int lane) {
+    constexpr int UF = STAGE_UF;
+#pragma unroll
+    for (int u = 0; u < UF; ++u) {
+        const int blk = warp + u * W;
+        float4 c0 = make_float4(0.f, 0.f, 0.f, 0.f), c1 = c0;
+        if (blk < p.B * p.nb) {
+            const float* y = p.gamma + (blk % p.nb) * QK + 8 * lane;
+            c0 = *reinterpret_cast<const float4*>(y);
+            c1 = *reinterpret_cast<const float4*>(y + 4);
+        }
+        gp[u][0] = c0.x; gp[u][1] = c0.y; gp[u][2] = c0.z; gp[u][3] = c0.w;
+        gp[u][4] = c1.x; gp[u][5] = c1.y; gp[u][6] = c1.z; gp[u][7] = c1.w;
+    }
+}
+
+// top_up(): called once by every warp after its first round of global loads
+// is issued (the warp's remaining weight copies go out behind them).
+template <int FOLD, int SRC, int W, class TopUp>
+__device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* red, int ctid,
+                                  const float (&gp)[STAGE_UF][8], TopUp&& top_up) {
     const int warp = ctid >> 5, lane = ctid & 31;
     const int nblk = p.B * p.nb;
     // Each warp stages blocks warp, warp+W, ...; U blocks at a time with all
@@ -83,6 +114,7 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
                     if (lane < 8) bw[u] = *reinterpret_cast<const uint32_t*>(src + 260 + 4 * lane);
                 }
             }
+            if (blk0 == warp) top_up();
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int blk = blk0 + u * W;
@@ -106,18 +138,18 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
                 }
             }
         }
+        top_up();  // (no-op for warps that already did)
         return;
     }
     // fp32 sources. When every warp's blocks fit one round (nblk <= W*UF, the
     // decode shapes), all global loads are issued at once and RMSNorm's sum
     // of squares is taken from the loaded registers: per block (lane sums in
-    // element order, then an xor butterfly), per column (the blocks' sums in
-    // block order, read back by every thread from shared memory). The order is
-    // fixed, so every CTA derives the same scale. Larger batches fall back to
-    // a separate strided pass for the sum of squares.
-    // (UF blocks per warp per round: one round covers the decode step's
-    // K = 4096 RMSNorm / quantize prologues and the K = 12288 SwiGLU one)
-    constexpr int UF = SRC == ACT_F32_SWIGLU ? 3 : 2;
+    // element order, then an xor butterfly), per column (the blocks' sums
+    // through shared memory, one per lane, then an xor butterfly, in every
+    // warp). The order is fixed, so every warp of every CTA derives the same
+    // scale. Larger batches fall back to a separate strided pass for the sum
+    // of squares.
+    constexpr int UF = stage_uf<SRC>();
     __shared__ float s_scale[BH_MAX_BATCH];
     const bool one_round = nblk <= W * UF;
     if (SRC == ACT_F32_RMSNORM && !one_round) {
@@ -153,20 +185,27 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
 #pragma unroll
             for (int t = 0; t < 8; ++t) { v[u][t] = 0.f; aux[u][t] = 0.f; }
             if (blk < nblk) {
-                const float* x = SRC == ACT_F32_SWIGLU ? p.xf + (int64_t)b * 2 * p.K + e0 : p.xf + (int64_t)b * p.K + e0;
+                const float* x = p.xf + (int64_t)b * p.K + e0;
                 const float4 a0 = *reinterpret_cast<const float4*>(x), a1 = *reinterpret_cast<const float4*>(x + 4);
                 v[u][0] = a0.x; v[u][1] = a0.y; v[u][2] = a0.z; v[u][3] = a0.w;
                 v[u][4] = a1.x; v[u][5] = a1.y; v[u][6] = a1.z; v[u][7] = a1.w;
-                if (SRC == ACT_F32_SWIGLU || SRC == ACT_F32_RMSNORM) {
-                    const float* y = SRC == ACT_F32_SWIGLU ? x + p.K : p.gamma + e0;
-                    const float4 c0 = *reinterpret_cast<const float4*>(y), c1 = *reinterpret_cast<const float4*>(y + 4);
-                    aux[u][0] = c0.x; aux[u][1] = c0.y; aux[u][2] = c0.z; aux[u][3] = c0.w;
-                    aux[u][4] = c1.x; aux[u][5] = c1.y; aux[u][6] = c1.z; aux[u][7] = c1.w;
+                if constexpr (SRC == ACT_F32_RMSNORM) {
+                    if (one_round) {
+#pragma unroll
+                        for (int t = 0; t < 8; ++t) aux[u][t] = gp[u][t];
+                    } else {
+                        const float* y = p.gamma + e0;
+                        const float4 c0 = *reinterpret_cast<const float4*>(y), c1 = *reinterpret_cast<const float4*>(y + 4);
+                        aux[u][0] = c0.x; aux[u][1] = c0.y; aux[u][2] = c0.z; aux[u][3] = c0.w;
+                        aux[u][4] = c1.x; aux[u][5] = c1.y; aux[u][6] = c1.z; aux[u][7] = c1.w;
+                    }
                 }
             }
         }
+        if (rd == 0) top_up();
+        float scale_u[UF];
         if (SRC == ACT_F32_RMSNORM && one_round) {
-            // red[blk]: sum of squares of block blk (nblk <= W*U entries)
+            // red[blk]: sum of squares of block blk (nblk <= W*UF entries)
 #pragma unroll
             for (int u = 0; u < UF; ++u) {
                 const int blk = blk0 + u * W;
@@ -178,13 +217,18 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
                 if (lane == 0 && blk < nblk) red[blk] = ss;
             }
             named_bar(1, W * 32);
-            if (ctid < p.B) {
-                float t = 0.f;
-                for (int i = 0; i < p.nb; ++i) t = __fadd_rn(t, red[ctid * p.nb + i]);
+            // every warp sums its blocks' columns itself: lane i takes block i
+            // of the column (nb <= 32 here), then an xor butterfly
+#pragma unroll
+            for (int u = 0; u < UF; ++u) {
+                const int blk = blk0 + u * W;
+                const int b = (blk < nblk ? blk : 0) / p.nb;
+                float t = lane < p.nb ? red[b * p.nb + lane] : 0.f;
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, off));
                 const float mean = __fdiv_rn(t, (float)p.K);
-                s_scale[ctid] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+                scale_u[u] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
             }
-            named_bar(1, W * 32);
         }
 #pragma unroll
         for (int u = 0; u < UF; ++u) {
@@ -194,12 +238,8 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
             float x[8];
 #pragma unroll
             for (int t = 0; t < 8; ++t) {
-                if (SRC == ACT_F32_SWIGLU) {
-                    // silu(gate) * up
-                    const float g = v[u][t];
-                    x[t] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), aux[u][t]);
-                } else if (SRC == ACT_F32_RMSNORM) {
-                    x[t] = __fmul_rn(__fmul_rn(v[u][t], s_scale[b]), aux[u][t]);
+                if (SRC == ACT_F32_RMSNORM) {
+                    x[t] = __fmul_rn(__fmul_rn(v[u][t], one_round ? scale_u[u] : s_scale[b]), aux[u][t]);
                 } else {
                     x[t] = v[u][t];
                 }
@@ -210,6 +250,7 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
             stage_scalars(dst, qb.d, qb.bsum16, lane);
         }
     }
+    top_up();  // (no-op after the first round's call)
 }
 
 // Per-row epilogue of the dense kernel.
@@ -248,6 +289,8 @@ __global__ void __launch_bounds__(dense_warps(NB) * 32, 1) q4k_matvec_kernel(con
 
     uint8_t* act = smem + p.act_off;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float gpre[STAGE_UF][8];
+    if (SRC == ACT_F32_RMSNORM) preload_gamma<W>(p, gpre, warp, lane);
     uint8_t* ring = smem + p.ring_off + (size_t)warp * p.stages * p.stage_bytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off) + warp * p.stages;
 
@@ -278,24 +321,39 @@ __global__ void __launch_bounds__(dense_warps(NB) * 32, 1) q4k_matvec_kernel(con
     int i_j = 0, i_c = 0, i_s = 0, issued = 0;
     auto issue_next = [&]() {
         if (lane == 0) {
-            int64_t local;
-            const int sg = seg_of(p, r_begin + (int64_t)(warp + i_j * W) * R, local);
-            mbar_arrive_expect_tx(&full[i_s], (uint32_t)p.stage_bytes);
-            tensor_g2s_2d(ring + (size_t)i_s * p.stage_bytes, &p.tmap[sg], i_c * p.kc * (Q4K_BYTES / 8), (int)local,
-                          &full[i_s], pol);
+            const int x = i_c * p.kc * (Q4K_BYTES / 8);
+            uint8_t* dst = ring + (size_t)i_s * p.stage_bytes;
+            mbar_arrive_expect_tx(&full[i_s], (uint32_t)p.tx_bytes);
+            if (EPI == EPI_SWIGLU) {
+                // R/2 gate rows, then the same R/2 up rows at half_off (a
+                // tensor copy's shared-memory destination is 128-byte aligned)
+                const int row = (int)((r_begin + (int64_t)(warp + i_j * W) * R) / 2);
+                tensor_g2s_2d(dst, &p.tmap[0], x, row, &full[i_s], pol);
+                tensor_g2s_2d(dst + p.half_off, &p.tmap[1], x, row, &full[i_s], pol);
+            } else {
+                int64_t local;
+                const int sg = seg_of(p, r_begin + (int64_t)(warp + i_j * W) * R, local);
+                tensor_g2s_2d(dst, &p.tmap[sg], x, (int)local, &full[i_s], pol);
+            }
         }
         __syncwarp();
         ++issued;
         if (++i_c == nkc) { i_c = 0; ++i_j; }
         if (++i_s == p.stages) i_s = 0;
     };
-    // weights do not depend on the previous kernel: start streaming now
-    const int prefill = min(p.stages, total);
+    // weights do not depend on the previous kernel: the first p.prefill
+    // stages of the ring go out now, the rest right behind the activation
+    // loads after the wait (so those loads do not queue behind a full ring)
+    const int ring_fill = min(p.stages, total);
+    const int prefill = p.prefill > 0 ? min(p.prefill, ring_fill) : ring_fill;
     for (int q = 0; q < prefill; ++q) issue_next();
     BH_TRACE_AT(1);
     pdl_trigger();
     pdl_wait();
-    stage_activations<FOLD, SRC, W>(p, act, s_red, threadIdx.x);
+    BH_TRACE_AT(5);
+    stage_activations<FOLD, SRC, W>(p, act, s_red, threadIdx.x, gpre, [&]() {
+        while (issued < ring_fill) issue_next();
+    });
     __syncthreads();
     BH_TRACE_AT(2);
 
@@ -333,7 +391,8 @@ __global__ void __launch_bounds__(dense_warps(NB) * 32, 1) q4k_matvec_kernel(con
             const int sbc = c * p.kc;
             const int kl = min(p.kc, p.nb - sbc);
             // rows past the end of the range read zero-filled stage bytes and are never stored
-            const uint8_t* rowp = ring + (size_t)c_s * p.stage_bytes + (size_t)rgrp * p.row_stride;
+            const uint8_t* rowp = ring + (size_t)c_s * p.stage_bytes + (size_t)rgrp * p.row_stride +
+                                  (EPI == EPI_SWIGLU && rgrp >= R / 2 ? p.half_off - (R / 2) * p.row_stride : 0);
             const uint8_t* actc = act + sbc * ACT_BLOCK_BYTES;
 BH_UNROLL(BH_KB_UNROLL)
             for (int kb = 0; kb < kl; ++kb) {
@@ -355,8 +414,20 @@ BH_UNROLL(BH_KB_UNROLL)
         if (!ok) break;
         BH_TRACE_AT(4);
 #pragma unroll
-        for (int b = 0; b < NB; ++b)
-            finish_row<FOLD, EPI, TPR>(p, acc[b], accm[b], rgrp, t, b, live, r_begin + rin, best_v[b], best_i[b]);
+        for (int b = 0; b < NB; ++b) {
+            if (EPI == EPI_SWIGLU) {
+                // gate row i in row group rgrp < R/2, its up row R/2 groups
+                // (16 lanes) further on
+                const float v = row_value<FOLD, TPR>(acc[b], accm[b], rgrp);
+                const float u = __shfl_down_sync(FULLM, v, 16);
+                if (live && t == 0 && rgrp < R / 2) {
+                    const int64_t i = (r_begin + (int64_t)(warp + j * W) * R) / 2 + rgrp;
+                    p.y[(int64_t)b * p.ldy + i] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.f, expf(-v))), u);
+                }
+            } else {
+                finish_row<FOLD, EPI, TPR>(p, acc[b], accm[b], rgrp, t, b, live, r_begin + rin, best_v[b], best_i[b]);
+            }
+        }
     }
     BH_TRACE_AT(6);
     if (!ok && lane == 0) {
@@ -405,7 +476,7 @@ BH_UNROLL(BH_KB_UNROLL)
 // (a CTA's range is at most ceil(tiles / grid) tiles), so a matrix with few
 // rows per CTA gives its working warps deeper rings, which fill before the
 // programmatic wait.
-int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int tpr) {
+int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int tpr, bool pairs) {
     if (grid < 1 || (tpr != 4 && tpr != 8)) return BH_EINVAL;
     const int R = 32 / tpr;
     const int W = dense_warps(p.B);
@@ -421,7 +492,11 @@ int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int t
         const int words = kc * (Q4K_BYTES / 4);
         const int padw = ((8 - (words % 32)) % 32 + 32) % 32;  // row stride == 8 words (mod 32 banks)
         const int stride = kc * Q4K_BYTES + 4 * padw;
-        const int stage = R * stride;
+        // (stride is 32 mod 128 bytes, so R * stride, R = 4 or 8, is a
+        // multiple of 128: every stage starts 128-byte aligned. A pair stage
+        // puts its up half at the next 128-byte boundary.)
+        const int half_off = pairs ? ((R / 2) * stride + 127) / 128 * 128 : 0;
+        const int stage = pairs ? (half_off + (R / 2) * stride + 127) / 128 * 128 : R * stride;
         const int avail = smem_cap - ring_off - 512;  // static shared memory of the kernel
         int stages = avail > 0 ? avail / (wbusy * (stage + 8)) : 0;
         if (stages > 8) stages = 8;
@@ -429,6 +504,8 @@ int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int t
         p.kc = kc;
         p.row_stride = stride;
         p.stage_bytes = stage;
+        p.tx_bytes = R * stride;
+        p.half_off = half_off;
         p.stages = stages;
         p.rows_per_tile = R;
         p.tpr = tpr;
@@ -498,15 +575,15 @@ static int launch_fold(const MatvecParams& p, int src, int epi, const LaunchOpts
         if (src != ACT_Q8K || epi != EPI_STORE) return BH_EINVAL;
         return launch_nb<FOLD, ACT_Q8K, EPI_STORE, true>(p, o, grid);
     }
-    switch (src * 3 + epi) {
-        case ACT_Q8K * 3 + EPI_STORE: return launch_nb<FOLD, ACT_Q8K, EPI_STORE, false>(p, o, grid);
-        case ACT_Q8K * 3 + EPI_ARGMAX: return launch_nb<FOLD, ACT_Q8K, EPI_ARGMAX, false>(p, o, grid);
-        case ACT_F32 * 3 + EPI_STORE: return launch_nb<FOLD, ACT_F32, EPI_STORE, false>(p, o, grid);
-        case ACT_F32 * 3 + EPI_ADD: return launch_nb<FOLD, ACT_F32, EPI_ADD, false>(p, o, grid);
-        case ACT_F32 * 3 + EPI_ARGMAX: return launch_nb<FOLD, ACT_F32, EPI_ARGMAX, false>(p, o, grid);
-        case ACT_F32_RMSNORM * 3 + EPI_STORE: return launch_nb<FOLD, ACT_F32_RMSNORM, EPI_STORE, false>(p, o, grid);
-        case ACT_F32_RMSNORM * 3 + EPI_ARGMAX: return launch_nb<FOLD, ACT_F32_RMSNORM, EPI_ARGMAX, false>(p, o, grid);
-        case ACT_F32_SWIGLU * 3 + EPI_ADD: return launch_nb<FOLD, ACT_F32_SWIGLU, EPI_ADD, false>(p, o, grid);
+    switch (src * 4 + epi) {
+        case ACT_Q8K * 4 + EPI_STORE: return launch_nb<FOLD, ACT_Q8K, EPI_STORE, false>(p, o, grid);
+        case ACT_Q8K * 4 + EPI_ARGMAX: return launch_nb<FOLD, ACT_Q8K, EPI_ARGMAX, false>(p, o, grid);
+        case ACT_F32 * 4 + EPI_STORE: return launch_nb<FOLD, ACT_F32, EPI_STORE, false>(p, o, grid);
+        case ACT_F32 * 4 + EPI_ADD: return launch_nb<FOLD, ACT_F32, EPI_ADD, false>(p, o, grid);
+        case ACT_F32 * 4 + EPI_ARGMAX: return launch_nb<FOLD, ACT_F32, EPI_ARGMAX, false>(p, o, grid);
+        case ACT_F32_RMSNORM * 4 + EPI_STORE: return launch_nb<FOLD, ACT_F32_RMSNORM, EPI_STORE, false>(p, o, grid);
+        case ACT_F32_RMSNORM * 4 + EPI_ARGMAX: return launch_nb<FOLD, ACT_F32_RMSNORM, EPI_ARGMAX, false>(p, o, grid);
+        case ACT_F32_RMSNORM * 4 + EPI_SWIGLU: return launch_nb<FOLD, ACT_F32_RMSNORM, EPI_SWIGLU, false>(p, o, grid);
         default: return BH_EINVAL;
     }
 }
@@ -547,8 +624,18 @@ int encode_q4k_map(CUtensorMap* map, const void* base, int64_t rows, int nb, int
     return BH_OK;
 }
 
-// One tensor map per segment; the box is the stage slice of one tile.
-static int encode_maps(MatvecParams& p) {
+// One tensor map per segment; the box is the stage slice of one tile (of
+// half a tile for gate/up pairs: two equal segments, N = 2 x rows each).
+static int encode_maps(MatvecParams& p, bool pair) {
+    if (pair) {
+        const int64_t half = p.seg_end[0];
+        if (2 * half != p.N || p.seg_end[1] != p.N || half % (p.rows_per_tile / 2)) return BH_EINVAL;
+        for (int sg = 0; sg < 2; ++sg) {
+            const int rc = encode_q4k_map(&p.tmap[sg], p.w[sg], half, p.nb, p.row_stride, p.rows_per_tile / 2);
+            if (rc != BH_OK) return rc;
+        }
+        return BH_OK;
+    }
     if (p.seg_end[0] < p.N && (p.seg_end[0] % MV_ROWS || p.seg_end[1] % MV_ROWS)) return BH_EINVAL;
     int64_t prev = 0;
     for (int sg = 0; sg < 3; ++sg) {
@@ -562,7 +649,10 @@ static int encode_maps(MatvecParams& p) {
 
 int launch_matvec(const MatvecParams& pin, int fold, int act_src, int epi, const LaunchOpts& o) {
     MatvecParams p = pin;
-    const int rc = encode_maps(p);
+    // a tensor copy's shared-memory destination must be 128-byte aligned
+    if (p.stage_bytes % 128 || (epi == EPI_SWIGLU && (p.partials || p.half_off % 128 || p.half_off == 0)))
+        return BH_EINVAL;
+    const int rc = encode_maps(p, epi == EPI_SWIGLU);
     if (rc != BH_OK) return rc;
     const int grid = o.grid;
     if (fold == BH_FOLD_X86) return launch_fold<BH_FOLD_X86>(p, act_src, epi, o, grid);
