@@ -199,6 +199,10 @@ typedef struct bh_stack_config {
 #define BH_T_V_CACHE 14
 #define BH_T_LOGITS 15
 #define BH_T_HIDDEN 16
+/* the last layer's activations of the last step: q|k|v as projected (before
+ * the per-head norm and RoPE), and the attention output [n_head * head_dim] */
+#define BH_T_QKV 17
+#define BH_T_ATTN 18
 
 /* The Qwen3-8B-shaped defaults (36 x 4096, 32/8 heads of 128, FFN 12288,
  * vocab 151936, 128 KV positions). */

@@ -76,7 +76,7 @@ W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN = range(7)
 W_PER_LAYER = 7
 W_OUTPUT = 7
 OP_QKV, OP_O, OP_GATE_UP, OP_DOWN, OP_LMHEAD, OP_ATTN = range(6)
-T_ATTN_NORM, T_FFN_NORM, T_Q_NORM, T_K_NORM, T_OUT_NORM, T_K_CACHE, T_V_CACHE, T_LOGITS, T_HIDDEN = range(8, 17)
+T_ATTN_NORM, T_FFN_NORM, T_Q_NORM, T_K_NORM, T_OUT_NORM, T_K_CACHE, T_V_CACHE, T_LOGITS, T_HIDDEN, T_QKV, T_ATTN = range(8, 19)
 
 
 def load(path: str = LIB_PATH) -> C.CDLL:

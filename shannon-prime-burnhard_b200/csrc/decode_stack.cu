@@ -23,6 +23,8 @@
 
 #include <vector>
 
+#include <cooperative_groups.h>
+
 #include "bh_common.cuh"
 #include "bh_ctx.cuh"
 #include "bh_kernels.cuh"
@@ -61,7 +63,7 @@ int fill_normal(float* out, int64_t n, int64_t first, uint64_t seed, double mean
 }
 
 // ---------------------------------------------------------------------------
-// attention for one decode token, one CTA per query head, head_dim threads
+// attention for one decode token
 // ---------------------------------------------------------------------------
 struct AttnParams {
     const float* qkv;        // [q_dim | kv_dim | kv_dim]
@@ -95,25 +97,28 @@ constexpr int64_t TRACE_LAUNCH = 256 * DENSE_MAX_WARPS * 8;
     } while (0)
 #endif
 
-// One CTA of ATTN_THREADS per query head (head_dim 128: lane l of a warp
-// holds dims 4l..4l+3 of a row). Every warp holds the head's q and this
-// token's k and v in registers: the per-head RMSNorm is a warp butterfly and
-// NeoX RoPE pairs dim d with d + 64, i.e. lane l with lane l ^ 16, so no
-// block barrier is needed before the scores. Positions are dealt
-// round-robin to the warps, ATTN_U per warp per round; each warp reads whole
-// K / V rows with one coalesced 512-byte load and keeps its own running
-// softmax (max, sum, weighted V). The K / V history (positions before this
-// token), the norm weights and the rotation angles do not depend on the
-// previous kernel, so the first round's rows, the weights and the
-// sines / cosines are taken before the programmatic-launch wait. The warps'
-// partial results are combined in warp order after one barrier.
+// Attention of one decode token, split over the positions (the K / V reads
+// are the cost, so they are spread over many SMs): CTA g * ATTN_CHUNKS + c
+// (chunk c of KV group g) works the `group` query heads of KV group g
+// over its share of the positions, ATTN_U consecutive positions per warp per
+// round (warp w: head w % group, positions sub = w / group of the CTA's
+// P = (ATTN_WARPS / group) * ATTN_U per round; chunk c takes positions
+// r * ATTN_CHUNKS * P + c * P + ... of round r). head_dim 128: lane l of a warp
+// holds dims 4l..4l+3 of a row. Every warp holds its head's q and this
+// token's k and v in registers (per-head RMSNorm = a warp butterfly; NeoX RoPE
+// pairs dim d with d + 64, i.e. lane l with lane l ^ 16) and keeps a running
+// softmax (max, sum, weighted V). The warps of a head are combined in the
+// CTA; the CTAs of a group form one thread-block cluster: each CTA stores its
+// per-head partials (o[128], max, sum) into the shared memory of the CTA that
+// combines that head, which sums them in chunk order after one cluster
+// barrier. The first round's K / V rows, the norm weights and the
+// rotation frequencies do not depend on the previous kernel and are loaded
+// before the programmatic-launch wait.
 constexpr int ATTN_THREADS = 256;
 constexpr int ATTN_WARPS = ATTN_THREADS / 32;
 constexpr int ATTN_HD = 128;
-#ifndef BH_ATTN_U
-#define BH_ATTN_U 16
-#endif
-constexpr int ATTN_U = BH_ATTN_U;  // positions per warp per round (16: 128 positions per round)
+constexpr int ATTN_U = 8;                 // positions per warp per round
+constexpr int ATTN_CHUNKS = 8;            // CTAs per KV group: one thread-block cluster
 
 __device__ __forceinline__ float4 f4_zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
 
@@ -160,7 +165,7 @@ __device__ __forceinline__ float4 mul4(float a, float4 x) {
     return make_float4(__fmul_rn(a, x.x), __fmul_rn(a, x.y), __fmul_rn(a, x.z), __fmul_rn(a, x.w));
 }
 
-// One round of a warp's positions t0 + u * ATTN_WARPS (u < U): K / V rows of
+// One round of a warp's positions t0 + u (u < U): K / V rows of
 // positions before pos in kv / vv, this token's k / v at pos, nothing past it.
 // Scores q.k * scale (a warp butterfly per position); the running max m, sum l
 // and weighted V o are rescaled to the round's maximum, then accumulated.
@@ -171,7 +176,7 @@ __device__ __forceinline__ void attn_round(const float4 (&kv)[U], const float4 (
     float mr = m;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-        const int t = t0 + u * ATTN_WARPS;
+        const int t = t0 + u;
         const float4 kk = t < pos ? kv[u] : k;  // (past pos: not used)
         sc[u] = t <= pos ? __fmul_rn(warp_sum(dot4(q, kk)), scale) : -INFINITY;
         mr = fmaxf(mr, sc[u]);
@@ -182,7 +187,7 @@ __device__ __forceinline__ void attn_round(const float4 (&kv)[U], const float4 (
     o = mul4(f, o);
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-        const int t = t0 + u * ATTN_WARPS;
+        const int t = t0 + u;
         const float p = expf(__fsub_rn(sc[u], mr));  // 0 past pos
         l = __fadd_rn(l, p);
         o = axpy4(p, t < pos ? vv[u] : t == pos ? v : f4_zero(), o);
@@ -193,24 +198,36 @@ __device__ __forceinline__ void attn_round(const float4 (&kv)[U], const float4 (
 __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnParams a) {
     __shared__ float s_m[ATTN_WARPS], s_l[ATTN_WARPS];
     __shared__ float4 s_o[ATTN_WARPS][ATTN_HD / 4];
-    constexpr int U = ATTN_U;
-    const int h = blockIdx.x, tid = threadIdx.x, HD = ATTN_HD;
-    const int group = a.n_head / a.n_head_kv, g = h / group;
-    const int q_dim = a.n_head * HD, kv_dim = a.n_head_kv * HD;
+    // (CTA c < group) the partials of head g * group + c from the cluster's chunks
+    __shared__ float4 s_po[ATTN_CHUNKS][ATTN_HD / 4];
+    __shared__ float s_pm[ATTN_CHUNKS], s_pl[ATTN_CHUNKS];
+    constexpr int U = ATTN_U, HD = ATTN_HD;
+    // one cluster of ATTN_CHUNKS CTAs per KV group, chunk = rank in the cluster
+    const int g = blockIdx.x / ATTN_CHUNKS, c = blockIdx.x % ATTN_CHUNKS, tid = threadIdx.x;
+    const int group = a.n_head / a.n_head_kv;
     const int lane = tid & 31, w = tid >> 5;
+    const int hl = w % group, sub = w / group, wph = ATTN_WARPS / group;
+    const int h = g * group + hl;
+    const int P = wph * U;                 // positions of one CTA round
+    const int stride_r = ATTN_CHUNKS * P;  // positions of one round of all chunks
+    const int q_dim = a.n_head * HD, kv_dim = a.n_head_kv * HD;
     const int64_t row_stride = (int64_t)a.n_head_kv * HD;
     const float* kbase = a.kc + (int64_t)g * HD;
     const float* vbase = a.vc + (int64_t)g * HD;
+    const int t_first = c * P + sub * U;   // this warp's first position
     ATTN_TRACE_AT(0);
+    // distributed shared memory may be written only once every CTA of the
+    // cluster runs: arrive now, wait before the first remote store
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
     // before the wait, nothing that makes the thread wait: loads of the first
-    // round's K / V cache rows (all of them, whatever the position: only
-    // those before pos are used), the norm weights, the rotation frequencies
-    // (lane l: dims 4l..4l+3, frequency index (4l mod 64) + j) and pos
+    // round's K / V cache rows (whatever the position: only those before pos
+    // are used), the norm weights, the rotation frequencies (lane l: dims
+    // 4l..4l+3, frequency index (4l mod 64) + j) and pos
     float4 kpre[U], vpre[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-        const int t = w + u * ATTN_WARPS;
+        const int t = t_first + u;
         kpre[u] = t < a.n_ctx ? reinterpret_cast<const float4*>(kbase + (int64_t)t * row_stride)[lane] : f4_zero();
         vpre[u] = t < a.n_ctx ? reinterpret_cast<const float4*>(vbase + (int64_t)t * row_stride)[lane] : f4_zero();
     }
@@ -222,8 +239,8 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnPar
     pdl_wait();
     ATTN_TRACE_AT(5);
 
-    // this head's q, this token's k and v (the rotation is computed while
-    // they load); per-head RMSNorm, NeoX RoPE
+    // this warp's head q, this token's k and v (the rotation is computed
+    // while they load); per-head RMSNorm, NeoX RoPE
     float4 q = reinterpret_cast<const float4*>(a.qkv + (int64_t)h * HD)[lane];
     float4 k = reinterpret_cast<const float4*>(a.qkv + q_dim + (int64_t)g * HD)[lane];
     const float4 v = reinterpret_cast<const float4*>(a.qkv + q_dim + kv_dim + (int64_t)g * HD)[lane];
@@ -237,49 +254,77 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnPar
     const bool low = lane < 16;
     q = rope4(scale4(q, rq, qn), cs, sn, low);
     k = rope4(scale4(k, rk, kn), cs, sn, low);
-    ATTN_TRACE_AT(1);
-    if (h % group == 0 && w == 0) {
+    if (c == 0 && w == 0) {
         reinterpret_cast<float4*>(a.kc + (int64_t)pos * row_stride + (int64_t)g * HD)[lane] = k;
         reinterpret_cast<float4*>(a.vc + (int64_t)pos * row_stride + (int64_t)g * HD)[lane] = v;
     }
+    ATTN_TRACE_AT(1);
 
-    // this warp's positions w, w + ATTN_WARPS, ...: scores, running softmax
-    // (the first round from the rows loaded before the wait)
+    // this warp's positions: scores, running softmax (the first round from
+    // the rows loaded before the wait)
     const float scale = __fdiv_rn(1.f, __fsqrt_rn((float)HD));
     float m = -INFINITY, l = 0.f;
     float4 o = f4_zero();
-    if (w <= pos) attn_round<U>(kpre, vpre, w, pos, q, k, v, scale, m, l, o);
-    for (int t0 = w + ATTN_WARPS * U; t0 <= pos; t0 += ATTN_WARPS * U) {
+    if (t_first <= pos) attn_round<U>(kpre, vpre, t_first, pos, q, k, v, scale, m, l, o);
+    for (int t0 = t_first + stride_r; t0 <= pos; t0 += stride_r) {
         float4 kv[U], vv[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            const int t = t0 + u * ATTN_WARPS;
+            const int t = t0 + u;
             kv[u] = t < pos ? reinterpret_cast<const float4*>(kbase + (int64_t)t * row_stride)[lane] : f4_zero();
             vv[u] = t < pos ? reinterpret_cast<const float4*>(vbase + (int64_t)t * row_stride)[lane] : f4_zero();
         }
         attn_round<U>(kv, vv, t0, pos, q, k, v, scale, m, l, o);
     }
     ATTN_TRACE_AT(2);
+
+    // the warps of each head, in sub order (a warp without positions has
+    // max -inf and weight 0), then this CTA's partial for head hl goes into
+    // slot c of CTA hl of the cluster (distributed shared memory); after one
+    // cluster barrier CTA c < group combines head c over the chunks in chunk
+    // order from its own shared memory
     if (lane == 0) {
         s_m[w] = m;
         s_l[w] = l;
     }
     s_o[w][lane] = o;
     __syncthreads();
-    ATTN_TRACE_AT(3);
-    if (w == 0) {
-        // warps in order; a warp without positions has m = -inf and weight 0
-        float mx = s_m[0];
-        for (int i = 1; i < ATTN_WARPS; ++i) mx = fmaxf(mx, s_m[i]);
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+    if (w < group) {
+        float mx = s_m[w];
+        for (int i = 1; i < wph; ++i) mx = fmaxf(mx, s_m[w + i * group]);
         float ls = 0.f;
         float4 r = f4_zero();
-        for (int i = 0; i < ATTN_WARPS; ++i) {
-            const float f = s_m[i] == -INFINITY ? 0.f : expf(__fsub_rn(s_m[i], mx));
-            ls = __fadd_rn(ls, __fmul_rn(s_l[i], f));
-            r = axpy4(f, s_o[i][lane], r);
+        for (int i = 0; i < wph; ++i) {
+            const int wi = w + i * group;
+            const float f = s_m[wi] == -INFINITY ? 0.f : expf(__fsub_rn(s_m[wi], mx));
+            ls = __fadd_rn(ls, __fmul_rn(s_l[wi], f));
+            r = axpy4(f, s_o[wi][lane], r);
+        }
+        cl.map_shared_rank(&s_po[c][0], w)[lane] = r;
+        if (lane == 0) {
+            *cl.map_shared_rank(&s_pm[c], w) = mx;
+            *cl.map_shared_rank(&s_pl[c], w) = ls;
+        }
+    }
+    cl.sync();  // (all partials have landed; nothing is read remotely after it)
+    ATTN_TRACE_AT(3);
+    if (c < group && w == 0) {
+        float mx = s_pm[0];
+#pragma unroll
+        for (int i = 1; i < ATTN_CHUNKS; ++i) mx = fmaxf(mx, s_pm[i]);
+        float ls = 0.f;
+        float4 r = f4_zero();
+#pragma unroll
+        for (int i = 0; i < ATTN_CHUNKS; ++i) {
+            const float f = s_pm[i] == -INFINITY ? 0.f : expf(__fsub_rn(s_pm[i], mx));
+            ls = __fadd_rn(ls, __fmul_rn(s_pl[i], f));
+            r = axpy4(f, s_po[i][lane], r);
         }
         const float4 res = make_float4(__fdiv_rn(r.x, ls), __fdiv_rn(r.y, ls), __fdiv_rn(r.z, ls), __fdiv_rn(r.w, ls));
-        reinterpret_cast<float4*>(a.out + (int64_t)h * HD)[lane] = res;
+        reinterpret_cast<float4*>(a.out + (int64_t)(g * group + c) * HD)[lane] = res;
     }
     ATTN_TRACE_AT(6);
 }
@@ -325,6 +370,8 @@ int check_cfg(const bh_stack_config* c) {
     if (c->n_layer < 1 || c->n_embd < 256 || c->n_embd % 256 || c->n_ff < 256 || c->n_ff % 256) return BH_EINVAL;
     if (c->head_dim != bh::ATTN_HD) return BH_EINVAL;  // the attention kernel is written for 128
     if (c->n_head < 1 || c->n_head_kv < 1 || c->n_head % c->n_head_kv) return BH_EINVAL;
+    // the attention CTA gives each of a group's query heads the same number of warps
+    if (bh::ATTN_WARPS % (c->n_head / c->n_head_kv)) return BH_EINVAL;
     if ((c->n_head * c->head_dim) % 256 || c->n_vocab < 1 || c->n_ctx < 1 || c->n_ctx > 8192) return BH_EINVAL;
     return BH_OK;
 }
@@ -372,7 +419,7 @@ int stack_matvec(bh_stack* st, bh::MatvecParams& p, int src, int epi, bool pdl) 
     return bh::run_matvec(&st->plan, p, BH_FOLD_X86, src, epi, st->stream, pdl);
 }
 
-// Attention of layer l over positions 0..pos (one CTA per query head).
+// Attention of layer l over positions 0..pos (ATTN_CHUNKS CTAs per KV group).
 int launch_attn(bh_stack* st, int l, bool pdl) {
     const bh_stack_config& c = st->cfg;
     const int64_t kvd = (int64_t)c.n_head_kv * c.head_dim;
@@ -396,15 +443,19 @@ int launch_attn(bh_stack* st, int l, bool pdl) {
     if (st->ctx->trace) a.trace = st->ctx->trace + st->launches * bh::TRACE_LAUNCH;
 #endif
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)c.n_head);
+    cfg.gridDim = dim3((unsigned)(c.n_head_kv * bh::ATTN_CHUNKS));
     cfg.blockDim = dim3((unsigned)bh::ATTN_THREADS);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st->stream;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = bh::ATTN_CHUNKS;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = pdl ? 2 : 1;
     static bool attr_set = false;
     if (!attr_set) {
         // the same shared-memory carveout as the matvecs around it
@@ -857,6 +908,8 @@ int bh_stack_tensor(bh_stack* st, int layer, int which, void** ptr, int64_t* row
             case BH_T_V_CACHE: *ptr = st->vc + (size_t)layer * c.n_ctx * kvd; r = c.n_ctx; k = kvd; break;
             case BH_T_LOGITS: *ptr = st->logits; r = 1; k = c.n_vocab; break;
             case BH_T_HIDDEN: *ptr = st->h; r = 1; k = c.n_embd; break;
+            case BH_T_QKV: *ptr = st->qkv; r = 1; k = (int64_t)(c.n_head + 2 * c.n_head_kv) * c.head_dim; break;
+            case BH_T_ATTN: *ptr = st->attn; r = 1; k = (int64_t)c.n_head * c.head_dim; break;
             default: return BH_EINVAL;
         }
     }
