@@ -76,7 +76,7 @@ namespace bh {
 //    smem_cap_small bytes; narrow ones one CTA per SM.
 // A non-zero sm_budget caps the shared memory one launch holds per SM, so the
 // next programmatic launch finds room to start its weight copies early.
-int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override, bool pairs) {
+int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override) {
     const int W = dense_warps(p.B);
     const int act_bytes = p.B * p.nb * ACT_BLOCK_BYTES;
     const bool small = act_bytes <= ctx->small_act_bytes;
@@ -109,7 +109,7 @@ int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override, bool pairs) {
     if (ctx->tpr_force) tpr = (ctx->tpr_force == 8 && p.B <= 2) ? 8 : 4;
     const int64_t ntile = (p.N + 32 / tpr - 1) / (32 / tpr);  // CTAs own whole tiles
     if ((int64_t)grid > ntile) grid = (int)ntile;
-    const int rc = matvec_plan(p, grid, cap, ctx->stage_bytes, tpr, pairs);
+    const int rc = matvec_plan(p, grid, cap, ctx->stage_bytes, tpr);
     p.prefill = ctx->prefill_stages;
     return rc == BH_OK ? grid : rc;
 }
@@ -133,7 +133,7 @@ MatvecParams base_params(bh_ctx* ctx, const void* W, int64_t N, int64_t K, int B
 }
 
 int run_matvec(bh_ctx* ctx, MatvecParams& p, int fold, int src, int epi, cudaStream_t s, bool pdl) {
-    const int grid = plan_for(ctx, p, 0, epi == EPI_SWIGLU);
+    const int grid = plan_for(ctx, p, 0);
     if (grid < 0) return grid;
     LaunchOpts o;
     o.stream = s;

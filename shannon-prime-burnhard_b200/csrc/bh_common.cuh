@@ -102,6 +102,17 @@ __device__ __forceinline__ void tensor_g2s_2d(void* dst, const CUtensorMap* tmap
         : "memory");
 }
 
+// 3-D tensor copy global -> shared (tile mode), coordinates (x, y, z); x * 8
+// bytes must be a multiple of 16.
+__device__ __forceinline__ void tensor_g2s_3d(void* dst, const CUtensorMap* tmap, int x, int y, int z, uint64_t* bar,
+                                              uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
 // Fetch a tensor map descriptor (generic address of the kernel parameter) ahead of the
 // first copy that uses it.
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* tmap) {

@@ -38,8 +38,7 @@ struct bh_ctx {
 namespace bh {
 // Grid and shared-memory plan for one matvec launch (fills p's tiling
 // fields); returns the grid size or a negative errno.
-// pairs: the launch uses the gate/up pair epilogue (EPI_SWIGLU).
-int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override, bool pairs = false);
+int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override);
 // MatvecParams for a single-segment weight matrix.
 MatvecParams base_params(bh_ctx* ctx, const void* W, int64_t N, int64_t K, int B, float* y);
 // plan_for + launch.

@@ -21,10 +21,10 @@ enum Epilogue : int {
     EPI_ADD = 1,     // y[b*ldy + r] += v   (residual add)
     EPI_ARGMAX = 2,  // y[b*ldy + r] = v, plus per-CTA (max, first index) candidates
     // Gate/up pairs: segment 0 holds the gate rows, segment 1 the up rows
-    // (N = 2 * n_ff virtual rows). Virtual tile j of R rows is gate rows
-    // [j*R/2, (j+1)*R/2) followed by the same up rows (one copy from each
-    // segment), so one warp has both values of row i:
-    // y[b*ldy + i] = silu(gate_i) * up_i, i < n_ff.
+    // (N = 2 * n_ff virtual rows; w[1] after w[0] in memory, 16-byte
+    // distance). Virtual tile j of R rows is gate rows [j*R/2, (j+1)*R/2)
+    // followed by the same up rows (one 3-D copy), so one warp has both
+    // values of row i: y[b*ldy + i] = silu(gate_i) * up_i, i < n_ff.
     EPI_SWIGLU = 3,
 };
 
@@ -52,9 +52,7 @@ struct MatvecParams {
     int tpr;               // threads per row: 4 or 8
     int kc;                // super-blocks per pipeline stage
     int row_stride;        // shared-memory bytes per row of a stage
-    int stage_bytes;       // shared-memory footprint of one stage (a multiple of 128)
-    int tx_bytes;          // bytes the stage's copies deliver: rows_per_tile * row_stride
-    int half_off;          // EPI_SWIGLU: offset of the up half in a stage (a multiple of 128)
+    int stage_bytes;       // rows_per_tile * row_stride (a multiple of 128)
     int stages;
     int prefill;           // stages per warp issued before the programmatic wait (0 = the whole ring)
     int act_off, ring_off, bar_off, smem_bytes;
@@ -139,13 +137,14 @@ int launch_moe_route(const MoeParams& p, const LaunchOpts& o);
 int launch_moe_combine(const float* dout, const float* w, int B, int k, int n_embd, float* out, bool residual,
                        const LaunchOpts& o);
 int encode_q4k_map(CUtensorMap* map, const void* base, int64_t rows, int nb, int row_stride, int box_rows);
+int encode_q4k_pair_map(CUtensorMap* map, const void* gate, int64_t rows, int nb, int64_t dist, int row_stride,
+                        int box_rows);
 // Seeded normal fill (splitmix64 -> Box-Muller in double, the oracle's
 // generator): out[i] = mean + std * z(seed, first + i).
 int fill_normal(float* out, int64_t n, int64_t first, uint64_t seed, double mean, double stddev, cudaStream_t s);
 
 // Fill tiling fields of p for the given grid; returns 0 or a negative errno.
-// pairs: the launch uses EPI_SWIGLU (two half-tile copies per stage).
-int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int tpr, bool pairs = false);
+int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int tpr);
 int launch_matvec(const MatvecParams& p, int fold, int act_src, int epi, const LaunchOpts& o);
 
 int launch_q8k_quantize(const float* x, int64_t K, int B, uint8_t* out, int* status, cudaStream_t s);

@@ -248,6 +248,7 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
             uint8_t* dst = act + blk * ACT_BLOCK_BYTES;
             stage_codes<FOLD>(dst, qb.q, lane);
             stage_scalars(dst, qb.d, qb.bsum16, lane);
+            if (rd == 0 && u == 0) BH_TRACE_AT(7);
         }
     }
     top_up();  // (no-op after the first round's call)
@@ -323,13 +324,11 @@ __global__ void __launch_bounds__(dense_warps(NB) * 32, 1) q4k_matvec_kernel(con
         if (lane == 0) {
             const int x = i_c * p.kc * (Q4K_BYTES / 8);
             uint8_t* dst = ring + (size_t)i_s * p.stage_bytes;
-            mbar_arrive_expect_tx(&full[i_s], (uint32_t)p.tx_bytes);
+            mbar_arrive_expect_tx(&full[i_s], (uint32_t)p.stage_bytes);
             if (EPI == EPI_SWIGLU) {
-                // R/2 gate rows, then the same R/2 up rows at half_off (a
-                // tensor copy's shared-memory destination is 128-byte aligned)
+                // one 3-D copy: R/2 gate rows, then the same R/2 up rows
                 const int row = (int)((r_begin + (int64_t)(warp + i_j * W) * R) / 2);
-                tensor_g2s_2d(dst, &p.tmap[0], x, row, &full[i_s], pol);
-                tensor_g2s_2d(dst + p.half_off, &p.tmap[1], x, row, &full[i_s], pol);
+                tensor_g2s_3d(dst, &p.tmap[0], x, row, 0, &full[i_s], pol);
             } else {
                 int64_t local;
                 const int sg = seg_of(p, r_begin + (int64_t)(warp + i_j * W) * R, local);
@@ -391,8 +390,7 @@ __global__ void __launch_bounds__(dense_warps(NB) * 32, 1) q4k_matvec_kernel(con
             const int sbc = c * p.kc;
             const int kl = min(p.kc, p.nb - sbc);
             // rows past the end of the range read zero-filled stage bytes and are never stored
-            const uint8_t* rowp = ring + (size_t)c_s * p.stage_bytes + (size_t)rgrp * p.row_stride +
-                                  (EPI == EPI_SWIGLU && rgrp >= R / 2 ? p.half_off - (R / 2) * p.row_stride : 0);
+            const uint8_t* rowp = ring + (size_t)c_s * p.stage_bytes + (size_t)rgrp * p.row_stride;
             const uint8_t* actc = act + sbc * ACT_BLOCK_BYTES;
 BH_UNROLL(BH_KB_UNROLL)
             for (int kb = 0; kb < kl; ++kb) {
@@ -476,7 +474,7 @@ BH_UNROLL(BH_KB_UNROLL)
 // (a CTA's range is at most ceil(tiles / grid) tiles), so a matrix with few
 // rows per CTA gives its working warps deeper rings, which fill before the
 // programmatic wait.
-int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int tpr, bool pairs) {
+int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int tpr) {
     if (grid < 1 || (tpr != 4 && tpr != 8)) return BH_EINVAL;
     const int R = 32 / tpr;
     const int W = dense_warps(p.B);
@@ -493,10 +491,9 @@ int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int t
         const int padw = ((8 - (words % 32)) % 32 + 32) % 32;  // row stride == 8 words (mod 32 banks)
         const int stride = kc * Q4K_BYTES + 4 * padw;
         // (stride is 32 mod 128 bytes, so R * stride, R = 4 or 8, is a
-        // multiple of 128: every stage starts 128-byte aligned. A pair stage
-        // puts its up half at the next 128-byte boundary.)
-        const int half_off = pairs ? ((R / 2) * stride + 127) / 128 * 128 : 0;
-        const int stage = pairs ? (half_off + (R / 2) * stride + 127) / 128 * 128 : R * stride;
+        // multiple of 128: every stage starts 128-byte aligned, as a tensor
+        // copy's shared-memory destination must)
+        const int stage = R * stride;
         const int avail = smem_cap - ring_off - 512;  // static shared memory of the kernel
         int stages = avail > 0 ? avail / (wbusy * (stage + 8)) : 0;
         if (stages > 8) stages = 8;
@@ -504,8 +501,6 @@ int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int t
         p.kc = kc;
         p.row_stride = stride;
         p.stage_bytes = stage;
-        p.tx_bytes = R * stride;
-        p.half_off = half_off;
         p.stages = stages;
         p.rows_per_tile = R;
         p.tpr = tpr;
@@ -624,17 +619,37 @@ int encode_q4k_map(CUtensorMap* map, const void* base, int64_t rows, int nb, int
     return BH_OK;
 }
 
-// One tensor map per segment; the box is the stage slice of one tile (of
-// half a tile for gate/up pairs: two equal segments, N = 2 x rows each).
+// A 3-D tensor map over a gate matrix and the up matrix `dist` bytes after it
+// (both `rows` x nb*144 bytes): box = row_stride bytes x box_rows rows x 2.
+int encode_q4k_pair_map(CUtensorMap* map, const void* gate, int64_t rows, int nb, int64_t dist, int row_stride,
+                        int box_rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return BH_EIO;
+    const int64_t rowbytes = (int64_t)nb * Q4K_BYTES;
+    const cuuint64_t dims[3] = {(cuuint64_t)(rowbytes / 8), (cuuint64_t)(rows > 0 ? rows : 1), 2};
+    const cuuint64_t strides[2] = {(cuuint64_t)rowbytes, (cuuint64_t)dist};
+    const cuuint32_t box[3] = {(cuuint32_t)(row_stride / 8), (cuuint32_t)box_rows, 2};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(gate), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return BH_EINVAL;
+    return BH_OK;
+}
+
+// One tensor map per segment; the box is the stage slice of one tile. Gate/up
+// pairs (two segments of `half` rows each) use one 3-D map over both
+// matrices: x = 8-byte element of a row, y = row, z = matrix (stride: the
+// distance from the gate to the up matrix); a box of R/2 rows x 2 matrices
+// lands as the R/2 gate rows followed by the same R/2 up rows.
 static int encode_maps(MatvecParams& p, bool pair) {
     if (pair) {
         const int64_t half = p.seg_end[0];
+        const int64_t rowbytes = (int64_t)p.nb * Q4K_BYTES;
+        const int64_t dist = p.w[1] - p.w[0];
         if (2 * half != p.N || p.seg_end[1] != p.N || half % (p.rows_per_tile / 2)) return BH_EINVAL;
-        for (int sg = 0; sg < 2; ++sg) {
-            const int rc = encode_q4k_map(&p.tmap[sg], p.w[sg], half, p.nb, p.row_stride, p.rows_per_tile / 2);
-            if (rc != BH_OK) return rc;
-        }
-        return BH_OK;
+        if (dist < half * rowbytes || dist % 16) return BH_EINVAL;  // up after gate, no overlap
+        return encode_q4k_pair_map(&p.tmap[0], p.w[0], half, p.nb, dist, p.row_stride, p.rows_per_tile / 2);
     }
     if (p.seg_end[0] < p.N && (p.seg_end[0] % MV_ROWS || p.seg_end[1] % MV_ROWS)) return BH_EINVAL;
     int64_t prev = 0;
@@ -650,8 +665,7 @@ static int encode_maps(MatvecParams& p, bool pair) {
 int launch_matvec(const MatvecParams& pin, int fold, int act_src, int epi, const LaunchOpts& o) {
     MatvecParams p = pin;
     // a tensor copy's shared-memory destination must be 128-byte aligned
-    if (p.stage_bytes % 128 || (epi == EPI_SWIGLU && (p.partials || p.half_off % 128 || p.half_off == 0)))
-        return BH_EINVAL;
+    if (p.stage_bytes % 128 || (epi == EPI_SWIGLU && p.partials)) return BH_EINVAL;
     const int rc = encode_maps(p, epi == EPI_SWIGLU);
     if (rc != BH_OK) return rc;
     const int grid = o.grid;
