@@ -125,6 +125,29 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
     return p;
 }
 
+// Staged Q8_K activation block in shared memory (layout in q8k_device.cuh):
+// lane m's codes at act_lane_off(m), then d and the paired bsums.
+constexpr int ACT_D_OFF = 272;
+constexpr int ACT_S_OFF = 288;
+__host__ __device__ constexpr int act_lane_off(int m) { return 32 * m + (m >= 4 ? 16 : 0); }
+
+// Small tensors every step reads again (norm weights, the KV cache) are
+// loaded with an L2 evict-last hint, so the step's weight stream (loaded
+// evict-first) does not push them out of the L2 between steps.
+__device__ __forceinline__ uint64_t policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ float4 ldg_f4_keep(const float* ptr, uint64_t pol) {
+    float4 v;
+    asm volatile("ld.global.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(ptr), "l"(pol));
+    return v;
+}
+
 // Programmatic dependent launch (no-ops when the launch did not opt in).
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

@@ -76,7 +76,7 @@ constexpr int MV_THREADS = MV_WARPS * 32;
 constexpr int DENSE_MAX_WARPS = 16;
 __host__ __device__ constexpr int dense_warps(int B) { return B <= 2 ? 16 : 8; }
 constexpr int MV_ROWS = 8;                  // largest tile (rows of one warp stage); segment boundaries align to it
-constexpr int ACT_BLOCK_BYTES = 304;   // staged Q8_K block: 256 q8 + 16 (d) + 32 (S)
+constexpr int ACT_BLOCK_BYTES = 304;   // staged Q8_K block: 272 (q8, lane-padded) + 16 (d) + 16 (S)
 
 // Routed-expert FFN (the stock MoE block of the reference, gate|up -> SwiGLU
 // -> down -> weighted sum over the top-k slots), one token batch of B <= 8.

@@ -224,16 +224,17 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnPar
     // round's K / V cache rows (whatever the position: only those before pos
     // are used), the norm weights, the rotation frequencies (lane l: dims
     // 4l..4l+3, frequency index (4l mod 64) + j) and pos
+    const uint64_t keep = policy_evict_last();
     float4 kpre[U], vpre[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
         const int t = t_first + u;
-        kpre[u] = t < a.n_ctx ? reinterpret_cast<const float4*>(kbase + (int64_t)t * row_stride)[lane] : f4_zero();
-        vpre[u] = t < a.n_ctx ? reinterpret_cast<const float4*>(vbase + (int64_t)t * row_stride)[lane] : f4_zero();
+        kpre[u] = t < a.n_ctx ? ldg_f4_keep(kbase + (int64_t)t * row_stride + 4 * lane, keep) : f4_zero();
+        vpre[u] = t < a.n_ctx ? ldg_f4_keep(vbase + (int64_t)t * row_stride + 4 * lane, keep) : f4_zero();
     }
-    const float4 qn = reinterpret_cast<const float4*>(a.q_norm)[lane];
-    const float4 kn = reinterpret_cast<const float4*>(a.k_norm)[lane];
-    const float4 fr = reinterpret_cast<const float4*>(a.rope_inv_freq)[lane & 15];
+    const float4 qn = ldg_f4_keep(a.q_norm + 4 * lane, keep);
+    const float4 kn = ldg_f4_keep(a.k_norm + 4 * lane, keep);
+    const float4 fr = ldg_f4_keep(a.rope_inv_freq + 4 * (lane & 15), keep);
     const int pos = *a.pos;
     pdl_trigger();
     pdl_wait();
@@ -271,8 +272,8 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnPar
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int t = t0 + u;
-            kv[u] = t < pos ? reinterpret_cast<const float4*>(kbase + (int64_t)t * row_stride)[lane] : f4_zero();
-            vv[u] = t < pos ? reinterpret_cast<const float4*>(vbase + (int64_t)t * row_stride)[lane] : f4_zero();
+            kv[u] = t < pos ? ldg_f4_keep(kbase + (int64_t)t * row_stride + 4 * lane, keep) : f4_zero();
+            vv[u] = t < pos ? ldg_f4_keep(vbase + (int64_t)t * row_stride + 4 * lane, keep) : f4_zero();
         }
         attn_round<U>(kv, vv, t0, pos, q, k, v, scale, m, l, o);
     }

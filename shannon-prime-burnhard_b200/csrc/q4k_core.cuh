@@ -119,14 +119,14 @@ template <int FOLD, bool PART, int TPR>
 __device__ __forceinline__ void fold_block(const RowBlk<TPR>& r, const uint8_t* A, int t, int32_t* part_dst,
                                            float (&acc)[8 / TPR], float& accm) {
     constexpr int L = RowBlk<TPR>::L;
-    const float yd = *reinterpret_cast<const float*>(A + 256);
-    const int spk = reinterpret_cast<const int*>(A + 272)[t & 3];
+    const float yd = *reinterpret_cast<const float*>(A + ACT_D_OFF);
+    const int spk = reinterpret_cast<const int*>(A + ACT_S_OFF)[t & 3];
     int li[L];
     int sub[L][8];
 #pragma unroll
     for (int e = 0; e < L; ++e) {
-        const int4 a0 = *reinterpret_cast<const int4*>(A + 32 * (t * L + e));
-        const int4 a1 = *reinterpret_cast<const int4*>(A + 32 * (t * L + e) + 16);
+        const int4 a0 = *reinterpret_cast<const int4*>(A + act_lane_off(t * L + e));
+        const int4 a1 = *reinterpret_cast<const int4*>(A + act_lane_off(t * L + e) + 16);
         li[e] = lane_sum(r.lo[e], r.hi[e], r.sc03, r.sc47, a0, a1, sub[e], PART);
     }
     const int mp = __dp2a_lo(spk, (int)r.mnk, 0);

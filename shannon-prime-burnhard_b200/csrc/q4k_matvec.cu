@@ -71,14 +71,15 @@ template <int W>
 __device__ __forceinline__ void preload_gamma(const MatvecParams& p, float (&gp)[STAGE_UF][8],
                                               int warp, int lane) {
     constexpr int UF = STAGE_UF;
+    const uint64_t keep = policy_evict_last();
 #pragma unroll
     for (int u = 0; u < UF; ++u) {
         const int blk = warp + u * W;
         float4 c0 = make_float4(0.f, 0.f, 0.f, 0.f), c1 = c0;
         if (blk < p.B * p.nb) {
             const float* y = p.gamma + (blk % p.nb) * QK + 8 * lane;
-            c0 = *reinterpret_cast<const float4*>(y);
-            c1 = *reinterpret_cast<const float4*>(y + 4);
+            c0 = ldg_f4_keep(y, keep);
+            c1 = ldg_f4_keep(y + 4, keep);
         }
         gp[u][0] = c0.x; gp[u][1] = c0.y; gp[u][2] = c0.z; gp[u][3] = c0.w;
         gp[u][4] = c1.x; gp[u][5] = c1.y; gp[u][6] = c1.z; gp[u][7] = c1.w;
@@ -131,10 +132,10 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
                         for (int b = 0; b < 4; ++b) dst[staged_byte_offset<FOLD>(4 * wi + b)] = (uint8_t)(w >> (8 * b));
                     }
                 }
-                if (lane == 0) *reinterpret_cast<float*>(dst + 256) = dv[u];
+                if (lane == 0) *reinterpret_cast<float*>(dst + ACT_D_OFF) = dv[u];
                 if (lane < 8) {
                     const int s = (int)(int16_t)(bw[u] & 0xffffu) + (int)(int16_t)(bw[u] >> 16);
-                    reinterpret_cast<int16_t*>(dst + 272)[lane] = (int16_t)s;
+                    reinterpret_cast<int16_t*>(dst + ACT_S_OFF)[lane] = (int16_t)s;
                 }
             }
         }
@@ -230,11 +231,9 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
                 scale_u[u] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
             }
         }
-#pragma unroll
-        for (int u = 0; u < UF; ++u) {
+        auto quantize_block = [&](int u) {
             const int blk = blk0 + u * W;
-            if (blk >= nblk) break;  // warp-uniform
-            const int b = blk / p.nb;
+            const int b = (blk < nblk ? blk : 0) / p.nb;
             float x[8];
 #pragma unroll
             for (int t = 0; t < 8; ++t) {
@@ -245,11 +244,21 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
                 }
             }
             const Q8Block qb = q8k_quantize_warp(x, lane);
-            uint8_t* dst = act + blk * ACT_BLOCK_BYTES;
-            stage_codes<FOLD>(dst, qb.q, lane);
-            stage_scalars(dst, qb.d, qb.bsum16, lane);
-            if (rd == 0 && u == 0) BH_TRACE_AT(7);
+            if (blk < nblk) {  // warp-uniform
+                uint8_t* dst = act + blk * ACT_BLOCK_BYTES;
+                stage_codes<FOLD>(dst, qb.q, lane);
+                stage_scalars(dst, qb.d, qb.bsum16, lane);
+            }
+        };
+        if (nblk <= W) {
+            quantize_block(0);  // one block per warp (the decode step's K = 4096 launches)
+        } else {
+            // every u is worked, so the UF quantize chains can interleave;
+            // blocks past nblk are zeros and are not stored
+#pragma unroll
+            for (int u = 0; u < UF; ++u) quantize_block(u);
         }
+        if (rd == 0) BH_TRACE_AT(7);
     }
     top_up();  // (no-op after the first round's call)
 }

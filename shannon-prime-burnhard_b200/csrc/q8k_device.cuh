@@ -57,9 +57,13 @@ __device__ __forceinline__ Q8Block q8k_quantize_warp(const float (&v)[8], int la
 }
 
 // Staged activation block (ACT_BLOCK_BYTES = 304):
-//   bytes   0..255 : q8 codes as 64 words, lane-major: word [lane*8 + slot]
-//   bytes 256..259 : d (float)
-//   bytes 272..287 : S[t] = bsums[2t] + bsums[2t+1], t = 0..7, as int16;
+//   bytes   0..271 : q8 codes as 64 words, lane-major: lane m's 8 words (32
+//                    bytes) at act_lane_off(m) = 32 m, plus 16 for m >= 4, so
+//                    the 16-byte reads of the lanes a warp reads together fall
+//                    on distinct banks (without the gap lanes m and m + 4 sit
+//                    128 bytes apart, on the same banks)
+//   bytes 272..275 : d (float)
+//   bytes 288..303 : S[t] = bsums[2t] + bsums[2t+1], t = 0..7, as int16;
 //                    word k = (S[2k], S[2k+1]) feeds one dp2a with two 6-bit mins
 // Word slot layout per fold (lane = the 8-way split of a row's work):
 //   FOLD_X86 (lane m):     slot 2j   = codes 64j + 4m .. +3       (low-nibble half)
@@ -71,11 +75,11 @@ template <int FOLD>
 __device__ __forceinline__ int staged_byte_offset(int p) {
     if (FOLD == BH_FOLD_X86) {
         const int g = p >> 6, h = (p >> 5) & 1, m = (p & 31) >> 2;
-        return (m * 8 + 2 * g + h) * 4 + (p & 3);
+        return act_lane_off(m) + (2 * g + h) * 4 + (p & 3);
     } else {
         const int g = p >> 6, h = (p >> 5) & 1, r = p & 31;
         const int l = r & 7, c = r >> 3;
-        return (l * 8 + 2 * g + h) * 4 + c;
+        return act_lane_off(l) + (2 * g + h) * 4 + c;
     }
 }
 
@@ -101,8 +105,8 @@ __device__ __forceinline__ void stage_codes(uint8_t* blk, const int (&q)[8], int
 // sum over lanes 2g, 2g+1; S[t] = bsum16(lane 4t) + bsum16(lane 4t+2)).
 __device__ __forceinline__ void stage_scalars(uint8_t* blk, float d, int bsum16, int lane) {
     const int pair = bsum16 + __shfl_xor_sync(0xffffffffu, bsum16, 2);
-    if (lane == 0) *reinterpret_cast<float*>(blk + 256) = d;
-    if ((lane & 3) == 0) reinterpret_cast<int16_t*>(blk + 272)[lane >> 2] = (int16_t)pair;
+    if (lane == 0) *reinterpret_cast<float*>(blk + ACT_D_OFF) = d;
+    if ((lane & 3) == 0) reinterpret_cast<int16_t*>(blk + ACT_S_OFF)[lane >> 2] = (int16_t)pair;
 }
 
 }  // namespace bh
