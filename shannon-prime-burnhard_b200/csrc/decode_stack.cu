@@ -652,16 +652,17 @@ int bh_stack_create(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, bh_s
     if (!st) return BH_ENOMEM;
     st->ctx = ctx;
     // Launch plan of the layer matvecs, unless the caller tuned a per-SM
-    // budget on ctx: at most 168 KiB of shared memory per SM, 1152-byte row
+    // budget on ctx: at most 168 KiB of shared memory per SM, 1440-byte row
     // slices per stage (one 16-warp CTA per SM; the planner picks the threads
     // per row), and one ring stage per warp issued before the programmatic
     // wait, the rest right after the activation loads (measured on B200:
-    // 1.74 ms per token against 1.76 with the whole ring before the wait and
-    // 1.79-1.87 with 864- or 576-byte slices). The LM head keeps ctx's plan.
+    // 1.557 ms per token against 1.575 with 1152-byte slices, 1.567 with
+    // 1728, 1.79-1.87 with 864 or 576; the whole ring before the wait cost
+    // ~0.02 ms). The LM head keeps ctx's plan.
     st->plan = *ctx;
     if (ctx->sm_budget == 0) {
         st->plan.sm_budget = 168 * 1024;
-        st->plan.stage_bytes = 1152;
+        st->plan.stage_bytes = 1440;
         st->plan.prefill_stages = 1;
     }
     st->cfg = *cfg;
