@@ -246,7 +246,8 @@ int bh_stack_tensor(bh_stack *st, int layer, int which, void **ptr, int64_t *row
  * then three ggml_mul_mat_id + ggml_silu + ggml_mul + weighted sum) and the
  * BURN_MOE custom op that replaces its expert half (burn_moe_op.h:47-59,
  * burn_moe_op.cpp:202-372). At most 8 tokens per call, k <= 8 selected
- * experts per token, n_expert <= 256; n_embd and n_ff multiples of 256.
+ * experts per token, n_expert <= 256; n_embd and n_ff multiples of 256,
+ * n_embd <= 16384.
  * ------------------------------------------------------------------------ */
 
 /* Router of n_tok tokens from logits [n_tok][n_expert]: probabilities by

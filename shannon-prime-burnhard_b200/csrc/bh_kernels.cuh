@@ -84,6 +84,7 @@ constexpr int MOE_MAX_TOK = 8;
 constexpr int MOE_MAX_K = 8;
 constexpr int MOE_MAX_PAIRS = MOE_MAX_TOK * MOE_MAX_K;
 constexpr int MOE_MAX_EXPERT = 256;
+constexpr int MOE_MAX_EMBD_BLOCKS = 64;  // n_embd <= 16384
 
 struct MoeParams {
     CUtensorMap tmap[3];   // gate bank, up bank, down bank (2-D, 8-byte elements)

@@ -30,7 +30,8 @@ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_
 
 bool moe_shape_ok(int n_tok, int n_expert, int n_embd, int n_ff, int k) {
     return n_tok >= 1 && n_tok <= bh::MOE_MAX_TOK && k >= 1 && k <= bh::MOE_MAX_K && n_expert >= k &&
-           n_expert <= bh::MOE_MAX_EXPERT && n_embd >= bh::QK && n_embd % bh::QK == 0 && n_ff >= bh::QK &&
+           n_expert <= bh::MOE_MAX_EXPERT && n_embd >= bh::QK && n_embd % bh::QK == 0 &&
+           n_embd <= bh::QK * bh::MOE_MAX_EMBD_BLOCKS && n_ff >= bh::QK &&
            n_ff % bh::QK == 0 && (int64_t)n_expert * n_ff < ((int64_t)1 << 31) &&
            (int64_t)n_expert * n_embd < ((int64_t)1 << 31);
 }

@@ -253,44 +253,105 @@ __device__ __forceinline__ void moe_route(const MoeParams& p, const float* logit
 // scale = 1 / sqrt(mean + eps), y = (x * scale) * gamma), quantized to Q8_K.
 template <int FOLD>
 __device__ void stage_tokens(const MoeParams& p, const float* gamma, uint8_t* act, float* s_scale) {
+    __shared__ double s_bss[MOE_MAX_TOK * MOE_MAX_EMBD_BLOCKS];  // per-block sums of squares
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int K = p.n_embd, nb = K / QK;
-    if (gamma) {
-        for (int b = warp; b < p.B; b += MV_WARPS) {
-            const float* h = p.h + (int64_t)b * K;
+    const int nblk = p.B * nb;
+    // Every warp takes blocks warp, warp + MV_WARPS, ... and issues all the
+    // loads of a round (h, gamma) before using any: the activations were just
+    // written by another kernel, so each round trip to the L2 is paid once
+    // per round. With RMSNorm the per-block sums of squares (lane sums and a
+    // butterfly, in double) are combined per token in block order; when one
+    // round covers every block the values wait in registers for the scale.
+    constexpr int UF = 4;
+    const bool one_round = nblk <= MV_WARPS * UF;
+    const int rounds = (nblk + MV_WARPS * UF - 1) / (MV_WARPS * UF);  // the same in every warp
+    const uint64_t keep = policy_evict_last();
+    auto scales = [&]() {
+        __syncthreads();
+        if (threadIdx.x < p.B) {
             double ss = 0.0;
-            for (int i = lane; i < K; i += 32) {
-                const float v = __ldcg(h + i);
-                ss = __dadd_rn(ss, (double)__fmul_rn(v, v));
-            }
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
-            if (lane == 0) {
-                const float mean = __double2float_rn(__ddiv_rn(ss, (double)K));
-                s_scale[b] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
-            }
+            for (int i = 0; i < nb; ++i) ss = __dadd_rn(ss, s_bss[threadIdx.x * nb + i]);
+            const float mean = __double2float_rn(__ddiv_rn(ss, (double)K));
+            s_scale[threadIdx.x] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
         }
         __syncthreads();
+    };
+    auto put = [&](int blk, const float (&x)[8]) {
+        const Q8Block qb = q8k_quantize_warp(x, lane);
+        uint8_t* dst = act + blk * ACT_BLOCK_BYTES;
+        stage_codes<FOLD>(dst, qb.q, lane);
+        stage_scalars(dst, qb.d, qb.bsum16, lane);
+    };
+    for (int rd = 0; rd < rounds; ++rd) {
+        const int blk0 = warp + rd * MV_WARPS * UF;
+        float v[UF][8], g[UF][8];
+#pragma unroll
+        for (int u = 0; u < UF; ++u) {
+            const int blk = blk0 + u * MV_WARPS;
+            const int b = blk / nb, i = blk - b * nb;
+            const int e0 = i * QK + 8 * lane;
+            float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0, g0 = a0, g1 = a0;
+            if (blk < nblk) {
+                const float4* x = reinterpret_cast<const float4*>(p.h + (int64_t)b * K + e0);
+                a0 = __ldcg(x);
+                a1 = __ldcg(x + 1);
+                if (gamma) {
+                    g0 = ldg_f4_keep(gamma + e0, keep);
+                    g1 = ldg_f4_keep(gamma + e0 + 4, keep);
+                }
+            }
+            v[u][0] = a0.x; v[u][1] = a0.y; v[u][2] = a0.z; v[u][3] = a0.w;
+            v[u][4] = a1.x; v[u][5] = a1.y; v[u][6] = a1.z; v[u][7] = a1.w;
+            g[u][0] = g0.x; g[u][1] = g0.y; g[u][2] = g0.z; g[u][3] = g0.w;
+            g[u][4] = g1.x; g[u][5] = g1.y; g[u][6] = g1.z; g[u][7] = g1.w;
+        }
+        if (!gamma) {
+#pragma unroll
+            for (int u = 0; u < UF; ++u)
+                if (blk0 + u * MV_WARPS < nblk) put(blk0 + u * MV_WARPS, v[u]);
+            continue;
+        }
+#pragma unroll
+        for (int u = 0; u < UF; ++u) {
+            double ss = 0.0;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) ss = __dadd_rn(ss, (double)__fmul_rn(v[u][t], v[u][t]));
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+            if (lane == 0 && blk0 + u * MV_WARPS < nblk) s_bss[blk0 + u * MV_WARPS] = ss;
+        }
+        if (one_round) {
+            scales();
+#pragma unroll
+            for (int u = 0; u < UF; ++u) {
+                const int blk = blk0 + u * MV_WARPS;
+                if (blk >= nblk) continue;  // warp-uniform
+                const float sc = s_scale[blk / nb];
+                float x[8];
+#pragma unroll
+                for (int t = 0; t < 8; ++t) x[t] = __fmul_rn(__fmul_rn(v[u][t], sc), g[u][t]);
+                put(blk, x);
+            }
+        }
     }
-    const int nblk = p.B * nb;
+    if (!gamma || one_round) return;
+    // several rounds (many tokens or a wide embedding): the scales from the
+    // block sums, then the blocks loaded again and quantized
+    scales();
     for (int blk = warp; blk < nblk; blk += MV_WARPS) {
         const int b = blk / nb, i = blk - b * nb;
         const int e0 = i * QK + 8 * lane;
         const float4* x = reinterpret_cast<const float4*>(p.h + (int64_t)b * K + e0);
         const float4 a0 = __ldcg(x), a1 = __ldcg(x + 1);
-        float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        if (gamma) {
-            const float4 g0 = *reinterpret_cast<const float4*>(gamma + e0);
-            const float4 g1 = *reinterpret_cast<const float4*>(gamma + e0 + 4);
-            const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-            const float sc = s_scale[b];
+        const float4 g0 = ldg_f4_keep(gamma + e0, keep), g1 = ldg_f4_keep(gamma + e0 + 4, keep);
+        const float hv[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const float sc = s_scale[b];
+        float xv[8];
 #pragma unroll
-            for (int t = 0; t < 8; ++t) v[t] = __fmul_rn(__fmul_rn(v[t], sc), g[t]);
-        }
-        const Q8Block qb = q8k_quantize_warp(v, lane);
-        uint8_t* dst = act + blk * ACT_BLOCK_BYTES;
-        stage_codes<FOLD>(dst, qb.q, lane);
-        stage_scalars(dst, qb.d, qb.bsum16, lane);
+        for (int t = 0; t < 8; ++t) xv[t] = __fmul_rn(__fmul_rn(hv[t], sc), gv[t]);
+        put(blk, xv);
     }
 }
 
@@ -310,25 +371,45 @@ __device__ void stage_pairs(const MoeParams& p, const MoeTable& tb, int u_lo, in
     __syncthreads();
     const int npairs = s_qbase[u_hi - u_lo + 1];
     const int nblk = npairs * nb;
-    for (int blk = warp; blk < nblk; blk += MV_WARPS) {
-        const int q = blk / nb, i = blk - q * nb;
-        int u = u_lo;
-        while (u < u_hi && s_qbase[u + 1 - u_lo] <= q) ++u;
-        const int j = q - s_qbase[u - u_lo];
-        const int pair = tb.col_tok[u][j] * p.k + tb.col_slot[u][j];
-        const int e0 = i * QK + 8 * lane;
-        const float4* g = reinterpret_cast<const float4*>(p.gu + (int64_t)pair * 2 * p.n_ff + e0);
-        const float4* up = reinterpret_cast<const float4*>(p.gu + (int64_t)pair * 2 * p.n_ff + p.n_ff + e0);
-        const float4 g0 = __ldcg(g), g1 = __ldcg(g + 1), u0 = __ldcg(up), u1 = __ldcg(up + 1);
-        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-        const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-        float v[8];
+    // UF blocks per warp per round, all their loads issued before any use
+    constexpr int UF = 4;
+    for (int blk0 = warp; blk0 < nblk; blk0 += MV_WARPS * UF) {
+        float4 ld[UF][4];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) v[t] = __fmul_rn(silu_cw(gv[t]), uv[t]);
-        const Q8Block qb = q8k_quantize_warp(v, lane);
-        uint8_t* dst = act + blk * ACT_BLOCK_BYTES;
-        stage_codes<FOLD>(dst, qb.q, lane);
-        stage_scalars(dst, qb.d, qb.bsum16, lane);
+        for (int r = 0; r < UF; ++r) {
+            const int blk = blk0 + r * MV_WARPS;
+            ld[r][0] = ld[r][1] = ld[r][2] = ld[r][3] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (blk < nblk) {
+                const int q = blk / nb, i = blk - q * nb;
+                int u = u_lo;
+                while (u < u_hi && s_qbase[u + 1 - u_lo] <= q) ++u;
+                const int j = q - s_qbase[u - u_lo];
+                const int pair = tb.col_tok[u][j] * p.k + tb.col_slot[u][j];
+                const int e0 = i * QK + 8 * lane;
+                const float4* g = reinterpret_cast<const float4*>(p.gu + (int64_t)pair * 2 * p.n_ff + e0);
+                const float4* up = reinterpret_cast<const float4*>(p.gu + (int64_t)pair * 2 * p.n_ff + p.n_ff + e0);
+                ld[r][0] = __ldcg(g);
+                ld[r][1] = __ldcg(g + 1);
+                ld[r][2] = __ldcg(up);
+                ld[r][3] = __ldcg(up + 1);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < UF; ++r) {
+            const int blk = blk0 + r * MV_WARPS;
+            if (blk >= nblk) break;  // warp-uniform
+            const float gv[8] = {ld[r][0].x, ld[r][0].y, ld[r][0].z, ld[r][0].w,
+                                 ld[r][1].x, ld[r][1].y, ld[r][1].z, ld[r][1].w};
+            const float uv[8] = {ld[r][2].x, ld[r][2].y, ld[r][2].z, ld[r][2].w,
+                                 ld[r][3].x, ld[r][3].y, ld[r][3].z, ld[r][3].w};
+            float v[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) v[t] = __fmul_rn(silu_cw(gv[t]), uv[t]);
+            const Q8Block qb = q8k_quantize_warp(v, lane);
+            uint8_t* dst = act + blk * ACT_BLOCK_BYTES;
+            stage_codes<FOLD>(dst, qb.q, lane);
+            stage_scalars(dst, qb.d, qb.bsum16, lane);
+        }
     }
 }
 
