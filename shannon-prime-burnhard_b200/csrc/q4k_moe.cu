@@ -136,41 +136,30 @@ __device__ __forceinline__ void moe_route(const MoeParams& p, const float* logit
         }
         __syncthreads();
         MOE_TRACE_R(1);
-        // rank of every (token, expert) by (p descending, index ascending);
-        // tpi threads share an item, each scanning every tpi-th group of 4
-        const int items = B * E;
-        int tpi = 1;
-        while (tpi < 32 && items * tpi * 2 <= MV_THREADS) tpi <<= 1;
-        const int per_pass = MV_THREADS / tpi;
-        for (int base = 0; base < items; base += per_pass) {
-            const int it = base + tid / tpi, sub = tid % tpi;
-            const bool valid = it < items;
-            const int b = valid ? it / E : 0, i = valid ? it - b * E : 0;
-            const float* pr = rs.p[b];
-            const float v = pr[i];
-            int rank = 0;
-            if (valid) {
-                if ((E & 3) == 0) {
-                    for (int c = sub; c < E / 4; c += tpi) {
-                        const float4 o = reinterpret_cast<const float4*>(pr)[c];
-                        const int j = 4 * c;
-                        rank += (o.x > v) | ((o.x == v) & (j < i));
-                        rank += (o.y > v) | ((o.y == v) & (j + 1 < i));
-                        rank += (o.z > v) | ((o.z == v) & (j + 2 < i));
-                        rank += (o.w > v) | ((o.w == v) & (j + 3 < i));
-                    }
-
-                } else {
-                    for (int j = sub; j < E; j += tpi) {
-                        const float o = pr[j];
-                        rank += (o > v) | ((o == v) & (j < i));
-                    }
+        // top-k of every token: warp b picks its token's k largest
+        // probabilities one at a time by a warp-wide argmax (value
+        // descending, lower index first on ties) and removes the winner
+        if (warp < B) {
+            constexpr int PER = MOE_MAX_EXPERT / 32;  // values per lane: index lane + 32 c
+            const float* pr = rs.p[warp];
+            float pv[PER];
+#pragma unroll
+            for (int c = 0; c < PER; ++c) pv[c] = lane + 32 * c < E ? pr[lane + 32 * c] : -1.f;  // p >= 0
+            for (int s = 0; s < k; ++s) {
+                // key = float bits + 1 (order-preserving for p >= 0), 0 once taken
+                uint32_t bkey = 0u;
+                int bi = 0x7fffffff;
+#pragma unroll
+                for (int c = 0; c < PER; ++c) {
+                    const uint32_t key = pv[c] >= 0.f ? __float_as_uint(pv[c]) + 1u : 0u;
+                    if (key > bkey) { bkey = key; bi = lane + 32 * c; }  // increasing index: ties keep the lower
                 }
-            }
-            for (int off = 1; off < tpi; off <<= 1) rank += __shfl_xor_sync(0xffffffffu, rank, off);
-            if (valid && sub == 0 && rank < k) {
-                const int slot = (k > 1 && rank < 2) ? 1 - rank : rank;  // top_k swaps slots 0 and 1
-                tb.ids[b][slot] = i;
+                const uint32_t mkey = __reduce_max_sync(0xffffffffu, bkey);
+                bi = (int)__reduce_min_sync(0xffffffffu, bkey == mkey ? (uint32_t)bi : 0xffffffffu);
+#pragma unroll
+                for (int c = 0; c < PER; ++c)
+                    if (lane + 32 * c == bi) pv[c] = -1.f;
+                if (lane == 0) tb.ids[warp][(k > 1 && s < 2) ? 1 - s : s] = bi;  // top_k swaps slots 0 and 1
             }
         }
         MOE_TRACE_R(5);
@@ -582,11 +571,15 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_moe_kernel(const __grid_con
             }
             if (++i_s == p.stages) i_s = 0;
         };
-        const int prefill = min(p.stages, total);
-        for (int q = 0; q < prefill; ++q) issue_next();
+        // two stages per warp now, the rest of the ring once the token
+        // activations are staged (their loads then do not queue behind a full
+        // ring of weight copies)
+        const int ring_fill = min(p.stages, total);
+        for (int q = 0; q < min(2, ring_fill); ++q) issue_next();
         MOE_TRACE_AT(2);
 
         stage_tokens<FOLD>(p, p.gamma ? p.gamma + l * p.gamma_ls : nullptr, act, s_scale);
+        while (issued < ring_fill) issue_next();
         __syncthreads();
         MOE_TRACE_AT(3);
 
