@@ -115,7 +115,7 @@ struct MoeParams {
     // other experts are set to -0.0, so summing the dout of all ranks
     // reproduces every value exactly) and out is not touched
     int e_lo, e_hi, combine;
-    unsigned int* gbar;    // grid barrier words {count, generation}, zero before first use
+    unsigned int* gbar;    // grid barrier word (arrivals, generation << 16), zero before first use
     int* status;
     int64_t* trace;        // timeline probe (builds with BH_TRACE only; else unused)
     // tiling, chosen on the host: both phases share one ring of `stages`

@@ -404,27 +404,27 @@ __device__ void stage_pairs(const MoeParams& p, const MoeTable& tb, int u_lo, in
 
 // Grid-wide barrier of a cooperative launch (every CTA resident). Writes of
 // the CTA before the barrier are visible to every CTA after it. Self-resetting:
-// the last arrival zeroes the count, then advances the generation the others
-// wait on. The wait is bounded; false after a timeout (status recorded).
+// the last arrival zeroes the count and advances the generation the others
+// wait on, in one atomic on the same word. The wait is bounded; false after a
+// timeout (status recorded).
 __device__ bool grid_barrier(unsigned int* gbar, int* status) {
     __shared__ int s_ok;
     __syncthreads();
     if (threadIdx.x == 0) {
-        unsigned int gen;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(gen) : "l"(gbar + 1) : "memory");
+        // one word: arrivals in the low 16 bits, the generation above them
         __threadfence();
-        const unsigned int arrived = atomicAdd(gbar, 1u);
+        const unsigned int old = atomicAdd(gbar, 1u);
+        const unsigned int gen = old >> 16;
         int ok = 1;
-        if (arrived == gridDim.x - 1) {
-            atomicExch(gbar, 0u);
+        if ((old & 0xffffu) == gridDim.x - 1) {
+            atomicAdd(gbar, (1u << 16) - gridDim.x);  // count back to zero, next generation
             __threadfence();
-            atomicAdd(gbar + 1, 1u);
         } else {
             const long long t0 = clock64();
             for (;;) {
                 unsigned int g;
-                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(g) : "l"(gbar + 1) : "memory");
-                if (g != gen) break;
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(g) : "l"(gbar) : "memory");
+                if ((g >> 16) != gen) break;
                 if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
                     ok = 0;
                     set_status(status, ST_TIMEOUT);
