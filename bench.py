@@ -152,6 +152,7 @@ def bench_lmhead_tp(bh, ctx, world: int, rank: int, reps: int) -> dict:
     rows = hi - lo
     w_local = ctx.q4k_quantize(torch.randn((rows, k), generator=g, device="cuda") * 0.02)
     head = sharding.TPLMHead(ctx, n, k, rank, world, w_local)
+    head.enable_peer_exchange()
     out = {"workload": "LM head 151936 x 4096 (config 5), rows split over the GPUs", "rows_per_gpu": rows}
     wbytes = n * (k // 256) * 144
     for b in (1, 4):
@@ -160,6 +161,11 @@ def bench_lmhead_tp(bh, ctx, world: int, rank: int, reps: int) -> dict:
             barrier(world)
             ms = max_over_ranks(time_events(lambda: head.forward(x, gather_logits=gl), reps), world)
             out[f"b{b}_{mode}"] = {"ms": round(ms, 4), "weight_GBps_all_gpus": round(wbytes / (ms / 1e3) / 1e9, 1)}
+        # the pick exchanged through peer memory by the reducing kernel (no collective call)
+        barrier(world)
+        ms = max_over_ranks(time_events(lambda: head.forward_peer(x), reps), world)
+        out[f"b{b}_peer_exchange"] = {"ms": round(ms, 4), "weight_GBps_all_gpus": round(wbytes / (ms / 1e3) / 1e9, 1)}
+    head.close_peer_exchange()
     del w_local, head
     torch.cuda.empty_cache()
     return out

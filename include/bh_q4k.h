@@ -156,6 +156,32 @@ int bh_q4k_lmhead_argmax(bh_ctx *ctx, const void *W_q4k, int64_t N, int64_t K, c
 int bh_q4k_lmhead_argmax_noalloc(const void *W_q4k, int64_t N, int64_t K, const float *x, int B,
                                  float *logits_opt, int32_t *tok_out, float *max_opt, int fold, void *stream);
 
+/* Row-split (tensor-parallel) LM head over the GPUs of one node, one process
+ * per GPU, with the greedy pick exchanged through peer memory instead of a
+ * collective library call (the reference's LM head and argmax,
+ * forward.cpp:3413 and engine.cpp:36-43, split by rows). Each rank owns a
+ * mailbox (bh_xchg_mailbox_alloc, zeroed, XCHG bytes) and maps the peers'
+ * mailboxes into its process with CUDA IPC (bh_xchg_ipc_handle on the owner,
+ * the 64-byte handle passed by the caller, bh_xchg_ipc_open on the others).
+ * bh_q4k_lmhead_argmax_tp computes this rank's rows [row_offset, row_offset +
+ * n_local) and, in the kernel that reduces them, stores its (max, first index)
+ * into every rank's mailbox, then waits (bounded, about a second) for all
+ * ranks' pairs in its own mailbox and merges them in rank order: tok_out is
+ * the global token on every rank, identical to one GPU over all rows.
+ * mailboxes[q] is rank q's mailbox as seen from this process (own at [rank]);
+ * epoch is the call's number, 1, 2, 3, ..., the same on every rank. A rank
+ * that does not arrive makes the others return BH_ETIMEDOUT (tok_out = -1)
+ * after the wait; calls of one group must not overlap. */
+size_t bh_xchg_mailbox_bytes(void);
+int bh_xchg_mailbox_alloc(bh_ctx *ctx, void **mailbox);
+int bh_xchg_mailbox_free(bh_ctx *ctx, void *mailbox);
+int bh_xchg_ipc_handle(bh_ctx *ctx, void *mailbox, void *handle_out /* 64 bytes */);
+int bh_xchg_ipc_open(bh_ctx *ctx, const void *handle, void **peer_mailbox);
+int bh_xchg_ipc_close(bh_ctx *ctx, void *peer_mailbox);
+int bh_q4k_lmhead_argmax_tp(bh_ctx *ctx, const void *W_local, int64_t n_local, int64_t K, const float *x, int B,
+                            int64_t row_offset, int rank, int world, void *const *mailboxes, uint32_t epoch,
+                            int32_t *tok_out, float *max_opt, int fold, void *stream);
+
 /* ------------------------------------------------------------------------
  * Decode block stack: the caller of the matvec in the reference engine's
  * per-token step (desktop/engine/src/forward.cpp:2663-2854 build_block_decode,

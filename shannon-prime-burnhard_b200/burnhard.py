@@ -98,6 +98,14 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.bh_q4k_mul_mat_host.argtypes = [_vp, _vp, _i64, _i64, _vp, C.c_int, _vp, C.c_int]
     L.bh_q4k_lmhead_argmax.argtypes = [_vp, _vp, _i64, _i64, _vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp]
     L.bh_q4k_lmhead_argmax_noalloc.argtypes = [_vp, _i64, _i64, _vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp]
+    L.bh_xchg_mailbox_bytes.restype = C.c_size_t
+    L.bh_xchg_mailbox_alloc.argtypes = [_vp, C.POINTER(_vp)]
+    L.bh_xchg_mailbox_free.argtypes = [_vp, _vp]
+    L.bh_xchg_ipc_handle.argtypes = [_vp, _vp, _vp]
+    L.bh_xchg_ipc_open.argtypes = [_vp, _vp, C.POINTER(_vp)]
+    L.bh_xchg_ipc_close.argtypes = [_vp, _vp]
+    L.bh_q4k_lmhead_argmax_tp.argtypes = [_vp, _vp, _i64, _i64, _vp, C.c_int, _i64, C.c_int, C.c_int, _vp,
+                                          C.c_uint32, _vp, _vp, C.c_int, _vp]
     L.bh_stack_default_config.argtypes = [C.POINTER(StackConfig)]
     L.bh_stack_default_config.restype = None
     L.bh_stack_create.argtypes = [_vp, C.POINTER(StackConfig), C.c_uint64, C.POINTER(_vp)]
@@ -342,6 +350,58 @@ def lmhead_argmax(ctx: Context, w, n: int, k: int, x, logits=None, fold: int = F
     mx = torch.empty(b, dtype=torch.float32, device=x.device)
     _check(lib.bh_q4k_lmhead_argmax(ctx.h, _dp(w), n, k, _dp(x), b, _dp(logits), _dp(tok), _dp(mx), fold,
                                     _stream(stream)), "bh_q4k_lmhead_argmax")
+    return tok, mx
+
+
+class PeerMailbox:
+    """This rank's mailbox for the peer-memory exchange of the row-split LM
+    head (bh_xchg_*): handle() gives the 64-byte CUDA IPC handle to share with
+    the other ranks, open(handle) maps a peer's mailbox into this process."""
+
+    def __init__(self, ctx: Context):
+        self.ctx = ctx
+        p = _vp()
+        _check(lib.bh_xchg_mailbox_alloc(ctx.h, C.byref(p)), "bh_xchg_mailbox_alloc")
+        self.ptr = p.value
+        self.opened: list[int] = []
+
+    def handle(self) -> bytes:
+        buf = C.create_string_buffer(64)
+        _check(lib.bh_xchg_ipc_handle(self.ctx.h, self.ptr, buf), "bh_xchg_ipc_handle")
+        return buf.raw
+
+    def open(self, handle: bytes) -> int:
+        buf = C.create_string_buffer(bytes(handle), 64)
+        p = _vp()
+        _check(lib.bh_xchg_ipc_open(self.ctx.h, buf, C.byref(p)), "bh_xchg_ipc_open")
+        self.opened.append(p.value)
+        return p.value
+
+    def close(self) -> None:
+        for q in self.opened:
+            lib.bh_xchg_ipc_close(self.ctx.h, q)
+        self.opened = []
+        if self.ptr:
+            lib.bh_xchg_mailbox_free(self.ctx.h, self.ptr)
+            self.ptr = None
+
+
+def lmhead_argmax_tp(ctx: Context, w_local, n_local: int, k: int, x, row_offset: int, rank: int, mailboxes,
+                     epoch: int, fold: int = FOLD_X86, stream=None):
+    """Global greedy pick of a row-split LM head (bh_q4k_lmhead_argmax_tp):
+    mailboxes = every rank's mailbox pointer as seen from this process (own
+    at [rank]); epoch = the call's number (1, 2, ...), the same on every
+    rank. Returns (tok [B] int32, max [B] fp32) on the device; a timed-out
+    exchange raises BHError(BH_ETIMEDOUT) once the stream is synchronized."""
+    import torch
+
+    b = x.shape[0]
+    tok = torch.empty(b, dtype=torch.int32, device=x.device)
+    mx = torch.empty(b, dtype=torch.float32, device=x.device)
+    arr = (_vp * len(mailboxes))(*mailboxes)
+    _check(lib.bh_q4k_lmhead_argmax_tp(ctx.h, _dp(w_local), n_local, k, _dp(x), b, row_offset, rank,
+                                       len(mailboxes), arr, epoch, _dp(tok), _dp(mx), fold, _stream(stream)),
+           "bh_q4k_lmhead_argmax_tp")
     return tok, mx
 
 

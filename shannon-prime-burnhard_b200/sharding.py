@@ -118,6 +118,38 @@ class TPLMHead:
         best_i, _ = merge_argmax(vals, idxs)
         return best_i, None
 
+    def enable_peer_exchange(self) -> None:
+        """Map every rank's exchange mailbox into this process (CUDA IPC; the
+        64-byte handles travel through the process group once). Afterwards
+        forward_peer() exchanges the greedy pick through peer memory."""
+        self.mbox = self.bh.PeerMailbox(self.ctx)
+        self.epoch = 0
+        if self.world == 1:
+            self.boxes = [self.mbox.ptr]
+            return
+        handles = [None] * self.world
+        dist.all_gather_object(handles, self.mbox.handle(), group=self.group)
+        self.boxes = [self.mbox.ptr if r == self.rank else self.mbox.open(handles[r]) for r in range(self.world)]
+        dist.barrier(group=self.group)  # every rank's mailbox is mapped before the first exchange
+
+    def forward_peer(self, x):
+        """x [B, K] -> global tokens [B] (int32, on the device), the same on
+        every rank: this rank's rows, then the (max, first index) pairs
+        exchanged through the mailboxes by the reducing kernel itself (no
+        collective call). Every rank calls it the same number of times."""
+        self.epoch += 1
+        n_r = self.hi - self.lo
+        tok, _ = self.bh.lmhead_argmax_tp(self.ctx, self.w, n_r, self.k, x, self.lo, self.rank, self.boxes,
+                                          self.epoch)
+        return tok
+
+    def close_peer_exchange(self) -> None:
+        if getattr(self, "mbox", None) is not None:
+            if self.world > 1:
+                dist.barrier(group=self.group)  # no rank still writes into a mailbox being unmapped
+            self.mbox.close()
+            self.mbox = None
+
 
 class EPMoE:
     """Expert-parallel routed-expert FFN: this rank holds the banks of experts

@@ -30,16 +30,22 @@ def main() -> int:
     w = ctx.q4k_quantize(torch.randn((N, K), generator=g, device="cuda") * 0.02)
     lo, hi = sharding.even_shards(N, world)[rank]
     head = sharding.TPLMHead(ctx, N, K, rank, world, sharding.TPLMHead.slice_rows(w, N, K, lo, hi))
-    for B in (1, 4):
+    head.enable_peer_exchange()
+    for B in (1, 4, 1, 8):
         x = torch.randn((B, K), generator=g, device="cuda")
         full = torch.empty((B, N), device="cuda")
         tok1, _ = bh.lmhead_argmax(ctx, w, N, K, x, logits=full)
         tok_g, logits_g = head.forward(x, gather_logits=True)
         tok_c, _ = head.forward(x, gather_logits=False)
+        tok_p = head.forward_peer(x)
+        torch.cuda.synchronize()
         if not torch.equal(logits_g.view(torch.int32), full.view(torch.int32)):
             fails.append(f"lmhead B={B}: gathered logits differ")
         if not (torch.equal(tok_g, tok1.to(torch.int64)) and torch.equal(tok_c, tok1.to(torch.int64))):
             fails.append(f"lmhead B={B}: tokens {tok_g.tolist()} {tok_c.tolist()} vs {tok1.tolist()}")
+        if not torch.equal(tok_p, tok1):
+            fails.append(f"lmhead B={B}: peer-exchange tokens {tok_p.tolist()} vs {tok1.tolist()}")
+    head.close_peer_exchange()
     del w, head
     # ---- expert-parallel MoE block
     E, D, F, k = 128, 2048, 768, 8

@@ -71,3 +71,51 @@ def test_tie_across_ctas(ctx, bh, oracle):
     tok, _ = bh.lmhead_argmax(ctx, dev(wq2), n, k, dev(x))
     y2 = oracle.matvec(wq2, n, k, oracle.quantize_q8k(x), 1, om.FOLD_X86)[0]
     assert int(host(tok)[0]) == first_argmax(y2) == min(top, 5, (top + 7000) % n, (top + 13000) % n)
+
+
+def test_peer_exchange_one_rank_matches_lmhead(ctx, bh, oracle):
+    """The peer-exchange LM head with a single rank (its own mailbox): the
+    same tokens and maxima as bh_q4k_lmhead_argmax, over consecutive epochs."""
+    import torch
+
+    n, k = 6000, 1024
+    g = torch.Generator(device="cuda").manual_seed(3)
+    w = ctx.q4k_quantize(torch.randn((n, k), generator=g, device="cuda") * 0.02)
+    box = bh.PeerMailbox(ctx)
+    try:
+        for epoch, b in enumerate((1, 3, 8, 1), start=1):
+            x = torch.randn((b, k), generator=g, device="cuda")
+            want_t, want_m = bh.lmhead_argmax(ctx, w, n, k, x)
+            got_t, got_m = bh.lmhead_argmax_tp(ctx, w, n, k, x, 0, 0, [box.ptr], epoch)
+            torch.cuda.synchronize()
+            assert torch.equal(got_t, want_t)
+            assert torch.equal(got_m.view(torch.int32), want_m.view(torch.int32))
+        assert ctx.status() == 0
+    finally:
+        box.close()
+
+
+def test_peer_exchange_times_out_when_a_rank_never_arrives(ctx, bh):
+    """Failure detection without a fault: a two-rank exchange whose second
+    mailbox nobody writes. The kernel's bounded wait (about a second) runs
+    out, the token is -1 and the device status reports BH_ETIMEDOUT; the
+    context stays usable."""
+    import torch
+
+    n, k = 512, 256
+    w = ctx.q4k_quantize(torch.randn((n, k), device="cuda") * 0.02)
+    own, silent = bh.PeerMailbox(ctx), bh.PeerMailbox(ctx)
+    try:
+        x = torch.randn((1, k), device="cuda")
+        # rank 0 of two: rank 1's pair never arrives in rank 0's mailbox
+        tok, _ = bh.lmhead_argmax_tp(ctx, w, n // 2, k, x, 0, 0, [own.ptr, silent.ptr], 1)
+        torch.cuda.synchronize()
+        assert int(tok[0]) == -1
+        assert ctx.status() == bh.BH_ETIMEDOUT
+        assert ctx.status() == 0  # cleared by the read above
+        t2, _ = bh.lmhead_argmax(ctx, w, n, k, x)  # the context still works
+        torch.cuda.synchronize()
+        assert 0 <= int(t2[0]) < n
+    finally:
+        own.close()
+        silent.close()
