@@ -251,12 +251,18 @@ def bench_moe(bh, ctx, world: int, rank: int, steps: int) -> dict:
     for name, rows, cols in (("gate", F, D), ("up", F, D), ("down", D, F)):
         own[name] = ctx.q4k_quantize(torch.randn(((hi - lo) * rows, cols), generator=g, device="cuda") * 0.02)
     ep = sharding.EPMoE(ctx, E, D, F, k, rank, world, own["gate"], own["up"], own["down"])
+    ep.enable_peer_exchange()
+    gi = torch.Generator(device="cuda").manual_seed(SEED + 7)  # the same tokens and logits on every rank
     for t in (1, 8):
-        cur = torch.randn((t, D), device="cuda")
-        lg = torch.randn((t, E), device="cuda")
+        cur = torch.randn((t, D), generator=gi, device="cuda")
+        lg = torch.randn((t, E), generator=gi, device="cuda")
         barrier(world)
         ms = max_over_ranks(time_events(lambda: ep.forward(cur, logits=lg), 20), world)
         res[f"tokens{t}_one_layer_expert_parallel"] = {"us": round(ms * 1e3, 2)}
+        barrier(world)
+        ms = max_over_ranks(time_events(lambda: ep.forward_peer(cur, logits=lg), 20), world)
+        res[f"tokens{t}_one_layer_expert_parallel_peer_exchange"] = {"us": round(ms * 1e3, 2)}
+    ep.close_peer_exchange()
     return res
 
 

@@ -174,13 +174,32 @@ int bh_q4k_lmhead_argmax_noalloc(const void *W_q4k, int64_t N, int64_t K, const 
  * after the wait; calls of one group must not overlap. */
 size_t bh_xchg_mailbox_bytes(void);
 int bh_xchg_mailbox_alloc(bh_ctx *ctx, void **mailbox);
-int bh_xchg_mailbox_free(bh_ctx *ctx, void *mailbox);
+int bh_xchg_mailbox_free(bh_ctx *ctx, void *mailbox); /* also frees bh_xchg_alloc buffers */
 int bh_xchg_ipc_handle(bh_ctx *ctx, void *mailbox, void *handle_out /* 64 bytes */);
 int bh_xchg_ipc_open(bh_ctx *ctx, const void *handle, void **peer_mailbox);
 int bh_xchg_ipc_close(bh_ctx *ctx, void *peer_mailbox);
 int bh_q4k_lmhead_argmax_tp(bh_ctx *ctx, const void *W_local, int64_t n_local, int64_t K, const float *x, int B,
                             int64_t row_offset, int rank, int world, void *const *mailboxes, uint32_t epoch,
                             int32_t *tok_out, float *max_opt, int fold, void *stream);
+
+/* The expert-parallel MoE exchange over peer memory instead of an
+ * all-reduce (the other half of bh_q4k_moe_ep + bh_moe_combine): after
+ * bh_q4k_moe_ep wrote this rank's pairs into dout_own, one kernel copies
+ * those rows into every other rank's receive buffer, publishes this rank's
+ * flag (epoch) in every rank's mailbox, waits (bounded, about a second, then
+ * BH_ETIMEDOUT) for all ranks' flags in its own, and forms out as
+ * bh_moe_combine does, each pair's row from dout_own when this rank owns
+ * the expert and from the receive buffer otherwise: bit-identical to one GPU.
+ * recv[q] / mailboxes[q]: rank q's receive buffer (bh_xchg_alloc of
+ * bh_moe_xchg_recv_bytes(n_embd) bytes, two banks for odd and even epochs) and
+ * mailbox as seen from this process (own at [rank]), mapped with
+ * bh_xchg_ipc_open; epoch as for bh_q4k_lmhead_argmax_tp. */
+int bh_xchg_alloc(bh_ctx *ctx, size_t bytes, void **buf);
+size_t bh_moe_xchg_recv_bytes(int n_embd);
+int bh_moe_ep_exchange_combine(bh_ctx *ctx, const float *dout_own, void *const *recv, void *const *mailboxes,
+                               const int32_t *selected, const float *weights, int n_tok, int k, int n_embd,
+                               int expert_lo, int expert_hi, int rank, int world, uint32_t epoch, float *out,
+                               int residual, void *stream);
 
 /* ------------------------------------------------------------------------
  * Decode block stack: the caller of the matvec in the reference engine's

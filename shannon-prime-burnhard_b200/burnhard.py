@@ -106,6 +106,11 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.bh_xchg_ipc_close.argtypes = [_vp, _vp]
     L.bh_q4k_lmhead_argmax_tp.argtypes = [_vp, _vp, _i64, _i64, _vp, C.c_int, _i64, C.c_int, C.c_int, _vp,
                                           C.c_uint32, _vp, _vp, C.c_int, _vp]
+    L.bh_xchg_alloc.argtypes = [_vp, C.c_size_t, C.POINTER(_vp)]
+    L.bh_moe_xchg_recv_bytes.argtypes = [C.c_int]
+    L.bh_moe_xchg_recv_bytes.restype = C.c_size_t
+    L.bh_moe_ep_exchange_combine.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int,
+                                             C.c_int, C.c_int, C.c_int, C.c_uint32, _vp, C.c_int, _vp]
     L.bh_stack_default_config.argtypes = [C.POINTER(StackConfig)]
     L.bh_stack_default_config.restype = None
     L.bh_stack_create.argtypes = [_vp, C.POINTER(StackConfig), C.c_uint64, C.POINTER(_vp)]
@@ -354,14 +359,18 @@ def lmhead_argmax(ctx: Context, w, n: int, k: int, x, logits=None, fold: int = F
 
 
 class PeerMailbox:
-    """This rank's mailbox for the peer-memory exchange of the row-split LM
-    head (bh_xchg_*): handle() gives the 64-byte CUDA IPC handle to share with
-    the other ranks, open(handle) maps a peer's mailbox into this process."""
+    """A zeroed device buffer of this rank for the peer-memory exchanges
+    (bh_xchg_*): the flag mailbox by default, or `nbytes` for a receive
+    buffer. handle() gives the 64-byte CUDA IPC handle to share with the other
+    ranks, open(handle) maps a peer's buffer into this process."""
 
-    def __init__(self, ctx: Context):
+    def __init__(self, ctx: Context, nbytes: int | None = None):
         self.ctx = ctx
         p = _vp()
-        _check(lib.bh_xchg_mailbox_alloc(ctx.h, C.byref(p)), "bh_xchg_mailbox_alloc")
+        if nbytes is None:
+            _check(lib.bh_xchg_mailbox_alloc(ctx.h, C.byref(p)), "bh_xchg_mailbox_alloc")
+        else:
+            _check(lib.bh_xchg_alloc(ctx.h, nbytes, C.byref(p)), "bh_xchg_alloc")
         self.ptr = p.value
         self.opened: list[int] = []
 
@@ -403,6 +412,25 @@ def lmhead_argmax_tp(ctx: Context, w_local, n_local: int, k: int, x, row_offset:
                                        len(mailboxes), arr, epoch, _dp(tok), _dp(mx), fold, _stream(stream)),
            "bh_q4k_lmhead_argmax_tp")
     return tok, mx
+
+
+def moe_ep_exchange_combine(ctx: Context, dout, selected, weights, expert_lo: int, expert_hi: int, rank: int,
+                            recv, mailboxes, epoch: int, out=None, residual: bool = False, stream=None):
+    """out [T, n_embd] of the expert-parallel block with the owned pairs
+    exchanged through peer memory (bh_moe_ep_exchange_combine)."""
+    import torch
+
+    t, k = selected.shape
+    n_embd = dout.shape[1]
+    if out is None:
+        out = torch.empty((t, n_embd), dtype=torch.float32, device=dout.device)
+    world = len(mailboxes)
+    ra = (_vp * world)(*recv)
+    ma = (_vp * world)(*mailboxes)
+    _check(lib.bh_moe_ep_exchange_combine(ctx.h, _dp(dout), ra, ma, _dp(selected), _dp(weights), t, k, n_embd,
+                                          expert_lo, expert_hi, rank, world, epoch, _dp(out), int(residual),
+                                          _stream(stream)), "bh_moe_ep_exchange_combine")
+    return out
 
 
 # ---------------------------------------------------------------------------

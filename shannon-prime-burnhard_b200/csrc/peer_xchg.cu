@@ -157,6 +157,83 @@ int launch_xchg_argmax(const float* cv, const int32_t* ci, int ncand, int B, int
     return cudaGetLastError() == cudaSuccess ? BH_OK : BH_EIO;
 }
 
+// ---------------------------------------------------------------------------
+// expert-parallel MoE: the owned pairs' expert outputs through peer memory,
+// fused with the slot-order combine
+// ---------------------------------------------------------------------------
+// Each rank computed the expert outputs of the (token, slot) pairs whose
+// expert it owns (bh_q4k_moe_ep, rows of its own dout). One CTA copies those
+// rows into the receive buffer of every other rank (same row), publishes its
+// flag in every rank's mailbox, waits (bounded) for every rank's flag in its
+// own mailbox, then forms out exactly as bh_moe_combine: per token, the slots
+// in order, fp32 product summed in double, each pair's row taken from its own
+// dout when it owns the expert and from the receive buffer otherwise. Rows of
+// a pair are written by exactly one rank, so the result is bit-identical to
+// one GPU. Receive buffers and flags have two banks (odd / even epochs).
+struct MoeXchgParams {
+    const float* dout;              // this rank's expert outputs [T*k][n_embd]
+    float* recv[XCHG_MAX_WORLD];    // every rank's receive bank of this epoch, own at [rank]
+    uint8_t* box[XCHG_MAX_WORLD];   // every rank's flag mailbox
+    const int32_t* sel;             // [T][k] selected experts
+    const float* w;                 // [T][k] weights
+    int T, k, n_embd, e_lo, e_hi, rank, world, residual;
+    uint32_t epoch;
+    float* out;
+    int* status;
+};
+
+__global__ void __launch_bounds__(1024) moe_xchg_combine_kernel(const MoeXchgParams a) {
+    __shared__ int s_ok;
+    const int tid = threadIdx.x;
+    const int n4 = a.n_embd / 4, npair = a.T * a.k;
+    for (int q = 0; q < npair; ++q) {
+        const int e = __ldcg(a.sel + q);
+        if (e < a.e_lo || e >= a.e_hi) continue;  // (the same q for every thread)
+        const float4* src = reinterpret_cast<const float4*>(a.dout + (int64_t)q * a.n_embd);
+        for (int r = 0; r < a.world; ++r) {
+            if (r == a.rank) continue;
+            float4* dst = reinterpret_cast<float4*>(a.recv[r] + (int64_t)q * a.n_embd);
+            for (int i = tid; i < n4; i += blockDim.x) dst[i] = __ldcg(src + i);
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        const size_t bank = (a.epoch & 1u) * XCHG_BANK;
+        __threadfence_system();
+        for (int r = 0; r < a.world; ++r)
+            st_release_sys(reinterpret_cast<uint32_t*>(a.box[r] + bank + XCHG_FLAGS_OFF) + a.rank, a.epoch);
+        const uint32_t* flags = reinterpret_cast<const uint32_t*>(a.box[a.rank] + bank + XCHG_FLAGS_OFF);
+        const long long t0 = clock64();
+        int ok = 1;
+        for (int r = 0; r < a.world && ok; ++r) {
+            while (ld_acquire_sys(flags + r) != a.epoch) {
+                if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+                    ok = 0;
+                    set_status(a.status, ST_TIMEOUT);
+                    break;
+                }
+            }
+        }
+        s_ok = ok;
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    const float* recv = a.recv[a.rank];
+    for (int idx = tid; idx < a.T * a.n_embd; idx += blockDim.x) {
+        const int t = idx / a.n_embd, i = idx - t * a.n_embd;
+        // ggml_mul (fp32 product) then ggml_sum_rows over the slots (double, in order)
+        double acc = 0.0;
+        for (int s = 0; s < a.k; ++s) {
+            const int q = t * a.k + s;
+            const int e = __ldcg(a.sel + q);
+            const float* row = (e >= a.e_lo && e < a.e_hi) ? a.dout : recv;
+            acc = __dadd_rn(acc, (double)__fmul_rn(__ldcv(row + (int64_t)q * a.n_embd + i), __ldcg(a.w + q)));
+        }
+        const float v = __double2float_rn(acc);
+        a.out[idx] = a.residual ? __fadd_rn(a.out[idx], v) : v;
+    }
+}
+
 }  // namespace bh
 
 // ---------------------------------------------------------------------------
@@ -196,6 +273,65 @@ int bh_xchg_mailbox_alloc(bh_ctx* ctx, void** mailbox) {
     }
     *mailbox = p;
     return BH_OK;
+}
+
+int bh_xchg_alloc(bh_ctx* ctx, size_t bytes, void** buf) {
+    if (!ctx || !buf || bytes == 0) return BH_EINVAL;
+    DeviceGuard g(ctx->device);
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return BH_ENOMEM;
+    }
+    if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        cudaFree(p);
+        return BH_EIO;
+    }
+    *buf = p;
+    return BH_OK;
+}
+
+size_t bh_moe_xchg_recv_bytes(int n_embd) {
+    return n_embd < 1 ? 0 : 2 * (size_t)bh::MOE_MAX_PAIRS * (size_t)n_embd * sizeof(float);
+}
+
+int bh_moe_ep_exchange_combine(bh_ctx* ctx, const float* dout_own, void* const* recv, void* const* mailboxes,
+                               const int32_t* selected, const float* weights, int n_tok, int k, int n_embd,
+                               int expert_lo, int expert_hi, int rank, int world, uint32_t epoch, float* out,
+                               int residual, void* stream) {
+    if (!ctx || !dout_own || !aligned_to(dout_own, 16) || !recv || !mailboxes || !selected || !weights || !out)
+        return BH_EINVAL;
+    if (n_tok < 1 || n_tok > bh::MOE_MAX_TOK || k < 1 || k > bh::MOE_MAX_K || n_embd < 4 || n_embd % 4 ||
+        expert_lo < 0 || expert_hi < expert_lo || world < 1 || world > bh::XCHG_MAX_WORLD || rank < 0 ||
+        rank >= world || epoch == 0)
+        return BH_EINVAL;
+    if (!aligned_to(selected, 4) || !aligned_to(weights, 4) || !aligned_to(out, 4)) return BH_EINVAL;
+    for (int q = 0; q < world; ++q)
+        if (!recv[q] || !aligned_to(recv[q], 256) || !mailboxes[q] || !aligned_to(mailboxes[q], 256))
+            return BH_EINVAL;
+    DeviceGuard g(ctx->device);
+    bh::MoeXchgParams a;
+    a.dout = dout_own;
+    const size_t bank = (epoch & 1u) * (size_t)bh::MOE_MAX_PAIRS * (size_t)n_embd;  // floats
+    for (int q = 0; q < bh::XCHG_MAX_WORLD; ++q) {
+        a.recv[q] = q < world ? static_cast<float*>(recv[q]) + bank : nullptr;
+        a.box[q] = q < world ? static_cast<uint8_t*>(mailboxes[q]) : nullptr;
+    }
+    a.sel = selected;
+    a.w = weights;
+    a.T = n_tok;
+    a.k = k;
+    a.n_embd = n_embd;
+    a.e_lo = expert_lo;
+    a.e_hi = expert_hi;
+    a.rank = rank;
+    a.world = world;
+    a.residual = residual != 0;
+    a.epoch = epoch;
+    a.out = out;
+    a.status = ctx->d_status;
+    bh::moe_xchg_combine_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(a);
+    return cudaGetLastError() == cudaSuccess ? BH_OK : BH_EIO;
 }
 
 int bh_xchg_mailbox_free(bh_ctx* ctx, void* mailbox) {

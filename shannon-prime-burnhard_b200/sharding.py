@@ -177,3 +177,36 @@ class EPMoE:
                                       self.n_ff, self.k, selected=selected, weights=weights, logits=logits)
         sum_expert_outputs(dout, self.world, self.group)
         return self.bh.moe_combine(self.ctx, dout, w, out=out, residual=residual)
+
+    def enable_peer_exchange(self) -> None:
+        """Map every rank's receive buffer and flag mailbox into this process
+        (CUDA IPC handles exchanged once over the process group)."""
+        bh = self.bh
+        self.recv = bh.PeerMailbox(self.ctx, bh.lib.bh_moe_xchg_recv_bytes(self.n_embd))
+        self.mbox = bh.PeerMailbox(self.ctx)
+        self.epoch = 0
+        if self.world == 1:
+            self.recvs, self.boxes = [self.recv.ptr], [self.mbox.ptr]
+            return
+        hs = [None] * self.world
+        dist.all_gather_object(hs, (self.recv.handle(), self.mbox.handle()), group=self.group)
+        self.recvs = [self.recv.ptr if r == self.rank else self.recv.open(hs[r][0]) for r in range(self.world)]
+        self.boxes = [self.mbox.ptr if r == self.rank else self.mbox.open(hs[r][1]) for r in range(self.world)]
+        dist.barrier(group=self.group)
+
+    def forward_peer(self, cur, logits=None, selected=None, weights=None, out=None, residual: bool = False):
+        """As forward(), with the owned pairs exchanged through peer memory by
+        the combining kernel instead of an all-reduce."""
+        dout, sel, w = self.bh.moe_ep(self.ctx, cur, self.gate, self.up, self.down, self.n_expert, self.lo, self.hi,
+                                      self.n_ff, self.k, selected=selected, weights=weights, logits=logits)
+        self.epoch += 1
+        return self.bh.moe_ep_exchange_combine(self.ctx, dout, sel, w, self.lo, self.hi, self.rank, self.recvs,
+                                               self.boxes, self.epoch, out=out, residual=residual)
+
+    def close_peer_exchange(self) -> None:
+        if getattr(self, "mbox", None) is not None:
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            self.recv.close()
+            self.mbox.close()
+            self.recv = self.mbox = None

@@ -55,13 +55,19 @@ def main() -> int:
     elo, ehi = sharding.even_shards(E, world)[rank]
     own = {n: sharding.EPMoE.slice_experts(b, E, elo, ehi) for n, b in banks.items()}
     ep = sharding.EPMoE(ctx, E, D, F, k, rank, world, own["gate"], own["up"], own["down"])
-    for T in (1, 4):
+    ep.enable_peer_exchange()
+    for T in (1, 4, 8, 1):
         cur = torch.randn((T, D), generator=g, device="cuda")
         lg = torch.randn((T, E), generator=g, device="cuda")
         ref, _, _ = bh.moe(ctx, cur, banks["gate"], banks["up"], banks["down"], E, F, k, logits=lg)
         out = ep.forward(cur, logits=lg)
+        outp = ep.forward_peer(cur, logits=lg)
+        torch.cuda.synchronize()
         if not torch.equal(out.view(torch.int32), ref.view(torch.int32)):
             fails.append(f"moe T={T}: expert-parallel output differs")
+        if not torch.equal(outp.view(torch.int32), ref.view(torch.int32)):
+            fails.append(f"moe T={T}: peer-exchange expert-parallel output differs")
+    ep.close_peer_exchange()
     torch.cuda.synchronize()
     st = ctx.status()
     if st != 0:

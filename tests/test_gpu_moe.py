@@ -198,3 +198,31 @@ def test_moe_stack_info_counts_distinct_experts(ctx, bh, oracle):
         want += len(set(ids.tolist())) * per_expert + act
     assert st.info()["step_bytes"] == want
     st.close()
+
+
+def test_moe_peer_exchange_one_rank_matches_moe(ctx, bh):
+    """The expert-parallel exchange fused with the combine, one rank owning
+    every expert (its own receive buffer and mailbox): bit-identical to
+    bh_q4k_moe over consecutive epochs."""
+    import torch
+
+    E, D, F, k = 16, 512, 256, 4
+    g = torch.Generator(device="cuda").manual_seed(21)
+    gate = ctx.q4k_quantize(torch.randn((E * F, D), generator=g, device="cuda") * 0.02)
+    up = ctx.q4k_quantize(torch.randn((E * F, D), generator=g, device="cuda") * 0.02)
+    down = ctx.q4k_quantize(torch.randn((E * D, F), generator=g, device="cuda") * 0.02)
+    recv = bh.PeerMailbox(ctx, bh.lib.bh_moe_xchg_recv_bytes(D))
+    box = bh.PeerMailbox(ctx)
+    try:
+        for epoch, T in enumerate((1, 3, 8, 2), start=1):
+            cur = torch.randn((T, D), generator=g, device="cuda")
+            lg = torch.randn((T, E), generator=g, device="cuda")
+            ref, _, _ = bh.moe(ctx, cur, gate, up, down, E, F, k, logits=lg)
+            dout, sel, w = bh.moe_ep(ctx, cur, gate, up, down, E, 0, E, F, k, logits=lg)
+            out = bh.moe_ep_exchange_combine(ctx, dout, sel, w, 0, E, 0, [recv.ptr], [box.ptr], epoch)
+            torch.cuda.synchronize()
+            assert torch.equal(out.view(torch.int32), ref.view(torch.int32))
+        assert ctx.status() == 0
+    finally:
+        recv.close()
+        box.close()
