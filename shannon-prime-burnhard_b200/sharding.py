@@ -79,6 +79,44 @@ def sum_expert_outputs(dout, world: int, group=None):
     return dout
 
 
+def _all_ok(ok: bool, world: int, group=None) -> bool:
+    """True on every rank iff ok on every rank (all ranks call it)."""
+    if world == 1:
+        return ok
+    flags = [None] * world
+    dist.all_gather_object(flags, bool(ok), group=group)
+    return all(flags)
+
+
+def _map_peers(bufs, rank: int, world: int, group=None) -> list[list[int]]:
+    """Exchange the CUDA IPC handles of this rank's buffers (bh.PeerMailbox)
+    and map the other ranks' ones: per buffer, every rank's pointer as seen
+    from this process (own at [rank]). All-or-nothing across the ranks: a
+    failure on any rank closes the mappings and raises on every rank, so no
+    rank is left waiting in a later collective."""
+    if world == 1:
+        return [[b.ptr] for b in bufs]
+    handles = None
+    try:
+        handles = [b.handle() for b in bufs]
+        ok = True
+    except Exception:
+        ok = False
+    if not _all_ok(ok, world, group):
+        raise RuntimeError("peer exchange: a rank could not export its buffers")
+    hs = [None] * world
+    dist.all_gather_object(hs, handles, group=group)
+    try:
+        out = [[b.ptr if r == rank else b.open(hs[r][i]) for r in range(world)] for i, b in enumerate(bufs)]
+        ok = True
+    except Exception:
+        out, ok = None, False
+    if not _all_ok(ok, world, group):
+        raise RuntimeError("peer exchange: a rank could not map the others' buffers")
+    dist.barrier(group=group)  # every rank's buffers are mapped before the first exchange
+    return out
+
+
 class TPLMHead:
     """Row-split Q4_K LM head with the greedy pick.
 
@@ -124,13 +162,7 @@ class TPLMHead:
         forward_peer() exchanges the greedy pick through peer memory."""
         self.mbox = self.bh.PeerMailbox(self.ctx)
         self.epoch = 0
-        if self.world == 1:
-            self.boxes = [self.mbox.ptr]
-            return
-        handles = [None] * self.world
-        dist.all_gather_object(handles, self.mbox.handle(), group=self.group)
-        self.boxes = [self.mbox.ptr if r == self.rank else self.mbox.open(handles[r]) for r in range(self.world)]
-        dist.barrier(group=self.group)  # every rank's mailbox is mapped before the first exchange
+        (self.boxes,) = _map_peers([self.mbox], self.rank, self.world, self.group)
 
     def forward_peer(self, x):
         """x [B, K] -> global tokens [B] (int32, on the device), the same on
@@ -185,14 +217,7 @@ class EPMoE:
         self.recv = bh.PeerMailbox(self.ctx, bh.lib.bh_moe_xchg_recv_bytes(self.n_embd))
         self.mbox = bh.PeerMailbox(self.ctx)
         self.epoch = 0
-        if self.world == 1:
-            self.recvs, self.boxes = [self.recv.ptr], [self.mbox.ptr]
-            return
-        hs = [None] * self.world
-        dist.all_gather_object(hs, (self.recv.handle(), self.mbox.handle()), group=self.group)
-        self.recvs = [self.recv.ptr if r == self.rank else self.recv.open(hs[r][0]) for r in range(self.world)]
-        self.boxes = [self.mbox.ptr if r == self.rank else self.mbox.open(hs[r][1]) for r in range(self.world)]
-        dist.barrier(group=self.group)
+        self.recvs, self.boxes = _map_peers([self.recv, self.mbox], self.rank, self.world, self.group)
 
     def forward_peer(self, cur, logits=None, selected=None, weights=None, out=None, residual: bool = False):
         """As forward(), with the owned pairs exchanged through peer memory by

@@ -117,3 +117,60 @@ def test_two_gloo_ranks(case):
         if p.is_alive():
             p.kill()
     assert results == {0: True, 1: True}, results
+
+
+def _peer_map_worker(rank, world, port, q, fail_rank):
+    import os
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import sharding
+
+    class FakeBuf:
+        # stands in for bh.PeerMailbox: a "handle" and an "open" that maps it
+        def __init__(self, r):
+            self.ptr = 1000 + r
+
+        def handle(self):
+            return bytes([rank]) * 64
+
+        def open(self, h):
+            if rank == fail_rank:
+                raise RuntimeError("cannot map")
+            return 1000 + h[0]
+
+    try:
+        out = sharding._map_peers([FakeBuf(rank)], rank, world)
+        q.put((rank, "ok", out))
+    except RuntimeError as e:
+        q.put((rank, "raised", str(e)))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fail_rank", [-1, 1])
+def test_peer_mapping_all_or_nothing(fail_rank):
+    """The IPC handle exchange of the peer-memory paths (host logic, gloo):
+    every rank gets every rank's buffer at its rank's position; when one
+    rank cannot map, every rank raises instead of waiting."""
+    import multiprocessing as mp
+    import socket
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_peer_map_worker, args=(r, 2, port, q, fail_rank)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(60)
+    if fail_rank < 0:
+        assert [r[1] for r in res] == ["ok", "ok"]
+        assert res[0][2] == [[1000, 1001]] and res[1][2] == [[1000, 1001]]
+    else:
+        assert [r[1] for r in res] == ["raised", "raised"]
