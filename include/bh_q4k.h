@@ -66,7 +66,10 @@ int bh_init(int device, bh_ctx **out);
 int bh_free(bh_ctx *ctx);
 /* Synchronize the context's device and report (and optionally clear) the
  * device-side status word that kernels set when a bounded wait runs out:
- * 0, or BH_ETIMEDOUT / BH_EINVAL. */
+ * 0, or BH_ETIMEDOUT / BH_EINVAL. A routed-expert launch whose grid-barrier
+ * wait ran out leaves that barrier's arrival count behind; clearing a timeout
+ * also resets every grid barrier of the context and of its MoE stacks, and
+ * MoE results computed between the timeout and that clear are not valid. */
 int bh_device_status(bh_ctx *ctx, int clear);
 
 /* Launch-shape tuning of a context (no effect on results): keys below.
@@ -95,6 +98,10 @@ int bh_device_status(bh_ctx *ctx, int clear);
  * programmatic-launch wait, 0..8 (0, the default: the whole ring); the rest
  * go out right after the activation loads that follow the wait. */
 #define BH_TUNE_PREFILL 8
+/* BH_TUNE_BARRIER_WAIT: log2 of the SM cycles a routed-expert grid barrier
+ * waits before it gives up and reports BH_ETIMEDOUT, 16..31 (default 31,
+ * about a second). */
+#define BH_TUNE_BARRIER_WAIT 9
 int bh_tune(bh_ctx *ctx, int key, int value);
 
 /* fp32 activations [B][K] -> B columns of Q8_K, byte-identical to
@@ -152,9 +159,16 @@ int bh_q4k_lmhead_argmax(bh_ctx *ctx, const void *W_q4k, int64_t N, int64_t K, c
  * looks up that array's address (cudaGetSymbolAddress) and must come before
  * any stream capture. Calls share the array: calls that overlap on the GPU
  * race, so serialize them. Runs on the current device. No counterpart in the
- * reference. */
+ * reference.
+ * Device-side failures (a bounded weight-copy wait that ran out) cannot be
+ * returned by the call itself, which returns before the kernels run: they set
+ * a second static status word, after which the call's tokens (and those of
+ * every later call until the word is cleared) are written as -1.
+ * bh_noalloc_status synchronizes the current device and returns that word as
+ * BH_OK / BH_ETIMEDOUT, clearing it when clear != 0. */
 int bh_q4k_lmhead_argmax_noalloc(const void *W_q4k, int64_t N, int64_t K, const float *x, int B,
                                  float *logits_opt, int32_t *tok_out, float *max_opt, int fold, void *stream);
+int bh_noalloc_status(int clear);
 
 /* Row-split (tensor-parallel) LM head over the GPUs of one node, one process
  * per GPU, with the greedy pick exchanged through peer memory instead of a
@@ -248,6 +262,12 @@ typedef struct bh_stack_config {
  * the per-head norm and RoPE), and the attention output [n_head * head_dim] */
 #define BH_T_QKV 17
 #define BH_T_ATTN 18
+/* the last layer's hidden state after the O projection and its residual add,
+ * its gate | up rows before the SwiGLU [2 * n_ff], and silu(gate) * up [n_ff]
+ * (the down projection's input) */
+#define BH_T_H_ATTN 19
+#define BH_T_GATE_UP 20
+#define BH_T_FFN_ACT 21
 
 /* The Qwen3-8B-shaped defaults (36 x 4096, 32/8 heads of 128, FFN 12288,
  * vocab 151936, 128 KV positions). */
@@ -371,6 +391,7 @@ typedef struct bh_moe_config {
 #define BH_MOE_SELECTED 5  /* [n_tok][k] int32, written by each step */
 #define BH_MOE_WEIGHTS 6   /* [n_tok][k] fp32, written by each step */
 #define BH_MOE_HIDDEN 7    /* [n_tok][n_embd] fp32 (layer == -1) */
+#define BH_MOE_BARRIER 8   /* the layer kernels' grid-barrier words, 256 bytes (layer == -1) */
 
 void bh_moe_default_config(bh_moe_config *cfg);
 int bh_moe_stack_create(bh_ctx *ctx, const bh_moe_config *cfg, uint64_t seed, bh_moe_stack **out);

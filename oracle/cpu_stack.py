@@ -4,12 +4,14 @@ TEST INFRASTRUCTURE ONLY: the checker for bh_stack_decode and the timed CPU
 path of bench.py's reference arm. The Q4_K matvecs go through a caller-chosen
 function: the reference's own ggml mul_mat compiled into oracle/_ref
 (quantize_row_q8_K + ggml_vec_dot_q4_K_q8_K, ggml-cpu.c:1241-1439), or the
-oracle's restatement of it. The glue between matvecs (RMSNorm, per-head q/k
-RMSNorm, NeoX RoPE, GQA softmax attention, SiLU(gate)*up, residual adds,
-first-index argmax of engine.cpp:36-43) is float32 numpy; it follows the
-same formulas as the device kernels but not their summation order, so the
-stack as a whole is compared within a tolerance, while each matvec is
-bit-exact given identical inputs.
+oracle's restatement of it. RMSNorm and SiLU(gate)*up are the oracle's
+C restatements of the reference's rms_norm_f32 and ggml_v_silu (bit-exact
+with the device); the per-head q/k RMSNorm, NeoX RoPE and GQA softmax
+attention are float32 numpy following the same formulas as the device
+kernels but not their summation order or sin/cos, so the stack as a whole is
+compared within a tolerance, while each matvec, RMSNorm and SwiGLU is
+bit-exact given identical inputs; residual adds and the first-index argmax of
+engine.cpp:36-43 are exact.
 """
 from __future__ import annotations
 
@@ -18,10 +20,28 @@ import numpy as np
 W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN = range(7)
 
 
+_ORACLE = None
+
+
+def _oracle():
+    global _ORACLE
+    if _ORACLE is None:
+        import oracle as om
+
+        _ORACLE = om.Oracle()
+    return _ORACLE
+
+
 def rmsnorm(x: np.ndarray, g: np.ndarray, eps: float) -> np.ndarray:
-    ss = np.float32(np.sum(x.astype(np.float64) ** 2))
-    r = np.float32(1.0) / np.sqrt(np.float32(ss / np.float32(x.size)) + np.float32(eps))
-    return (x * r * g).astype(np.float32)
+    """rms_norm_f32 then ggml_mul (the oracle's C restatement: binary32
+    squares summed sequentially in double, mean = (float)(sum / n),
+    1 / sqrtf(mean + eps), x * scale * g)."""
+    return _oracle().rmsnorm(np.asarray(x, dtype=np.float32), g, eps)
+
+
+def swiglu(g: np.ndarray, u: np.ndarray) -> np.ndarray:
+    """ggml_silu (ggml_v_silu lane by lane) then ggml_mul."""
+    return (_oracle().silu(np.asarray(g, dtype=np.float32)) * u).astype(np.float32)
 
 
 def rope_neox(x: np.ndarray, pos: int, theta: float) -> np.ndarray:
@@ -90,7 +110,7 @@ class CpuStack:
             xn = rmsnorm(h, self.norms["ffn_norm"][l], eps)
             g = self.mv(l, W_GATE, F, E, xn)
             u = self.mv(l, W_UP, F, E, xn)
-            act = (g / (np.float32(1.0) + np.exp(-g)) * u).astype(np.float32)
+            act = swiglu(g, u)
             h = (h + self.mv(l, W_DOWN, E, F, act)).astype(np.float32)
         xn = rmsnorm(h, self.norms["out_norm"], eps)
         logits = self.matvec(self.w[(-1, 7)], c["n_vocab"], E, xn.reshape(1, E))[0]

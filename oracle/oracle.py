@@ -203,6 +203,7 @@ class Reference:
         L.ref_mul_mat.argtypes = [_vp, _vp, C.c_int64, C.c_int64, _vp, C.c_int, _vp, _vp]
         L.ref_soft_max.argtypes = [_vp, C.c_int, _vp]
         L.ref_silu.argtypes = [_vp, C.c_int, _vp]
+        L.ref_vexpf.argtypes = [_vp, C.c_int, _vp]
         self.has_avx2 = bool(L.ref_has_avx2())
         self._pool = None
 
@@ -246,6 +247,14 @@ class Reference:
         y = np.empty_like(x)
         for i in range(x.shape[0]):
             self.lib.ref_soft_max(_ptr(x[i]), x.shape[1], _ptr(y[i]))
+        return y
+
+    def expf(self, x: np.ndarray) -> np.ndarray:
+        """ggml_v_expf (AVX2) of every element; x.size must be a multiple of 8."""
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+        assert x.size % 8 == 0
+        y = np.empty_like(x)
+        self.lib.ref_vexpf(_ptr(x), x.size, _ptr(y))
         return y
 
     def silu(self, x: np.ndarray) -> np.ndarray:

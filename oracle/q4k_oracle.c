@@ -514,32 +514,39 @@ int64_t bho_argmax(const float *v, int64_t n) {
 /* routed-expert FFN glue (desktop/engine/src/forward.cpp:1001-1118)   */
 /* ------------------------------------------------------------------ */
 
-/* exp by Cody-Waite reduction and a degree-7 Taylor polynomial; the same
- * operation sequence as the GPU's exp_cw (csrc/bh_math.cuh), so the two
- * agree bit for bit. The reference itself uses ggml_v_expf
- * (ggml-cpu/vec.h:1233-1271) or expf; the difference is a few ulp. */
+/* exp as ggml's AVX2 kernel evaluates it, one lane of ggml_v_expf
+ * (ggml-cpu/vec.h:1233-1271; the method of ARM's optimized-routines expf:
+ * n = round(x / ln2) through the 1.5*2^23 shift, b = x - n*ln2 in two fused
+ * steps, a degree-5 polynomial j ~ exp(b) - 1 in Estrin form, then
+ * k = 2^n built in the exponent field and exp = k + k*j; |n| > 126 takes
+ * the two-factor scaling s2*s1 so subnormal and overflowing results round
+ * once, |n| > 192 saturates to s1*s1). Every step is one correctly
+ * rounded binary32 operation, as the intrinsics are, so the GPU's
+ * exp_ggml (csrc/bh_math.cuh) and the reference agree bit for bit.
+ * The reference's scalar tails (n % 8 elements of soft_max, SiLU of
+ * lengths not a multiple of 8) call libm expf instead. */
 float bho_expf(float x) {
-    if (x != x) return x;
-    if (x > 0x1.62e430p+6f) return INFINITY;
-    if (x < -103.972084f) return 0.0f;
-    const float n = rintf(x * 0x1.715476p+0f);
-    float r = fmaf(-n, 0x1.62e400p-1f, x);
-    r = fmaf(-n, 0x1.7f7d1cp-20f, r);
-    float q = 0x1.a01a02p-13f;
-    q = fmaf(q, r, 0x1.6c16c2p-10f);
-    q = fmaf(q, r, 0x1.111112p-7f);
-    q = fmaf(q, r, 0x1.555556p-5f);
-    q = fmaf(q, r, 0x1.555556p-3f);
-    q = fmaf(q, r, 0.5f);
-    q = fmaf(q, r, 1.0f);
-    q = fmaf(q, r, 1.0f);
-    const int ni = (int)n;
-    const int n1 = ni >> 1, n2 = ni - n1;
-    return (q * u2f((uint32_t)(n1 + 127) << 23)) * u2f((uint32_t)(n2 + 127) << 23);
+    const float r = 0x1.8p23f;
+    const float z = fmaf(x, 0x1.715476p+0f, r);
+    const float n = z - r;
+    const float b = fmaf(-n, 0x1.7f7d1cp-20f, fmaf(-n, 0x1.62e4p-1f, x));
+    const uint32_t e = f2u(z) << 23;
+    const float k = u2f(e + 0x3f800000u);
+    const int c = fabsf(n) > 126.0f;
+    const float u = b * b;
+    const float j = fmaf(fmaf(fmaf(0x1.0e4020p-7f, b, 0x1.573e2ep-5f), u, fmaf(0x1.555e66p-3f, b, 0x1.fffdb6p-2f)),
+                         u, 0x1.ffffecp-1f * b);
+    if (!c) return fmaf(j, k, k);
+    const uint32_t g = n <= 0.0f ? 0x82000000u : 0u;
+    const float s1 = u2f(g + 0x7f000000u);
+    const float s2 = u2f(e - g);
+    if (fabsf(n) > 192.0f) return s1 * s1;
+    return fmaf(s2, j, s2) * s1;
 }
 
-/* ggml_silu_f32 (ggml-cpu/vec.h:1064): x / (1 + exp(-x)) */
-float bho_silu(float x) { return x / (1.0f + bho_expf(-x)); }
+/* ggml_v_silu, one lane (ggml-cpu/vec.h:1273-1280, ggml_vec_silu_f32 at
+ * vec.cpp:396): x / (1 + exp(0 - x)) */
+float bho_silu(float x) { return x / (1.0f + bho_expf(0.0f - x)); }
 
 void bho_expf_n(const float *x, int64_t n, float *y) { for (int64_t i = 0; i < n; ++i) y[i] = bho_expf(x[i]); }
 void bho_silu_n(const float *x, int64_t n, float *y) { for (int64_t i = 0; i < n; ++i) y[i] = bho_silu(x[i]); }

@@ -69,7 +69,7 @@ void bho_partials(const void *W, int64_t N, int64_t K, const void *Xq, int B, in
 int64_t bho_argmax(const float *v, int64_t n);
 
 /* ---- routed-expert FFN glue (forward.cpp:1001-1118), see q4k_oracle.c ---- */
-float bho_expf(float x);   /* Cody-Waite + degree-7 Taylor; identical to the GPU's */
+float bho_expf(float x);   /* one lane of ggml's AVX2 ggml_v_expf; identical to the GPU's */
 float bho_silu(float x);   /* x / (1 + exp(-x)) */
 void  bho_expf_n(const float *x, int64_t n, float *y);
 void  bho_silu_n(const float *x, int64_t n, float *y);

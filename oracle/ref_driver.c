@@ -214,3 +214,8 @@ void ref_soft_max(const float *x, int n, float *y) {
 }
 
 void ref_silu(const float *x, int n, float *y) { ggml_vec_silu_f32(n, y, x); }
+
+/* exp through the reference's own SIMD kernel: ggml_vec_soft_max_f32 with
+ * max 0 stores ggml_v_expf(x - 0) = ggml_v_expf(x) for every group of 8
+ * (n % 8 tail elements go through libm expf). */
+void ref_vexpf(const float *x, int n, float *y) { (void)ggml_vec_soft_max_f32(n, y, x, 0.0f); }

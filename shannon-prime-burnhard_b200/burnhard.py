@@ -30,6 +30,7 @@ TUNE_TPR = 4
 TUNE_SM_BUDGET = 5
 TUNE_SMALL_ACT = 7
 TUNE_PREFILL = 8
+TUNE_BARRIER_WAIT = 9
 BH_EIO = -5
 BH_ENOMEM = -12
 BH_ENODEV = -19
@@ -70,13 +71,14 @@ class MoeConfig(C.Structure):
         return {name: getattr(self, name) for name, _ in self._fields_}
 
 
-MOE_GATE, MOE_UP, MOE_DOWN, MOE_LOGITS, MOE_NORM, MOE_SELECTED, MOE_WEIGHTS, MOE_HIDDEN = range(8)
+MOE_GATE, MOE_UP, MOE_DOWN, MOE_LOGITS, MOE_NORM, MOE_SELECTED, MOE_WEIGHTS, MOE_HIDDEN, MOE_BARRIER = range(9)
 
 W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN = range(7)
 W_PER_LAYER = 7
 W_OUTPUT = 7
 OP_QKV, OP_O, OP_GATE_UP, OP_DOWN, OP_LMHEAD, OP_ATTN = range(6)
-T_ATTN_NORM, T_FFN_NORM, T_Q_NORM, T_K_NORM, T_OUT_NORM, T_K_CACHE, T_V_CACHE, T_LOGITS, T_HIDDEN, T_QKV, T_ATTN = range(8, 19)
+(T_ATTN_NORM, T_FFN_NORM, T_Q_NORM, T_K_NORM, T_OUT_NORM, T_K_CACHE, T_V_CACHE, T_LOGITS, T_HIDDEN, T_QKV, T_ATTN,
+ T_H_ATTN, T_GATE_UP, T_FFN_ACT) = range(8, 22)
 
 
 def load(path: str = LIB_PATH) -> C.CDLL:
@@ -98,6 +100,7 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.bh_q4k_mul_mat_host.argtypes = [_vp, _vp, _i64, _i64, _vp, C.c_int, _vp, C.c_int]
     L.bh_q4k_lmhead_argmax.argtypes = [_vp, _vp, _i64, _i64, _vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp]
     L.bh_q4k_lmhead_argmax_noalloc.argtypes = [_vp, _i64, _i64, _vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp]
+    L.bh_noalloc_status.argtypes = [C.c_int]
     L.bh_xchg_mailbox_bytes.restype = C.c_size_t
     L.bh_xchg_mailbox_alloc.argtypes = [_vp, C.POINTER(_vp)]
     L.bh_xchg_mailbox_free.argtypes = [_vp, _vp]
@@ -558,7 +561,7 @@ class MoeStack:
         ptr, nb = self.tensor(layer, which)
         if which in (MOE_GATE, MOE_UP, MOE_DOWN):
             t = device_view(ptr, nb, "|u1")
-        elif which == MOE_SELECTED:
+        elif which in (MOE_SELECTED, MOE_BARRIER):
             t = device_view(ptr, nb // 4, "<i4")
         else:
             t = device_view(ptr, nb // 4, "<f4")

@@ -132,6 +132,20 @@ MatvecParams base_params(bh_ctx* ctx, const void* W, int64_t N, int64_t K, int B
     return p;
 }
 
+void register_barrier_words(bh_ctx* ctx, void* words) {
+    std::lock_guard<std::mutex> lock(ctx->barrier_mu.m);
+    ctx->barrier_words.push_back(words);
+}
+
+void unregister_barrier_words(bh_ctx* ctx, void* words) {
+    std::lock_guard<std::mutex> lock(ctx->barrier_mu.m);
+    for (size_t i = 0; i < ctx->barrier_words.size(); ++i)
+        if (ctx->barrier_words[i] == words) {
+            ctx->barrier_words.erase(ctx->barrier_words.begin() + (long)i);
+            return;
+        }
+}
+
 int run_matvec(bh_ctx* ctx, MatvecParams& p, int fold, int src, int epi, cudaStream_t s, bool pdl) {
     const int grid = plan_for(ctx, p, 0);
     if (grid < 0) return grid;
@@ -254,6 +268,10 @@ int bh_tune(bh_ctx* ctx, int key, int value) {
             if (value != 0 && (value < 48 * 1024 || value > 228 * 1024)) return BH_EINVAL;
             ctx->sm_budget = value;
             return BH_OK;
+        case BH_TUNE_BARRIER_WAIT:
+            if (value < 16 || value > 31) return BH_EINVAL;
+            ctx->barrier_wait_cycles = 1ll << value;
+            return BH_OK;
         default:
             return BH_EINVAL;
     }
@@ -266,6 +284,14 @@ int bh_device_status(bh_ctx* ctx, int clear) {
     int st = 0;
     if (cudaMemcpy(&st, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return BH_EIO;
     if (clear && st) cudaMemset(ctx->d_status, 0, sizeof(int));
+    if (clear && st == bh::ST_TIMEOUT) {
+        // CTAs that gave up on a grid barrier left their arrivals counted:
+        // start every barrier of this context from zero again
+        std::lock_guard<std::mutex> lock(ctx->barrier_mu.m);
+        for (void* w : ctx->barrier_words)
+            if (cudaMemset(w, 0, 256) != cudaSuccess) return BH_EIO;
+        if (cudaDeviceSynchronize() != cudaSuccess) return BH_EIO;
+    }
     if (st == bh::ST_TIMEOUT) return BH_ETIMEDOUT;
     if (st != 0) return BH_EINVAL;
     return BH_OK;

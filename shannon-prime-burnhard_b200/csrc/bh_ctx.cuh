@@ -4,9 +4,20 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <mutex>
+#include <vector>
 #include <cuda_runtime.h>
 
 #include "bh_kernels.cuh"
+
+// A mutex that copies as a fresh one (a context is copied only as a launch
+// plan, which never touches the lock of the original).
+struct bh_copyable_mutex {
+    std::mutex m;
+    bh_copyable_mutex() = default;
+    bh_copyable_mutex(const bh_copyable_mutex&) {}
+    bh_copyable_mutex& operator=(const bh_copyable_mutex&) { return *this; }
+};
 
 struct bh_ctx {
     int device = 0;
@@ -32,6 +43,15 @@ struct bh_ctx {
     // outputs of every pair, routing
     uint8_t* moe_scratch = nullptr;
     size_t moe_scratch_bytes = 0;
+    // Grid-barrier words of the cooperative MoE launches made through this
+    // context (its own scratch and those of its MoE stacks). A CTA whose
+    // bounded barrier wait ran out returns early and leaves its arrivals
+    // counted, so bh_device_status zeroes every registered word when it finds
+    // a timeout; until then later MoE results are not valid.
+    bh_copyable_mutex barrier_mu;
+    std::vector<void*> barrier_words;  // 256 bytes each
+    // bound of the MoE grid-barrier wait in SM cycles (default ~1 s)
+    long long barrier_wait_cycles = 1ll << 31;
 };
 
 
@@ -41,6 +61,9 @@ namespace bh {
 int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override);
 // MatvecParams for a single-segment weight matrix.
 MatvecParams base_params(bh_ctx* ctx, const void* W, int64_t N, int64_t K, int B, float* y);
+// Grid-barrier words (256 bytes) that bh_device_status zeroes after a timeout.
+void register_barrier_words(bh_ctx* ctx, void* words);
+void unregister_barrier_words(bh_ctx* ctx, void* words);
 // plan_for + launch.
 int run_matvec(bh_ctx* ctx, MatvecParams& p, int fold, int src, int epi, cudaStream_t s, bool pdl);
 // Plan and launch one routed-expert FFN batch (one cooperative launch; the

@@ -2,11 +2,28 @@
 // and the C-ABI layer.
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace bh {
+
+// Function attributes (dynamic shared-memory limit, carveout) are per device:
+// `done` keeps one bit per device on which `set` already ran for one kernel
+// (a function-local static of that kernel's launcher). Safe from several host
+// threads: two threads may both run `set` once, which is harmless. Returns
+// true when the attributes hold on the current device.
+template <class F>
+inline bool attrs_on_device(std::atomic<uint64_t>& done, F&& set) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    const uint64_t bit = 1ull << dev;
+    if (done.load(std::memory_order_acquire) & bit) return true;
+    if (!set()) return false;
+    done.fetch_or(bit, std::memory_order_acq_rel);
+    return true;
+}
 
 // Where the matvec prologue takes its activations from.
 enum ActSrc : int {
@@ -47,6 +64,10 @@ struct MatvecParams {
     int32_t* cand_idx;     // EPI_ARGMAX: [gridDim][B] first index of the maxima
     int* status;           // device status word
     int64_t* trace;        // timeline probe (builds with BH_TRACE only; else unused)
+    // optional copy of the epilogue's values (null: none): EPI_ADD the sums
+    // [B][ldy] it stores, EPI_SWIGLU the gate and up rows [B][2][ldy] before
+    // the SwiGLU (the decode stack keeps its last layer's for parity checks)
+    float* capture;
     // tiling, chosen on the host
     int rows_per_tile;     // rows of one warp stage: 32 / tpr
     int tpr;               // threads per row: 4 or 8
@@ -116,6 +137,7 @@ struct MoeParams {
     // reproduces every value exactly) and out is not touched
     int e_lo, e_hi, combine;
     unsigned int* gbar;    // grid barrier word (arrivals, generation << 16), zero before first use
+    long long gbar_wait;   // bound of a grid-barrier wait, SM cycles
     int* status;
     int64_t* trace;        // timeline probe (builds with BH_TRACE only; else unused)
     // tiling, chosen on the host: both phases share one ring of `stages`
@@ -151,7 +173,9 @@ int launch_matvec(const MatvecParams& p, int fold, int act_src, int epi, const L
 int launch_q8k_quantize(const float* x, int64_t K, int B, uint8_t* out, int* status, cudaStream_t s);
 int launch_q4k_quantize(const float* w, int64_t N, int64_t K, uint8_t* out, cudaStream_t s);
 int launch_q4k_dequantize(const uint8_t* w, int64_t N, int64_t K, float* out, cudaStream_t s);
+// status (may be null): when the word is nonzero as the finisher runs (an
+// earlier bounded wait ran out), every token is written as -1.
 int launch_argmax_finish(const float* cand_val, const int32_t* cand_idx, int ncand, int B,
-                         int32_t* tok_out, float* val_out, cudaStream_t s, bool pdl);
+                         int32_t* tok_out, float* val_out, cudaStream_t s, bool pdl, const int* status = nullptr);
 
 }  // namespace bh

@@ -1,48 +1,53 @@
-// bh_math.cuh — the exponential used by the routed-expert glue (softmax of
-// the router logits, SiLU of the gate), written so that the CPU oracle can
-// evaluate the identical sequence of correctly rounded binary32 operations
-// and the GPU results match it bit for bit.
+// bh_math.cuh — the exponential and SiLU of the decode glue (SwiGLU of the
+// dense FFN and of the routed experts, softmax of the router logits),
+// evaluated exactly as the reference's x86 CPU backend evaluates them, so
+// the device and the reference agree bit for bit.
 //
-// Method: Cody–Waite argument reduction (W. J. Cody and W. Waite, "Software
-// Manual for the Elementary Functions", 1980): x = n*ln2 + r with
-// n = round(x * log2(e)) and ln2 split into a 15-bit-exact high part and a
-// low part, |r| <= ~0.35; then exp(r) from its Taylor series to degree 7
-// (coefficients 1/k!, each rounded to binary32) in Horner form with fused
-// multiply-adds; then the scale 2^n applied as two exact powers of two so a
-// subnormal result is rounded once. The truncation error is below 0.13 ulp
-// and the evaluated error stays within 1 ulp of exp(x) (checked on the CPU
-// against a double-precision exp over the float range the callers use).
+// exp_ggml is one lane of ggml's AVX2 ggml_v_expf (ggml-cpu/vec.h:1233-1271),
+// itself the method of ARM's optimized-routines expf: n = round(x / ln2)
+// through the 1.5*2^23 shift, the reduced argument b = x - n*ln2 in two
+// fused steps (ln2 split in a high and a low part), a degree-5 polynomial
+// j ~ exp(b) - 1 in Estrin form, k = 2^n assembled in the exponent field,
+// and exp = k + k*j; for |n| > 126 the scale is applied as two factors
+// (s2 * s1) so a subnormal or overflowing result rounds once, and |n| > 192
+// saturates to s1*s1 (0 or inf). Every step is a single correctly rounded
+// binary32 operation (the intrinsics the reference uses are too), written
+// with the __f*_rn intrinsics so no contraction or reassociation can change
+// it. The oracle (oracle/q4k_oracle.c bho_expf) restates the same sequence
+// in C, and both are checked against the reference's compiled vec.cpp.
 //
-// The reference evaluates these with ggml's SIMD exponential
-// (ggml-cpu/vec.h, ggml_v_expf) or libm expf; results agree with it to a few
-// ulp, which is within the fp32 tolerance of the path.
+// The reference evaluates the n % 8 tail of a soft_max row or a SiLU row
+// with libm expf instead; every length on this path (128 experts, n_ff
+// multiples of 256) has no tail.
 #pragma once
 
 #include "bh_common.cuh"
 
 namespace bh {
 
-__device__ __forceinline__ float exp_cw(float x) {
-    if (!(x == x)) return x;                                    // NaN
-    if (x > 0x1.62e430p+6f) return __int_as_float(0x7f800000);  // above ln(FLT_MAX): +inf
-    if (x < -103.972084f) return 0.f;                           // below ln(2^-150): rounds to zero
-    const float n = rintf(__fmul_rn(x, 0x1.715476p+0f));        // round(x / ln2), ties to even
-    float r = __fmaf_rn(-n, 0x1.62e400p-1f, x);                 // ln2 high part (n * hi is exact)
-    r = __fmaf_rn(-n, 0x1.7f7d1cp-20f, r);                      // ln2 low part
-    float q = 0x1.a01a02p-13f;                                  // 1/7!
-    q = __fmaf_rn(q, r, 0x1.6c16c2p-10f);                       // 1/6!
-    q = __fmaf_rn(q, r, 0x1.111112p-7f);                        // 1/5!
-    q = __fmaf_rn(q, r, 0x1.555556p-5f);                        // 1/4!
-    q = __fmaf_rn(q, r, 0x1.555556p-3f);                        // 1/3!
-    q = __fmaf_rn(q, r, 0.5f);
-    q = __fmaf_rn(q, r, 1.f);
-    q = __fmaf_rn(q, r, 1.f);
-    const int ni = (int)n;                                      // -150 .. 128
-    const int n1 = ni >> 1, n2 = ni - n1;                       // both within [-75, 64]
-    return __fmul_rn(__fmul_rn(q, __int_as_float((n1 + 127) << 23)), __int_as_float((n2 + 127) << 23));
+__device__ __forceinline__ float exp_ggml(float x) {
+    const float r = 0x1.8p23f;
+    const float z = __fmaf_rn(x, 0x1.715476p+0f, r);
+    const float n = __fsub_rn(z, r);
+    const float b = __fmaf_rn(-n, 0x1.7f7d1cp-20f, __fmaf_rn(-n, 0x1.62e4p-1f, x));
+    const uint32_t e = __float_as_uint(z) << 23;
+    const float k = __uint_as_float(e + 0x3f800000u);
+    const float u = __fmul_rn(b, b);
+    const float j = __fmaf_rn(__fmaf_rn(__fmaf_rn(0x1.0e4020p-7f, b, 0x1.573e2ep-5f), u,
+                                        __fmaf_rn(0x1.555e66p-3f, b, 0x1.fffdb6p-2f)),
+                              u, __fmul_rn(0x1.ffffecp-1f, b));
+    if (!(fabsf(n) > 126.f)) return __fmaf_rn(j, k, k);
+    const uint32_t g = n <= 0.f ? 0x82000000u : 0u;
+    const float s1 = __uint_as_float(g + 0x7f000000u);
+    const float s2 = __uint_as_float(e - g);
+    if (fabsf(n) > 192.f) return __fmul_rn(s1, s1);
+    return __fmul_rn(__fmaf_rn(s2, j, s2), s1);
 }
 
-// silu(x) = x / (1 + exp(-x))   (ggml_silu_f32, ggml-cpu/vec.h:1064)
-__device__ __forceinline__ float silu_cw(float x) { return __fdiv_rn(x, __fadd_rn(1.f, exp_cw(-x))); }
+// silu(x) = x / (1 + exp(0 - x)), one lane of ggml_v_silu (ggml-cpu/vec.h:
+// 1273-1280) as ggml_vec_silu_f32 (vec.cpp:396) applies it.
+__device__ __forceinline__ float silu_ggml(float x) {
+    return __fdiv_rn(x, __fadd_rn(1.f, exp_ggml(__fsub_rn(0.f, x))));
+}
 
 }  // namespace bh

@@ -351,6 +351,7 @@ struct bh_stack {
     float* rope_inv_freq;           // [head_dim / 2]
     float *kc, *vc;
     float *x_in, *h, *qkv, *attn, *gu, *logits, *cand_val;
+    float *cap_h_attn, *cap_gate_up;  // the last layer's h after O + residual, its gate | up rows
     int32_t *cand_idx, *tok;
     int* pos;
     int32_t* host_tok = nullptr;    // pinned
@@ -457,14 +458,13 @@ int launch_attn(bh_stack* st, int l, bool pdl) {
     at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl ? 2 : 1;
-    static bool attr_set = false;
-    if (!attr_set) {
-        // the same shared-memory carveout as the matvecs around it
-        if (cudaFuncSetAttribute(bh::attn_decode_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                 cudaSharedmemCarveoutMaxShared) != cudaSuccess)
-            return BH_EIO;
-        attr_set = true;
-    }
+    static std::atomic<uint64_t> attr_devices{0};
+    // the same shared-memory carveout as the matvecs around it
+    if (!bh::attrs_on_device(attr_devices, [] {
+            return cudaFuncSetAttribute(bh::attn_decode_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                        cudaSharedmemCarveoutMaxShared) == cudaSuccess;
+        }))
+        return BH_EIO;
     return cudaLaunchKernelEx(&cfg, bh::attn_decode_kernel, a) == cudaSuccess ? BH_OK : BH_EIO;
 }
 
@@ -500,12 +500,15 @@ int enqueue_step(bh_stack* st) {
         if ((rc = launch_attn(st, l, true)) != BH_OK) return rc;
         st->launches += 1;
         // 3. O projection, residual add
+        const bool last = l == c.n_layer - 1;
         p = bh::base_params(ctx, W[BH_W_O], c.n_embd, qd, 1, st->h);
         p.xf = st->attn;
+        if (last) p.capture = st->cap_h_attn;
         if ((rc = stack_matvec(st, p, bh::ACT_F32, bh::EPI_ADD, true)) != BH_OK) return rc;
         account(p, (int)qd * 4, p.N);
         // 4. gate / up in row pairs, silu(gate) * up in the epilogue
         p = gate_up_params(st, l);
+        if (last) p.capture = st->cap_gate_up;
         if ((rc = stack_matvec(st, p, bh::ACT_F32_RMSNORM, bh::EPI_SWIGLU, true)) != BH_OK) return rc;
         account(p, c.n_embd * 4, c.n_ff);
         // 5. down, residual add
@@ -704,6 +707,7 @@ int bh_stack_create(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, bh_s
     const size_t o_x = take(c.n_embd), o_h = take(c.n_embd), o_qkv = take(qd + 2 * kvd), o_at = take(qd);
     const size_t o_gu = take(2 * (int64_t)c.n_ff), o_lg = take(c.n_vocab), o_cv = take(cand_max);
     const size_t o_ci = take(cand_max), o_tk = take(1), o_ps = take(1), o_rf = take(c.head_dim / 2);
+    const size_t o_ch = take(c.n_embd), o_cg = take(2 * (int64_t)c.n_ff);
     if (cudaMalloc(&st->fbuf, fl * sizeof(float)) != cudaSuccess ||
         cudaMallocHost(&st->host_tok, sizeof(int32_t)) != cudaSuccess ||
         cudaMallocHost(&st->host_x, sizeof(float) * c.n_embd) != cudaSuccess) {
@@ -720,6 +724,8 @@ int bh_stack_create(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, bh_s
     st->tok = reinterpret_cast<int32_t*>(F + o_tk);
     st->pos = reinterpret_cast<int*>(F + o_ps);
     st->rope_inv_freq = F + o_rf;
+    st->cap_h_attn = F + o_ch;
+    st->cap_gate_up = F + o_cg;
     {
         // NeoX RoPE frequencies theta^(-2j / head_dim), evaluated in double once per stack
         std::vector<float> rf((size_t)c.head_dim / 2);
@@ -912,6 +918,9 @@ int bh_stack_tensor(bh_stack* st, int layer, int which, void** ptr, int64_t* row
             case BH_T_HIDDEN: *ptr = st->h; r = 1; k = c.n_embd; break;
             case BH_T_QKV: *ptr = st->qkv; r = 1; k = (int64_t)(c.n_head + 2 * c.n_head_kv) * c.head_dim; break;
             case BH_T_ATTN: *ptr = st->attn; r = 1; k = (int64_t)c.n_head * c.head_dim; break;
+            case BH_T_H_ATTN: *ptr = st->cap_h_attn; r = 1; k = c.n_embd; break;
+            case BH_T_GATE_UP: *ptr = st->cap_gate_up; r = 1; k = 2 * (int64_t)c.n_ff; break;
+            case BH_T_FFN_ACT: *ptr = st->gu; r = 1; k = c.n_ff; break;
             default: return BH_EINVAL;
         }
     }

@@ -21,6 +21,10 @@
 //    Nothing in it needs to start at zero (each CTA writes its slots before
 //    the finisher reads them), but calls that overlap on the GPU race on it:
 //    serialize them (one stream, or events).
+//  - Device-side failures: a second static word holds the status that the
+//    kernels set when a bounded wait runs out. It is sticky: once set, every
+//    later call writes -1 as its token, until bh_noalloc_status(1) reads and
+//    clears it (the word starts at zero when the library loads).
 #include <climits>
 #include <mutex>
 
@@ -34,25 +38,31 @@ constexpr int NOALLOC_SLOTS = 4096;
 constexpr size_t NOALLOC_SCRATCH_BYTES = (size_t)NOALLOC_SLOTS * (sizeof(float) + sizeof(int32_t));
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+static __device__ int g_noalloc_status;
 
 constexpr int MAX_DEVICES = 64;
 std::mutex g_mu;
 void* g_scratch_dev[MAX_DEVICES];
+int* g_status_dev[MAX_DEVICES];
 
-// Device address of the scratch array on the current device (set-up on the
-// first call per device).
-int scratch_address(int device, unsigned char** out) {
+// Device addresses of the scratch array and the status word on the current
+// device (set-up on the first call per device).
+int scratch_address(int device, unsigned char** out, int** status) {
     if (device < 0 || device >= MAX_DEVICES) return BH_ENODEV;
     std::lock_guard<std::mutex> lock(g_mu);
     if (!g_scratch_dev[device]) {
         void* ptr = nullptr;
-        if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) {
+        void* sptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr ||
+            cudaGetSymbolAddress(&sptr, g_noalloc_status) != cudaSuccess || !sptr) {
             cudaGetLastError();
             return BH_EIO;
         }
+        g_status_dev[device] = static_cast<int*>(sptr);
         g_scratch_dev[device] = ptr;
     }
     *out = static_cast<unsigned char*>(g_scratch_dev[device]);
+    *status = g_status_dev[device];
     return BH_OK;
 }
 
@@ -73,7 +83,8 @@ extern "C" int bh_q4k_lmhead_argmax_noalloc(const void* W_q4k, int64_t N, int64_
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess) return BH_ENODEV;
     unsigned char* scratch = nullptr;
-    int rc = scratch_address(device, &scratch);
+    int* status = nullptr;
+    int rc = scratch_address(device, &scratch, &status);
     if (rc != BH_OK) return rc;
 
     // a context on the stack: launch tuning defaults, no device memory
@@ -82,7 +93,7 @@ extern "C" int bh_q4k_lmhead_argmax_noalloc(const void* W_q4k, int64_t N, int64_
     if (cudaDeviceGetAttribute(&local.num_sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
         return BH_ENODEV;
     bh::MatvecParams p = bh::base_params(&local, W_q4k, N, K, B, logits_opt);
-    p.status = nullptr;
+    p.status = status;
     p.xf = x;
     const int grid = bh::plan_for(&local, p, 0);
     if (grid < 0) return grid;
@@ -93,5 +104,21 @@ extern "C" int bh_q4k_lmhead_argmax_noalloc(const void* W_q4k, int64_t N, int64_
     o.stream = static_cast<cudaStream_t>(stream);
     o.grid = grid;
     if ((rc = bh::launch_matvec(p, fold, bh::ACT_F32, bh::EPI_ARGMAX, o)) != BH_OK) return rc;
-    return bh::launch_argmax_finish(p.cand_val, p.cand_idx, grid, B, tok_out, max_opt, o.stream, false);
+    return bh::launch_argmax_finish(p.cand_val, p.cand_idx, grid, B, tok_out, max_opt, o.stream, false, status);
+}
+
+extern "C" int bh_noalloc_status(int clear) {
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return BH_ENODEV;
+    unsigned char* scratch = nullptr;
+    int* status = nullptr;
+    int rc = scratch_address(device, &scratch, &status);
+    if (rc != BH_OK) return rc;
+    // the word is read after every kernel queued on this device has finished
+    if (cudaDeviceSynchronize() != cudaSuccess) return BH_EIO;
+    int st = 0;
+    if (cudaMemcpy(&st, status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return BH_EIO;
+    if (clear && st && cudaMemset(status, 0, sizeof(int)) != cudaSuccess) return BH_EIO;
+    if (st == bh::ST_TIMEOUT) return BH_ETIMEDOUT;
+    return st == bh::ST_OK ? BH_OK : BH_EINVAL;
 }

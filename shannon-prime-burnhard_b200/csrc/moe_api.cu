@@ -40,6 +40,7 @@ int ensure_moe_scratch(bh_ctx* ctx, size_t bytes) {
     if (ctx->moe_scratch_bytes >= bytes) return BH_OK;
     if (ctx->moe_scratch) {
         cudaDeviceSynchronize();
+        bh::unregister_barrier_words(ctx, ctx->moe_scratch);
         cudaFree(ctx->moe_scratch);
         ctx->moe_scratch = nullptr;
         ctx->moe_scratch_bytes = 0;
@@ -55,6 +56,7 @@ int ensure_moe_scratch(bh_ctx* ctx, size_t bytes) {
         return BH_EIO;
     }
     ctx->moe_scratch_bytes = bytes;
+    bh::register_barrier_words(ctx, ctx->moe_scratch);
     return BH_OK;
 }
 
@@ -70,6 +72,7 @@ bh::MoeParams moe_base(bh_ctx* ctx, int n_tok, int n_expert, int n_embd, int n_f
     p.e_lo = 0;
     p.e_hi = n_expert;
     p.combine = 1;
+    p.gbar_wait = ctx->barrier_wait_cycles;
     p.status = ctx->d_status;
 #ifdef BH_TRACE
     p.trace = ctx->trace;
@@ -340,7 +343,10 @@ int bh_moe_stack_free(bh_moe_stack* st) {
     if (st->wbuf) cudaFree(st->wbuf);
     if (st->fbuf) cudaFree(st->fbuf);
     if (st->ids) cudaFree(st->ids);
-    if (st->gbar) cudaFree(st->gbar);
+    if (st->gbar) {
+        bh::unregister_barrier_words(st->ctx, st->gbar);
+        cudaFree(st->gbar);
+    }
     if (st->host_h) cudaFreeHost(st->host_h);
     if (st->stream) cudaStreamDestroy(st->stream);
     delete st;
@@ -375,6 +381,7 @@ int bh_moe_stack_create(bh_ctx* ctx, const bh_moe_config* cfg, uint64_t seed, bh
         bh_moe_stack_free(st);
         return BH_ENOMEM;
     }
+    bh::register_barrier_words(ctx, st->gbar);
     float* f = st->fbuf;
     st->logits = f; f += up4(n_logit);
     st->norm = f; f += up4(n_norm);
@@ -493,6 +500,11 @@ int bh_moe_stack_tensor(bh_moe_stack* st, int layer, int which, void** ptr, int6
     if (which == BH_MOE_HIDDEN) {
         *ptr = st->h;
         if (bytes) *bytes = (int64_t)c.n_tok * c.n_embd * 4;
+        return BH_OK;
+    }
+    if (which == BH_MOE_BARRIER) {
+        *ptr = st->gbar;
+        if (bytes) *bytes = 256;
         return BH_OK;
     }
     if (layer < 0 || layer >= c.n_layer) return BH_EINVAL;

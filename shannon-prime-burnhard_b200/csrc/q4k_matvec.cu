@@ -15,6 +15,7 @@
 //    reproduces the reference's integer sums and fp32 fold bit for bit.
 #include "bh_common.cuh"
 #include "bh_kernels.cuh"
+#include "bh_math.cuh"
 #include "q4k_core.cuh"
 #include "q8k_device.cuh"
 
@@ -89,7 +90,7 @@ __device__ __forceinline__ void preload_gamma(const MatvecParams& p, float (&gp)
 // top_up(): called once by every warp after its first round of global loads
 // is issued (the warp's remaining weight copies go out behind them).
 template <int FOLD, int SRC, int W, class TopUp>
-__device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* red, int ctid,
+__device__ void stage_activations(const MatvecParams& p, uint8_t* act, double* red, int ctid,
                                   const float (&gp)[STAGE_UF][8], TopUp&& top_up) {
     const int warp = ctid >> 5, lane = ctid & 31;
     const int nblk = p.B * p.nb;
@@ -142,32 +143,41 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
         top_up();  // (no-op for warps that already did)
         return;
     }
-    // fp32 sources. When every warp's blocks fit one round (nblk <= W*UF, the
-    // decode shapes), all global loads are issued at once and RMSNorm's sum
-    // of squares is taken from the loaded registers: per block (lane sums in
-    // element order, then an xor butterfly), per column (the blocks' sums
-    // through shared memory, one per lane, then an xor butterfly, in every
-    // warp). The order is fixed, so every warp of every CTA derives the same
-    // scale. Larger batches fall back to a separate strided pass for the sum
-    // of squares.
+    // fp32 sources. RMSNorm follows rms_norm_f32 (ggml-cpu/ops.cpp): every
+    // square is a binary32 product, the squares are summed in double,
+    // mean = (float)(sum / K), scale = 1 / sqrtf(mean + eps), x * scale, then
+    // the norm weight (ggml_mul). The reference sums sequentially; here the
+    // double sum runs as a tree, which changes the double result only in its
+    // last bits and the binary32 mean only when the sum lies within that of a
+    // binary32 rounding boundary. When every warp's blocks fit one round
+    // (nblk <= W*UF, the decode shapes), all global loads are issued at once
+    // and the sum of squares is taken from the loaded registers: per block
+    // (lane sums in element order, then an xor butterfly), per column (the
+    // blocks' sums through shared memory, one per lane, then an xor
+    // butterfly, in every warp). The order is fixed, so every warp of every
+    // CTA derives the same scale. Larger batches fall back to a separate
+    // strided pass for the sum of squares.
     constexpr int UF = stage_uf<SRC>();
     __shared__ float s_scale[BH_MAX_BATCH];
     const bool one_round = nblk <= W * UF;
+    auto rms_scale = [&](double sum) {
+        const float mean = __double2float_rn(__ddiv_rn(sum, (double)p.K));
+        return __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+    };
     if (SRC == ACT_F32_RMSNORM && !one_round) {
         for (int b = 0; b < p.B; ++b) {
             const float* h = p.xf + (int64_t)b * p.K;
-            float ss = 0.f;
+            double ss = 0.0;
 #pragma unroll 4
-            for (int i = ctid; i < p.K; i += W * 32) ss = __fadd_rn(ss, __fmul_rn(h[i], h[i]));
+            for (int i = ctid; i < p.K; i += W * 32) ss = __dadd_rn(ss, (double)__fmul_rn(h[i], h[i]));
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+            for (int off = 16; off > 0; off >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
             if (lane == 0) red[warp] = ss;
             named_bar(1, W * 32);
             if (ctid == 0) {
-                float t = 0.f;
-                for (int w = 0; w < W; ++w) t = __fadd_rn(t, red[w]);
-                const float mean = __fdiv_rn(t, (float)p.K);
-                s_scale[b] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+                double t = 0.0;
+                for (int w = 0; w < W; ++w) t = __dadd_rn(t, red[w]);
+                s_scale[b] = rms_scale(t);
             }
             named_bar(1, W * 32);
         }
@@ -210,11 +220,11 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
 #pragma unroll
             for (int u = 0; u < UF; ++u) {
                 const int blk = blk0 + u * W;
-                float ss = 0.f;
+                double ss = 0.0;
 #pragma unroll
-                for (int t = 0; t < 8; ++t) ss = __fadd_rn(ss, __fmul_rn(v[u][t], v[u][t]));
+                for (int t = 0; t < 8; ++t) ss = __dadd_rn(ss, (double)__fmul_rn(v[u][t], v[u][t]));
 #pragma unroll
-                for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+                for (int off = 16; off > 0; off >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
                 if (lane == 0 && blk < nblk) red[blk] = ss;
             }
             named_bar(1, W * 32);
@@ -224,11 +234,10 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, float* re
             for (int u = 0; u < UF; ++u) {
                 const int blk = blk0 + u * W;
                 const int b = (blk < nblk ? blk : 0) / p.nb;
-                float t = lane < p.nb ? red[b * p.nb + lane] : 0.f;
+                double t = lane < p.nb ? red[b * p.nb + lane] : 0.0;
 #pragma unroll
-                for (int off = 16; off > 0; off >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, off));
-                const float mean = __fdiv_rn(t, (float)p.K);
-                scale_u[u] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+                for (int off = 16; off > 0; off >>= 1) t = __dadd_rn(t, __shfl_xor_sync(0xffffffffu, t, off));
+                scale_u[u] = rms_scale(t);
             }
         }
         auto quantize_block = [&](int u) {
@@ -270,8 +279,13 @@ __device__ __forceinline__ void finish_row(const MatvecParams& p, const float (&
     const float v = row_value<FOLD, TPR>(acc, accm, rgrp);
     if (has_row && t == 0) {
         float* yp = p.y + (int64_t)b * p.ldy + row;
-        if (EPI == EPI_ADD) *yp = __fadd_rn(*yp, v);
-        else if (EPI != EPI_ARGMAX || p.y) *yp = v;
+        if (EPI == EPI_ADD) {
+            const float hv = __fadd_rn(*yp, v);  // ggml_add(x, W.a)
+            *yp = hv;
+            if (p.capture) p.capture[(int64_t)b * p.ldy + row] = hv;
+        } else if (EPI != EPI_ARGMAX || p.y) {
+            *yp = v;
+        }
         if (EPI == EPI_ARGMAX && v > best_v) { best_v = v; best_i = (int)row; }
     }
 }
@@ -293,8 +307,9 @@ __global__ void __launch_bounds__(dense_warps(NB) * 32, 1) q4k_matvec_kernel(con
     constexpr int R = 32 / TPR;
     constexpr int L = 8 / TPR;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float s_red[DENSE_MAX_WARPS * 4];
+    __shared__ float s_red[DENSE_MAX_WARPS];
     __shared__ int s_redi[DENSE_MAX_WARPS];
+    __shared__ double s_ssq[DENSE_MAX_WARPS * STAGE_UF];  // RMSNorm: per-block (or per-warp) sums of squares
     BH_TRACE_AT(0);
 
     uint8_t* act = smem + p.act_off;
@@ -359,7 +374,7 @@ __global__ void __launch_bounds__(dense_warps(NB) * 32, 1) q4k_matvec_kernel(con
     pdl_trigger();
     pdl_wait();
     BH_TRACE_AT(5);
-    stage_activations<FOLD, SRC, W>(p, act, s_red, threadIdx.x, gpre, [&]() {
+    stage_activations<FOLD, SRC, W>(p, act, s_ssq, threadIdx.x, gpre, [&]() {
         while (issued < ring_fill) issue_next();
     });
     __syncthreads();
@@ -429,7 +444,11 @@ BH_UNROLL(BH_KB_UNROLL)
                 const float u = __shfl_down_sync(FULLM, v, 16);
                 if (live && t == 0 && rgrp < R / 2) {
                     const int64_t i = (r_begin + (int64_t)(warp + j * W) * R) / 2 + rgrp;
-                    p.y[(int64_t)b * p.ldy + i] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.f, expf(-v))), u);
+                    p.y[(int64_t)b * p.ldy + i] = __fmul_rn(silu_ggml(v), u);  // ggml_silu then ggml_mul
+                    if (p.capture) {  // the gate and up rows before the SwiGLU
+                        p.capture[(int64_t)b * 2 * p.ldy + i] = v;
+                        p.capture[(int64_t)b * 2 * p.ldy + p.ldy + i] = u;
+                    }
                 }
             } else {
                 finish_row<FOLD, EPI, TPR>(p, acc[b], accm[b], rgrp, t, b, live, r_begin + rin, best_v[b], best_i[b]);
@@ -525,17 +544,17 @@ int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int t
 template <int FOLD, int NB, int SRC, int EPI, bool PART, int TPR>
 static int launch_t(const MatvecParams& p, const LaunchOpts& o, int grid) {
     auto kern = q4k_matvec_kernel<FOLD, NB, SRC, EPI, PART, TPR>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        // all kernels of a step ask for the same (largest) shared-memory
-        // carveout, so consecutive launches can share an SM without the SM
-        // having to drain and reconfigure between them
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
-            cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                 cudaSharedmemCarveoutMaxShared) != cudaSuccess)
-            return BH_EIO;
-        attr_set = true;
-    }
+    static std::atomic<uint64_t> attr_devices{0};
+    // all kernels of a step ask for the same (largest) shared-memory
+    // carveout, so consecutive launches can share an SM without the SM
+    // having to drain and reconfigure between them
+    if (!attrs_on_device(attr_devices, [&] {
+            return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) ==
+                       cudaSuccess &&
+                   cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                        cudaSharedmemCarveoutMaxShared) == cudaSuccess;
+        }))
+        return BH_EIO;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(dense_warps(NB) * 32);

@@ -114,7 +114,7 @@ __device__ __forceinline__ void moe_route(const MoeParams& p, const float* logit
             for (int i = lane; i < E; i += 32) mx = fmaxf(mx, pr[i]);
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-            for (int i = lane; i < E; i += 32) pr[i] = exp_cw(__fsub_rn(pr[i], mx));
+            for (int i = lane; i < E; i += 32) pr[i] = exp_ggml(__fsub_rn(pr[i], mx));
             __syncwarp();
             // per-8 fp32 partial sums ((p4+p0)+(p6+p2)) + ((p5+p1)+(p7+p3)), summed in double
             const int ng = E / 8;
@@ -393,7 +393,7 @@ __device__ void stage_pairs(const MoeParams& p, const MoeTable& tb, int u_lo, in
                                  ld[r][3].x, ld[r][3].y, ld[r][3].z, ld[r][3].w};
             float v[8];
 #pragma unroll
-            for (int t = 0; t < 8; ++t) v[t] = __fmul_rn(silu_cw(gv[t]), uv[t]);
+            for (int t = 0; t < 8; ++t) v[t] = __fmul_rn(silu_ggml(gv[t]), uv[t]);
             const Q8Block qb = q8k_quantize_warp(v, lane);
             uint8_t* dst = act + blk * ACT_BLOCK_BYTES;
             stage_codes<FOLD>(dst, qb.q, lane);
@@ -407,7 +407,7 @@ __device__ void stage_pairs(const MoeParams& p, const MoeTable& tb, int u_lo, in
 // the last arrival zeroes the count and advances the generation the others
 // wait on, in one atomic on the same word. The wait is bounded; false after a
 // timeout (status recorded).
-__device__ bool grid_barrier(unsigned int* gbar, int* status) {
+__device__ bool grid_barrier(unsigned int* gbar, int* status, long long wait_cycles) {
     __shared__ int s_ok;
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -425,7 +425,7 @@ __device__ bool grid_barrier(unsigned int* gbar, int* status) {
                 unsigned int g;
                 asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(g) : "l"(gbar) : "memory");
                 if ((g >> 16) != gen) break;
-                if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+                if (clock64() - t0 > wait_cycles) {
                     ok = 0;
                     set_status(status, ST_TIMEOUT);
                     break;
@@ -613,7 +613,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_moe_kernel(const __grid_con
         for (int ph = 0; ph < 2; ++ph) {
             if (ph == 1) {
                 MOE_TRACE_AT(5);
-                ok = grid_barrier(p.gbar, p.status) && ok;
+                ok = grid_barrier(p.gbar, p.status, p.gbar_wait) && ok;
                 if (dn.t_end > dn.t_begin && __syncthreads_and(ok)) stage_pairs<FOLD>(p, tb, u_lo, u_hi, act, s_qbase);
                 __syncthreads();
                 MOE_TRACE_AT(6);
@@ -672,7 +672,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_moe_kernel(const __grid_con
         }
         MOE_TRACE_AT(7);
         if (!p.combine) return;  // the caller sums dout over the ranks, then combines
-        ok = grid_barrier(p.gbar, p.status) && ok;
+        ok = grid_barrier(p.gbar, p.status, p.gbar_wait) && ok;
         if (!__syncthreads_and(ok)) return;
 
         // ---- combine: ggml_mul (fp32 product) then ggml_sum_rows over the
@@ -689,7 +689,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_moe_kernel(const __grid_con
             p.out[idx] = p.residual ? __fadd_rn(p.out[idx], r) : r;
         }
         // the next layer's RMSNorm reads every CTA's slice of h
-        if (l + 1 < p.n_layer && !grid_barrier(p.gbar, p.status)) return;
+        if (l + 1 < p.n_layer && !grid_barrier(p.gbar, p.status, p.gbar_wait)) return;
     }
 }
 
@@ -773,14 +773,14 @@ int moe_plan(MoeParams& p, int smem_cap, int stage_target) {
 template <int FOLD, int NB>
 static int launch_moe_t(const MoeParams& p, const LaunchOpts& o) {
     auto kern = q4k_moe_kernel<FOLD, NB>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
-            cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                 cudaSharedmemCarveoutMaxShared) != cudaSuccess)
-            return BH_EIO;
-        attr_set = true;
-    }
+    static std::atomic<uint64_t> attr_devices{0};
+    if (!attrs_on_device(attr_devices, [&] {
+            return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) ==
+                       cudaSuccess &&
+                   cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                        cudaSharedmemCarveoutMaxShared) == cudaSuccess;
+        }))
+        return BH_EIO;
     // every CTA must be resident (grid barriers): clamp to what fits
     int dev = 0, nsm = 0, occ = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||

@@ -262,8 +262,11 @@ int launch_q4k_dequantize(const uint8_t* w, int64_t N, int64_t K, float* out, cu
 // candidates carry the smallest index among equal maxima.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) argmax_finish_kernel(const float* __restrict__ cv, const int32_t* __restrict__ ci,
-                                                            int ncand, int B, int32_t* tok, float* val) {
+                                                            int ncand, int B, int32_t* tok, float* val,
+                                                            const int* status) {
     pdl_wait();
+    // a bounded wait of the matvec before it ran out (status set): no token
+    const bool failed = status && *reinterpret_cast<const volatile int*>(status) != ST_OK;
     __shared__ float sv[8];
     __shared__ int si[8];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -287,7 +290,7 @@ __global__ void __launch_bounds__(256) argmax_finish_kernel(const float* __restr
             for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
                 if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
             if (bi == 0x7fffffff) bi = 0;  // all candidates NaN: index 0, as the CPU loop leaves it
-            tok[b] = bi;
+            tok[b] = failed ? -1 : bi;
             if (val) val[b] = bv;
         }
         __syncthreads();
@@ -295,7 +298,7 @@ __global__ void __launch_bounds__(256) argmax_finish_kernel(const float* __restr
 }
 
 int launch_argmax_finish(const float* cand_val, const int32_t* cand_idx, int ncand, int B, int32_t* tok_out,
-                         float* val_out, cudaStream_t s, bool pdl) {
+                         float* val_out, cudaStream_t s, bool pdl, const int* status) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1);
     cfg.blockDim = dim3(256);
@@ -305,15 +308,14 @@ int launch_argmax_finish(const float* cand_val, const int32_t* cand_idx, int nca
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl ? 1 : 0;
-    static bool attr_set = false;
-    if (!attr_set) {
-        // the same shared-memory carveout as the matvec it follows (no SM reconfiguration between them)
-        if (cudaFuncSetAttribute(argmax_finish_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                 cudaSharedmemCarveoutMaxShared) != cudaSuccess)
-            return BH_EIO;
-        attr_set = true;
-    }
-    return cudaLaunchKernelEx(&cfg, argmax_finish_kernel, cand_val, cand_idx, ncand, B, tok_out, val_out) ==
+    static std::atomic<uint64_t> attr_devices{0};
+    // the same shared-memory carveout as the matvec it follows (no SM reconfiguration between them)
+    if (!attrs_on_device(attr_devices, [] {
+            return cudaFuncSetAttribute(argmax_finish_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                        cudaSharedmemCarveoutMaxShared) == cudaSuccess;
+        }))
+        return BH_EIO;
+    return cudaLaunchKernelEx(&cfg, argmax_finish_kernel, cand_val, cand_idx, ncand, B, tok_out, val_out, status) ==
                    cudaSuccess
                ? BH_OK
                : BH_EIO;

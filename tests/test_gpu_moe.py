@@ -226,3 +226,39 @@ def test_moe_peer_exchange_one_rank_matches_moe(ctx, bh):
     finally:
         recv.close()
         box.close()
+
+
+def test_moe_barrier_timeout_then_bit_exact(bh, oracle):
+    """A grid-barrier wait that runs out leaves its arrivals counted; clearing
+    the timeout through bh_device_status resets the barrier, and the next
+    step is bit-exact again. The timeout is made without a fault: the barrier
+    word is preset so that no arrival is ever the last one (a flag nothing
+    sets), with a short wait bound, so every CTA gives up and returns."""
+    import torch
+
+    ctx = bh.Context(0)
+    try:
+        ctx.tune(bh.TUNE_BARRIER_WAIT, 20)  # ~0.5 ms per barrier wait
+        cfg = bh.default_moe_config(**SMALL, n_tok=2)
+        st = bh.MoeStack(ctx, cfg, seed=41)
+        h0 = oracle.normal((2, cfg.n_embd), 42, 0.0, 1.0)
+        ref = stack_oracle_step(oracle, st, bh, h0)
+        out = torch.empty((2, cfg.n_embd), device="cuda")
+        st.step(to_dev(h0), out)
+        torch.cuda.synchronize()
+        assert (out.cpu().numpy().view(np.uint32) == ref.view(np.uint32)).all()
+        ptr, nbytes = st.tensor(-1, bh.MOE_BARRIER)
+        words = bh.device_view(ptr, nbytes // 4, "<u4")
+        words[0] = 0x8000  # arrivals start at 32768: the count never reaches the grid size
+        torch.cuda.synchronize()
+        st.step(to_dev(h0), out)
+        assert ctx.status(clear=True) == bh.BH_ETIMEDOUT
+        assert int(words.cpu()[0]) == 0  # reset with the clear
+        out.fill_(0)
+        st.step(to_dev(h0), out)
+        torch.cuda.synchronize()
+        assert (out.cpu().numpy().view(np.uint32) == ref.view(np.uint32)).all()
+        assert ctx.status() == 0
+        st.close()
+    finally:
+        ctx.close()

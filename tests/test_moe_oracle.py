@@ -10,27 +10,33 @@ import pytest
 import oracle as om
 
 
-def test_expf_within_one_ulp(oracle):
-    x = np.concatenate([np.linspace(-103.9, 88.7, 400_001, dtype=np.float32),
-                        oracle.normal((200_000,), 5, 0.0, 8.0)]).astype(np.float32)
-    y = oracle.expf(x).astype(np.float64)
+def test_expf_bit_exact_with_reference(oracle, reference):
+    """The oracle's exp is one lane of ggml's AVX2 ggml_v_expf: equal bit for
+    bit to the reference's compiled kernel over the whole range it is used
+    on, including the two-factor scaling (|n| > 126) and saturation
+    (|n| > 192) branches, and within ggml's stated bound (1.45 + 0.5 ulp) of
+    the true exponential."""
+    x = np.concatenate([np.linspace(-110.0, 95.0, 800_000, dtype=np.float32),
+                        oracle.normal((200_000,), 5, 0.0, 8.0),
+                        np.array([0.0, -0.0, 88.3, 88.8, -87.0, -100.0, -104.0, 1e-30, -1e-30,
+                                  np.inf, -np.inf, np.nan, 200.0, -200.0, 135.0, -135.0], np.float32)])
+    x = np.concatenate([x, np.zeros((-x.size) % 8, np.float32)]).astype(np.float32)
+    a, b = oracle.expf(x), reference.expf(x)
+    nan = np.isnan(x)
+    assert np.isnan(a[nan]).all() and np.isnan(b[nan]).all()  # (NaN payloads may differ)
+    assert np.array_equal(a[~nan].view(np.uint32), b[~nan].view(np.uint32))
+    y = a.astype(np.float64)
     ref = np.exp(x.astype(np.float64))
-    normal = (ref > 1.2e-38) & (ref < 3.4e38)
+    normal = np.isfinite(x) & (ref > 1.2e-38) & (ref < 3.4e38)
     ulp = np.spacing(ref[normal].astype(np.float32)).astype(np.float64)
-    assert (np.abs(y[normal] - ref[normal]) / ulp).max() <= 1.0
-    assert oracle.expf(np.array([0.0], np.float32))[0] == 1.0
-    specials = oracle.expf(np.array([np.nan, np.inf, -np.inf, 100.0, -200.0], np.float32))
-    assert np.isnan(specials[0]) and specials[1] == np.inf and specials[2] == 0.0
-    assert specials[3] == np.inf and specials[4] == 0.0
+    assert (np.abs(y[normal] - ref[normal]) / ulp).max() <= 1.96
 
 
-def test_silu_matches_reference(oracle, reference):
-    x = oracle.normal((200_000,), 3, 0.0, 4.0)
+def test_silu_bit_exact_with_reference(oracle, reference):
+    x = np.concatenate([oracle.normal((200_000,), 3, 0.0, 4.0),
+                        np.linspace(-120.0, 120.0, 4000, dtype=np.float32)]).astype(np.float32)
     a, b = oracle.silu(x), reference.silu(x)
-    rel = np.abs(a - b) / np.maximum(np.abs(b), 1e-30)
-    # ggml_v_silu's own exp differs by a few ulp
-    assert rel.max() < 6e-7
-    assert np.mean(a == b) > 0.5
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
 def ref_route(reference, logits, k, norm=True):
@@ -52,11 +58,18 @@ def ref_route(reference, logits, k, norm=True):
 
 @pytest.mark.parametrize("n_expert,k", [(128, 8), (64, 4), (256, 8), (16, 1), (9, 2)])
 def test_route_matches_reference(oracle, reference, n_expert, k):
+    """Routing equals the reference's soft_max + top-k + renormalisation bit
+    for bit when n_expert is a multiple of 8 (all through ggml_v_expf); the
+    reference's n % 8 tail goes through libm expf, which the restatement does
+    not reproduce, so 9 experts are held to 1e-5 / 1e-6."""
     logits = oracle.normal((32, n_expert), 100 + n_expert + k, 0.0, 1.0)
     ids, w = oracle.moe_route(logits, k)
     rids, rw = ref_route(reference, logits, k)
     assert (ids == rids).all()
-    np.testing.assert_allclose(w, rw, rtol=1e-5, atol=1e-6)
+    if n_expert % 8 == 0:
+        assert np.array_equal(w.view(np.uint32), rw.view(np.uint32))
+    else:
+        np.testing.assert_allclose(w, rw, rtol=1e-5, atol=1e-6)
     assert np.allclose(w.sum(1), 1.0, atol=1e-6)
 
 
@@ -74,7 +87,7 @@ def test_route_unnormalised_is_softmax(oracle, reference):
     ids, w = oracle.moe_route(logits, 8, norm=False)
     p = reference.soft_max(logits)
     for t in range(8):
-        np.testing.assert_allclose(w[t], p[t][ids[t]], rtol=1e-5, atol=1e-7)
+        assert np.array_equal(w[t].view(np.uint32), p[t][ids[t]].view(np.uint32))
 
 
 def test_rmsnorm_restatement(oracle):
@@ -119,8 +132,8 @@ def test_moe_ffn_internal_consistency(oracle):
 
 def test_moe_ffn_vs_reference_kernels(oracle, reference):
     """The same block composed from the reference's own Q8_K quantizer, x86
-    vec_dot and SiLU: only the SiLU exp differs, so outputs agree to a small
-    tolerance (an occasional Q8_K code of silu(gate)*up flips)."""
+    vec_dot and SiLU (ggml_vec_silu_f32) with the slot-order double sum: the
+    restatement equals it bit for bit."""
     E, D, F, k, T = 8, 512, 256, 4, 2
     gate, up, down = small_banks(oracle, E, D, F, 70)
     cur = oracle.normal((T, D), 80, 0.0, 1.0)
@@ -138,5 +151,4 @@ def test_moe_ffn_vs_reference_kernels(oracle, reference):
             d = reference.matvec_rows(db[e], D, F, reference.quantize_q8k(par[None]), 1, om.FOLD_X86)[0]
             acc += (d * w[t, s]).astype(np.float64)
         ref_out = acc.astype(np.float32)
-        scale = np.abs(ref_out).max()
-        assert np.abs(out[t] - ref_out).max() <= 5e-3 * scale
+        assert np.array_equal(out[t].view(np.uint32), ref_out.view(np.uint32))
