@@ -13,9 +13,12 @@ e2e    = the same metric through bh_stack_decode_host: the embedding comes
 N > 1  = one process per GPU, each decoding its own sequence with its own
          copy of the weights (replicas: no data-path collective); the value is
          the sum over ranks, timed as the slowest rank.
---impl reference times the reference's own CPU path (ggml quantize_row_q8_K +
-ggml_vec_dot_q4_K_q8_K through oracle/_ref, all host threads) on the same
-weights and the same step.
+--impl reference times the reference's own CPU implementation of the step:
+the decode graph the reference engine builds (forward.cpp build_block_decode
++ LM head) on the reference's own ggml CPU backend (oracle/_ref, compiled
+from the reference tree), all host threads, weights generated and quantized
+on the host (ggml_quantize_chunk); it loads nothing of this repository's
+product library.
 """
 from __future__ import annotations
 
@@ -267,44 +270,126 @@ def bench_moe(bh, ctx, world: int, rank: int, steps: int) -> dict:
 
 
 # ---------------------------------------------------------------- CPU path
-def cpu_reference_step_fn(st, nthreads: int):
-    """The reference's CPU decode step on host copies of the stack."""
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_graph_stack(cfg: dict, nthreads: int):
+    """The reference's decode step on the host (oracle/ref_stack.py): the
+    engine's ggml graph on the reference's ggml CPU backend, host-generated
+    weights (4 distinct layers cycled over the 36, plus the LM head)."""
+    import ref_stack
+
+    return ref_stack.make_host_stack(cfg, SEED, nthreads, n_distinct=4, kv_pos=KV_POS)
+
+
+def cpu_legs(nthreads: int, budget_s: float = 3.0) -> dict:
+    """BASELINE.md's three CPU legs on config 1 (Q4_K 4096 x 4096, batch 1):
+    (a) one ggml_mul_mat graph node on all host threads, (b) the same on one
+    thread, (c) the direct ggml_vec_dot_q4_K_q8_K row loop (one thread).
+    Each rep reads another of 64 weight copies (604 MB, beyond any host
+    cache), so the figures are DRAM-bound. GB/s = weight + activation +
+    output bytes of one matvec / time."""
     import numpy as np
 
     import oracle as om
-    from cpu_stack import CpuStack, stack_to_cpu
 
-    cfg, w, norms, kc, vc = stack_to_cpu(st)
-    if os.path.exists(om.REF_SO) and om.Reference().has_avx2:
-        ref = om.Reference()
-        scratch = {}
+    n = k = 4096
+    L = om.graph_lib()
+    w0 = np.empty(n * om.q4k_row_bytes(k), np.uint8)
+    tmp = np.empty((n, k), np.float32)
+    L.rg_fill_normal(om._ptr(tmp), tmp.size, 0, SEED + 1, 0.0, 0.02, nthreads)
+    L.rg_quantize_q4k(om._ptr(tmp), om._ptr(w0), n, k, nthreads)
+    copies = np.empty((64, w0.size), np.uint8)
+    copies[:] = w0
+    x = np.ascontiguousarray(np.random.default_rng(SEED).standard_normal((1, k)), dtype=np.float32)
+    y = np.empty((1, n), np.float32)
+    by = n * (k // 256) * 144 + (k // 256) * 292 + n * 4
+    out = {"workload": "Q4_K 4096 x 4096 matvec, batch 1 (config 1)", "cpu": cpu_model(),
+           "isa": "x86 AVX2/FMA/F16C branch of ggml (arch/x86/quants.c)" if L.rg_has_avx2() else "generic",
+           "weight_copies": 64}
 
-        def mv(wb, n, k, x):
-            key = (n, k)
-            if key not in scratch:
-                scratch[key] = (np.empty(x.shape[0] * om.q8k_row_bytes(k), np.uint8), np.empty((x.shape[0], n), np.float32))
-            xq, y = scratch[key]
-            return ref.mul_mat(wb, n, k, x, nthreads, xq_scratch=xq, out=y).copy()
+    def run(fn):
+        fn(0)
+        t0 = time.perf_counter()
+        reps = 0
+        while reps < 8 or time.perf_counter() - t0 < budget_s:
+            fn(reps % 64)
+            reps += 1
+            if reps >= 4096:
+                break
+        sec = (time.perf_counter() - t0) / reps
+        return {"us": round(sec * 1e6, 1), "GBps": round(by / sec / 1e9, 2), "reps": reps}
 
-        kind = "reference"
-    else:
-        o = om.Oracle()
-
-        def mv(wb, n, k, x):
-            return o.matvec(wb, n, k, o.quantize_q8k(x), x.shape[0], om.FOLD_X86, nthreads)
-
-        kind = "port"
-    cpu = CpuStack(cfg, w, norms, kc, vc, mv)
-    return cpu, kind
+    out["a_graph_all_threads"] = dict(run(lambda i: om.graph_mul_mat(copies[i], n, k, x, nthreads, out=y)),
+                                      threads=nthreads)
+    out["b_graph_one_thread"] = dict(run(lambda i: om.graph_mul_mat(copies[i], n, k, x, 1, out=y)), threads=1)
+    out["c_direct_row_loop"] = dict(run(lambda i: L.rg_vec_dot_rows(om._ptr(copies[i]), n, k, om._ptr(x),
+                                                                    om._ptr(y))), threads=1)
+    return out
 
 
-def time_cpu_steps(cpu, x, steps: int, budget_s: float):
+def time_cpu_steps(g, x, pos: int, nthreads: int, steps: int, budget_s: float | None):
     t0 = time.perf_counter()
     n = 0
-    while n < steps and (n == 0 or time.perf_counter() - t0 < budget_s):
-        cpu.step(x, KV_POS)
+    while n < steps and (budget_s is None or n == 0 or time.perf_counter() - t0 < budget_s):
+        g.decode(x, pos, nthreads, logits=False)
         n += 1
     return (time.perf_counter() - t0) / n, n
+
+
+def step_bytes_of(cfg: dict) -> int:
+    """Algorithmic bytes of one decode step's matvecs (the same count as
+    bh_stack_info's): weights, the activations each reads (fp32 input, twice
+    for the RMSNorm prologues), and the outputs."""
+    qd, kvd = cfg["n_head"] * cfg["head_dim"], cfg["n_head_kv"] * cfg["head_dim"]
+    E, F = cfg["n_embd"], cfg["n_ff"]
+
+    def w(r, k):
+        return r * (k // 256) * 144
+
+    layer = (w(qd + 2 * kvd, E) + E * 4 + (qd + 2 * kvd) * 4 + w(E, qd) + qd * 4 + E * 4 +
+             w(2 * F, E) + E * 4 + F * 4 + w(E, F) + F * 4 + E * 4)
+    return cfg["n_layer"] * layer + w(cfg["n_vocab"], E) + E * 4 + cfg["n_vocab"] * 4
+
+
+def run_reference_arm(args, cfg: dict, workload: dict) -> None:
+    """--impl reference: rank 0 times the reference's CPU step; others exit."""
+    import numpy as np
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    nthreads = len(os.sched_getaffinity(0))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    g = cpu_graph_stack(cfg, nthreads)
+    x = np.random.default_rng(X_SEED).standard_normal(cfg["n_embd"]).astype(np.float32)
+    for _ in range(args.warmup):
+        g.decode(x, KV_POS, nthreads, logits=False)
+    sec, n = time_cpu_steps(g, x, KV_POS, nthreads, args.steps, None)
+    g.close()
+    v = step_bytes_of(cfg) / sec / 1e9
+    legs = cpu_legs(nthreads)
+    sample = (f"{n} full decode steps ({cfg['n_layer']} layers + {cfg['n_vocab']}-row LM head) of the reference "
+              f"engine's ggml graph on the reference's ggml CPU backend, {nthreads} host threads; weights: "
+              f"{min(4, cfg['n_layer'])} distinct seeded layers cycled over the {cfg['n_layer']}, quantized by "
+              f"ggml_quantize_chunk on the host")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": n, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
+        "tokens_per_s": round(1.0 / sec, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q4_K x q8_K (int8 dot, fp32 fold)", "data": "synthetic",
+        "config": workload,
+        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": nthreads, "kind": "reference",
+                         "sample": sample, "cpu": cpu_model()},
+        "cpu_legs": legs,
+        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
 
 
 # ---------------------------------------------------------------- main
@@ -320,6 +405,19 @@ def main() -> None:
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
+    # BASELINE config 2 (the values of bh_stack_default_config)
+    cfg_d = dict(n_layer=args.layers or 36, n_embd=4096, n_head=32, n_head_kv=8, head_dim=128, n_ff=12288,
+                 n_vocab=151936, n_ctx=128, rms_eps=1e-6, rope_theta=1e6)
+    world_env = int(os.environ.get("WORLD_SIZE", "1"))
+    workload = {"workload": "qwen3-8b-shaped decode block stack (config 2), batch 1",
+                **{k: cfg_d[k] for k in ("n_layer", "n_embd", "n_head", "n_head_kv", "head_dim", "n_ff", "n_vocab")},
+                "kv_positions": KV_POS + 1, "weights": "random-init N(0,0.02) quantized to Q4_K",
+                "l2": "no flush needed: 4.26 GB of weights streamed per step >> 126 MB L2",
+                "parallelism": f"replicas x{world_env}" if world_env > 1 else "single GPU"}
+    if args.impl == "reference":
+        run_reference_arm(args, cfg_d, workload)
+        return
+
     world, rank, local = dist_setup()
     import numpy as np
     import torch
@@ -331,38 +429,6 @@ def main() -> None:
     cfg = bh.default_stack_config()
     if args.layers:
         cfg.n_layer = args.layers
-    workload = {"workload": "qwen3-8b-shaped decode block stack (config 2), batch 1",
-                "n_layer": cfg.n_layer, "n_embd": cfg.n_embd, "n_head": cfg.n_head, "n_head_kv": cfg.n_head_kv,
-                "head_dim": cfg.head_dim, "n_ff": cfg.n_ff, "n_vocab": cfg.n_vocab,
-                "kv_positions": KV_POS + 1, "weights": "random-init N(0,0.02) quantized to Q4_K",
-                "l2": "no flush needed: 4.26 GB of weights streamed per step >> 126 MB L2",
-                "parallelism": f"replicas x{world}" if world > 1 else "single GPU"}
-
-    if args.impl == "reference":
-        if rank != 0:
-            return
-        ctx = bh.Context(local)
-        st = bh.Stack(ctx, cfg, SEED)
-        st.fill_kv(KV_POS, SEED + 1)
-        st.set_pos(KV_POS)
-        step_bytes = st.info()["step_bytes"]
-        cpu, kind = cpu_reference_step_fn(st, nthreads)
-        x = np.asarray(__import__("oracle").Oracle().normal((cfg.n_embd,), X_SEED, 0.0, 1.0))
-        for _ in range(min(args.warmup, 2)):
-            cpu.step(x, KV_POS)
-        sec, n = time_cpu_steps(cpu, x, args.steps, budget_s=120.0)
-        v = step_bytes / sec / 1e9
-        print(json.dumps({
-            "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": world,
-            "steps": n, "warmup": min(args.warmup, 2), "ms_per_step": round(sec * 1e3, 3),
-            "tokens_per_s": round(1.0 / sec, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "q4_K x q8_K (int8 dot, fp32 fold)", "data": "synthetic",
-            "config": workload,
-            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": nthreads, "kind": kind,
-                             "sample": f"{n} full decode steps (all 36 layers + LM head) on {nthreads} host threads"},
-            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        }), flush=True)
-        return
 
     ctx = bh.Context(local)
     st = bh.Stack(ctx, cfg, SEED)
@@ -440,12 +506,18 @@ def main() -> None:
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu, kind = cpu_reference_step_fn(st, nthreads)
-        cpu.step(x_host, KV_POS)  # warm the caches of the CPU path
-        sec, n = time_cpu_steps(cpu, x_host, 50, budget_s=12.0)
-        cpu_baseline = {"value": round(step_bytes / sec / 1e9, 3), "unit": "GB/s", "cores": nthreads, "kind": kind,
-                        "tokens_per_s": round(1.0 / sec, 3),
-                        "sample": f"{n} full decode steps of the same stack (same weights) in ~12 s"}
+        # the reference's CPU step (its ggml graph on its ggml CPU backend),
+        # bounded to ~12 s of steps, plus the three config-1 legs
+        g = cpu_graph_stack(cfg_d, nthreads)
+        g.decode(x_host, KV_POS, nthreads, logits=False)  # warm the caches of the CPU path
+        sec, n = time_cpu_steps(g, x_host, KV_POS, nthreads, 50, budget_s=12.0)
+        g.close()
+        cpu_baseline = {"value": round(step_bytes_of(cfg_d) / sec / 1e9, 3), "unit": "GB/s", "cores": nthreads,
+                        "kind": "reference", "tokens_per_s": round(1.0 / sec, 3), "cpu": cpu_model(),
+                        "sample": f"{n} full decode steps ({cfg_d['n_layer']} layers + LM head) of the reference "
+                                  f"engine's ggml graph on the reference's ggml CPU backend in ~12 s, {nthreads} "
+                                  f"threads; host-generated weights, {min(4, cfg_d['n_layer'])} distinct layers cycled",
+                        "legs": cpu_legs(nthreads)}
 
     if rank == 0:
         line = {

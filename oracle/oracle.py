@@ -1,10 +1,12 @@
 """ctypes bindings for the test-infrastructure libraries in this folder.
 
 TEST INFRASTRUCTURE ONLY: the parity checker (``Oracle`` -> liboracle.so, the
-CPU restatement of the reference's Q4_K x Q8_K arithmetic) and the compiled
+CPU restatement of the reference's Q4_K x Q8_K arithmetic), the compiled
 reference (``Reference`` -> _ref/libq4k_ref.so, the reference's own
-ggml-quants.c / ggml-cpu quants sources). Nothing on the product path imports
-this module; tests/, __graft_entry__.smoke() and bench.py's CPU legs do.
+ggml-quants.c / ggml-cpu quants sources) and the reference's whole ggml CPU
+backend driven through its graph API (``GraphStack`` / ``graph_mul_mat`` ->
+_ref/libggml_graph.so). Nothing on the product path imports this module;
+tests/, __graft_entry__.smoke() and bench.py's CPU legs do.
 """
 from __future__ import annotations
 
@@ -17,6 +19,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libq4k_ref.so")
+GRAPH_SO = os.path.join(HERE, "_ref", "libggml_graph.so")
 
 QK = 256
 Q4K_BYTES = 144
@@ -287,3 +290,127 @@ class Reference:
                 self.lib.ref_pool_free(self._pool)
         except Exception:
             pass
+
+
+# ---------------------------------------------------------------------------
+# the reference's ggml CPU backend through its graph API (oracle/_ref)
+# ---------------------------------------------------------------------------
+class RgConfig(C.Structure):
+    _fields_ = [("n_layer", C.c_int), ("n_embd", C.c_int), ("n_head", C.c_int), ("n_head_kv", C.c_int),
+                ("head_dim", C.c_int), ("n_ff", C.c_int), ("n_vocab", C.c_int), ("n_ctx", C.c_int),
+                ("rms_eps", C.c_float), ("rope_theta", C.c_float), ("n_distinct", C.c_int)]
+
+
+_GRAPH = None
+
+
+def graph_lib():
+    global _GRAPH
+    if _GRAPH is None:
+        if not os.path.exists(GRAPH_SO):
+            raise FileNotFoundError(f"{GRAPH_SO} not built (make -C oracle graph)")
+        L = C.CDLL(GRAPH_SO)
+        L.rg_stack_create.argtypes = [C.POINTER(RgConfig)]
+        L.rg_stack_create.restype = _vp
+        L.rg_stack_free.argtypes = [_vp]
+        L.rg_stack_tensor.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(C.c_size_t)]
+        L.rg_stack_tensor.restype = _vp
+        L.rg_stack_decode.argtypes = [_vp, _vp, C.c_int, C.c_int, _vp, _vp]
+        L.rg_mul_mat.argtypes = [_vp, C.c_int64, C.c_int64, _vp, C.c_int, _vp, C.c_int]
+        L.rg_quantize_q4k.argtypes = [_vp, _vp, C.c_int64, C.c_int64, C.c_int]
+        L.rg_fill_normal.argtypes = [_vp, C.c_int64, C.c_int64, C.c_uint64, C.c_double, C.c_double, C.c_int]
+        L.rg_has_avx2.restype = C.c_int
+        L.rg_vec_dot_rows.argtypes = [_vp, C.c_int64, C.c_int64, _vp, _vp]
+        _GRAPH = L
+    return _GRAPH
+
+
+def graph_mul_mat(w: np.ndarray, n: int, k: int, x: np.ndarray, nthreads: int, out: np.ndarray | None = None):
+    """One ggml_mul_mat node (Q4_K weight, f32 activations [B][K]) computed by
+    the reference's CPU backend on nthreads threads: y [B][N]."""
+    L = graph_lib()
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, k)
+    y = out if out is not None else np.empty((x.shape[0], n), dtype=np.float32)
+    if L.rg_mul_mat(_ptr(np.ascontiguousarray(w)), n, k, _ptr(x), x.shape[0], _ptr(y), nthreads) != 0:
+        raise RuntimeError("rg_mul_mat failed")
+    return y
+
+
+def graph_quantize_q4k(w: np.ndarray, nthreads: int) -> np.ndarray:
+    """fp32 [rows][k] -> Q4_K bytes through ggml_quantize_chunk, rows over threads."""
+    L = graph_lib()
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, k = w.shape
+    out = np.empty(rows * q4k_row_bytes(k), dtype=np.uint8)
+    L.rg_quantize_q4k(_ptr(w), _ptr(out), rows, k, nthreads)
+    return out
+
+
+class GraphStack:
+    """The decode step as the reference engine's ggml graph (forward.cpp
+    build_block_decode + LM head) on the reference's CPU backend. Tensor ids
+    follow include/bh_q4k.h; ``fill(layer, which, array)`` copies host data in."""
+
+    def __init__(self, cfg: dict, n_distinct: int = 0):
+        L = graph_lib()
+        c = RgConfig(**{f: cfg[f] for f, _ in RgConfig._fields_ if f != "n_distinct"}, n_distinct=n_distinct)
+        self.cfg = dict(cfg)
+        self.h = L.rg_stack_create(C.byref(c))
+        if not self.h:
+            raise MemoryError("rg_stack_create failed")
+        self.L = L
+
+    def tensor(self, layer: int, which: int) -> np.ndarray:
+        """A numpy view of one tensor's host memory (uint8 for Q4_K weights, else float32)."""
+        nb = C.c_size_t(0)
+        p = self.L.rg_stack_tensor(self.h, layer, which, C.byref(nb))
+        if not p:
+            raise IndexError((layer, which))
+        dt = np.uint8 if which <= 7 else np.float32
+        n = nb.value // np.dtype(dt).itemsize
+        return np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_uint8 if dt == np.uint8 else C.c_float)), shape=(n,))
+
+    def fill(self, layer: int, which: int, a: np.ndarray) -> None:
+        t = self.tensor(layer, which)
+        src = np.ascontiguousarray(a).reshape(-1).view(t.dtype)
+        assert src.size == t.size, (layer, which, src.size, t.size)
+        t[:] = src
+
+    def decode(self, x: np.ndarray, pos: int, nthreads: int, logits: bool = True):
+        """(token, logits [n_vocab] or None, hidden [n_embd]) of one step at pos."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        lg = np.empty(self.cfg["n_vocab"], np.float32) if logits else None
+        hid = np.empty(self.cfg["n_embd"], np.float32)
+        tok = self.L.rg_stack_decode(self.h, _ptr(x), pos, nthreads, _ptr(lg) if logits else None, _ptr(hid))
+        if tok < 0:
+            raise RuntimeError("rg_stack_decode failed")
+        return tok, lg, hid
+
+    def close(self) -> None:
+        if self.h:
+            self.L.rg_stack_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def graph_stack_from_cpu(cfg: dict, w: dict, norms: dict, kc: list | None, vc: list | None) -> GraphStack:
+    """A GraphStack holding the given host copies (cpu_stack.stack_to_cpu's layout)."""
+    g = GraphStack(cfg)
+    for l in range(cfg["n_layer"]):
+        for which in range(7):
+            g.fill(l, which, w[(l, which)])
+        g.fill(l, 8, norms["attn_norm"][l])
+        g.fill(l, 9, norms["ffn_norm"][l])
+        g.fill(l, 10, norms["q_norm"][l])
+        g.fill(l, 11, norms["k_norm"][l])
+        if kc is not None:
+            g.fill(l, 13, kc[l])
+            g.fill(l, 14, vc[l])
+    g.fill(-1, 7, w[(-1, 7)])
+    g.fill(-1, 12, norms["out_norm"])
+    return g

@@ -1,0 +1,76 @@
+"""GPU: the device decode stack against the reference's own CPU decode step.
+
+The reference step is the graph the reference engine builds for one token
+(forward.cpp build_block_decode, LM head, engine.cpp argmax) computed by the
+reference's own ggml CPU backend (oracle/_ref/libggml_graph.so, compiled from
+the reference tree), holding host copies of the device stack's weights, norms
+and KV history. Tokens are decoded at consecutive positions, each path
+appending its own K/V. Every matvec, RMSNorm and SwiGLU is bit-exact given
+equal inputs (tests/test_gpu_stack_exact.py); the attention evaluates RoPE
+and softmax in another order, so hidden states and logits are compared
+within a tolerance, and the greedy token must be equal wherever the
+reference's top-2 logit margin is not a near-tie.
+"""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+
+import oracle as om
+from cpu_stack import stack_to_cpu
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not os.path.exists(om.GRAPH_SO), reason="oracle/_ref not built (no reference tree)")]
+
+
+def run_both(bh, ctx, oracle, cfg_over, n_pos, seed, threads):
+    import torch
+
+    st = bh.Stack(ctx, bh.default_stack_config(**cfg_over), seed=seed)
+    cfg, w, norms, kc, vc = stack_to_cpu(st)
+    g = om.graph_stack_from_cpu(cfg, w, norms, kc, vc)
+    del w
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rows = []
+    for pos in range(n_pos):
+        x = oracle.normal((cfg["n_embd"],), 5000 + pos, 0.0, 1.0)
+        st.set_pos(pos)
+        st.decode(torch.from_numpy(x).cuda(), tok)
+        torch.cuda.synchronize()
+        t_dev = int(tok.cpu()[0])
+        lg_dev = st.to_host(-1, bh.T_LOGITS)[0]
+        h_dev = st.to_host(-1, bh.T_HIDDEN)[0]
+        t_ref, lg_ref, h_ref = g.decode(x, pos, threads)
+        rows.append((t_dev, t_ref, lg_dev, lg_ref, h_dev, h_ref))
+    assert ctx.status() == 0
+    g.close()
+    st.close()
+    return rows
+
+
+def check(rows, h_tol, lg_tol, margin):
+    agree = 0
+    for t_dev, t_ref, lg_dev, lg_ref, h_dev, h_ref in rows:
+        assert np.abs(h_dev - h_ref).max() <= h_tol * np.abs(h_ref).max()
+        assert np.abs(lg_dev - lg_ref).max() <= lg_tol * np.abs(lg_ref).max()
+        srt = np.sort(lg_ref)
+        if srt[-1] - srt[-2] > margin * np.abs(lg_ref).max():
+            assert t_dev == t_ref
+        agree += t_dev == t_ref
+    return agree
+
+
+def test_small_stack_tokens_match_reference_graph(ctx, bh, oracle):
+    cfg = dict(n_layer=3, n_embd=1024, n_head=8, n_head_kv=2, head_dim=128, n_ff=2048, n_vocab=5000, n_ctx=32)
+    rows = run_both(bh, ctx, oracle, cfg, 32, 17, len(os.sched_getaffinity(0)))
+    assert check(rows, 2e-3, 2e-2, 1e-2) >= 31
+
+
+def test_config2_36_layers_tokens_match_reference_graph(ctx, bh, oracle):
+    """BASELINE config 2 at full size (36 layers, 151936-row LM head): 128
+    tokens at positions 0..127, device against the reference's ggml graph."""
+    cfg = dict(n_layer=36, n_embd=4096, n_head=32, n_head_kv=8, head_dim=128, n_ff=12288, n_vocab=151936, n_ctx=128)
+    rows = run_both(bh, ctx, oracle, cfg, 128, 20261201, len(os.sched_getaffinity(0)))
+    assert check(rows, 5e-3, 5e-2, 1e-2) >= 126
