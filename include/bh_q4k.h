@@ -95,13 +95,17 @@ int bh_device_status(bh_ctx *ctx, int clear);
  * default 24 KiB) for which a matvec may run several CTAs per SM. */
 #define BH_TUNE_SMALL_ACT 7
 /* BH_TUNE_PREFILL: ring stages per warp a matvec issues before its
- * programmatic-launch wait, 0..8 (0, the default: the whole ring); the rest
- * go out right after the activation loads that follow the wait. */
+ * programmatic-launch wait, -1..8 (0, the default: the whole ring; -1: none);
+ * the rest go out right after the activation loads that follow the wait. */
 #define BH_TUNE_PREFILL 8
 /* BH_TUNE_BARRIER_WAIT: log2 of the SM cycles a routed-expert grid barrier
  * waits before it gives up and reports BH_ETIMEDOUT, 16..31 (default 31,
  * about a second). */
 #define BH_TUNE_BARRIER_WAIT 9
+/* BH_TUNE_PREFETCH_MB: decode stacks created after the call prefetch into
+ * the L2, from each launch, this many MiB of the weights the step streams
+ * next (0 = off, -1 = the stack's default, at most 120). */
+#define BH_TUNE_PREFETCH_MB 10
 int bh_tune(bh_ctx *ctx, int key, int value);
 
 /* fp32 activations [B][K] -> B columns of Q8_K, byte-identical to

@@ -12,7 +12,8 @@ import os
 import re
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libbh_q4k.so")
+# the in-tree build, unless BH_Q4K_LIB names another build of the same library
+LIB_PATH = os.environ.get("BH_Q4K_LIB") or os.path.join(HERE, "libbh_q4k.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "bh_q4k.h")
 
 QK = 256
@@ -31,6 +32,7 @@ TUNE_SM_BUDGET = 5
 TUNE_SMALL_ACT = 7
 TUNE_PREFILL = 8
 TUNE_BARRIER_WAIT = 9
+TUNE_PREFETCH_MB = 10
 BH_EIO = -5
 BH_ENOMEM = -12
 BH_ENODEV = -19

@@ -84,7 +84,7 @@ int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override) {
     if (grid_override > 0) {
         grid = grid_override;
         cap = 200 * 1024;
-    } else if (W == DENSE_MAX_WARPS) {
+    } else if (p.B <= 2) {
         grid = ctx->num_sms;
         cap = 200 * 1024;
         const int64_t tiles8 = ((p.N + MV_ROWS - 1) / MV_ROWS + grid - 1) / grid;
@@ -257,7 +257,7 @@ int bh_tune(bh_ctx* ctx, int key, int value) {
             ctx->smem_cap_small = value;
             return BH_OK;
         case BH_TUNE_PREFILL:
-            if (value < 0 || value > 8) return BH_EINVAL;
+            if (value < -1 || value > 8) return BH_EINVAL;
             ctx->prefill_stages = value;
             return BH_OK;
         case BH_TUNE_SMALL_ACT:
@@ -267,6 +267,10 @@ int bh_tune(bh_ctx* ctx, int key, int value) {
         case BH_TUNE_SM_BUDGET:
             if (value != 0 && (value < 48 * 1024 || value > 228 * 1024)) return BH_EINVAL;
             ctx->sm_budget = value;
+            return BH_OK;
+        case BH_TUNE_PREFETCH_MB:
+            if (value < -1 || value > 120) return BH_EINVAL;
+            ctx->prefetch_bytes = value < 0 ? -1 : (int64_t)value << 20;
             return BH_OK;
         case BH_TUNE_BARRIER_WAIT:
             if (value < 16 || value > 31) return BH_EINVAL;

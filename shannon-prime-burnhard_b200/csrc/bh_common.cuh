@@ -113,6 +113,29 @@ __device__ __forceinline__ void tensor_g2s_3d(void* dst, const CUtensorMap* tmap
         : "memory");
 }
 
+// Bring [src, src + bytes) of this GPU's global memory into the L2 without
+// waiting for it (cp.async.bulk.prefetch.L2, no multicast): a later load of
+// those bytes hits the L2. src and bytes must be multiples of 16. The lines
+// get the normal eviction priority, so they outlive the evict-first lines of
+// the weight stream that is being consumed meanwhile.
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// Warp `wg` of `nw` warps issues its share of an L2 prefetch of `bytes`
+// bytes at `base`: pieces of PREFETCH_PIECE bytes, piece i by warp i % nw
+// (lane 0 issues; nothing waits on them).
+constexpr uint32_t PREFETCH_PIECE = 32768;
+__device__ __forceinline__ void prefetch_share(const uint8_t* base, int64_t bytes, int64_t wg, int64_t nw, int lane) {
+    if (lane != 0 || !base || bytes <= 0) return;
+    const int64_t pieces = (bytes + PREFETCH_PIECE - 1) / PREFETCH_PIECE;
+    for (int64_t i = wg; i < pieces; i += nw) {
+        const int64_t off = i * PREFETCH_PIECE;
+        const int64_t n = bytes - off < (int64_t)PREFETCH_PIECE ? bytes - off : (int64_t)PREFETCH_PIECE;
+        prefetch_l2(base + off, (uint32_t)(n & ~(int64_t)15));
+    }
+}
+
 // Fetch a tensor map descriptor (generic address of the kernel parameter) ahead of the
 // first copy that uses it.
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* tmap) {

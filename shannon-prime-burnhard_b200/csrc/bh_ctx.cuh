@@ -34,7 +34,10 @@ struct bh_ctx {
     int small_act_bytes = 24 * 1024;
     int tpr_force = 0;  // threads per matvec row: 0 = planner's choice, else 4 or 8
     int sm_budget = 0;  // shared memory one matvec launch may hold per SM (0 = no limit)
-    int prefill_stages = 0;  // ring stages per warp a matvec issues before its programmatic wait (0 = all)
+    int prefill_stages = 0;  // ring stages per warp a matvec issues before its programmatic wait (0 = all, -1 = none)
+    // decode stacks: bytes of the weights after a launch's own that it
+    // prefetches into the L2 (-1: the stack's default)
+    int64_t prefetch_bytes = -1;
     int64_t* trace = nullptr;  // timeline probe buffer (trace builds only)
     // argmax candidates of the LM-head entry point: [num_sms * 4][BH_MAX_BATCH]
     float* cand_val = nullptr;

@@ -68,6 +68,12 @@ struct MatvecParams {
     // [B][ldy] it stores, EPI_SWIGLU the gate and up rows [B][2][ldy] before
     // the SwiGLU (the decode stack keeps its last layer's for parity checks)
     float* capture;
+    // optional L2 prefetch of weights a later launch streams (null: none):
+    // every warp issues its share once its own weight copies are all issued
+    // (warps without rows right after the programmatic wait), so the HBM
+    // stream continues through this launch's tail and the next one's start
+    const uint8_t* pf_ptr;
+    int64_t pf_bytes;
     // tiling, chosen on the host
     int rows_per_tile;     // rows of one warp stage: 32 / tpr
     int tpr;               // threads per row: 4 or 8
@@ -75,7 +81,7 @@ struct MatvecParams {
     int row_stride;        // shared-memory bytes per row of a stage
     int stage_bytes;       // rows_per_tile * row_stride (a multiple of 128)
     int stages;
-    int prefill;           // stages per warp issued before the programmatic wait (0 = the whole ring)
+    int prefill;           // stages per warp issued before the programmatic wait (0 = the whole ring, -1 = none)
     int act_off, ring_off, bar_off, smem_bytes;
 };
 
@@ -95,7 +101,14 @@ constexpr int MV_THREADS = MV_WARPS * 32;
 // per-block chain; ~100 registers a thread); larger batches hold more
 // accumulators per thread and run 8-warp CTAs.
 constexpr int DENSE_MAX_WARPS = 16;
-__host__ __device__ constexpr int dense_warps(int B) { return B <= 2 ? 16 : 8; }
+#ifndef BH_DENSE_W12
+#define BH_DENSE_W12 16
+#endif
+__host__ __device__ constexpr int dense_warps(int B) { return B <= 2 ? BH_DENSE_W12 : 8; }
+// CTAs per SM a dense matvec kernel is compiled for: 8-warp CTAs at batch 1-2
+// are kept within half the register file, so the next launch of a step can be
+// resident beside them (and start its weight copies) while they finish.
+__host__ __device__ constexpr int dense_min_blocks(int B) { return (B <= 2 && dense_warps(B) == 8) ? 2 : 1; }
 constexpr int MV_ROWS = 8;                  // largest tile (rows of one warp stage); segment boundaries align to it
 constexpr int ACT_BLOCK_BYTES = 304;   // staged Q8_K block: 272 (q8, lane-padded) + 16 (d) + 16 (S)
 

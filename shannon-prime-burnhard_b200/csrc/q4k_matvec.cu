@@ -213,8 +213,8 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, double* r
                 }
             }
         }
-        if (rd == 0) top_up();
         float scale_u[UF];
+        if (rd == 0) top_up();
         if (SRC == ACT_F32_RMSNORM && one_round) {
             // red[blk]: sum of squares of block blk (nblk <= W*UF entries)
 #pragma unroll
@@ -227,6 +227,7 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, double* r
                 for (int off = 16; off > 0; off >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
                 if (lane == 0 && blk < nblk) red[blk] = ss;
             }
+            BH_TRACE_AT(1);
             named_bar(1, W * 32);
             // every warp sums its blocks' columns itself: lane i takes block i
             // of the column (nb <= 32 here), then an xor butterfly
@@ -302,7 +303,7 @@ __device__ __forceinline__ void finish_row(const MatvecParams& p, const float (&
 // cross-warp handshake). Thread (r, t) works row r of the tile; its fp32
 // fold runs in registers as the blocks stream by.
 template <int FOLD, int NB, int SRC, int EPI, bool PART, int TPR>
-__global__ void __launch_bounds__(dense_warps(NB) * 32, 1) q4k_matvec_kernel(const __grid_constant__ MatvecParams p) {
+__global__ void __launch_bounds__(dense_warps(NB) * 32, dense_min_blocks(NB)) q4k_matvec_kernel(const __grid_constant__ MatvecParams p) {
     constexpr int W = dense_warps(NB);
     constexpr int R = 32 / TPR;
     constexpr int L = 8 / TPR;
@@ -368,12 +369,19 @@ __global__ void __launch_bounds__(dense_warps(NB) * 32, 1) q4k_matvec_kernel(con
     // stages of the ring go out now, the rest right behind the activation
     // loads after the wait (so those loads do not queue behind a full ring)
     const int ring_fill = min(p.stages, total);
-    const int prefill = p.prefill > 0 ? min(p.prefill, ring_fill) : ring_fill;
+    const int prefill = p.prefill > 0 ? min(p.prefill, ring_fill) : (p.prefill < 0 ? 0 : ring_fill);
     for (int q = 0; q < prefill; ++q) issue_next();
-    BH_TRACE_AT(1);
     pdl_trigger();
     pdl_wait();
     BH_TRACE_AT(5);
+    // this warp's share of the L2 prefetch of a later launch's weights: now
+    // when it has no copies of its own, else right after its last copy
+    const int64_t wg = (int64_t)blockIdx.x * W + warp, nwg = (int64_t)gridDim.x * W;
+    bool prefetched = false;
+    if (total == 0) {
+        prefetch_share(p.pf_ptr, p.pf_bytes, wg, nwg, lane);
+        prefetched = true;
+    }
     stage_activations<FOLD, SRC, W>(p, act, s_ssq, threadIdx.x, gpre, [&]() {
         while (issued < ring_fill) issue_next();
     });
@@ -430,6 +438,9 @@ BH_UNROLL(BH_KB_UNROLL)
             if (issued < total) {
                 fence_proxy_async_smem();
                 issue_next();
+            } else if (!prefetched) {
+                prefetch_share(p.pf_ptr, p.pf_bytes, wg, nwg, lane);
+                prefetched = true;
             }
             if (++c_s == p.stages) { c_s = 0; c_ph ^= 1u; }
         }
