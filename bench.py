@@ -174,16 +174,53 @@ def bench_lmhead_tp(bh, ctx, world: int, rank: int, reps: int) -> dict:
     return out
 
 
-def bench_batch_sweep(bh, ctx) -> dict:
-    """Config 3: the FFN matvecs 12288x4096 and 4096x12288 at batch 1, 2, 4, 8
-    (fp32 activations quantized in the prologue), standalone launch plan.
-    Each timed launch reads a different copy of the weights (the copies
-    together exceed the L2 several times); back-to-back launches in a CUDA
-    graph, CUDA events. GB/s = weight + activation + output bytes / time."""
+def bench_batch_sweep(bh, ctx, peak: float) -> dict:
+    """Config 1 (4096x4096) and config 3 (the FFN matvecs 12288x4096 and
+    4096x12288) at batch 1, 2, 4, 8 from fp32 activations (quantized to Q8_K
+    in the prologue), standalone launch plan; beside each, the reference's
+    own GPU kernel for the same product (ggml-cuda mul_mat_vec_q<Q4_K> with
+    its Q8_1 quantizer, built for sm_100a from the reference tree) when
+    oracle/_ref holds it. Each timed launch reads a different copy of the
+    weights (the copies together exceed the L2 several times); back-to-back
+    launches captured in a CUDA graph, CUDA events. GB/s = weight +
+    activation + output bytes / time."""
     import torch
 
-    out = {"workload": "FFN matvecs 12288x4096 / 4096x12288, batch 1-8 (config 3)"}
-    for n, k in ((12288, 4096), (4096, 12288)):
+    import oracle as om
+
+    ref = None
+    if os.path.exists(om.MMVQ_SO):
+        try:
+            ref = om.RefMMVQ()
+        except Exception:
+            ref = None
+    out = {"workload": "Q4_K matvecs 4096x4096 (config 1), 12288x4096 and 4096x12288 (config 3), batch 1-8",
+           "peak_GBps": peak,
+           "gpu_reference": "ggml-cuda mul_mat_vec_q<Q4_K> + quantize_q8_1 (vendored ggml, sm_100a)" if ref else None}
+
+    def graph_us(launch, ncopy):
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            for i in range(3):
+                launch(i, s)
+            s.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=s):
+                for i in range(ncopy):
+                    launch(i, s)
+            gr.replay()
+            s.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(5):
+                gr.replay()
+            e1.record(s)
+            e1.synchronize()
+        del gr
+        return e0.elapsed_time(e1) * 1e3 / (5 * ncopy)
+
+    for n, k in ((4096, 4096), (12288, 4096), (4096, 12288)):
         wbytes = n * (k // 256) * 144
         ncopy = max(8, int(4 * 126e6 // wbytes) + 1)
         g = torch.Generator(device="cuda").manual_seed(SEED + 3)
@@ -192,28 +229,17 @@ def bench_batch_sweep(bh, ctx) -> dict:
         for b in (1, 2, 4, 8):
             x = torch.randn((b, k), generator=g, device="cuda")
             y = torch.empty((b, n), device="cuda")
-            s = torch.cuda.Stream()
-            with torch.cuda.stream(s):
-                for i in range(3):
-                    ctx.matvec_f32(ws[i], n, k, x, y=y, stream=s)
-                s.synchronize()
-                gr = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(gr, stream=s):
-                    for i in range(ncopy):
-                        ctx.matvec_f32(ws[i], n, k, x, y=y, stream=s)
-                gr.replay()
-                s.synchronize()
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
-                e0.record(s)
-                for _ in range(5):
-                    gr.replay()
-                e1.record(s)
-                e1.synchronize()
-            us = e0.elapsed_time(e1) * 1e3 / (5 * ncopy)
             by = wbytes + b * k * 4 + b * n * 4
-            out[f"{n}x{k}_b{b}"] = {"us": round(us, 2), "GBps": round(by / us / 1e3, 1)}
-            del gr
+            us = graph_us(lambda i, s: ctx.matvec_f32(ws[i], n, k, x, y=y, stream=s), ncopy)
+            e = {"us": round(us, 2), "GBps": round(by / us / 1e3, 1), "frac_of_peak": round(by / us / 1e3 / peak, 4)}
+            if ref is not None:
+                xq = torch.empty(ref.xq_bytes(k, b), dtype=torch.uint8, device="cuda")
+                yr = torch.empty((b, n), device="cuda")
+                rus = graph_us(lambda i, s: ref.matvec(ws[i].data_ptr(), n, k, x.data_ptr(), b, xq.data_ptr(),
+                                                       yr.data_ptr(), s.cuda_stream), ncopy)
+                e.update({"ref_us": round(rus, 2), "ref_GBps": round(by / rus / 1e3, 1),
+                          "speedup_vs_ref": round(rus / us, 3)})
+            out[f"{n}x{k}_b{b}"] = e
         del ws, w0
         torch.cuda.empty_cache()
     return out
@@ -500,7 +526,7 @@ def main() -> None:
         except Exception as e:
             extra["moe"] = {"error": repr(e)}
         try:
-            extra["batch_sweep"] = bench_batch_sweep(bh, ctx)
+            extra["batch_sweep"] = bench_batch_sweep(bh, ctx, peaks()[0])
         except Exception as e:
             extra["batch_sweep"] = {"error": repr(e)}
 

@@ -130,6 +130,14 @@ int bh_q4k_matvec(bh_ctx *ctx, const void *W_q4k, int64_t N, int64_t K, const vo
 int bh_q4k_matvec_f32(bh_ctx *ctx, const void *W_q4k, int64_t N, int64_t K, const float *x, int B,
                       float *y, int fold, void *stream);
 
+/* y[b*N + r] = W_q6k[r] . x_q8k[b] for Q6_K weights (210-byte block_q6_K,
+ * ggml-common.h:352-357: the matrices a Q4_K_M model file keeps in 6 bits),
+ * batch 1..8, bit-identical to the x86 AVX2 ggml_vec_dot_q6_K_q8_K
+ * (ggml-cpu/arch/x86/quants.c:2288-2370); fold must be BH_FOLD_X86. W_q6k is
+ * 16-byte aligned (its blocks are then 2-byte aligned, as in a GGUF file). */
+int bh_q6k_matvec(bh_ctx *ctx, const void *W_q6k, int64_t N, int64_t K, const void *x_q8k, int B, float *y,
+                  int fold, void *stream);
+
 /* fp32 weights [N][K] -> Q4_K, byte-identical to quantize_row_q4_K_ref
  * (ggml-quants.c:1395-1465) evaluated without FMA contraction; the
  * offline weight-prep step of ggml_quantize_chunk (ggml-quants.c:1564-1576). */

@@ -20,9 +20,13 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libq4k_ref.so")
 GRAPH_SO = os.path.join(HERE, "_ref", "libggml_graph.so")
+MMVQ_SO = os.path.join(HERE, "_ref", "libmmvq_ref.so")
 
 QK = 256
 Q4K_BYTES = 144
+Q6K_BYTES = 210
+GGML_TYPE_Q4_K = 12
+GGML_TYPE_Q6_K = 14
 Q8K_BYTES = 292
 FOLD_X86 = 0
 FOLD_GENERIC = 1
@@ -76,6 +80,7 @@ class Oracle:
         L.bho_argmax.argtypes = [_vp, C.c_int64]
         L.bho_argmax.restype = C.c_int64
         L.bho_expf_n.argtypes = [_vp, C.c_int64, _vp]
+        L.bho_matvec_q6k.argtypes = [_vp, C.c_int64, C.c_int64, _vp, C.c_int, _vp, C.c_int]
         L.bho_silu_n.argtypes = [_vp, C.c_int64, _vp]
         L.bho_rmsnorm.argtypes = [_vp, _vp, C.c_int, C.c_float, _vp]
         L.bho_moe_route.argtypes = [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp]
@@ -114,6 +119,13 @@ class Oracle:
         y = np.empty((b, n), dtype=np.float32)
         self.lib.bho_matvec(_ptr(np.ascontiguousarray(w)), n, k, _ptr(np.ascontiguousarray(xq)), b,
                             _ptr(y), fold, nthreads or (os.cpu_count() or 1))
+        return y
+
+    def matvec_q6k(self, w: np.ndarray, n: int, k: int, xq: np.ndarray, b: int, nthreads: int = 0) -> np.ndarray:
+        """Q6_K rows x Q8_K columns, the x86 fold: y [b][n]."""
+        y = np.empty((b, n), dtype=np.float32)
+        self.lib.bho_matvec_q6k(_ptr(np.ascontiguousarray(w)), n, k, _ptr(np.ascontiguousarray(xq)), b, _ptr(y),
+                                nthreads or (os.cpu_count() or 1))
         return y
 
     def partials(self, w: np.ndarray, n: int, k: int, xq: np.ndarray, b: int) -> np.ndarray:
@@ -321,6 +333,8 @@ def graph_lib():
         L.rg_fill_normal.argtypes = [_vp, C.c_int64, C.c_int64, C.c_uint64, C.c_double, C.c_double, C.c_int]
         L.rg_has_avx2.restype = C.c_int
         L.rg_vec_dot_rows.argtypes = [_vp, C.c_int64, C.c_int64, _vp, _vp]
+        L.rg_vec_dot_rows_type.argtypes = [C.c_int, _vp, C.c_int64, C.c_int64, _vp, _vp]
+        L.rg_quantize_q6k.argtypes = [_vp, _vp, C.c_int64, C.c_int64]
         _GRAPH = L
     return _GRAPH
 
@@ -414,3 +428,49 @@ def graph_stack_from_cpu(cfg: dict, w: dict, norms: dict, kc: list | None, vc: l
     g.fill(-1, 7, w[(-1, 7)])
     g.fill(-1, 12, norms["out_norm"])
     return g
+
+
+# ---------------------------------------------------------------------------
+# the reference's own GPU Q4_K matvec (ggml-cuda mul_mat_vec_q, oracle/_ref)
+# ---------------------------------------------------------------------------
+class RefMMVQ:
+    """ggml-cuda's mul_mat_vec_q<Q4_K> with its Q8_1 activation quantizer,
+    built for sm_100a from the reference tree: the GPU comparison point. Its
+    activations are Q8_1 (32-value blocks), so its results are close to, not
+    equal to, the Q4_K x Q8_K path."""
+
+    def __init__(self, path: str = MMVQ_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} not built (make -C oracle mmvq)")
+        L = C.CDLL(path)
+        L.refmmvq_xq_bytes.argtypes = [C.c_int]
+        L.refmmvq_xq_bytes.restype = C.c_size_t
+        L.refmmvq_q4k.argtypes = [_vp, C.c_int, C.c_int, _vp, C.c_int, _vp, _vp, _vp]
+        self.lib = L
+
+    def xq_bytes(self, k: int, b: int) -> int:
+        return int(self.lib.refmmvq_xq_bytes(k)) * b
+
+    def matvec(self, w_ptr: int, n: int, k: int, x_ptr: int, b: int, xq_ptr: int, y_ptr: int, stream: int = 0) -> None:
+        """Device pointers: y [b][n] = W . x [b][k]; xq scratch of xq_bytes(k, b)."""
+        if self.lib.refmmvq_q4k(w_ptr, n, k, x_ptr, b, xq_ptr, y_ptr, stream) != 0:
+            raise RuntimeError("refmmvq_q4k failed")
+
+
+def graph_quantize_q6k(w: np.ndarray) -> np.ndarray:
+    """fp32 [rows][k] -> Q6_K bytes through the reference's ggml_quantize_chunk."""
+    L = graph_lib()
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, k = w.shape
+    out = np.empty(rows * (k // QK) * Q6K_BYTES, dtype=np.uint8)
+    L.rg_quantize_q6k(_ptr(w), _ptr(out), rows, k)
+    return out
+
+
+def graph_vec_dot_rows(ggml_type: int, w: np.ndarray, n: int, k: int, x: np.ndarray) -> np.ndarray:
+    """The reference CPU backend's vec_dot for each row against from_float(x) (one column)."""
+    y = np.empty(n, np.float32)
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    if graph_lib().rg_vec_dot_rows_type(ggml_type, _ptr(np.ascontiguousarray(w)), n, k, _ptr(x), _ptr(y)) != 0:
+        raise RuntimeError("rg_vec_dot_rows_type failed")
+    return y

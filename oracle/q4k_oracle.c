@@ -433,6 +433,82 @@ float bho_vec_dot_x86(int n, const void *vw, const void *vx) {
     return h + hm;
 }
 
+/* ggml-cpu/arch/x86/quants.c:2288-2370 (AVX2 branch of
+ * ggml_vec_dot_q6_K_q8_K), restated lane by lane. block_q6_K
+ * (ggml-common.h:352-357): ql[128] low 4 bits, qh[64] high 2 bits,
+ * scales[16] int8 (one per 16 values), fp16 d; 210 bytes per 256 values.
+ * Per 128-value half j and 32-value vector x (is = 4j + x) the 6-bit codes are
+ *   x=0: ql[64j + b] & 15 | (qh[32j + b] & 3) << 4
+ *   x=1: ql[64j + 32 + b] & 15 | (qh[32j + b] >> 2 & 3) << 4
+ *   x=2: ql[64j + b] >> 4 | (qh[32j + b] >> 4 & 3) << 4
+ *   x=3: ql[64j + 32 + b] >> 4 | (qh[32j + b] >> 6) << 4
+ * for bytes b = 0..31 against q8[128j + 32x + b]. Lane m of the int32
+ * accumulator takes bytes 4m..4m+3 of every vector, scaled by scales[2 is]
+ * (m < 4) or scales[2 is + 1] (m >= 4), minus 32 * (bsums[2m] scales[2m] +
+ * bsums[2m+1] scales[2m+1]); then acc[m] = fma(y.d * fp16(d), (float)sumi[m],
+ * acc[m]) and hsum_float_8 at the end. */
+float bho_vec_dot_q6k_x86(int n, const void *vw, const void *vx) {
+    const uint8_t *w = (const uint8_t *)vw;
+    const uint8_t *xq = (const uint8_t *)vx;
+    const int nb = n / BHO_QK;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int i = 0; i < nb; ++i, w += BHO_Q6K_BYTES, xq += BHO_Q8K_BYTES) {
+        const float d = rdf32(xq) * bho_fp16_to_fp32(rd16(w + 208));
+        const uint8_t *ql = w, *qh = w + 128;
+        const int8_t *sc = (const int8_t *)(w + 192);
+        const int8_t *q8 = (const int8_t *)(xq + 4);
+        int32_t sumi[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int j = 0; j < 2; ++j)
+            for (int x = 0; x < 4; ++x) {
+                const int is = 4 * j + x;
+                for (int b = 0; b < 32; ++b) {
+                    const uint8_t lo = ql[64 * j + 32 * (x & 1) + b];
+                    const int q = ((x & 2) ? (lo >> 4) : (lo & 15)) | (((qh[32 * j + b] >> (2 * x)) & 3) << 4);
+                    const int m = b >> 2;
+                    sumi[m] += sc[2 * is + (m >= 4)] * (q * q8[128 * j + 32 * x + b]);
+                }
+            }
+        for (int m = 0; m < 8; ++m) {
+            const int32_t sub = rds16(xq + 260 + 4 * m) * sc[2 * m] + rds16(xq + 262 + 4 * m) * sc[2 * m + 1];
+            sumi[m] -= sub << 5;
+            acc[m] = fmaf(d, (float)sumi[m], acc[m]);
+        }
+    }
+    return ((acc[4] + acc[0]) + (acc[6] + acc[2])) + ((acc[5] + acc[1]) + (acc[7] + acc[3]));
+}
+
+typedef struct {
+    const uint8_t *W;
+    const uint8_t *X;
+    float *Y;
+    int64_t N, K, r0, r1;
+    int B;
+} q6_job;
+
+static void *q6_worker(void *arg) {
+    const q6_job *j = (const q6_job *)arg;
+    const int64_t nb = j->K / BHO_QK;
+    const int64_t wrow = nb * BHO_Q6K_BYTES, xcol = nb * BHO_Q8K_BYTES;
+    for (int b = 0; b < j->B; ++b)
+        for (int64_t r = j->r0; r < j->r1; ++r)
+            j->Y[(int64_t)b * j->N + r] = bho_vec_dot_q6k_x86((int)j->K, j->W + r * wrow, j->X + b * xcol);
+    return NULL;
+}
+
+/* Y[b][r] = W_q6k[r] . Xq[b] over nthreads threads (x86 fold). */
+void bho_matvec_q6k(const void *W, int64_t N, int64_t K, const void *Xq, int B, float *Y, int nthreads) {
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 256) nthreads = 256;
+    if ((int64_t)nthreads > N) nthreads = (int)(N > 0 ? N : 1);
+    pthread_t th[256];
+    q6_job jobs[256];
+    for (int t = 0; t < nthreads; ++t)
+        jobs[t] = (q6_job){(const uint8_t *)W, (const uint8_t *)Xq, Y, N, K, N * t / nthreads, N * (t + 1) / nthreads, B};
+    for (int t = 1; t < nthreads; ++t) pthread_create(&th[t], NULL, q6_worker, &jobs[t]);
+    q6_worker(&jobs[0]);
+    for (int t = 1; t < nthreads; ++t) pthread_join(th[t], NULL);
+}
+
 /* ------------------------------------------------------------------ */
 /* matvec, partials, argmax                                            */
 /* ------------------------------------------------------------------ */

@@ -57,6 +57,10 @@ float bho_vec_dot_generic(int n, const void *w_row, const void *x_q8k);
 float bho_vec_dot_x86(int n, const void *w_row, const void *x_q8k);
 
 /* Y[b*N + r] = W[r] . X[b]   (GGML dst [N, B], column b contiguous) */
+/* Q6_K (210-byte blocks) x Q8_K, the x86 AVX2 fold of ggml_vec_dot_q6_K_q8_K */
+#define BHO_Q6K_BYTES 210
+float bho_vec_dot_q6k_x86(int n, const void *vw, const void *vx);
+void bho_matvec_q6k(const void *W, int64_t N, int64_t K, const void *Xq, int B, float *Y, int nthreads);
 void bho_matvec(const void *W, int64_t N, int64_t K, const void *Xq, int B,
                 float *Y, int fold, int nthreads);
 

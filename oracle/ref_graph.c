@@ -366,16 +366,28 @@ int rg_has_avx2(void) { return ggml_cpu_has_avx2() && ggml_cpu_has_fma() && ggml
  * one thread, through the CPU backend's own type-traits entry for Q4_K
  * (ggml_vec_dot_q4_K_q8_K, arch/x86/quants.c:1900 on AVX2 hosts); xq is the
  * Q8_K activation from the backend's own from_float (quantize_row_q8_K). */
-int rg_vec_dot_rows(const void *w, int64_t n, int64_t k, const float *x, float *y) {
+int rg_vec_dot_rows_type(int type, const void *w, int64_t n, int64_t k, const float *x, float *y) {
     ggml_cpu_init();
-    const struct ggml_type_traits_cpu *tq = ggml_get_type_traits_cpu(GGML_TYPE_Q4_K);
+    if (type != GGML_TYPE_Q4_K && type != GGML_TYPE_Q6_K) return -1;
+    const struct ggml_type_traits_cpu *tq = ggml_get_type_traits_cpu((enum ggml_type)type);
     const struct ggml_type_traits_cpu *t8 = ggml_get_type_traits_cpu(GGML_TYPE_Q8_K);
     if (!tq || !tq->vec_dot || !t8 || !t8->from_float) return -1;
-    const size_t rb = ggml_row_size(GGML_TYPE_Q4_K, k);
+    const size_t rb = ggml_row_size((enum ggml_type)type, k);
     void *xq = malloc(ggml_row_size(GGML_TYPE_Q8_K, k));
     if (!xq) return -1;
     t8->from_float(x, xq, k);
     for (int64_t r = 0; r < n; ++r) tq->vec_dot((int)k, y + r, 0, (const char *)w + (size_t)r * rb, 0, xq, 0, 1);
     free(xq);
+    return 0;
+}
+
+int rg_vec_dot_rows(const void *w, int64_t n, int64_t k, const float *x, float *y) {
+    return rg_vec_dot_rows_type(GGML_TYPE_Q4_K, w, n, k, x, y);
+}
+
+/* rows x k fp32 -> Q6_K (ggml_quantize_chunk -> quantize_row_q6_K_ref), one thread */
+int rg_quantize_q6k(const float *src, void *dst, int64_t rows, int64_t k) {
+    ggml_cpu_init();
+    ggml_quantize_chunk(GGML_TYPE_Q6_K, src, dst, 0, rows, k, NULL);
     return 0;
 }

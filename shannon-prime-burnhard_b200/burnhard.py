@@ -97,6 +97,7 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.bh_q8k_quantize.argtypes = [_vp, _vp, _i64, C.c_int, _vp, _vp]
     L.bh_q4k_matvec.argtypes = [_vp, _vp, _i64, _i64, _vp, C.c_int, _vp, _vp, C.c_int, _vp]
     L.bh_q4k_matvec_f32.argtypes = [_vp, _vp, _i64, _i64, _vp, C.c_int, _vp, C.c_int, _vp]
+    L.bh_q6k_matvec.argtypes = [_vp, _vp, _i64, _i64, _vp, C.c_int, _vp, C.c_int, _vp]
     L.bh_q4k_quantize.argtypes = [_vp, _vp, _i64, _i64, _vp, _vp]
     L.bh_q4k_dequantize.argtypes = [_vp, _vp, _i64, _i64, _vp, _vp]
     L.bh_q4k_mul_mat_host.argtypes = [_vp, _vp, _i64, _i64, _vp, C.c_int, _vp, C.c_int]
@@ -236,6 +237,16 @@ class Context:
             y = torch.empty((b, n), dtype=torch.float32, device=w.device)
         _check(lib.bh_q4k_matvec_f32(self.h, _dp(w), n, k, _dp(x), b, _dp(y), fold, _stream(stream)),
                "bh_q4k_matvec_f32")
+        return y
+
+    def q6k_matvec(self, w, n: int, k: int, xq, b: int, y=None, stream=None):
+        """Q6_K weights [n rows of k] x Q8_K columns xq [b]: y [b][n] (x86 fold)."""
+        import torch
+
+        if y is None:
+            y = torch.empty((b, n), dtype=torch.float32, device=w.device)
+        _check(lib.bh_q6k_matvec(self.h, _dp(w), n, k, _dp(xq), b, _dp(y), FOLD_X86, _stream(stream)),
+               "bh_q6k_matvec")
         return y
 
     def q4k_quantize(self, w_f32, out=None, stream=None):

@@ -28,6 +28,7 @@
 #include "bh_common.cuh"
 #include "bh_ctx.cuh"
 #include "bh_kernels.cuh"
+#include "bh_math.cuh"
 
 namespace bh {
 
@@ -72,10 +73,11 @@ struct AttnParams {
     const float* q_norm;     // [head_dim]
     const float* k_norm;     // [head_dim]
     const int* pos;          // device scalar: position of this token (set before the step)
-    const float* rope_inv_freq;  // [head_dim / 2]: theta^(-2j / head_dim)
+    const float2* rope;      // [n_ctx][head_dim / 2]: (cos, sin) of every rotation angle
     float* out;              // [q_dim]
     int n_head, n_head_kv, head_dim, n_ctx;
-    float eps, theta;
+    float eps;
+    float qk_scale;          // 1.0f / sqrtf(head_dim), as the reference computes it
     int64_t* trace;          // timeline probe (builds with BH_TRACE only; else unused)
     const uint8_t* pf_ptr;   // L2 prefetch of the weights streamed next (null: none)
     int64_t pf_bytes;
@@ -99,238 +101,253 @@ constexpr int64_t TRACE_LAUNCH = 256 * DENSE_MAX_WARPS * 8;
     } while (0)
 #endif
 
-// Attention of one decode token, split over the positions (the K / V reads
-// are the cost, so they are spread over many SMs): CTA g * ATTN_CHUNKS + c
-// (chunk c of KV group g) works the `group` query heads of KV group g
-// over its share of the positions, ATTN_U consecutive positions per warp per
-// round (warp w: head w % group, positions sub = w / group of the CTA's
-// P = (ATTN_WARPS / group) * ATTN_U per round; chunk c takes positions
-// r * ATTN_CHUNKS * P + c * P + ... of round r). head_dim 128: lane l of a warp
-// holds dims 4l..4l+3 of a row. Every warp holds its head's q and this
-// token's k and v in registers (per-head RMSNorm = a warp butterfly; NeoX RoPE
-// pairs dim d with d + 64, i.e. lane l with lane l ^ 16) and keeps a running
-// softmax (max, sum, weighted V). The warps of a head are combined in the
-// CTA; the CTAs of a group form one thread-block cluster: each CTA stores its
-// per-head partials (o[128], max, sum) into the shared memory of the CTA that
-// combines that head, which sums them in chunk order after one cluster
-// barrier. The first round's K / V rows, the norm weights and the
-// rotation frequencies do not depend on the previous kernel and are loaded
-// before the programmatic-launch wait.
+// Attention of one decode token, one CTA per query head, evaluated in the
+// reference CPU backend's own order so that its output equals the engine's
+// ggml graph (forward.cpp build_block_decode) bit for bit:
+//  - per-head rms_norm (binary32 squares summed in double, 1/sqrtf(mean +
+//    eps)) times the q / k norm weight;
+//  - NeoX RoPE: x0' = x0 c - x1 s, x1' = x0 s + x1 c for the pairs (i, i + 64),
+//    (c, s) from a table the host fills exactly as ggml's rope cache does
+//    (theta = pos, theta *= powf(base, -2/n_dims) per pair, cosf / sinf);
+//  - K.Q per position as ggml_vec_dot_f32's AVX2 path: lane l of a warp holds
+//    the fma accumulator of elements l, l + 32, l + 64, l + 96 (the 4 x 8
+//    vector accumulators), reduced in GGML_F32x8_REDUCE's order by shuffles;
+//    then ggml_scale (one multiply);
+//  - soft_max: max, exp(x - max) by ggml_v_expf for every whole group of 8
+//    (the n % 8 tail as (float)exp(double)), the per-8 float sums
+//    ((p4+p0)+(p6+p2))+((p5+p1)+(p7+p3)) accumulated in double in group
+//    order, then each p times (float)(1 / sum);
+//  - V . p per dimension as ggml_vec_dot_f32 over the positions: thread d
+//    keeps the 32 accumulators of positions t % 32 and reduces them in the
+//    same order, the n % 32 tail added one by one in float.
+// The new token's K (after RoPE) and V are appended at pos by the first head
+// of each KV group; the other heads use their own copy of the same values for
+// position pos and read only positions before it from the cache.
 constexpr int ATTN_THREADS = 256;
 constexpr int ATTN_WARPS = ATTN_THREADS / 32;
 constexpr int ATTN_HD = 128;
-constexpr int ATTN_U = 8;                 // positions per warp per round
-constexpr int ATTN_CHUNKS = 8;            // CTAs per KV group: one thread-block cluster
+// positions whose double sum of group partials is taken in order (beyond: a
+// fixed tree, which differs from the reference's order only in the last bits
+// of the double sum)
+constexpr int ATTN_SEQ_GROUPS = 64;
 
 __device__ __forceinline__ float4 f4_zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
 
-__device__ __forceinline__ float warp_sum(float v) {
+// sum of the lane's 4 binary32 squares in double, then over the warp
+__device__ __forceinline__ double warp_sumsq_d(float4 v) {
+    double s = __dadd_rn(__dadd_rn((double)__fmul_rn(v.x, v.x), (double)__fmul_rn(v.y, v.y)),
+                         __dadd_rn((double)__fmul_rn(v.z, v.z), (double)__fmul_rn(v.w, v.w)));
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
-    return v;
+    for (int off = 16; off > 0; off >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+    return s;
 }
 
-__device__ __forceinline__ float sumsq4(float4 v) {
-    return __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
-                     __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w)));
-}
-
-__device__ __forceinline__ float dot4(float4 a, float4 b) {
-    return __fadd_rn(__fadd_rn(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y)),
-                     __fadd_rn(__fmul_rn(a.z, b.z), __fmul_rn(a.w, b.w)));
-}
-
-// x * r * w per component (the per-head RMSNorm)
-__device__ __forceinline__ float4 scale4(float4 x, float r, float4 w) {
+// rms_norm over head_dim = 128 values (4 per lane) then the norm weight:
+// mean = (float)(sum / 128) (an exact power-of-two scaling), 1 / sqrtf(mean + eps)
+__device__ __forceinline__ float4 head_rmsnorm(float4 x, float4 w, float eps) {
+    const float mean = __double2float_rn(__dmul_rn(warp_sumsq_d(x), 1.0 / 128.0));
+    const float r = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, eps)));
     return make_float4(__fmul_rn(__fmul_rn(x.x, r), w.x), __fmul_rn(__fmul_rn(x.y, r), w.y),
                        __fmul_rn(__fmul_rn(x.z, r), w.z), __fmul_rn(__fmul_rn(x.w, r), w.w));
 }
 
-// NeoX rotation of the dims this lane holds; p = the partner lane's values
-__device__ __forceinline__ float rot1(float x, float p, float c, float s, bool low) {
-    return low ? __fsub_rn(__fmul_rn(x, c), __fmul_rn(p, s)) : __fadd_rn(__fmul_rn(x, c), __fmul_rn(p, s));
+// NeoX rotation of the 4 dims this lane holds (4l..4l+3); lanes l and l ^ 16
+// hold the two halves of the same pairs; cs[j] = (cos, sin) of pair (4l + j) mod 64
+__device__ __forceinline__ float rope1(float own, float other, float2 cs, bool low) {
+    return low ? __fsub_rn(__fmul_rn(own, cs.x), __fmul_rn(other, cs.y))    // x0 c - x1 s
+               : __fadd_rn(__fmul_rn(other, cs.y), __fmul_rn(own, cs.x));   // x0 s + x1 c
 }
-
-__device__ __forceinline__ float4 rope4(float4 x, const float (&c)[4], const float (&s)[4], bool low) {
+__device__ __forceinline__ float4 rope4(float4 x, const float2 (&cs)[4], bool low) {
     const float4 p = make_float4(__shfl_xor_sync(0xffffffffu, x.x, 16), __shfl_xor_sync(0xffffffffu, x.y, 16),
                                  __shfl_xor_sync(0xffffffffu, x.z, 16), __shfl_xor_sync(0xffffffffu, x.w, 16));
-    return make_float4(rot1(x.x, p.x, c[0], s[0], low), rot1(x.y, p.y, c[1], s[1], low),
-                       rot1(x.z, p.z, c[2], s[2], low), rot1(x.w, p.w, c[3], s[3], low));
+    return make_float4(rope1(x.x, p.x, cs[0], low), rope1(x.y, p.y, cs[1], low), rope1(x.z, p.z, cs[2], low),
+                       rope1(x.w, p.w, cs[3], low));
 }
 
-__device__ __forceinline__ float4 axpy4(float a, float4 x, float4 y) {
-    return make_float4(__fadd_rn(y.x, __fmul_rn(a, x.x)), __fadd_rn(y.y, __fmul_rn(a, x.y)),
-                       __fadd_rn(y.z, __fmul_rn(a, x.z)), __fadd_rn(y.w, __fmul_rn(a, x.w)));
+// GGML_F32x8_REDUCE over a warp whose lane l = 8 j + e holds vector
+// accumulator j, element e: x0 += x2, x1 += x3; x0 += x1; then the 8 elements
+// (e + e+4, two horizontal adds). The result is in lane 0.
+__device__ __forceinline__ float ggml_reduce_warp(float v) {
+    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 16));
+    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 8));
+    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 4));
+    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1));
+    return __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2));
 }
 
-__device__ __forceinline__ float4 mul4(float a, float4 x) {
-    return make_float4(__fmul_rn(a, x.x), __fmul_rn(a, x.y), __fmul_rn(a, x.z), __fmul_rn(a, x.w));
-}
-
-// One round of a warp's positions t0 + u (u < U): K / V rows of
-// positions before pos in kv / vv, this token's k / v at pos, nothing past it.
-// Scores q.k * scale (a warp butterfly per position); the running max m, sum l
-// and weighted V o are rescaled to the round's maximum, then accumulated.
-template <int U>
-__device__ __forceinline__ void attn_round(const float4 (&kv)[U], const float4 (&vv)[U], int t0, int pos, float4 q,
-                                           float4 k, float4 v, float scale, float& m, float& l, float4& o) {
-    float sc[U];
-    float mr = m;
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-        const int t = t0 + u;
-        const float4 kk = t < pos ? kv[u] : k;  // (past pos: not used)
-        sc[u] = t <= pos ? __fmul_rn(warp_sum(dot4(q, kk)), scale) : -INFINITY;
-        mr = fmaxf(mr, sc[u]);
-    }
-    // mr is finite: position t0 <= pos is in this round
-    const float f = expf(__fsub_rn(m, mr));  // 0 on a warp's first round (m = -inf)
-    l = __fmul_rn(l, f);
-    o = mul4(f, o);
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-        const int t = t0 + u;
-        const float p = expf(__fsub_rn(sc[u], mr));  // 0 past pos
-        l = __fadd_rn(l, p);
-        o = axpy4(p, t < pos ? vv[u] : t == pos ? v : f4_zero(), o);
-    }
-    m = mr;
-}
-
-__global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnParams a) {
-    __shared__ float s_m[ATTN_WARPS], s_l[ATTN_WARPS];
-    __shared__ float4 s_o[ATTN_WARPS][ATTN_HD / 4];
-    // (CTA c < group) the partials of head g * group + c from the cluster's chunks
-    __shared__ float4 s_po[ATTN_CHUNKS][ATTN_HD / 4];
-    __shared__ float s_pm[ATTN_CHUNKS], s_pl[ATTN_CHUNKS];
-    constexpr int U = ATTN_U, HD = ATTN_HD;
-    // one cluster of ATTN_CHUNKS CTAs per KV group, chunk = rank in the cluster
-    const int g = blockIdx.x / ATTN_CHUNKS, c = blockIdx.x % ATTN_CHUNKS, tid = threadIdx.x;
-    const int group = a.n_head / a.n_head_kv;
-    const int lane = tid & 31, w = tid >> 5;
-    const int hl = w % group, sub = w / group, wph = ATTN_WARPS / group;
-    const int h = g * group + hl;
-    const int P = wph * U;                 // positions of one CTA round
-    const int stride_r = ATTN_CHUNKS * P;  // positions of one round of all chunks
+__global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParams a) {
+    extern __shared__ float s_p[];                 // [n_ctx]: scores, then probabilities
+    __shared__ float s_q[ATTN_HD], s_k[ATTN_HD], s_v[ATTN_HD];
+    __shared__ float s_red[ATTN_WARPS];
+    __shared__ float s_gsum[ATTN_SEQ_GROUPS];
+    __shared__ float s_inv;
+    constexpr int HD = ATTN_HD;
+    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int group = a.n_head / a.n_head_kv, g = h / group;
     const int q_dim = a.n_head * HD, kv_dim = a.n_head_kv * HD;
-    const int64_t row_stride = (int64_t)a.n_head_kv * HD;
+    const int64_t row_stride = (int64_t)kv_dim;
     const float* kbase = a.kc + (int64_t)g * HD;
     const float* vbase = a.vc + (int64_t)g * HD;
-    const int t_first = c * P + sub * U;   // this warp's first position
     ATTN_TRACE_AT(0);
-    // distributed shared memory may be written only once every CTA of the
-    // cluster runs: arrive now, wait before the first remote store
-    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
-    // before the wait, nothing that makes the thread wait: loads of the first
-    // round's K / V cache rows (whatever the position: only those before pos
-    // are used), the norm weights, the rotation frequencies (lane l: dims
-    // 4l..4l+3, frequency index (4l mod 64) + j) and pos
+    // before the wait, nothing that makes the thread wait: the norm weights,
+    // the rotation table row of pos (pos is set before the step), and the
+    // cache rows of the first positions (only those before pos are used)
     const uint64_t keep = policy_evict_last();
-    float4 kpre[U], vpre[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-        const int t = t_first + u;
-        kpre[u] = t < a.n_ctx ? ldg_f4_keep(kbase + (int64_t)t * row_stride + 4 * lane, keep) : f4_zero();
-        vpre[u] = t < a.n_ctx ? ldg_f4_keep(vbase + (int64_t)t * row_stride + 4 * lane, keep) : f4_zero();
-    }
-    const float4 qn = ldg_f4_keep(a.q_norm + 4 * lane, keep);
-    const float4 kn = ldg_f4_keep(a.k_norm + 4 * lane, keep);
-    const float4 fr = ldg_f4_keep(a.rope_inv_freq + 4 * (lane & 15), keep);
     const int pos = *a.pos;
-    // the attention streams no weights: its warps keep the HBM busy with the
-    // L2 prefetch of the weights the next launches stream
+    const int n = pos + 1;
+    float4 qn = f4_zero(), kn = f4_zero();
+    float2 cs[4];
+    if (w == 0) {
+        qn = ldg_f4_keep(a.q_norm + 4 * lane, keep);
+        kn = ldg_f4_keep(a.k_norm + 4 * lane, keep);
+        const float4* rt = reinterpret_cast<const float4*>(a.rope + (int64_t)pos * (HD / 2) + 4 * (lane & 15));
+        const float4 r01 = rt[0], r23 = rt[1];
+        cs[0] = make_float2(r01.x, r01.y); cs[1] = make_float2(r01.z, r01.w);
+        cs[2] = make_float2(r23.x, r23.y); cs[3] = make_float2(r23.z, r23.w);
+    }
+    // positions of this warp: t = w + 8 i; the first 2 rows (4 values a lane each) now
+    constexpr int PRE = 2;
+    float kpre[PRE][4];
+#pragma unroll
+    for (int i = 0; i < PRE; ++i) {
+        const int t = w + ATTN_WARPS * i;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            kpre[i][c] = t < a.n_ctx ? __ldg(kbase + (int64_t)t * row_stride + 32 * c + lane) : 0.f;
+    }
     prefetch_share(a.pf_ptr, a.pf_bytes, (int64_t)blockIdx.x * ATTN_WARPS + w, (int64_t)gridDim.x * ATTN_WARPS, lane);
     pdl_trigger();
     pdl_wait();
     ATTN_TRACE_AT(5);
 
-    // this warp's head q, this token's k and v (the rotation is computed
-    // while they load); per-head RMSNorm, NeoX RoPE
-    float4 q = reinterpret_cast<const float4*>(a.qkv + (int64_t)h * HD)[lane];
-    float4 k = reinterpret_cast<const float4*>(a.qkv + q_dim + (int64_t)g * HD)[lane];
-    const float4 v = reinterpret_cast<const float4*>(a.qkv + q_dim + kv_dim + (int64_t)g * HD)[lane];
-    float cs[4], sn[4];
-    sincosf(__fmul_rn((float)pos, fr.x), &sn[0], &cs[0]);
-    sincosf(__fmul_rn((float)pos, fr.y), &sn[1], &cs[1]);
-    sincosf(__fmul_rn((float)pos, fr.z), &sn[2], &cs[2]);
-    sincosf(__fmul_rn((float)pos, fr.w), &sn[3], &cs[3]);
-    const float rq = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(warp_sum(sumsq4(q)), (float)HD), a.eps)));
-    const float rk = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(warp_sum(sumsq4(k)), (float)HD), a.eps)));
-    const bool low = lane < 16;
-    q = rope4(scale4(q, rq, qn), cs, sn, low);
-    k = rope4(scale4(k, rk, kn), cs, sn, low);
-    if (c == 0 && w == 0) {
-        reinterpret_cast<float4*>(a.kc + (int64_t)pos * row_stride + (int64_t)g * HD)[lane] = k;
-        reinterpret_cast<float4*>(a.vc + (int64_t)pos * row_stride + (int64_t)g * HD)[lane] = v;
+    // this head's q, the group's k and v of this token: norm, rotation
+    if (w == 0) {
+        const float4 q = reinterpret_cast<const float4*>(a.qkv + (int64_t)h * HD)[lane];
+        const float4 k = reinterpret_cast<const float4*>(a.qkv + q_dim + (int64_t)g * HD)[lane];
+        const float4 v = reinterpret_cast<const float4*>(a.qkv + q_dim + kv_dim + (int64_t)g * HD)[lane];
+        const bool low = lane < 16;
+        const float4 qr = rope4(head_rmsnorm(q, qn, a.eps), cs, low);
+        const float4 kr = rope4(head_rmsnorm(k, kn, a.eps), cs, low);
+        reinterpret_cast<float4*>(s_q)[lane] = qr;
+        reinterpret_cast<float4*>(s_k)[lane] = kr;
+        reinterpret_cast<float4*>(s_v)[lane] = v;
+        if (h % group == 0) {
+            reinterpret_cast<float4*>(a.kc + (int64_t)pos * row_stride + (int64_t)g * HD)[lane] = kr;
+            reinterpret_cast<float4*>(a.vc + (int64_t)pos * row_stride + (int64_t)g * HD)[lane] = v;
+        }
     }
+    __syncthreads();
     ATTN_TRACE_AT(1);
 
-    // this warp's positions: scores, running softmax (the first round from
-    // the rows loaded before the wait)
-    const float scale = __fdiv_rn(1.f, __fsqrt_rn((float)HD));
-    float m = -INFINITY, l = 0.f;
-    float4 o = f4_zero();
-    if (t_first <= pos) attn_round<U>(kpre, vpre, t_first, pos, q, k, v, scale, m, l, o);
-    for (int t0 = t_first + stride_r; t0 <= pos; t0 += stride_r) {
-        float4 kv[U], vv[U];
+    // scores: warp w takes positions w, w + 8, ...
+    float qv[4];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int t = t0 + u;
-            kv[u] = t < pos ? ldg_f4_keep(kbase + (int64_t)t * row_stride + 4 * lane, keep) : f4_zero();
-            vv[u] = t < pos ? ldg_f4_keep(vbase + (int64_t)t * row_stride + 4 * lane, keep) : f4_zero();
+    for (int c = 0; c < 4; ++c) qv[c] = s_q[32 * c + lane];
+    float wmax = -INFINITY;
+    auto score = [&](int t, const float (&kv)[4]) {
+        float acc = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc = __fmaf_rn(kv[c], qv[c], acc);
+        const float sc = __fmul_rn(ggml_reduce_warp(acc), a.qk_scale);  // ggml_scale
+        if (lane == 0) s_p[t] = sc;
+        wmax = fmaxf(wmax, sc);
+    };
+#pragma unroll
+    for (int i = 0; i < PRE; ++i) {
+        const int t = w + ATTN_WARPS * i;
+        if (t < n) {
+            float kv[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) kv[c] = t == pos ? s_k[32 * c + lane] : kpre[i][c];
+            score(t, kv);
         }
-        attn_round<U>(kv, vv, t0, pos, q, k, v, scale, m, l, o);
     }
-    ATTN_TRACE_AT(2);
-
-    // the warps of each head, in sub order (a warp without positions has
-    // max -inf and weight 0), then this CTA's partial for head hl goes into
-    // slot c of CTA hl of the cluster (distributed shared memory); after one
-    // cluster barrier CTA c < group combines head c over the chunks in chunk
-    // order from its own shared memory
-    if (lane == 0) {
-        s_m[w] = m;
-        s_l[w] = l;
+    for (int t = w + ATTN_WARPS * PRE; t < n; t += ATTN_WARPS) {
+        float kv[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            kv[c] = t == pos ? s_k[32 * c + lane] : __ldg(kbase + (int64_t)t * row_stride + 32 * c + lane);
+        score(t, kv);
     }
-    s_o[w][lane] = o;
+    wmax = __shfl_sync(0xffffffffu, wmax, 0);
+    if (lane == 0) s_red[w] = wmax;
     __syncthreads();
-    namespace cg = cooperative_groups;
-    cg::cluster_group cl = cg::this_cluster();
-    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
-    if (w < group) {
-        float mx = s_m[w];
-        for (int i = 1; i < wph; ++i) mx = fmaxf(mx, s_m[w + i * group]);
-        float ls = 0.f;
-        float4 r = f4_zero();
-        for (int i = 0; i < wph; ++i) {
-            const int wi = w + i * group;
-            const float f = s_m[wi] == -INFINITY ? 0.f : expf(__fsub_rn(s_m[wi], mx));
-            ls = __fadd_rn(ls, __fmul_rn(s_l[wi], f));
-            r = axpy4(f, s_o[wi][lane], r);
+    ATTN_TRACE_AT(2);
+    float mx = s_red[0];
+#pragma unroll
+    for (int i = 1; i < ATTN_WARPS; ++i) mx = fmaxf(mx, s_red[i]);
+
+    // soft_max: p = exp(s - max); group sums of 8 in float; their double sum
+    const int n8 = n & ~7, ng = n8 >> 3;
+    for (int t = tid; t < n; t += ATTN_THREADS) {
+        const float x = __fsub_rn(s_p[t], mx);
+        s_p[t] = t < n8 ? exp_ggml(x) : __double2float_rn(exp((double)x));
+    }
+    __syncthreads();
+    for (int gi = tid; gi < ng && gi < ATTN_SEQ_GROUPS; gi += ATTN_THREADS) {
+        const float* v = s_p + 8 * gi;
+        s_gsum[gi] = __fadd_rn(__fadd_rn(__fadd_rn(v[4], v[0]), __fadd_rn(v[6], v[2])),
+                               __fadd_rn(__fadd_rn(v[5], v[1]), __fadd_rn(v[7], v[3])));
+    }
+    __syncthreads();
+    if (w == 0) {
+        double sum = 0.0;
+        if (ng <= ATTN_SEQ_GROUPS) {
+            if (lane == 0)
+                for (int gi = 0; gi < ng; ++gi) sum = __dadd_rn(sum, (double)s_gsum[gi]);
+        } else {
+            for (int gi = lane; gi < ng; gi += 32) {
+                const float* v = s_p + 8 * gi;
+                const float gs = __fadd_rn(__fadd_rn(__fadd_rn(v[4], v[0]), __fadd_rn(v[6], v[2])),
+                                           __fadd_rn(__fadd_rn(v[5], v[1]), __fadd_rn(v[7], v[3])));
+                sum = __dadd_rn(sum, (double)gs);
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) sum = __dadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, off));
         }
-        cl.map_shared_rank(&s_po[c][0], w)[lane] = r;
         if (lane == 0) {
-            *cl.map_shared_rank(&s_pm[c], w) = mx;
-            *cl.map_shared_rank(&s_pl[c], w) = ls;
+            for (int t = n8; t < n; ++t) sum = __dadd_rn(sum, (double)s_p[t]);
+            s_inv = __double2float_rn(__ddiv_rn(1.0, sum));
         }
     }
-    cl.sync();  // (all partials have landed; nothing is read remotely after it)
+    __syncthreads();
+    const float inv = s_inv;
+    for (int t = tid; t < n; t += ATTN_THREADS) s_p[t] = __fmul_rn(s_p[t], inv);
+    __syncthreads();
     ATTN_TRACE_AT(3);
-    if (c < group && w == 0) {
-        float mx = s_pm[0];
+
+    // out[d] = V[.][d] . p: thread d, 32 accumulators over t mod 32
+    if (tid < HD) {
+        const int d = tid;
+        const int np = n & ~31;
+        float acc[32];
 #pragma unroll
-        for (int i = 1; i < ATTN_CHUNKS; ++i) mx = fmaxf(mx, s_pm[i]);
-        float ls = 0.f;
-        float4 r = f4_zero();
+        for (int r = 0; r < 32; ++r) acc[r] = 0.f;
+        for (int t0 = 0; t0 < np; t0 += 32) {
 #pragma unroll
-        for (int i = 0; i < ATTN_CHUNKS; ++i) {
-            const float f = s_pm[i] == -INFINITY ? 0.f : expf(__fsub_rn(s_pm[i], mx));
-            ls = __fadd_rn(ls, __fmul_rn(s_pl[i], f));
-            r = axpy4(f, s_po[i][lane], r);
+            for (int r = 0; r < 32; ++r) {
+                const int t = t0 + r;
+                const float v = t == pos ? s_v[d] : __ldg(vbase + (int64_t)t * row_stride + d);
+                acc[r] = __fmaf_rn(v, s_p[t], acc[r]);
+            }
         }
-        const float4 res = make_float4(__fdiv_rn(r.x, ls), __fdiv_rn(r.y, ls), __fdiv_rn(r.z, ls), __fdiv_rn(r.w, ls));
-        reinterpret_cast<float4*>(a.out + (int64_t)(g * group + c) * HD)[lane] = res;
+        // GGML_F32x8_REDUCE: accumulator j element e is acc[8 j + e]
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            acc[e] = __fadd_rn(acc[e], acc[16 + e]);
+            acc[8 + e] = __fadd_rn(acc[8 + e], acc[24 + e]);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = __fadd_rn(acc[e], acc[8 + e]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[e] = __fadd_rn(acc[e], acc[e + 4]);
+        float sumf = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+        for (int t = np; t < n; ++t) {
+            const float v = t == pos ? s_v[d] : __ldg(vbase + (int64_t)t * row_stride + d);
+            sumf = __fadd_rn(sumf, __fmul_rn(v, s_p[t]));
+        }
+        a.out[(int64_t)h * HD + d] = sumf;
     }
     ATTN_TRACE_AT(6);
 }
@@ -353,7 +370,7 @@ struct bh_stack {
     const uint8_t** wq = nullptr;   // [n_layer * BH_W_PER_LAYER] then the LM head
     float* fbuf = nullptr;          // norms, KV caches, activations
     float *attn_norm, *ffn_norm, *q_norm, *k_norm, *out_norm;
-    float* rope_inv_freq;           // [head_dim / 2]
+    float2* rope;                   // [n_ctx][head_dim / 2] (cos, sin) of the rotation angles
     float *kc, *vc;
     float *x_in, *h, *qkv, *attn, *gu, *logits, *cand_val;
     float *cap_h_attn, *cap_gate_up;  // the last layer's h after O + residual, its gate | up rows
@@ -377,8 +394,6 @@ int check_cfg(const bh_stack_config* c) {
     if (c->n_layer < 1 || c->n_embd < 256 || c->n_embd % 256 || c->n_ff < 256 || c->n_ff % 256) return BH_EINVAL;
     if (c->head_dim != bh::ATTN_HD) return BH_EINVAL;  // the attention kernel is written for 128
     if (c->n_head < 1 || c->n_head_kv < 1 || c->n_head % c->n_head_kv) return BH_EINVAL;
-    // the attention CTA gives each of a group's query heads the same number of warps
-    if (bh::ATTN_WARPS % (c->n_head / c->n_head_kv)) return BH_EINVAL;
     if ((c->n_head * c->head_dim) % 256 || c->n_vocab < 1 || c->n_ctx < 1 || c->n_ctx > 8192) return BH_EINVAL;
     return BH_OK;
 }
@@ -450,7 +465,7 @@ int stack_matvec(bh_stack* st, bh::MatvecParams& p, int src, int epi, bool pdl) 
     return bh::run_matvec(&st->plan, p, BH_FOLD_X86, src, epi, st->stream, pdl);
 }
 
-// Attention of layer l over positions 0..pos (ATTN_CHUNKS CTAs per KV group).
+// Attention of layer l over positions 0..pos (one CTA per query head).
 int launch_attn(bh_stack* st, int l, bool pdl) {
     const bh_stack_config& c = st->cfg;
     const int64_t kvd = (int64_t)c.n_head_kv * c.head_dim;
@@ -461,41 +476,37 @@ int launch_attn(bh_stack* st, int l, bool pdl) {
     a.q_norm = st->q_norm + (size_t)l * c.head_dim;
     a.k_norm = st->k_norm + (size_t)l * c.head_dim;
     a.pos = st->pos;
+    a.rope = st->rope;
     a.out = st->attn;
     a.n_head = c.n_head;
     a.n_head_kv = c.n_head_kv;
     a.head_dim = c.head_dim;
     a.n_ctx = c.n_ctx;
     a.eps = c.rms_eps;
-    a.theta = c.rope_theta;
-    a.rope_inv_freq = st->rope_inv_freq;
+    a.qk_scale = 1.0f / std::sqrt((float)c.head_dim);  // forward.cpp: 1.0f / sqrtf((float)head_dim)
     set_prefetch(st, mat_end(st, l * BH_W_PER_LAYER + BH_W_V), &a.pf_ptr, &a.pf_bytes);
     a.trace = nullptr;
 #ifdef BH_TRACE
     if (st->ctx->trace) a.trace = st->ctx->trace + st->launches * bh::TRACE_LAUNCH;
 #endif
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(c.n_head_kv * bh::ATTN_CHUNKS));
+    cfg.gridDim = dim3((unsigned)c.n_head);
     cfg.blockDim = dim3((unsigned)bh::ATTN_THREADS);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = sizeof(float) * (size_t)c.n_ctx;
     cfg.stream = st->stream;
-    cudaLaunchAttribute at[2];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = bh::ATTN_CHUNKS;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = pdl ? 2 : 1;
+    cfg.numAttrs = pdl ? 1 : 0;
     static std::atomic<uint64_t> attr_devices{0};
     // the same shared-memory carveout as the matvecs around it
     if (!bh::attrs_on_device(attr_devices, [] {
-            return cudaFuncSetAttribute(bh::attn_decode_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+            return cudaFuncSetAttribute(bh::attn_head_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                                         cudaSharedmemCarveoutMaxShared) == cudaSuccess;
         }))
         return BH_EIO;
-    return cudaLaunchKernelEx(&cfg, bh::attn_decode_kernel, a) == cudaSuccess ? BH_OK : BH_EIO;
+    return cudaLaunchKernelEx(&cfg, bh::attn_head_kernel, a) == cudaSuccess ? BH_OK : BH_EIO;
 }
 
 // Enqueue one decode step on st->stream (captured into the graph).
@@ -744,7 +755,8 @@ int bh_stack_create(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, bh_s
     const size_t o_kc = take((int64_t)c.n_layer * c.n_ctx * kvd), o_vc = take((int64_t)c.n_layer * c.n_ctx * kvd);
     const size_t o_x = take(c.n_embd), o_h = take(c.n_embd), o_qkv = take(qd + 2 * kvd), o_at = take(qd);
     const size_t o_gu = take(2 * (int64_t)c.n_ff), o_lg = take(c.n_vocab), o_cv = take(cand_max);
-    const size_t o_ci = take(cand_max), o_tk = take(1), o_ps = take(1), o_rf = take(c.head_dim / 2);
+    const size_t o_ci = take(cand_max), o_tk = take(1), o_ps = take(1);
+    const size_t o_rf = take((int64_t)c.n_ctx * c.head_dim);  // (cos, sin) per position and pair
     const size_t o_ch = take(c.n_embd), o_cg = take(2 * (int64_t)c.n_ff);
     if (cudaMalloc(&st->fbuf, fl * sizeof(float)) != cudaSuccess ||
         cudaMallocHost(&st->host_tok, sizeof(int32_t)) != cudaSuccess ||
@@ -761,16 +773,30 @@ int bh_stack_create(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, bh_s
     st->cand_idx = reinterpret_cast<int32_t*>(F + o_ci);
     st->tok = reinterpret_cast<int32_t*>(F + o_tk);
     st->pos = reinterpret_cast<int*>(F + o_ps);
-    st->rope_inv_freq = F + o_rf;
+    st->rope = reinterpret_cast<float2*>(F + o_rf);
     st->cap_h_attn = F + o_ch;
     st->cap_gate_up = F + o_cg;
     {
-        // NeoX RoPE frequencies theta^(-2j / head_dim), evaluated in double once per stack
-        std::vector<float> rf((size_t)c.head_dim / 2);
-        for (int j = 0; j < c.head_dim / 2; ++j)
-            rf[(size_t)j] = (float)std::exp(-(2.0 * j / c.head_dim) * std::log((double)c.rope_theta));
-        if (cudaMemcpyAsync(st->rope_inv_freq, rf.data(), rf.size() * sizeof(float), cudaMemcpyHostToDevice,
-                            st->stream) != cudaSuccess ||
+        // The rotation table, computed the way the reference's CPU backend
+        // fills its rope cache (ggml-cpu/ops.cpp ggml_rope_cache_init with
+        // freq_scale 1, ext_factor 0, attn_factor 1): theta_scale =
+        // powf(base, -2.0f / n_dims); per position theta starts at (float)pos
+        // and is multiplied by theta_scale after every pair, in binary32;
+        // (cosf(theta), sinf(theta)) with the host C library, as the
+        // reference evaluates them.
+        const int half = c.head_dim / 2;
+        std::vector<float2> rt((size_t)c.n_ctx * half);
+        const float theta_scale = powf(c.rope_theta, -2.0f / (float)c.head_dim);
+        for (int ps = 0; ps < c.n_ctx; ++ps) {
+            volatile float theta = (float)ps;
+            for (int i = 0; i < half; ++i) {
+                const float th = theta;
+                rt[(size_t)ps * half + i] = make_float2(cosf(th), sinf(th));
+                theta = th * theta_scale;
+            }
+        }
+        if (cudaMemcpyAsync(st->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice, st->stream) !=
+                cudaSuccess ||
             cudaStreamSynchronize(st->stream) != cudaSuccess) {
             bh_stack_free(st);
             return BH_EIO;

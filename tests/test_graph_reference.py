@@ -107,3 +107,15 @@ def test_graph_direct_row_loop_equals_oracle(oracle):
     assert om.graph_lib().rg_vec_dot_rows(om._ptr(np.ascontiguousarray(w)), n, k, om._ptr(x), om._ptr(y)) == 0
     want = oracle.matvec(w, n, k, oracle.quantize_q8k(x), 1, om.FOLD_X86)[0]
     assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("n,k", [(64, 256), (100, 768), (200, 4096), (16, 12288)])
+def test_q6k_oracle_equals_reference_vec_dot(oracle, n, k):
+    """The oracle's Q6_K restatement (the AVX2 lane structure) equals the
+    reference's own ggml_vec_dot_q6_K_q8_K bit for bit, on weights from the
+    reference's Q6_K quantizer."""
+    w = om.graph_quantize_q6k(oracle.normal((n, k), 40 + k, 0.0, 0.02))
+    x = oracle.normal((1, k), 41 + n, 0.0, 1.0)
+    want = om.graph_vec_dot_rows(om.GGML_TYPE_Q6_K, w, n, k, x)
+    got = oracle.matvec_q6k(w, n, k, oracle.quantize_q8k(x), 1)[0]
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
