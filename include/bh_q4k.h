@@ -420,6 +420,39 @@ int bh_moe_stack_info(bh_moe_stack *st, int64_t *weight_bytes, int64_t *step_byt
 /* Device pointer and bytes of one tensor (ids above) of a layer. */
 int bh_moe_stack_tensor(bh_moe_stack *st, int layer, int which, void **ptr, int64_t *bytes);
 
+/* ------------------------------------------------------------------------
+ * GGUF tensor reader -> device upload: the weights of a model file (the
+ * reference engine's loader, desktop/engine/src/gguf_loader.cpp, binding
+ * tensors in llama_weights.cpp:866-950). GGUF v2/v3 (vendor/ggml/include/
+ * gguf.h); the file is memory-mapped read-only and every offset is checked
+ * against its size (a truncated or corrupt file returns BH_EINVAL). Tensor
+ * bytes are the GGML block rows the matvecs consume, uploaded unchanged.
+ * ------------------------------------------------------------------------ */
+typedef struct bh_gguf bh_gguf;
+int bh_gguf_open(const char *path, bh_gguf **out);
+int bh_gguf_close(bh_gguf *g);
+int64_t bh_gguf_n_tensors(const bh_gguf *g);
+int64_t bh_gguf_n_keys(const bh_gguf *g);
+/* Index of a tensor / key by name, or -1. */
+int64_t bh_gguf_find_tensor(const bh_gguf *g, const char *name);
+int64_t bh_gguf_find_key(const bh_gguf *g, const char *key);
+/* Name, ggml type id, dimensions, ne[4] (unused dims 1), byte offset in the
+ * file and byte size (0 for a ggml type whose block size is not known here). */
+int bh_gguf_tensor_info(const bh_gguf *g, int64_t i, const char **name, int *ggml_type, int *n_dims, int64_t *ne4,
+                        uint64_t *file_offset, uint64_t *bytes);
+/* The tensor's bytes in the mapping (host memory, valid until close). */
+const void *bh_gguf_tensor_host(const bh_gguf *g, int64_t i);
+/* Copy tensor i into device memory dst (dst_bytes >= its size) on stream;
+ * returns once the copy has completed. */
+int bh_gguf_upload(bh_ctx *ctx, const bh_gguf *g, int64_t i, void *dst, size_t dst_bytes, void *stream);
+/* Key k's name and GGUF value type; its value as an integer (any integer or
+ * bool type), a float (float or integer types) or a string (not
+ * NUL-terminated; len bytes). */
+int bh_gguf_key(const bh_gguf *g, int64_t k, const char **key, int *type);
+int bh_gguf_get_int(const bh_gguf *g, int64_t k, int64_t *v);
+int bh_gguf_get_float(const bh_gguf *g, int64_t k, double *v);
+int bh_gguf_get_str(const bh_gguf *g, int64_t k, const char **s, uint64_t *len);
+
 /* ggml_vec_dot_t-shaped shim (ggml-cpu.h:113) for the type_traits slot of
  * GGML_TYPE_Q4_K: one row of K = n values, HOST pointers vx (block_q4_K)
  * and vy (block_q8_K), nrc must be 1. Runs on device 0 through a

@@ -44,15 +44,53 @@ def swiglu(g: np.ndarray, u: np.ndarray) -> np.ndarray:
     return (_oracle().silu(np.asarray(g, dtype=np.float32)) * u).astype(np.float32)
 
 
+_LIBM = None
+
+
+def _libm():
+    global _LIBM
+    if _LIBM is None:
+        import ctypes as C
+        import ctypes.util
+
+        L = C.CDLL(ctypes.util.find_library("m") or "libm.so.6")
+        for f in ("powf", "cosf", "sinf"):
+            getattr(L, f).restype = C.c_float
+        L.powf.argtypes = [C.c_float, C.c_float]
+        L.cosf.argtypes = [C.c_float]
+        L.sinf.argtypes = [C.c_float]
+        _LIBM = L
+    return _LIBM
+
+
+def rope_table(pos: int, head_dim: int, theta: float):
+    """(cos, sin) of the NeoX rotation angles of one position, as the
+    reference's CPU backend fills its rope cache (ggml-cpu/ops.cpp
+    ggml_rope_cache_init): theta_scale = powf(base, -2.0f / n_dims); theta
+    starts at (float)pos and is multiplied by theta_scale after every pair in
+    binary32; cosf / sinf of the host C library."""
+    L = _libm()
+    half = head_dim // 2
+    scale = np.float32(L.powf(np.float32(theta), np.float32(-2.0) / np.float32(head_dim)))
+    c = np.empty(half, np.float32)
+    s = np.empty(half, np.float32)
+    th = np.float32(pos)
+    for i in range(half):
+        c[i] = L.cosf(th)
+        s[i] = L.sinf(th)
+        th = np.float32(th * scale)
+    return c, s
+
+
 def rope_neox(x: np.ndarray, pos: int, theta: float) -> np.ndarray:
+    """NeoX rotation of the pairs (i, i + head_dim/2): x0 c - x1 s, x0 s + x1 c
+    in binary32 (ggml-cpu/ops.cpp rotate_pairs)."""
+    x = np.asarray(x, dtype=np.float32)
     hd = x.shape[-1]
     half = hd // 2
-    j = np.arange(half, dtype=np.float64)
-    inv = np.exp(-(2.0 * j / hd) * np.log(float(theta))).astype(np.float32)
-    ang = (np.float32(pos) * inv).astype(np.float32)
-    c, s = np.cos(ang), np.sin(ang)
+    c, s = rope_table(pos, hd, theta)
     x1, x2 = x[..., :half], x[..., half:]
-    return np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s], axis=-1).astype(np.float32)
+    return np.concatenate([(x1 * c) - (x2 * s), (x1 * s) + (x2 * c)], axis=-1).astype(np.float32)
 
 
 class CpuStack:

@@ -335,6 +335,10 @@ def graph_lib():
         L.rg_vec_dot_rows.argtypes = [_vp, C.c_int64, C.c_int64, _vp, _vp]
         L.rg_vec_dot_rows_type.argtypes = [C.c_int, _vp, C.c_int64, C.c_int64, _vp, _vp]
         L.rg_quantize_q6k.argtypes = [_vp, _vp, C.c_int64, C.c_int64]
+        L.rg_gguf_write.argtypes = [C.c_char_p, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_int),
+                                    C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(_vp), C.c_int,
+                                    C.POINTER(C.c_char_p), C.POINTER(C.c_uint32), C.c_char_p, C.c_char_p,
+                                    C.c_char_p, C.c_float]
         _GRAPH = L
     return _GRAPH
 
@@ -474,3 +478,24 @@ def graph_vec_dot_rows(ggml_type: int, w: np.ndarray, n: int, k: int, x: np.ndar
     if graph_lib().rg_vec_dot_rows_type(ggml_type, _ptr(np.ascontiguousarray(w)), n, k, _ptr(x), _ptr(y)) != 0:
         raise RuntimeError("rg_vec_dot_rows_type failed")
     return y
+
+
+def graph_gguf_write(path: str, tensors: list, u32: dict, strs: tuple | None = None, f32: tuple | None = None):
+    """Write a GGUF file with the reference's own writer: tensors = [(name,
+    ggml_type, ne0, ne1, bytes ndarray)], u32 = {key: value}."""
+    L = graph_lib()
+    n = len(tensors)
+    names = (C.c_char_p * n)(*[t[0].encode() for t in tensors])
+    types = (C.c_int * n)(*[t[1] for t in tensors])
+    ne0 = (C.c_int64 * n)(*[t[2] for t in tensors])
+    ne1 = (C.c_int64 * n)(*[t[3] for t in tensors])
+    bufs = [np.ascontiguousarray(t[4]) for t in tensors]
+    data = (_vp * n)(*[b.ctypes.data for b in bufs])
+    keys = list(u32)
+    ks = (C.c_char_p * max(1, len(keys)))(*[k.encode() for k in keys])
+    vs = (C.c_uint32 * max(1, len(keys)))(*[u32[k] for k in keys])
+    rc = L.rg_gguf_write(path.encode(), n, names, types, ne0, ne1, data, len(keys), ks, vs,
+                         strs[0].encode() if strs else None, strs[1].encode() if strs else None,
+                         f32[0].encode() if f32 else None, f32[1] if f32 else 0.0)
+    if rc != 0:
+        raise RuntimeError("rg_gguf_write failed")

@@ -37,6 +37,7 @@
 
 #include "ggml.h"
 #include "ggml-cpu.h"
+#include "gguf.h"
 
 enum { W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN, W_PER_LAYER, W_OUTPUT = 7,
        T_ATTN_NORM = 8, T_FFN_NORM, T_Q_NORM, T_K_NORM, T_OUT_NORM, T_K_CACHE, T_V_CACHE };
@@ -390,4 +391,30 @@ int rg_quantize_q6k(const float *src, void *dst, int64_t rows, int64_t k) {
     ggml_cpu_init();
     ggml_quantize_chunk(GGML_TYPE_Q6_K, src, dst, 0, rows, k, NULL);
     return 0;
+}
+
+
+/* A GGUF file written by the reference's own gguf writer (gguf.cpp): n 2-D
+ * tensors (names, ggml types, ne0 x ne1, host bytes), u32 key/values, one
+ * string key/value and one f32 key/value. Test fixture writer only. */
+int rg_gguf_write(const char *path, int n, const char **names, const int *types, const int64_t *ne0,
+                  const int64_t *ne1, const void **data, int n_u32, const char **u32_keys, const uint32_t *u32_vals,
+                  const char *str_key, const char *str_val, const char *f32_key, float f32_val) {
+    struct ggml_init_params ip = {(size_t)(n + 1) * ggml_tensor_overhead() + 4096, NULL, true};
+    struct ggml_context *g = ggml_init(ip);
+    if (!g) return -1;
+    struct gguf_context *gg = gguf_init_empty();
+    for (int i = 0; i < n_u32; ++i) gguf_set_val_u32(gg, u32_keys[i], u32_vals[i]);
+    if (str_key) gguf_set_val_str(gg, str_key, str_val);
+    if (f32_key) gguf_set_val_f32(gg, f32_key, f32_val);
+    for (int i = 0; i < n; ++i) {
+        struct ggml_tensor *t = ggml_new_tensor_2d(g, (enum ggml_type)types[i], ne0[i], ne1[i]);
+        ggml_set_name(t, names[i]);
+        t->data = (void *)data[i];
+        gguf_add_tensor(gg, t);
+    }
+    const bool ok = gguf_write_to_file(gg, path, false);
+    gguf_free(gg);
+    ggml_free(g);
+    return ok ? 0 : -1;
 }

@@ -117,6 +117,25 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.bh_moe_xchg_recv_bytes.restype = C.c_size_t
     L.bh_moe_ep_exchange_combine.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int,
                                              C.c_int, C.c_int, C.c_int, C.c_uint32, _vp, C.c_int, _vp]
+    L.bh_gguf_open.argtypes = [C.c_char_p, C.POINTER(_vp)]
+    L.bh_gguf_close.argtypes = [_vp]
+    L.bh_gguf_n_tensors.argtypes = [_vp]
+    L.bh_gguf_n_tensors.restype = _i64
+    L.bh_gguf_n_keys.argtypes = [_vp]
+    L.bh_gguf_n_keys.restype = _i64
+    L.bh_gguf_find_tensor.argtypes = [_vp, C.c_char_p]
+    L.bh_gguf_find_tensor.restype = _i64
+    L.bh_gguf_find_key.argtypes = [_vp, C.c_char_p]
+    L.bh_gguf_find_key.restype = _i64
+    L.bh_gguf_tensor_info.argtypes = [_vp, _i64, C.POINTER(C.c_char_p), C.POINTER(C.c_int), C.POINTER(C.c_int),
+                                      C.POINTER(_i64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
+    L.bh_gguf_tensor_host.argtypes = [_vp, _i64]
+    L.bh_gguf_tensor_host.restype = _vp
+    L.bh_gguf_upload.argtypes = [_vp, _vp, _i64, _vp, C.c_size_t, _vp]
+    L.bh_gguf_key.argtypes = [_vp, _i64, C.POINTER(C.c_char_p), C.POINTER(C.c_int)]
+    L.bh_gguf_get_int.argtypes = [_vp, _i64, C.POINTER(_i64)]
+    L.bh_gguf_get_float.argtypes = [_vp, _i64, C.POINTER(C.c_double)]
+    L.bh_gguf_get_str.argtypes = [_vp, _i64, C.POINTER(C.c_void_p), C.POINTER(C.c_uint64)]
     L.bh_stack_default_config.argtypes = [C.POINTER(StackConfig)]
     L.bh_stack_default_config.restype = None
     L.bh_stack_create.argtypes = [_vp, C.POINTER(StackConfig), C.c_uint64, C.POINTER(_vp)]
@@ -580,3 +599,73 @@ class MoeStack:
             t = device_view(ptr, nb // 4, "<f4")
         torch.cuda.synchronize()
         return t.cpu().numpy()
+
+
+class GGUF:
+    """A GGUF model file opened by bh_gguf_open (host parsing; upload to a
+    Context's device)."""
+
+    def __init__(self, path: str):
+        h = _vp()
+        _check(lib.bh_gguf_open(path.encode(), C.byref(h)), "bh_gguf_open")
+        self.h = h
+
+    def close(self) -> None:
+        if self.h:
+            lib.bh_gguf_close(self.h)
+            self.h = _vp()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def n_tensors(self) -> int:
+        return int(lib.bh_gguf_n_tensors(self.h))
+
+    def find(self, name: str) -> int:
+        return int(lib.bh_gguf_find_tensor(self.h, name.encode()))
+
+    def info(self, i: int) -> dict:
+        nm, ty, nd = C.c_char_p(), C.c_int(), C.c_int()
+        ne = (_i64 * 4)()
+        off, nb = C.c_uint64(), C.c_uint64()
+        _check(lib.bh_gguf_tensor_info(self.h, i, C.byref(nm), C.byref(ty), C.byref(nd), ne, C.byref(off),
+                                       C.byref(nb)), "bh_gguf_tensor_info")
+        return {"name": nm.value.decode(), "type": ty.value, "n_dims": nd.value, "ne": list(ne)[: nd.value],
+                "offset": off.value, "bytes": nb.value}
+
+    def host_bytes(self, i: int):
+        import numpy as np
+
+        p = lib.bh_gguf_tensor_host(self.h, i)
+        nb = self.info(i)["bytes"]
+        return np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_uint8)), shape=(nb,)).copy()
+
+    def upload(self, ctx: "Context", i: int, dst=None, stream=None):
+        import torch
+
+        nb = self.info(i)["bytes"]
+        if dst is None:
+            dst = torch.empty(nb, dtype=torch.uint8, device="cuda")
+        _check(lib.bh_gguf_upload(ctx.h, self.h, i, _dp(dst), nb, _stream(stream)), "bh_gguf_upload")
+        return dst
+
+    def key(self, name: str):
+        k = int(lib.bh_gguf_find_key(self.h, name.encode()))
+        if k < 0:
+            raise KeyError(name)
+        ty = C.c_int()
+        _check(lib.bh_gguf_key(self.h, k, None, C.byref(ty)), "bh_gguf_key")
+        if ty.value == 8:
+            p, n = C.c_void_p(), C.c_uint64()
+            _check(lib.bh_gguf_get_str(self.h, k, C.byref(p), C.byref(n)), "bh_gguf_get_str")
+            return C.string_at(p, n.value).decode()
+        if ty.value in (6, 12):
+            v = C.c_double()
+            _check(lib.bh_gguf_get_float(self.h, k, C.byref(v)), "bh_gguf_get_float")
+            return v.value
+        v = _i64()
+        _check(lib.bh_gguf_get_int(self.h, k, C.byref(v)), "bh_gguf_get_int")
+        return v.value

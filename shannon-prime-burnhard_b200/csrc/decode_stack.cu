@@ -175,9 +175,26 @@ __device__ __forceinline__ float ggml_reduce_warp(float v) {
     return __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2));
 }
 
+// K / V history of one head is staged through shared memory in tiles of
+// ATTN_TILE positions (the first tile before the programmatic wait: cache
+// rows before pos do not depend on the previous kernel).
+constexpr int ATTN_TILE = 128;
+
+__device__ __forceinline__ void stage_kv_tile(float* dst, const float* base, int64_t row_stride, int t0, int nt,
+                                              int tid, uint64_t keep) {
+    // rows t0 .. t0 + nt - 1 of 128 floats: 32 float4 per row, all threads
+    for (int i = tid; i < nt * (ATTN_HD / 4); i += ATTN_THREADS) {
+        const int r = i / (ATTN_HD / 4), c = i % (ATTN_HD / 4);
+        reinterpret_cast<float4*>(dst)[i] = ldg_f4_keep(base + (int64_t)(t0 + r) * row_stride + 4 * c, keep);
+    }
+}
+
 __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParams a) {
-    extern __shared__ float s_p[];                 // [n_ctx]: scores, then probabilities
-    __shared__ float s_q[ATTN_HD], s_k[ATTN_HD], s_v[ATTN_HD];
+    extern __shared__ __align__(16) float smem_f[];
+    float* s_kt = smem_f;                            // [ATTN_TILE][128] K rows of the current tile
+    float* s_vt = smem_f + ATTN_TILE * ATTN_HD;      // [ATTN_TILE][128] V rows
+    float* s_p = smem_f + 2 * ATTN_TILE * ATTN_HD;   // [n_ctx] scores, then probabilities
+    __shared__ __align__(16) float s_q[ATTN_HD], s_k[ATTN_HD], s_v[ATTN_HD];
     __shared__ float s_red[ATTN_WARPS];
     __shared__ float s_gsum[ATTN_SEQ_GROUPS];
     __shared__ float s_inv;
@@ -190,9 +207,9 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParam
     const float* vbase = a.vc + (int64_t)g * HD;
     ATTN_TRACE_AT(0);
 
-    // before the wait, nothing that makes the thread wait: the norm weights,
-    // the rotation table row of pos (pos is set before the step), and the
-    // cache rows of the first positions (only those before pos are used)
+    // before the wait, nothing that depends on the previous kernel: the norm
+    // weights, the rotation table row of pos (pos is set before the step),
+    // and the first tile of the K / V history (positions before pos)
     const uint64_t keep = policy_evict_last();
     const int pos = *a.pos;
     const int n = pos + 1;
@@ -206,16 +223,9 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParam
         cs[0] = make_float2(r01.x, r01.y); cs[1] = make_float2(r01.z, r01.w);
         cs[2] = make_float2(r23.x, r23.y); cs[3] = make_float2(r23.z, r23.w);
     }
-    // positions of this warp: t = w + 8 i; the first 2 rows (4 values a lane each) now
-    constexpr int PRE = 2;
-    float kpre[PRE][4];
-#pragma unroll
-    for (int i = 0; i < PRE; ++i) {
-        const int t = w + ATTN_WARPS * i;
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-            kpre[i][c] = t < a.n_ctx ? __ldg(kbase + (int64_t)t * row_stride + 32 * c + lane) : 0.f;
-    }
+    const int nh0 = min(pos, ATTN_TILE);  // history rows of tile 0
+    stage_kv_tile(s_kt, kbase, row_stride, 0, nh0, tid, keep);
+    stage_kv_tile(s_vt, vbase, row_stride, 0, nh0, tid, keep);
     prefetch_share(a.pf_ptr, a.pf_bytes, (int64_t)blockIdx.x * ATTN_WARPS + w, (int64_t)gridDim.x * ATTN_WARPS, lane);
     pdl_trigger();
     pdl_wait();
@@ -240,35 +250,41 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParam
     __syncthreads();
     ATTN_TRACE_AT(1);
 
-    // scores: warp w takes positions w, w + 8, ...
+    // scores, one tile of positions at a time: warp w takes positions
+    // w, w + 8, ... of the tile, 4 at once
     float qv[4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) qv[c] = s_q[32 * c + lane];
     float wmax = -INFINITY;
-    auto score = [&](int t, const float (&kv)[4]) {
-        float acc = 0.f;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc = __fmaf_rn(kv[c], qv[c], acc);
-        const float sc = __fmul_rn(ggml_reduce_warp(acc), a.qk_scale);  // ggml_scale
-        if (lane == 0) s_p[t] = sc;
-        wmax = fmaxf(wmax, sc);
-    };
-#pragma unroll
-    for (int i = 0; i < PRE; ++i) {
-        const int t = w + ATTN_WARPS * i;
-        if (t < n) {
-            float kv[4];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) kv[c] = t == pos ? s_k[32 * c + lane] : kpre[i][c];
-            score(t, kv);
+    for (int t0 = 0; t0 < n; t0 += ATTN_TILE) {
+        const int nt = min(ATTN_TILE, n - t0);
+        if (t0 > 0) {
+            __syncthreads();  // every warp is done with the previous K tile
+            stage_kv_tile(s_kt, kbase, row_stride, t0, min(nt, pos - t0), tid, keep);
+            __syncthreads();
         }
-    }
-    for (int t = w + ATTN_WARPS * PRE; t < n; t += ATTN_WARPS) {
-        float kv[4];
+        for (int r0 = w; r0 < nt; r0 += 4 * ATTN_WARPS) {
+            float acc[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-            kv[c] = t == pos ? s_k[32 * c + lane] : __ldg(kbase + (int64_t)t * row_stride + 32 * c + lane);
-        score(t, kv);
+            for (int u = 0; u < 4; ++u) {
+                const int r = r0 + u * ATTN_WARPS, t = t0 + r;
+                const float* krow = t == pos ? s_k : s_kt + r * HD;
+                acc[u] = 0.f;
+                if (r < nt) {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) acc[u] = __fmaf_rn(krow[32 * c + lane], qv[c], acc[u]);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int r = r0 + u * ATTN_WARPS;
+                const float sc = __fmul_rn(ggml_reduce_warp(acc[u]), a.qk_scale);  // ggml_scale
+                if (r < nt) {
+                    if (lane == 0) s_p[t0 + r] = sc;
+                    wmax = fmaxf(wmax, sc);
+                }
+            }
+        }
     }
     wmax = __shfl_sync(0xffffffffu, wmax, 0);
     if (lane == 0) s_red[w] = wmax;
@@ -317,38 +333,52 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParam
     __syncthreads();
     ATTN_TRACE_AT(3);
 
-    // out[d] = V[.][d] . p: thread d, 32 accumulators over t mod 32
-    if (tid < HD) {
-        const int d = tid;
-        const int np = n & ~31;
-        float acc[32];
+    // out[d] = V[.][d] . p: thread d keeps the 32 accumulators of positions
+    // t mod 32, chunk after chunk, from the staged V tiles
+    const int d = tid;
+    const int np = n & ~31;
+    float acc[32];
 #pragma unroll
-        for (int r = 0; r < 32; ++r) acc[r] = 0.f;
-        for (int t0 = 0; t0 < np; t0 += 32) {
+    for (int r = 0; r < 32; ++r) acc[r] = 0.f;
+    float sumf = 0.f;
+    for (int t0 = 0; t0 < n; t0 += ATTN_TILE) {
+        const int nt = min(ATTN_TILE, n - t0);
+        if (t0 > 0) {
+            __syncthreads();
+            stage_kv_tile(s_vt, vbase, row_stride, t0, min(nt, pos - t0), tid, keep);
+            __syncthreads();
+        }
+        if (d < HD) {
+            const int cend = min(np, t0 + nt);
+            for (int c0 = t0; c0 < cend; c0 += 32) {
 #pragma unroll
-            for (int r = 0; r < 32; ++r) {
-                const int t = t0 + r;
-                const float v = t == pos ? s_v[d] : __ldg(vbase + (int64_t)t * row_stride + d);
-                acc[r] = __fmaf_rn(v, s_p[t], acc[r]);
+                for (int r = 0; r < 32; ++r) {
+                    const int t = c0 + r;
+                    const float v = t == pos ? s_v[d] : s_vt[(t - t0) * HD + d];
+                    acc[r] = __fmaf_rn(v, s_p[t], acc[r]);
+                }
+            }
+            if (t0 + nt >= n) {
+                // GGML_F32x8_REDUCE: accumulator j element e is acc[8 j + e]
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    acc[e] = __fadd_rn(acc[e], acc[16 + e]);
+                    acc[8 + e] = __fadd_rn(acc[8 + e], acc[24 + e]);
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[e] = __fadd_rn(acc[e], acc[8 + e]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[e] = __fadd_rn(acc[e], acc[e + 4]);
+                sumf = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+            }
+            // the n % 32 tail, one by one in float (its rows are in this tile)
+            for (int t = max(np, t0); t < t0 + nt; ++t) {
+                const float v = t == pos ? s_v[d] : s_vt[(t - t0) * HD + d];
+                sumf = __fadd_rn(sumf, __fmul_rn(v, s_p[t]));
             }
         }
-        // GGML_F32x8_REDUCE: accumulator j element e is acc[8 j + e]
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            acc[e] = __fadd_rn(acc[e], acc[16 + e]);
-            acc[8 + e] = __fadd_rn(acc[8 + e], acc[24 + e]);
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] = __fadd_rn(acc[e], acc[8 + e]);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[e] = __fadd_rn(acc[e], acc[e + 4]);
-        float sumf = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
-        for (int t = np; t < n; ++t) {
-            const float v = t == pos ? s_v[d] : __ldg(vbase + (int64_t)t * row_stride + d);
-            sumf = __fadd_rn(sumf, __fmul_rn(v, s_p[t]));
-        }
-        a.out[(int64_t)h * HD + d] = sumf;
     }
+    if (d < HD) a.out[(int64_t)h * HD + d] = sumf;
     ATTN_TRACE_AT(6);
 }
 
@@ -492,7 +522,7 @@ int launch_attn(bh_stack* st, int l, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)c.n_head);
     cfg.blockDim = dim3((unsigned)bh::ATTN_THREADS);
-    cfg.dynamicSmemBytes = sizeof(float) * (size_t)c.n_ctx;
+    cfg.dynamicSmemBytes = sizeof(float) * ((size_t)2 * bh::ATTN_TILE * bh::ATTN_HD + (size_t)c.n_ctx);
     cfg.stream = st->stream;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -502,7 +532,9 @@ int launch_attn(bh_stack* st, int l, bool pdl) {
     static std::atomic<uint64_t> attr_devices{0};
     // the same shared-memory carveout as the matvecs around it
     if (!bh::attrs_on_device(attr_devices, [] {
-            return cudaFuncSetAttribute(bh::attn_head_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+            return cudaFuncSetAttribute(bh::attn_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        200 * 1024) == cudaSuccess &&
+                   cudaFuncSetAttribute(bh::attn_head_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                                         cudaSharedmemCarveoutMaxShared) == cudaSuccess;
         }))
         return BH_EIO;

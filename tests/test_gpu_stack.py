@@ -115,8 +115,9 @@ def test_stack_rejects_bad_config(ctx, bh):
 def test_stack_attention_kernel(ctx, bh, oracle, n_head, n_head_kv, n_ctx, pos):
     """The attention launch alone: the last layer's q|k|v as the device
     projected them, through per-head RMSNorm, NeoX RoPE, the KV append and
-    softmax attention over positions 0..pos, against the CPU restatement
-    (fp32; the device sums in another order and uses its own sin/cos)."""
+    softmax attention over positions 0..pos, against a float64 restatement
+    (the device follows the reference's binary32 order; the reference graph
+    comparison of tests/test_gpu_stack_reference.py checks that bit for bit)."""
     import torch
 
     from cpu_stack import rmsnorm, rope_neox
@@ -148,7 +149,8 @@ def test_stack_attention_kernel(ctx, bh, oracle, n_head, n_head_kv, n_ctx, pos):
     kc_dev = st.to_host(L, bh.T_K_CACHE).reshape(n_ctx, n_head_kv, hd)
     vc_dev = st.to_host(L, bh.T_V_CACHE).reshape(n_ctx, n_head_kv, hd)
     assert np.array_equal(vc_dev[pos], v)
-    assert np.abs(kc_dev[pos] - kr).max() <= 1e-5 * np.abs(kr).max()
+    # RMSNorm and the ggml rotation table: equal up to the double sum's order
+    assert np.abs(kc_dev[pos] - kr).max() <= 1e-6 * np.abs(kr).max()
     group = n_head // n_head_kv
     scale = np.float32(1.0) / np.sqrt(np.float32(hd))
     want = np.empty((n_head, hd), dtype=np.float64)

@@ -25,16 +25,21 @@ pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(not os.path.exists(om.GRAPH_SO), reason="oracle/_ref not built (no reference tree)")]
 
 
-def run_both(bh, ctx, oracle, cfg_over, n_pos, seed, threads):
+def run_both(bh, ctx, oracle, cfg_over, positions, seed, threads, kv_fill=0):
+    """Decode at the given positions on the device stack and on the
+    reference graph holding copies of its weights (and of a seeded K/V
+    history of kv_fill positions); rows of (tokens, logits, hidden)."""
     import torch
 
     st = bh.Stack(ctx, bh.default_stack_config(**cfg_over), seed=seed)
+    if kv_fill:
+        st.fill_kv(kv_fill, seed + 1)
     cfg, w, norms, kc, vc = stack_to_cpu(st)
     g = om.graph_stack_from_cpu(cfg, w, norms, kc, vc)
     del w
     tok = torch.zeros(1, dtype=torch.int32, device="cuda")
     rows = []
-    for pos in range(n_pos):
+    for pos in positions:
         x = oracle.normal((cfg["n_embd"],), 5000 + pos, 0.0, 1.0)
         st.set_pos(pos)
         st.decode(torch.from_numpy(x).cuda(), tok)
@@ -50,12 +55,16 @@ def run_both(bh, ctx, oracle, cfg_over, n_pos, seed, threads):
     return rows
 
 
+def bit_identical(rows):
+    return [bool(np.array_equal(h_dev.view(np.uint32), h_ref.view(np.uint32)) and
+                 np.array_equal(lg_dev.view(np.uint32), lg_ref.view(np.uint32)) and t_dev == t_ref)
+            for t_dev, t_ref, lg_dev, lg_ref, h_dev, h_ref in rows]
+
+
 def check(rows, h_tol, lg_tol, margin):
     """Per position: hidden and logit errors relative to the reference's
-    largest magnitude, token equality where the top-2 margin is clear.
-    Returns (tokens equal, positions whose hidden state and logits are
-    bit-identical)."""
-    agree, exact, errs = 0, 0, []
+    largest magnitude, token equality where the top-2 margin is clear."""
+    agree, errs = 0, []
     for t_dev, t_ref, lg_dev, lg_ref, h_dev, h_ref in rows:
         eh = float(np.abs(h_dev - h_ref).max() / np.abs(h_ref).max())
         el = float(np.abs(lg_dev - lg_ref).max() / np.abs(lg_ref).max())
@@ -63,28 +72,39 @@ def check(rows, h_tol, lg_tol, margin):
         clear = srt[-1] - srt[-2] > margin * np.abs(lg_ref).max()
         errs.append((round(eh, 7), round(el, 7), t_dev == t_ref, bool(clear)))
         agree += t_dev == t_ref
-        exact += np.array_equal(h_dev.view(np.uint32), h_ref.view(np.uint32)) and \
-            np.array_equal(lg_dev.view(np.uint32), lg_ref.view(np.uint32))
     for eh, el, same, clear in errs:
         assert eh <= h_tol and el <= lg_tol and (same or not clear), errs
-    return agree, exact, errs
+    return agree, errs
 
 
-def test_small_stack_tokens_match_reference_graph(ctx, bh, oracle):
-    cfg = dict(n_layer=3, n_embd=1024, n_head=8, n_head_kv=2, head_dim=128, n_ff=2048, n_vocab=5000, n_ctx=40)
-    rows = run_both(bh, ctx, oracle, cfg, 40, 17, len(os.sched_getaffinity(0)))
-    agree, exact, errs = check(rows, 2e-2, 5e-2, 1e-2)
-    assert agree == len(rows), errs
-    # the attention reproduces the reference's order: bit-identical except
-    # where a softmax tail element's exp or a double sum's last bit differs
-    assert exact >= len(rows) - 4, (exact, errs)
+# Positions whose attention covers a multiple of 8 positions: every softmax
+# element then goes through ggml_v_expf, which the device restates exactly.
+# (The n % 8 tail of a softmax row is evaluated by the reference with the
+# host's libm expf, not restated here.)
+WHOLE = [8 * i + 7 for i in range(16)]
 
 
-def test_config2_36_layers_tokens_match_reference_graph(ctx, bh, oracle):
-    """BASELINE config 2 at full size (36 layers, 151936-row LM head): 128
-    tokens at positions 0..127, device against the reference's ggml graph."""
+def test_small_stack_bit_identical_to_reference_graph(ctx, bh, oracle):
+    cfg = dict(n_layer=3, n_embd=1024, n_head=8, n_head_kv=2, head_dim=128, n_ff=2048, n_vocab=5000, n_ctx=128)
+    rows = run_both(bh, ctx, oracle, cfg, WHOLE, 17, len(os.sched_getaffinity(0)), kv_fill=128)
+    assert all(bit_identical(rows)), bit_identical(rows)
+
+
+def test_config2_36_layers_bit_identical_to_reference_graph(ctx, bh, oracle):
+    """BASELINE config 2 at full size (36 layers, 151936-row LM head): the
+    device step and the reference engine's ggml graph on the reference's CPU
+    backend give the same hidden state, logits and token, bit for bit, at 16
+    positions (each appending its K/V for the next)."""
     cfg = dict(n_layer=36, n_embd=4096, n_head=32, n_head_kv=8, head_dim=128, n_ff=12288, n_vocab=151936, n_ctx=128)
-    rows = run_both(bh, ctx, oracle, cfg, 128, 20261201, len(os.sched_getaffinity(0)))
-    agree, exact, errs = check(rows, 5e-2, 1e-1, 1e-2)
+    rows = run_both(bh, ctx, oracle, cfg, WHOLE, 20261201, len(os.sched_getaffinity(0)), kv_fill=128)
+    assert all(bit_identical(rows)), bit_identical(rows)
+
+
+def test_sequential_positions_tokens_match_reference_graph(ctx, bh, oracle):
+    """Positions 0..39 in order from an empty cache: where a softmax row has an
+    n % 8 tail the two exps may differ in the last bit, and the 3-layer stack
+    stays within a small tolerance with equal tokens."""
+    cfg = dict(n_layer=3, n_embd=1024, n_head=8, n_head_kv=2, head_dim=128, n_ff=2048, n_vocab=5000, n_ctx=40)
+    rows = run_both(bh, ctx, oracle, cfg, range(40), 23, len(os.sched_getaffinity(0)))
+    agree, errs = check(rows, 2e-2, 5e-2, 1e-2)
     assert agree == len(rows), errs
-    print("bit-identical positions:", exact, "of", len(rows))
