@@ -81,6 +81,7 @@ struct AttnParams {
     int64_t* trace;          // timeline probe (builds with BH_TRACE only; else unused)
     const uint8_t* pf_ptr;   // L2 prefetch of the weights streamed next (null: none)
     int64_t pf_bytes;
+    int* status;             // device status word (a bounded copy wait that ran out)
 };
 
 #ifdef BH_TRACE
@@ -109,10 +110,10 @@ constexpr int64_t TRACE_LAUNCH = 256 * DENSE_MAX_WARPS * 8;
 //  - NeoX RoPE: x0' = x0 c - x1 s, x1' = x0 s + x1 c for the pairs (i, i + 64),
 //    (c, s) from a table the host fills exactly as ggml's rope cache does
 //    (theta = pos, theta *= powf(base, -2/n_dims) per pair, cosf / sinf);
-//  - K.Q per position as ggml_vec_dot_f32's AVX2 path: lane l of a warp holds
-//    the fma accumulator of elements l, l + 32, l + 64, l + 96 (the 4 x 8
-//    vector accumulators), reduced in GGML_F32x8_REDUCE's order by shuffles;
-//    then ggml_scale (one multiply);
+//  - K.Q per position as ggml_vec_dot_f32's AVX2 path: one thread per
+//    position keeps the 32 fma accumulators (the 4 x 8 vector accumulators;
+//    accumulator l takes elements l, l + 32, l + 64, l + 96) and reduces them
+//    in registers in GGML_F32x8_REDUCE's order; then ggml_scale (one multiply);
 //  - soft_max: max, exp(x - max) by ggml_v_expf for every whole group of 8
 //    (the n % 8 tail as (float)exp(double)), the per-8 float sums
 //    ((p4+p0)+(p6+p2))+((p5+p1)+(p7+p3)) accumulated in double in group
@@ -164,40 +165,50 @@ __device__ __forceinline__ float4 rope4(float4 x, const float2 (&cs)[4], bool lo
                        rope1(x.w, p.w, cs[3], low));
 }
 
-// GGML_F32x8_REDUCE over a warp whose lane l = 8 j + e holds vector
-// accumulator j, element e: x0 += x2, x1 += x3; x0 += x1; then the 8 elements
-// (e + e+4, two horizontal adds). The result is in lane 0.
-__device__ __forceinline__ float ggml_reduce_warp(float v) {
-    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 16));
-    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 8));
-    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 4));
-    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1));
-    return __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2));
+// K / V history of one head is staged through shared memory in tiles of
+// ATTN_TILE positions by bulk copies (one 512-byte row each, this GPU's own
+// memory, no multicast) completing on an mbarrier; the first tile is issued
+// before the programmatic wait (cache rows before pos do not depend on the
+// previous kernel) and waited for only when the scores need it. Rows are
+// ATTN_KROW floats apart: 16-byte reads of consecutive rows by consecutive
+// threads then fall in distinct bank groups.
+constexpr int ATTN_TILE = 128;
+constexpr int ATTN_KROW = ATTN_HD + 4;
+
+// Issue the bulk copies of rows t0 .. t0 + nh - 1 into dst (lane 0 of every
+// warp takes rows w, w + 8, ...); the barrier was armed for nh * 512 bytes.
+__device__ __forceinline__ void issue_kv_rows(float* dst, const float* base, int64_t row_stride, int t0, int nh,
+                                              uint64_t* bar, int w, int lane, uint64_t pol) {
+    if (lane != 0) return;
+    for (int r = w; r < nh; r += ATTN_WARPS)
+        bulk_g2s(dst + r * ATTN_KROW, base + (int64_t)(t0 + r) * row_stride, ATTN_HD * 4, bar, pol);
 }
 
-// K / V history of one head is staged through shared memory in tiles of
-// ATTN_TILE positions (the first tile before the programmatic wait: cache
-// rows before pos do not depend on the previous kernel).
-constexpr int ATTN_TILE = 128;
-
-__device__ __forceinline__ void stage_kv_tile(float* dst, const float* base, int64_t row_stride, int t0, int nt,
-                                              int tid, uint64_t keep) {
-    // rows t0 .. t0 + nt - 1 of 128 floats: 32 float4 per row, all threads
-    for (int i = tid; i < nt * (ATTN_HD / 4); i += ATTN_THREADS) {
-        const int r = i / (ATTN_HD / 4), c = i % (ATTN_HD / 4);
-        reinterpret_cast<float4*>(dst)[i] = ldg_f4_keep(base + (int64_t)(t0 + r) * row_stride + 4 * c, keep);
+// Arm (thread 0) and issue one tile of K and V rows.
+__device__ __forceinline__ void load_kv_tile(float* s_kt, float* s_vt, const float* kbase, const float* vbase,
+                                             int64_t row_stride, int t0, int nh, uint64_t* bar_k, uint64_t* bar_v,
+                                             bool want_k, bool want_v, int tid, uint64_t pol) {
+    if (tid == 0) {
+        if (want_k) mbar_arrive_expect_tx(bar_k, (uint32_t)(nh * ATTN_HD * 4));
+        if (want_v) mbar_arrive_expect_tx(bar_v, (uint32_t)(nh * ATTN_HD * 4));
     }
+    __syncthreads();
+    const int w = tid >> 5, lane = tid & 31;
+    if (want_k) issue_kv_rows(s_kt, kbase, row_stride, t0, nh, bar_k, w, lane, pol);
+    if (want_v) issue_kv_rows(s_vt, vbase, row_stride, t0, nh, bar_v, w, lane, pol);
 }
 
 __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParams a) {
-    extern __shared__ __align__(16) float smem_f[];
-    float* s_kt = smem_f;                            // [ATTN_TILE][128] K rows of the current tile
-    float* s_vt = smem_f + ATTN_TILE * ATTN_HD;      // [ATTN_TILE][128] V rows
-    float* s_p = smem_f + 2 * ATTN_TILE * ATTN_HD;   // [n_ctx] scores, then probabilities
+    extern __shared__ __align__(128) float smem_f[];
+    float* s_kt = smem_f;                              // [ATTN_TILE][ATTN_KROW] K rows of the current tile
+    float* s_vt = smem_f + ATTN_TILE * ATTN_KROW;      // [ATTN_TILE][ATTN_KROW] V rows
+    float* s_p = smem_f + 2 * ATTN_TILE * ATTN_KROW;   // [n_ctx] scores, then probabilities
     __shared__ __align__(16) float s_q[ATTN_HD], s_k[ATTN_HD], s_v[ATTN_HD];
     __shared__ float s_red[ATTN_WARPS];
     __shared__ float s_gsum[ATTN_SEQ_GROUPS];
     __shared__ float s_inv;
+    __shared__ __align__(8) uint64_t bar_k, bar_v;
+    __shared__ int s_ok;
     constexpr int HD = ATTN_HD;
     const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int group = a.n_head / a.n_head_kv, g = h / group;
@@ -209,10 +220,16 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParam
 
     // before the wait, nothing that depends on the previous kernel: the norm
     // weights, the rotation table row of pos (pos is set before the step),
-    // and the first tile of the K / V history (positions before pos)
+    // and the copies of the first tile of the K / V history
     const uint64_t keep = policy_evict_last();
     const int pos = *a.pos;
     const int n = pos + 1;
+    if (tid == 0) {
+        mbar_init(&bar_k, 1);
+        mbar_init(&bar_v, 1);
+        fence_mbar_init();
+        s_ok = 1;
+    }
     float4 qn = f4_zero(), kn = f4_zero();
     float2 cs[4];
     if (w == 0) {
@@ -223,9 +240,8 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParam
         cs[0] = make_float2(r01.x, r01.y); cs[1] = make_float2(r01.z, r01.w);
         cs[2] = make_float2(r23.x, r23.y); cs[3] = make_float2(r23.z, r23.w);
     }
-    const int nh0 = min(pos, ATTN_TILE);  // history rows of tile 0
-    stage_kv_tile(s_kt, kbase, row_stride, 0, nh0, tid, keep);
-    stage_kv_tile(s_vt, vbase, row_stride, 0, nh0, tid, keep);
+    load_kv_tile(s_kt, s_vt, kbase, vbase, row_stride, 0, min(pos, ATTN_TILE), &bar_k, &bar_v, true, true, tid, keep);
+    uint32_t ph_k = 0, ph_v = 0;
     prefetch_share(a.pf_ptr, a.pf_bytes, (int64_t)blockIdx.x * ATTN_WARPS + w, (int64_t)gridDim.x * ATTN_WARPS, lane);
     pdl_trigger();
     pdl_wait();
@@ -247,49 +263,74 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParam
             reinterpret_cast<float4*>(a.vc + (int64_t)pos * row_stride + (int64_t)g * HD)[lane] = v;
         }
     }
-    __syncthreads();
     ATTN_TRACE_AT(1);
 
-    // scores, one tile of positions at a time: warp w takes positions
-    // w, w + 8, ... of the tile, 4 at once
-    float qv[4];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) qv[c] = s_q[32 * c + lane];
-    float wmax = -INFINITY;
-    for (int t0 = 0; t0 < n; t0 += ATTN_TILE) {
+    // scores: thread r of a tile computes position t0 + r whole, in
+    // ggml_vec_dot_f32's order (accumulator l = element l of the 4 x 8
+    // vectors, fma over the 4 steps of 32), then GGML_F32x8_REDUCE in
+    // registers and ggml_scale
+    float tmax = -INFINITY;
+    bool ok = true;
+    for (int t0 = 0; t0 < n && ok; t0 += ATTN_TILE) {
         const int nt = min(ATTN_TILE, n - t0);
         if (t0 > 0) {
-            __syncthreads();  // every warp is done with the previous K tile
-            stage_kv_tile(s_kt, kbase, row_stride, t0, min(nt, pos - t0), tid, keep);
-            __syncthreads();
+            __syncthreads();  // every thread is done with the previous K tile
+            fence_proxy_async_smem();
+            load_kv_tile(s_kt, s_vt, kbase, vbase, row_stride, t0, min(nt, pos - t0), &bar_k, &bar_v, true, false,
+                         tid, keep);
         }
-        for (int r0 = w; r0 < nt; r0 += 4 * ATTN_WARPS) {
-            float acc[4];
+        // one decision for the whole block (and s_q / s_k of warp 0 visible)
+        ok = __syncthreads_and(mbar_wait_bounded(&bar_k, ph_k)) != 0;
+        if (!ok) break;
+        ph_k ^= 1u;
+        for (int r = tid; r < nt; r += ATTN_THREADS) {
+            const int t = t0 + r;
+            const float4* krow = reinterpret_cast<const float4*>(t == pos ? s_k : s_kt + r * ATTN_KROW);
+            const float4* qv = reinterpret_cast<const float4*>(s_q);
+            float acc[32];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int r = r0 + u * ATTN_WARPS, t = t0 + r;
-                const float* krow = t == pos ? s_k : s_kt + r * HD;
-                acc[u] = 0.f;
-                if (r < nt) {
+            for (int l = 0; l < 32; ++l) acc[l] = 0.f;
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) acc[u] = __fmaf_rn(krow[32 * c + lane], qv[c], acc[u]);
+            for (int i0 = 0; i0 < 4; ++i0) {
+#pragma unroll
+                for (int l4 = 0; l4 < 8; ++l4) {
+                    const float4 kx = krow[8 * i0 + l4], qx = qv[8 * i0 + l4];
+                    acc[4 * l4 + 0] = __fmaf_rn(kx.x, qx.x, acc[4 * l4 + 0]);
+                    acc[4 * l4 + 1] = __fmaf_rn(kx.y, qx.y, acc[4 * l4 + 1]);
+                    acc[4 * l4 + 2] = __fmaf_rn(kx.z, qx.z, acc[4 * l4 + 2]);
+                    acc[4 * l4 + 3] = __fmaf_rn(kx.w, qx.w, acc[4 * l4 + 3]);
                 }
             }
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int r = r0 + u * ATTN_WARPS;
-                const float sc = __fmul_rn(ggml_reduce_warp(acc[u]), a.qk_scale);  // ggml_scale
-                if (r < nt) {
-                    if (lane == 0) s_p[t0 + r] = sc;
-                    wmax = fmaxf(wmax, sc);
-                }
+            for (int e = 0; e < 8; ++e) {
+                acc[e] = __fadd_rn(acc[e], acc[16 + e]);
+                acc[8 + e] = __fadd_rn(acc[8 + e], acc[24 + e]);
             }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] = __fadd_rn(acc[e], acc[8 + e]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[e] = __fadd_rn(acc[e], acc[e + 4]);
+            const float sc = __fmul_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3])), a.qk_scale);
+            s_p[t] = sc;
+            tmax = fmaxf(tmax, sc);
         }
     }
-    wmax = __shfl_sync(0xffffffffu, wmax, 0);
-    if (lane == 0) s_red[w] = wmax;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+    if (lane == 0) s_red[w] = tmax;
+    if (!ok && tid == 0) s_ok = 0;
     __syncthreads();
     ATTN_TRACE_AT(2);
+    if (!s_ok) {
+        // a copy wait ran out: report, give the copies in flight (the K tile
+        // waited for, the first V tile) a second bounded wait, write no output
+        if (tid == 0) {
+            set_status(a.status, ST_TIMEOUT);
+            mbar_wait_bounded(&bar_k, ph_k);
+            mbar_wait_bounded(&bar_v, ph_v);
+        }
+        return;
+    }
     float mx = s_red[0];
 #pragma unroll
     for (int i = 1; i < ATTN_WARPS; ++i) mx = fmaxf(mx, s_red[i]);
@@ -345,16 +386,25 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParam
         const int nt = min(ATTN_TILE, n - t0);
         if (t0 > 0) {
             __syncthreads();
-            stage_kv_tile(s_vt, vbase, row_stride, t0, min(nt, pos - t0), tid, keep);
-            __syncthreads();
+            fence_proxy_async_smem();
+            load_kv_tile(s_kt, s_vt, kbase, vbase, row_stride, t0, min(nt, pos - t0), &bar_k, &bar_v, false, true,
+                         tid, keep);
         }
+        if (!__syncthreads_and(mbar_wait_bounded(&bar_v, ph_v))) {
+            if (tid == 0) {
+                set_status(a.status, ST_TIMEOUT);
+                mbar_wait_bounded(&bar_v, ph_v);  // (this tile's copies are the last in flight)
+            }
+            return;
+        }
+        ph_v ^= 1u;
         if (d < HD) {
             const int cend = min(np, t0 + nt);
             for (int c0 = t0; c0 < cend; c0 += 32) {
 #pragma unroll
                 for (int r = 0; r < 32; ++r) {
                     const int t = c0 + r;
-                    const float v = t == pos ? s_v[d] : s_vt[(t - t0) * HD + d];
+                    const float v = t == pos ? s_v[d] : s_vt[(t - t0) * ATTN_KROW + d];
                     acc[r] = __fmaf_rn(v, s_p[t], acc[r]);
                 }
             }
@@ -373,7 +423,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParam
             }
             // the n % 32 tail, one by one in float (its rows are in this tile)
             for (int t = max(np, t0); t < t0 + nt; ++t) {
-                const float v = t == pos ? s_v[d] : s_vt[(t - t0) * HD + d];
+                const float v = t == pos ? s_v[d] : s_vt[(t - t0) * ATTN_KROW + d];
                 sumf = __fadd_rn(sumf, __fmul_rn(v, s_p[t]));
             }
         }
@@ -514,6 +564,7 @@ int launch_attn(bh_stack* st, int l, bool pdl) {
     a.n_ctx = c.n_ctx;
     a.eps = c.rms_eps;
     a.qk_scale = 1.0f / std::sqrt((float)c.head_dim);  // forward.cpp: 1.0f / sqrtf((float)head_dim)
+    a.status = st->ctx->d_status;
     set_prefetch(st, mat_end(st, l * BH_W_PER_LAYER + BH_W_V), &a.pf_ptr, &a.pf_bytes);
     a.trace = nullptr;
 #ifdef BH_TRACE
@@ -522,7 +573,7 @@ int launch_attn(bh_stack* st, int l, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)c.n_head);
     cfg.blockDim = dim3((unsigned)bh::ATTN_THREADS);
-    cfg.dynamicSmemBytes = sizeof(float) * ((size_t)2 * bh::ATTN_TILE * bh::ATTN_HD + (size_t)c.n_ctx);
+    cfg.dynamicSmemBytes = sizeof(float) * ((size_t)2 * bh::ATTN_TILE * bh::ATTN_KROW + (size_t)c.n_ctx);
     cfg.stream = st->stream;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
