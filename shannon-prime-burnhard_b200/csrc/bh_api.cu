@@ -70,13 +70,16 @@ namespace bh {
 //  - Batch 1-2 (16-warp CTAs, whose registers fill an SM): one CTA per SM.
 //    Matrices with fewer than 32 eight-row tiles per CTA (everything but the
 //    LM-head-sized ones) run 8 threads per row, i.e. 4-row tiles: twice the
-//    working warps, each with half the arithmetic per block.
+//    working warps, each with half the arithmetic per block. (16 threads per
+//    row, 2-row tiles, is available through BH_TUNE_TPR: for the 4096-row
+//    matrices of the decode step it puts 14 of 16 warps to work instead of 7,
+//    but measured slower there, 1.76 against 1.68 ms per token.)
 //  - Larger batches (8-warp CTAs): wide matrices (at least one 8-row tile per
 //    warp with ctas_per_sm CTAs per SM) run that many CTAs per SM, each with
 //    smem_cap_small bytes; narrow ones one CTA per SM.
 // A non-zero sm_budget caps the shared memory one launch holds per SM, so the
 // next programmatic launch finds room to start its weight copies early.
-int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override) {
+int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override, int fold) {
     const int W = dense_warps(p.B);
     const int act_bytes = p.B * p.nb * ACT_BLOCK_BYTES;
     const bool small = act_bytes <= ctx->small_act_bytes;
@@ -106,7 +109,11 @@ int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override) {
         const int per = grid > ctx->num_sms ? per_sm : 1;
         if (cap * per > ctx->sm_budget) cap = ctx->sm_budget / per;
     }
-    if (ctx->tpr_force) tpr = (ctx->tpr_force == 8 && p.B <= 2) ? 8 : 4;
+    if (ctx->tpr_force) {
+        tpr = 4;
+        if (ctx->tpr_force == 8 && p.B <= 2) tpr = 8;
+        if (ctx->tpr_force == 16 && p.B <= 2) tpr = (fold == BH_FOLD_X86 && !p.partials) ? 16 : 8;
+    }
     const int64_t ntile = (p.N + 32 / tpr - 1) / (32 / tpr);  // CTAs own whole tiles
     if ((int64_t)grid > ntile) grid = (int)ntile;
     const int rc = matvec_plan(p, grid, cap, ctx->stage_bytes, tpr);
@@ -147,7 +154,7 @@ void unregister_barrier_words(bh_ctx* ctx, void* words) {
 }
 
 int run_matvec(bh_ctx* ctx, MatvecParams& p, int fold, int src, int epi, cudaStream_t s, bool pdl) {
-    const int grid = plan_for(ctx, p, 0);
+    const int grid = plan_for(ctx, p, 0, fold);
     if (grid < 0) return grid;
     LaunchOpts o;
     o.stream = s;
@@ -249,7 +256,7 @@ int bh_tune(bh_ctx* ctx, int key, int value) {
             ctx->stage_bytes = value;
             return BH_OK;
         case BH_TUNE_TPR:
-            if (value != 0 && value != 4 && value != 8) return BH_EINVAL;
+            if (value != 0 && value != 4 && value != 8 && value != 16) return BH_EINVAL;
             ctx->tpr_force = value;
             return BH_OK;
         case BH_TUNE_SMEM_CAP:
@@ -366,7 +373,7 @@ int bh_q4k_lmhead_argmax(bh_ctx* ctx, const void* W_q4k, int64_t N, int64_t K, c
     p.xf = x;
     p.cand_val = ctx->cand_val;
     p.cand_idx = ctx->cand_idx;
-    const int grid = plan_for(ctx, p, 0);
+    const int grid = plan_for(ctx, p, 0, fold);
     if (grid < 0) return grid;
     bh::LaunchOpts o;
     o.stream = s;

@@ -61,7 +61,7 @@ struct bh_ctx {
 namespace bh {
 // Grid and shared-memory plan for one matvec launch (fills p's tiling
 // fields); returns the grid size or a negative errno.
-int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override);
+int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override, int fold);
 // MatvecParams for a single-segment weight matrix.
 MatvecParams base_params(bh_ctx* ctx, const void* W, int64_t N, int64_t K, int B, float* y);
 // Grid-barrier words (256 bytes) that bh_device_status zeroes after a timeout.

@@ -657,7 +657,7 @@ int enqueue_step(bh_stack* st) {
 #ifdef BH_TRACE
     if (ctx->trace) p.trace = ctx->trace + st->launches * bh::TRACE_LAUNCH;
 #endif
-    const int grid = bh::plan_for(ctx, p, 0);
+    const int grid = bh::plan_for(ctx, p, 0, BH_FOLD_X86);
     if (grid < 0) return grid;
     st->lm_grid = grid;
     bh::LaunchOpts o;
@@ -688,7 +688,7 @@ int enqueue_op(bh_stack* st, int op) {
         p.eps = c.rms_eps;
         p.cand_val = st->cand_val;
         p.cand_idx = st->cand_idx;
-        const int grid = bh::plan_for(ctx, p, 0);
+        const int grid = bh::plan_for(ctx, p, 0, BH_FOLD_X86);
         if (grid < 0) return grid;
         bh::LaunchOpts o;
         o.stream = st->stream;

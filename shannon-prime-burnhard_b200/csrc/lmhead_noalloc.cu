@@ -95,7 +95,7 @@ extern "C" int bh_q4k_lmhead_argmax_noalloc(const void* W_q4k, int64_t N, int64_
     bh::MatvecParams p = bh::base_params(&local, W_q4k, N, K, B, logits_opt);
     p.status = status;
     p.xf = x;
-    const int grid = bh::plan_for(&local, p, 0);
+    const int grid = bh::plan_for(&local, p, 0, fold);
     if (grid < 0) return grid;
     if ((int64_t)grid * B > NOALLOC_SLOTS) return BH_EINVAL;  // more candidates than the static scratch holds
     p.cand_val = reinterpret_cast<float*>(scratch);

@@ -388,7 +388,7 @@ int bh_q4k_lmhead_argmax_tp(bh_ctx* ctx, const void* W_local, int64_t n_local, i
     p.xf = x;
     p.cand_val = ctx->cand_val;
     p.cand_idx = ctx->cand_idx;
-    const int grid = bh::plan_for(ctx, p, 0);
+    const int grid = bh::plan_for(ctx, p, 0, fold);
     if (grid < 0) return grid;
     bh::LaunchOpts o;
     o.stream = s;

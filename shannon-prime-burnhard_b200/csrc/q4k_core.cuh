@@ -3,8 +3,10 @@
 // the exact integer lane sums, and the reference's fp32 fold.
 //
 // TPR threads work one row (TPR = 4: thread t owns reference lanes 2t, 2t+1;
-// TPR = 8: thread t owns lane t). Integer sums are exact (|partial| < 2^24),
-// so only the fp32 order matters, and it is reproduced operation by
+// TPR = 8: thread t owns lane t; TPR = 16, x86 fold only: threads t and t ^ 8
+// share lane t & 7, each taking two of the four 32-byte quant groups, and add
+// their integer halves before the fold). Integer sums are exact (|partial| <
+// 2^24), so only the fp32 order matters, and it is reproduced operation by
 // operation:
 //   FOLD_X86     (ggml-cpu/arch/x86/quants.c:1900-1983): lane m = bytes
 //                4m..4m+3 of every 32-byte quant group; acc = fma(d, sumi, acc).
@@ -20,14 +22,16 @@ namespace bh {
 // per-super-block work of one thread
 // ---------------------------------------------------------------------------
 // TPR threads work one row (TPR = 4: thread t owns reference lanes 2t, 2t+1;
-// TPR = 8: thread t owns lane t); every thread also computes min lane t & 3
-// (threads 4..7 of a TPR = 8 row repeat 0..3 and are not summed).
+// TPR = 8: thread t owns lane t; TPR = 16: thread t owns half t >> 3 of lane
+// t & 7); every thread also computes min lane t & 3 (the threads above 3
+// repeat 0..3 and are not summed).
 template <int TPR>
 struct RowBlk {
-    static constexpr int L = 8 / TPR;  // reference lanes per thread
+    static constexpr int L = TPR >= 8 ? 1 : 8 / TPR;  // reference lanes per thread
+    static constexpr int G = TPR == 16 ? 2 : 4;       // 32-byte quant groups per thread
     float fd, fdm;
     uint32_t sc03, sc47, mnk;          // mnk: the two mins of min lane t & 3 in bytes 0..1
-    uint32_t lo[L][4], hi[L][4];
+    uint32_t lo[L][G], hi[L][G];       // (TPR = 16: sc03 holds the scales of this thread's groups)
 };
 
 template <int FOLD, int TPR>
@@ -46,7 +50,18 @@ __device__ __forceinline__ RowBlk<TPR> decode_row(const uint8_t* blk, int t) {
     const uint32_t mn = (k & 2) ? (((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u)) : (h.z & 0x3f3f3f3fu);
     r.mnk = mn >> ((k & 1) * 16);
     const uint32_t* qs = reinterpret_cast<const uint32_t*>(blk + 16);
-    if (FOLD == BH_FOLD_X86) {
+    static_assert(TPR != 16 || FOLD == BH_FOLD_X86, "16 threads per row: x86 fold only");
+    if (TPR == 16) {
+        // groups 2h, 2h + 1 (sub-blocks 4h .. 4h + 3) of lane t & 7, h = t >> 3
+        const int h2 = t >> 3, m = t & 7;
+        if (h2) r.sc03 = r.sc47;
+#pragma unroll
+        for (int g = 0; g < RowBlk<TPR>::G; ++g) {
+            const uint32_t w = qs[8 * (2 * h2 + g) + m];
+            r.lo[0][g] = w & 0x0f0f0f0fu;
+            r.hi[0][g] = (w >> 4) & 0x0f0f0f0fu;
+        }
+    } else if (FOLD == BH_FOLD_X86) {
         // lane m = bytes 4m..4m+3 of each 32-byte group: word m
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
@@ -104,6 +119,16 @@ __device__ __forceinline__ int lane_sum(const uint32_t (&lo)[4], const uint32_t 
     return __dp2a_hi((int)__byte_perm((uint32_t)d6, (uint32_t)d7, 0x5410), (int)sc47, s);
 }
 
+// Half a lane's sum (two quant groups = four sub-blocks, their scales in the
+// bytes of sc): the TPR = 16 split.
+__device__ __forceinline__ int lane_sum_half(const uint32_t (&lo)[2], const uint32_t (&hi)[2], uint32_t sc,
+                                             const int4 a) {
+    const int d0 = dp4a((int)lo[0], a.x, 0), d1 = dp4a((int)hi[0], a.y, 0);
+    const int d2 = dp4a((int)lo[1], a.z, 0), d3 = dp4a((int)hi[1], a.w, 0);
+    const int s = __dp2a_lo((int)__byte_perm((uint32_t)d0, (uint32_t)d1, 0x5410), (int)sc, 0);
+    return __dp2a_hi((int)__byte_perm((uint32_t)d2, (uint32_t)d3, 0x5410), (int)sc, s);
+}
+
 // Sum over the 4 min lanes held by threads t & 3 = 0..3 of a row (exact ints).
 template <int TPR>
 __device__ __forceinline__ int sum_min_lanes(int v) {
@@ -117,17 +142,25 @@ __device__ __forceinline__ int sum_min_lanes(int v) {
 // part_dst is non-null, written by thread 0 as 9 int32.
 template <int FOLD, bool PART, int TPR>
 __device__ __forceinline__ void fold_block(const RowBlk<TPR>& r, const uint8_t* A, int t, int32_t* part_dst,
-                                           float (&acc)[8 / TPR], float& accm) {
+                                           float (&acc)[RowBlk<TPR>::L], float& accm) {
     constexpr int L = RowBlk<TPR>::L;
+    static_assert(TPR != 16 || !PART, "16 threads per row: no partials");
     const float yd = *reinterpret_cast<const float*>(A + ACT_D_OFF);
     const int spk = reinterpret_cast<const int*>(A + ACT_S_OFF)[t & 3];
     int li[L];
     int sub[L][8];
+    if constexpr (TPR == 16) {
+        // this thread's half of lane t & 7, then the other half from thread t ^ 8
+        const int4 a = *reinterpret_cast<const int4*>(A + act_lane_off(t & 7) + 16 * (t >> 3));
+        const int hs = lane_sum_half(r.lo[0], r.hi[0], r.sc03, a);
+        li[0] = hs + __shfl_xor_sync(0xffffffffu, hs, 8);
+    } else {
 #pragma unroll
-    for (int e = 0; e < L; ++e) {
-        const int4 a0 = *reinterpret_cast<const int4*>(A + act_lane_off(t * L + e));
-        const int4 a1 = *reinterpret_cast<const int4*>(A + act_lane_off(t * L + e) + 16);
-        li[e] = lane_sum(r.lo[e], r.hi[e], r.sc03, r.sc47, a0, a1, sub[e], PART);
+        for (int e = 0; e < L; ++e) {
+            const int4 a0 = *reinterpret_cast<const int4*>(A + act_lane_off(t * L + e));
+            const int4 a1 = *reinterpret_cast<const int4*>(A + act_lane_off(t * L + e) + 16);
+            li[e] = lane_sum(r.lo[e], r.hi[e], r.sc03, r.sc47, a0, a1, sub[e], PART);
+        }
     }
     const int mp = __dp2a_lo(spk, (int)r.mnk, 0);
     if (FOLD == BH_FOLD_X86) {
@@ -166,7 +199,7 @@ __device__ __forceinline__ void fold_block(const RowBlk<TPR>& r, const uint8_t* 
 // The row's dot product from its threads' lane accumulators, combined in the
 // reference's order; every thread of the row returns the same value.
 template <int FOLD, int TPR>
-__device__ __forceinline__ float row_value(const float (&acc)[8 / TPR], float accm, int rgrp) {
+__device__ __forceinline__ float row_value(const float (&acc)[RowBlk<TPR>::L], float accm, int rgrp) {
     const unsigned FULLM = 0xffffffffu;
     if (FOLD == BH_FOLD_X86) {
         // hsum_float_8 (arch/x86/quants.c:43-49): ((a4+a0)+(a6+a2)) + ((a5+a1)+(a7+a3))
@@ -174,12 +207,12 @@ __device__ __forceinline__ float row_value(const float (&acc)[8 / TPR], float ac
         if (TPR == 4) {
             // thread t holds lanes 2t (acc[0]) and 2t+1 (acc[1])
             const float x0 = __fadd_rn(acc[0], __shfl_xor_sync(FULLM, acc[0], 2));  // t0: a0+a4, t1: a2+a6
-            const float x1 = __fadd_rn(acc[8 / TPR - 1], __shfl_xor_sync(FULLM, acc[8 / TPR - 1], 2));
+            const float x1 = __fadd_rn(acc[RowBlk<TPR>::L - 1], __shfl_xor_sync(FULLM, acc[RowBlk<TPR>::L - 1], 2));
             const float y0 = __fadd_rn(x0, __shfl_xor_sync(FULLM, x0, 1));
             const float y1 = __fadd_rn(x1, __shfl_xor_sync(FULLM, x1, 1));
             hs = __fadd_rn(y0, y1);
         } else {
-            // thread t holds lane t
+            // thread t holds lane t & 7 (TPR = 16: both halves hold it)
             const float t1 = __fadd_rn(acc[0], __shfl_xor_sync(FULLM, acc[0], 4));  // t0: a0+a4
             const float t2 = __fadd_rn(t1, __shfl_xor_sync(FULLM, t1, 2));          // t0: (a0+a4)+(a2+a6)
             hs = __fadd_rn(t2, __shfl_xor_sync(FULLM, t2, 1));
@@ -190,7 +223,7 @@ __device__ __forceinline__ float row_value(const float (&acc)[8 / TPR], float ac
         return __fadd_rn(hs, hm);
     } else {
         // sumf (the min chain) += sums[0..7] in order
-        constexpr int L = 8 / TPR;
+        constexpr int L = RowBlk<TPR>::L;
         float v = accm;
 #pragma unroll
         for (int l = 0; l < 8; ++l) v = __fadd_rn(v, __shfl_sync(FULLM, acc[l % L], rgrp * TPR + l / L));

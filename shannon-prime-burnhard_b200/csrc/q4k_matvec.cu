@@ -275,7 +275,7 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, double* r
 
 // Per-row epilogue of the dense kernel.
 template <int FOLD, int EPI, int TPR>
-__device__ __forceinline__ void finish_row(const MatvecParams& p, const float (&acc)[8 / TPR], float accm, int rgrp,
+__device__ __forceinline__ void finish_row(const MatvecParams& p, const float (&acc)[RowBlk<TPR>::L], float accm, int rgrp,
                                            int t, int b, bool has_row, int64_t row, float& best_v, int& best_i) {
     const float v = row_value<FOLD, TPR>(acc, accm, rgrp);
     if (has_row && t == 0) {
@@ -306,7 +306,7 @@ template <int FOLD, int NB, int SRC, int EPI, bool PART, int TPR>
 __global__ void __launch_bounds__(dense_warps(NB) * 32, dense_min_blocks(NB)) q4k_matvec_kernel(const __grid_constant__ MatvecParams p) {
     constexpr int W = dense_warps(NB);
     constexpr int R = 32 / TPR;
-    constexpr int L = 8 / TPR;
+    constexpr int L = RowBlk<TPR>::L;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float s_red[DENSE_MAX_WARPS];
     __shared__ int s_redi[DENSE_MAX_WARPS];
@@ -349,7 +349,7 @@ __global__ void __launch_bounds__(dense_warps(NB) * 32, dense_min_blocks(NB)) q4
         if (lane == 0) {
             const int x = i_c * p.kc * (Q4K_BYTES / 8);
             uint8_t* dst = ring + (size_t)i_s * p.stage_bytes;
-            mbar_arrive_expect_tx(&full[i_s], (uint32_t)p.stage_bytes);
+            mbar_arrive_expect_tx(&full[i_s], (uint32_t)(R * p.row_stride));  // one box (the stage may be padded)
             if (EPI == EPI_SWIGLU) {
                 // one 3-D copy: R/2 gate rows, then the same R/2 up rows
                 const int row = (int)((r_begin + (int64_t)(warp + i_j * W) * R) / 2);
@@ -514,7 +514,7 @@ BH_UNROLL(BH_KB_UNROLL)
 // rows per CTA gives its working warps deeper rings, which fill before the
 // programmatic wait.
 int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int tpr) {
-    if (grid < 1 || (tpr != 4 && tpr != 8)) return BH_EINVAL;
+    if (grid < 1 || (tpr != 4 && tpr != 8 && tpr != 16)) return BH_EINVAL;
     const int R = 32 / tpr;
     const int W = dense_warps(p.B);
     const int64_t tiles_cta = ((p.N + R - 1) / R + grid - 1) / grid;
@@ -530,9 +530,10 @@ int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int t
         const int padw = ((8 - (words % 32)) % 32 + 32) % 32;  // row stride == 8 words (mod 32 banks)
         const int stride = kc * Q4K_BYTES + 4 * padw;
         // (stride is 32 mod 128 bytes, so R * stride, R = 4 or 8, is a
-        // multiple of 128: every stage starts 128-byte aligned, as a tensor
-        // copy's shared-memory destination must)
-        const int stage = R * stride;
+        // multiple of 128; two-row stages are padded to one: every stage
+        // starts 128-byte aligned, as a tensor copy's shared-memory
+        // destination must)
+        const int stage = (R * stride + 127) / 128 * 128;
         const int avail = smem_cap - ring_off - 512;  // static shared memory of the kernel
         int stages = avail > 0 ? avail / (wbusy * (stage + 8)) : 0;
         if (stages > 8) stages = 8;
@@ -581,6 +582,17 @@ static int launch_t(const MatvecParams& p, const LaunchOpts& o, int grid) {
 
 template <int FOLD, int SRC, int EPI, bool PART>
 static int launch_nb(const MatvecParams& p, const LaunchOpts& o, int grid) {
+    if (p.tpr == 16) {
+        // sixteen threads per row: matrices with at most 2 rows per warp, batch <= 2, x86 fold
+        if constexpr (FOLD == BH_FOLD_X86 && !PART) {
+            switch (p.B) {
+                case 1: return launch_t<FOLD, 1, SRC, EPI, PART, 16>(p, o, grid);
+                case 2: return launch_t<FOLD, 2, SRC, EPI, PART, 16>(p, o, grid);
+                default: return BH_EINVAL;
+            }
+        }
+        return BH_EINVAL;
+    }
     if (p.tpr == 8) {
         // eight threads per row: narrow matrices, batch <= 2
         switch (p.B) {

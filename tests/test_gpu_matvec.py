@@ -193,10 +193,11 @@ def test_fp16_scale_conversion_matches_oracle(ctx, oracle):
     assert np.array_equal(host(ctx.q4k_quantize(dev(w))), oracle.quantize_q4k(w).reshape(-1))
 
 
-@pytest.mark.parametrize("tpr", [4, 8])
+@pytest.mark.parametrize("tpr", [4, 8, 16])
 @pytest.mark.parametrize("n,k,b", [(4096, 4096, 1), (4096, 12288, 2), (1000, 768, 1), (33, 2048, 2), (151936 // 16, 4096, 1)])
 def test_forced_threads_per_row_bit_exact(ctx, bh, oracle, tpr, n, k, b):
-    """4 or 8 threads per row (the planner picks by shape) give the same bits."""
+    """4, 8 or 16 threads per row (the planner picks by shape; 16 falls back
+    to 8 for the generic fold and the partials) give the same bits."""
     w = oracle.normal((n, k), 31 + n + k, 0.0, 0.02)
     wq = oracle.quantize_q4k(w)
     x = oracle.normal((b, k), 41 + k, 0.0, 1.0)
@@ -211,6 +212,27 @@ def test_forced_threads_per_row_bit_exact(ctx, bh, oracle, tpr, n, k, b):
             P = torch_zeros_int((b, n, k // 256, 9))
             ctx.matvec(dev(wq), n, k, dev(xq), b, partials=P, fold=fold)
             assert np.array_equal(host(P), oracle.partials(wq, n, k, xq, b))
+    finally:
+        ctx.tune(bh.TUNE_TPR, 0)
+
+
+@pytest.mark.parametrize("tpr", [8, 16])
+@pytest.mark.parametrize("n,k,b", [(4096, 4096, 1), (2000, 12288, 2), (4736, 4096, 1)])
+def test_threads_per_row_argmax(ctx, bh, oracle, tpr, n, k, b):
+    """The LM-head argmax epilogue (fp32 input quantized in the prologue) at 8
+    and 16 threads per row gives the oracle's logits, maxima and tokens."""
+    w = oracle.normal((n, k), 77 + n + k, 0.0, 0.02)
+    wq = oracle.quantize_q4k(w)
+    x = oracle.normal((b, k), 78 + k, 0.0, 1.0)
+    xq = oracle.quantize_q8k(x)
+    want = oracle.matvec(wq, n, k, xq, b, 0).reshape(b, n)
+    ctx.tune(bh.TUNE_TPR, tpr)
+    try:
+        logits = dev(np.zeros((b, n), np.float32))
+        tok, mx = bh.lmhead_argmax(ctx, dev(wq), n, k, dev(x), logits=logits)
+        assert_bits_equal(host(logits).reshape(b, n), want, f"argmax logits tpr{tpr}")
+        assert list(host(tok)) == [int(np.argmax(want[i])) for i in range(b)]
+        assert np.array_equal(host(mx), want.max(axis=1))
     finally:
         ctx.tune(bh.TUNE_TPR, 0)
 
