@@ -10,9 +10,15 @@ value  = algorithmic bytes of all matvecs of the step x ranks / step time
          (GB/s); tokens/s is reported beside it.
 e2e    = the same metric through bh_stack_decode_host: the embedding comes
          from pinned host memory and the token is read back every step.
-N > 1  = one process per GPU, each decoding its own sequence with its own
-         copy of the weights (replicas: no data-path collective); the value is
-         the sum over ranks, timed as the slowest rank.
+N > 1  = one process per GPU running the row-split (tensor-parallel) step:
+         every rank holds 1/N of every matrix's rows and of the heads, the
+         vectors each next launch reads whole are completed by peer stores over
+         NVLink from the producing launch's epilogue (bh_stack_create_tp; the
+         NCCL communicator that connects the ranks comes from the library's
+         non-blocking bh_tp_comm_init). value = the whole model's algorithmic
+         bytes per step / the slowest rank's step time (strong scaling: the
+         same one-sequence step on N GPUs). Replicas (each GPU its own sequence
+         and weights, no exchange) are reported beside it.
 --impl reference times the reference's own CPU implementation of the step:
 the decode graph the reference engine builds (forward.cpp build_block_decode
 + LM head) on the reference's own ggml CPU backend (oracle/_ref, compiled
@@ -439,7 +445,8 @@ def main() -> None:
                 **{k: cfg_d[k] for k in ("n_layer", "n_embd", "n_head", "n_head_kv", "head_dim", "n_ff", "n_vocab")},
                 "kv_positions": KV_POS + 1, "weights": "random-init N(0,0.02) quantized to Q4_K",
                 "l2": "no flush needed: 4.26 GB of weights streamed per step >> 126 MB L2",
-                "parallelism": f"replicas x{world_env}" if world_env > 1 else "single GPU"}
+                "parallelism": (f"row-split tensor parallel x{world_env} (peer-memory exchange in the epilogues)"
+                                if world_env > 1 else "single GPU")}
     if args.impl == "reference":
         run_reference_arm(args, cfg_d, workload)
         return
@@ -457,37 +464,64 @@ def main() -> None:
         cfg.n_layer = args.layers
 
     ctx = bh.Context(local)
-    st = bh.Stack(ctx, cfg, SEED)
-    st.fill_kv(KV_POS, SEED + 1)
-    st.set_pos(KV_POS)
-    info = st.info()
-    step_bytes, launches = info["step_bytes"], info["launches"]
     x_host = np.asarray(__import__("oracle").Oracle().normal((cfg.n_embd,), X_SEED, 0.0, 1.0))
     x_dev = torch.from_numpy(x_host).cuda()
     tok = torch.zeros(1, dtype=torch.int32, device="cuda")
     stream = torch.cuda.Stream()
 
+    def timed_steps(stk, steps: int, warmup: int) -> float:
+        """Device ms per step (CUDA events on the launching stream, the
+        slowest rank), after warm-up; every rank runs the same steps."""
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                stk.decode(x_dev, tok, stream)
+            stream.synchronize()
+            time.sleep(0.3)
+            barrier(world)
+            torch.cuda.synchronize()
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record(stream)
+            for _ in range(steps):
+                stk.decode(x_dev, tok, stream)
+            ev1.record(stream)
+            ev1.synchronize()
+            torch.cuda.synchronize()
+            barrier(world)
+        return max_over_ranks(ev0.elapsed_time(ev1) / steps, world)
+
+    comm = None
+    if world > 1:
+        # the headline: the row-split step; the ranks are connected through
+        # the library's own non-blocking NCCL communicator
+        import torch.distributed as dist
+
+        obj = [bh.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        comm = bh.tp_comm_init(local, obj[0], world, rank, 120000)
+        st = bh.Stack(ctx, cfg, SEED, rank=rank, world=world)
+        st.tp_connect_comm(comm, 120000)
+    else:
+        st = bh.Stack(ctx, cfg, SEED)
+    st.fill_kv(KV_POS, SEED + 1)
+    st.set_pos(KV_POS)
+    info = st.info()
+    step_bytes, launches = info["step_bytes"], info["launches"]
+    if world > 1:
+        t = torch.tensor([float(step_bytes)], device="cuda")
+        import torch.distributed as dist
+
+        dist.all_reduce(t)
+        job_bytes = int(t.item())  # the whole model's bytes of one step, over all ranks
+    else:
+        job_bytes = step_bytes
+
     clock_file = os.path.join(tempfile.gettempdir(), f"bh_clocks_{os.getpid()}.csv")
     sampler = start_clock_sampler(clock_file)
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            st.decode(x_dev, tok, stream)
-        stream.synchronize()
-        time.sleep(0.3)
-        barrier(world)
-        torch.cuda.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            st.decode(x_dev, tok, stream)
-        e1.record(stream)
-        e1.synchronize()
-        torch.cuda.synchronize()
-        barrier(world)
+    ms = timed_steps(st, args.steps, args.warmup)
     clocks = stop_clock_sampler(sampler, clock_file, local)
-    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
-    value = step_bytes * world / (ms / 1e3) / 1e9
+    value = job_bytes / (ms / 1e3) / 1e9
+    first_tok = int(tok.item())
 
     # e2e through the host-buffer entry point (pinned input, token read back)
     pinned = torch.from_numpy(x_host).pin_memory()
@@ -499,7 +533,25 @@ def main() -> None:
     for _ in range(e2e_steps):
         st.decode_host(pinned)
     e2e_ms = max_over_ranks((time.perf_counter() - t0) / e2e_steps * 1e3, world)
-    e2e_value = step_bytes * world / (e2e_ms / 1e3) / 1e9
+    e2e_value = job_bytes / (e2e_ms / 1e3) / 1e9
+    status = ctx.status()
+
+    replicas = None
+    if world > 1:
+        torch.cuda.synchronize()
+        barrier(world)  # every rank done with the peers' exchange regions
+        st.close()
+        bh.tp_comm_free(comm, 60000)
+        # beside it: N replicas of the one-GPU step (no exchange)
+        st = bh.Stack(ctx, cfg, SEED)
+        st.fill_kv(KV_POS, SEED + 1)
+        st.set_pos(KV_POS)
+        rms = timed_steps(st, args.steps, args.warmup)
+        replicas = {"value": round(st.info()["step_bytes"] * world / (rms / 1e3) / 1e9, 2), "unit": "GB/s",
+                    "ms_per_step": round(rms, 4), "tokens_per_s": round(world * 1e3 / rms, 2), "scaling": "weak",
+                    "what": f"{world} independent one-GPU decode steps (own weights, own sequence), no exchange"}
+        if int(tok.item()) != first_tok:
+            replicas["token_mismatch"] = [first_tok, int(tok.item())]
 
     # dominant kernel: the fused gate|up matvec (52% of the step's bytes)
     op_ms, op_bytes = st.time_op(bh.OP_GATE_UP, reps=3)
@@ -548,18 +600,20 @@ def main() -> None:
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 4), "tokens_per_s": round(world * 1e3 / ms, 2),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "tokens_per_s": round(1e3 / ms, 2),
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
             "dtype": "q4_K x q8_K (int8 dot, fp32 fold)", "data": "synthetic", "config": workload,
-            "step_bytes": step_bytes, "frac_of_hbm_peak": round(value / world / peak, 4),
+            "step_bytes": job_bytes, "frac_of_hbm_peak": round(value / world / peak, 4),
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
-                    "h2d_bytes_per_step": cfg.n_embd * 4, "d2h_bytes_per_step": 4},
+                    "h2d_bytes_per_step": cfg.n_embd * 4 * world, "d2h_bytes_per_step": 4 * world},
+            "token": first_tok,
+            "replicas_beside": replicas,
             "roofline": {"bound": "hbm", "kernel": "q4k_matvec (fused gate|up, 24576 x 4096)",
                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "bytes_per_launch": op_bytes, "ms_per_launch": round(op_ms, 5)},
             "cpu_baseline": cpu_baseline,
-            "gpu_launches": launches * args.steps,
+            "gpu_launches": launches * args.steps * world,
             "configs_beside": extra,
             "clocks": clocks,
             "device_status": status,

@@ -301,7 +301,7 @@ int bh_stack_decode(bh_stack *st, const float *x, int32_t *tok_out, void *stream
 int bh_stack_decode_host(bh_stack *st, const float *host_x, int32_t *host_tok);
 /* Bytes of all Q4_K weights, algorithmic bytes of one step (weights plus
  * activations read and outputs written by the matvecs) and kernel launches
- * per step. */
+ * per step (on a row split: this rank's). */
 int bh_stack_info(bh_stack *st, int64_t *weight_bytes, int64_t *step_bytes, int64_t *launches);
 /* Average device time of one op of the step (CUDA events around reps
  * eager repetitions over all layers on the stack's stream, the same launch
@@ -317,6 +317,66 @@ int bh_stack_time_op(bh_stack *st, int op, int reps, float *avg_ms, int64_t *byt
 /* Device pointer and shape of one tensor (ids above); Q4_K matrices are
  * rows x cols in values, the rest fp32. */
 int bh_stack_tensor(bh_stack *st, int layer, int which, void **ptr, int64_t *rows, int64_t *cols);
+
+/* Row-split (tensor-parallel) decode over `world` GPUs of one node, one
+ * process (and one context) per GPU. Rank r holds query heads
+ * [r n_head / world, ...) with their KV heads, rows [r n_embd / world, ...)
+ * of O and down, [r n_ff / world, ...) of gate and up, and an even share of
+ * the LM head's rows, generated from the same seed as the one-GPU stack (the
+ * same bytes for the same rows). Every matvec output row is computed whole
+ * on one rank, so tokens and hidden states equal one GPU's bit for bit.
+ * world in 1..8 dividing n_head_kv, n_embd / 8 and n_ff / 8; world 1 is
+ * bh_stack_create. The launches that produce a vector the next launch reads
+ * whole (attention output, h after O and after down, the SwiGLU output) also
+ * store their rows into the peers' copies over NVLink and signal per CTA;
+ * the reading launch waits for the peers' signals (bounded, about a second:
+ * then BH_ETIMEDOUT through bh_device_status and the stack must be
+ * recreated). The LM head's pick is merged through peer mailboxes. Replaces
+ * the reference's single-device path through forward.cpp:2706-2854 and the
+ * NCCL all-gather of ggml-cuda.cu:1216. */
+int bh_stack_create_tp(bh_ctx *ctx, const bh_stack_config *cfg, uint64_t seed, int rank, int world,
+                       bh_stack **out);
+/* CUDA IPC handle (64 bytes) of this rank's exchange region. */
+int bh_stack_tp_handle(bh_stack *st, void *handle_out);
+/* Map the peers' exchange regions: handles = world x 64 bytes in rank order
+ * (this rank's own entry is ignored). Decoding needs it when world > 1. */
+int bh_stack_tp_connect(bh_stack *st, const void *handles);
+/* Rank, world and the owned ranges as (first, count) pairs: query heads, KV
+ * heads, O / down rows, gate / up rows, LM head rows (10 int64). */
+int bh_stack_tp_info(bh_stack *st, int *rank, int *world, int64_t *row_ranges);
+/* On a row split: bh_stack_free after every rank's last decode has
+ * completed (a host barrier), since the peers store into this rank's
+ * exchange region; bh_stack_time_op is for one GPU only (BH_EINVAL). */
+
+/* ------------------------------------------------------------------------
+ * NCCL communicators from C (tp_comm.cu). A communicator is a void*
+ * (ncclComm_t). Creation is non-blocking (ncclCommInitRankConfig with
+ * blocking = 0) and every wait is polled against timeout_ms of wall clock
+ * (ncclCommGetAsyncError, cudaStreamQuery); when it runs out the
+ * communicator is aborted (ncclCommAbort) and the call returns BH_ETIMEDOUT:
+ * a rank that never joins or stops does not hang the others. NCCL is opened
+ * at run time ($BH_NCCL_LIB, else libnccl.so.2); without it the calls return
+ * BH_ENODEV.
+ * ------------------------------------------------------------------------ */
+/* ncclGetUniqueId on one rank; the 128 bytes reach the others through the
+ * caller's own channel. */
+int bh_tp_unique_id(void *id_out);
+/* Join rank `rank` of `world` on `device` (-1: the current device). */
+int bh_tp_comm_init(int device, const void *unique_id, int world, int rank, int timeout_ms, void **comm_out);
+int bh_tp_comm_abort(void *comm);
+/* ncclCommFinalize, bounded, then ncclCommDestroy (aborted on timeout). */
+int bh_tp_comm_free(void *comm, int timeout_ms);
+int bh_tp_comm_info(void *comm, int *rank, int *world);
+/* recv [world][bytes_per_rank] <- every rank's send, completed on stream
+ * before returning. */
+int bh_tp_allgather(void *comm, const void *send, void *recv, size_t bytes_per_rank, void *stream, int timeout_ms);
+/* buf <- the elementwise sum over ranks (the expert-parallel MoE's exchange:
+ * bh_q4k_moe_ep writes -0.0 in the rows it does not own, so each sum has one
+ * nonzero term and equals one GPU's value), completed before returning. */
+int bh_tp_allreduce_sum_f32(void *comm, float *buf, size_t count, void *stream, int timeout_ms);
+/* bh_stack_tp_connect with the handles all-gathered over comm (whose rank
+ * and size must be the stack's). */
+int bh_stack_tp_connect_comm(bh_stack *st, void *comm, int timeout_ms);
 
 /* ------------------------------------------------------------------------
  * Routed-expert FFN (MoE): the stock block of desktop/engine/src/forward.cpp
@@ -334,9 +394,8 @@ int bh_stack_tensor(bh_stack *st, int layer, int which, void **ptr, int64_t *row
  * and 1 swapped, as ggml_top_k writes them (ggml-cpu/ops.cpp:8157-8194;
  * equal probabilities lower index first); their probabilities, divided by
  * their double sum when norm_topk != 0. selected_out / weights_out are
- * device [n_tok][k]. exp is evaluated by the library's own Cody-Waite
- * routine, within 1 ulp of exp (the reference's SIMD exp differs by a few
- * ulp). */
+ * device [n_tok][k]. exp is the reference's AVX2 ggml_v_expf, lane for lane
+ * (ggml-cpu/vec.h), so probabilities and weights equal the reference's. */
 int bh_moe_route(bh_ctx *ctx, const float *logits, int n_tok, int n_expert, int k, int norm_topk,
                  int32_t *selected_out, float *weights_out, void *stream);
 

@@ -147,6 +147,18 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.bh_stack_info.argtypes = [_vp, C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i64)]
     L.bh_stack_time_op.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(_i64)]
     L.bh_stack_tensor.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(_vp), C.POINTER(_i64), C.POINTER(_i64)]
+    L.bh_stack_create_tp.argtypes = [_vp, C.POINTER(StackConfig), C.c_uint64, C.c_int, C.c_int, C.POINTER(_vp)]
+    L.bh_stack_tp_handle.argtypes = [_vp, _vp]
+    L.bh_stack_tp_connect.argtypes = [_vp, _vp]
+    L.bh_stack_tp_info.argtypes = [_vp, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(_i64)]
+    L.bh_stack_tp_connect_comm.argtypes = [_vp, _vp, C.c_int]
+    L.bh_tp_unique_id.argtypes = [_vp]
+    L.bh_tp_comm_init.argtypes = [C.c_int, _vp, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]
+    L.bh_tp_comm_abort.argtypes = [_vp]
+    L.bh_tp_comm_free.argtypes = [_vp, C.c_int]
+    L.bh_tp_comm_info.argtypes = [_vp, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+    L.bh_tp_allgather.argtypes = [_vp, _vp, _vp, C.c_size_t, _vp, C.c_int]
+    L.bh_tp_allreduce_sum_f32.argtypes = [_vp, _vp, C.c_size_t, _vp, C.c_int]
     L.bh_moe_route.argtypes = [_vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp]
     L.bh_q4k_moe.argtypes = [_vp, _vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int,
                              C.c_int, _vp, _vp, _vp, C.c_int, _vp]
@@ -294,6 +306,45 @@ class Context:
         return host_y
 
 
+def tp_unique_id() -> bytes:
+    """ncclGetUniqueId through the library (bh_tp_unique_id): 128 bytes."""
+    buf = C.create_string_buffer(128)
+    _check(lib.bh_tp_unique_id(buf), "bh_tp_unique_id")
+    return buf.raw
+
+
+def tp_comm_init(device: int, unique_id: bytes, world: int, rank: int, timeout_ms: int = 30000):
+    """A non-blocking NCCL communicator (bh_tp_comm_init): returns the
+    ncclComm_t as an int, or raises BHError (BH_ETIMEDOUT when a rank never
+    joined within timeout_ms; the communicator was then aborted)."""
+    comm = _vp()
+    _check(lib.bh_tp_comm_init(device, unique_id, world, rank, timeout_ms, C.byref(comm)), "bh_tp_comm_init")
+    return comm.value
+
+
+def tp_comm_init_rc(device: int, unique_id: bytes, world: int, rank: int, timeout_ms: int):
+    """bh_tp_comm_init's status code and communicator, without raising."""
+    comm = _vp()
+    rc = lib.bh_tp_comm_init(device, unique_id, world, rank, timeout_ms, C.byref(comm))
+    return rc, comm.value
+
+
+def tp_comm_free(comm, timeout_ms: int = 30000) -> None:
+    _check(lib.bh_tp_comm_free(comm, timeout_ms), "bh_tp_comm_free")
+
+
+def tp_allgather(comm, send, recv, timeout_ms: int = 30000, stream=None) -> None:
+    """recv [world * n] <- every rank's send [n] (device tensors)."""
+    nbytes = send.numel() * send.element_size()
+    _check(lib.bh_tp_allgather(comm, _dp(send), _dp(recv), nbytes, _stream(stream), timeout_ms), "bh_tp_allgather")
+
+
+def tp_allreduce_sum(comm, buf, timeout_ms: int = 30000, stream=None) -> None:
+    """buf (fp32, device) <- elementwise sum over ranks."""
+    _check(lib.bh_tp_allreduce_sum_f32(comm, _dp(buf), buf.numel(), _stream(stream), timeout_ms),
+           "bh_tp_allreduce_sum_f32")
+
+
 def default_stack_config(**overrides) -> StackConfig:
     cfg = StackConfig()
     lib.bh_stack_default_config(C.byref(cfg))
@@ -303,14 +354,42 @@ def default_stack_config(**overrides) -> StackConfig:
 
 
 class Stack:
-    """A decode block stack (bh_stack_*) on a Context's device."""
+    """A decode block stack (bh_stack_*) on a Context's device; with world >
+    1, rank `rank`'s share of a row-split stack (bh_stack_create_tp), to be
+    connected to its peers (tp_connect / tp_connect_comm) before decoding."""
 
-    def __init__(self, ctx: Context, cfg: StackConfig, seed: int):
+    def __init__(self, ctx: Context, cfg: StackConfig, seed: int, rank: int = 0, world: int = 1):
         h = _vp()
-        _check(lib.bh_stack_create(ctx.h, C.byref(cfg), seed & (2**64 - 1), C.byref(h)), "bh_stack_create")
+        if world == 1:
+            _check(lib.bh_stack_create(ctx.h, C.byref(cfg), seed & (2**64 - 1), C.byref(h)), "bh_stack_create")
+        else:
+            _check(lib.bh_stack_create_tp(ctx.h, C.byref(cfg), seed & (2**64 - 1), rank, world, C.byref(h)),
+                   "bh_stack_create_tp")
         self.h = h
         self.ctx = ctx
         self.cfg = cfg
+        self.rank, self.world = rank, world
+
+    def tp_handle(self) -> bytes:
+        buf = C.create_string_buffer(64)
+        _check(lib.bh_stack_tp_handle(self.h, buf), "bh_stack_tp_handle")
+        return buf.raw
+
+    def tp_connect(self, handles) -> None:
+        """handles: every rank's tp_handle() in rank order."""
+        blob = b"".join(handles)
+        _check(lib.bh_stack_tp_connect(self.h, blob), "bh_stack_tp_connect")
+
+    def tp_connect_comm(self, comm, timeout_ms: int = 30000) -> None:
+        _check(lib.bh_stack_tp_connect_comm(self.h, comm, timeout_ms), "bh_stack_tp_connect_comm")
+
+    def tp_info(self) -> dict:
+        r, w = C.c_int(0), C.c_int(0)
+        rr = (_i64 * 10)()
+        _check(lib.bh_stack_tp_info(self.h, C.byref(r), C.byref(w), rr), "bh_stack_tp_info")
+        v = list(rr)
+        return {"rank": r.value, "world": w.value, "q_heads": (v[0], v[1]), "kv_heads": (v[2], v[3]),
+                "embd_rows": (v[4], v[5]), "ff_rows": (v[6], v[7]), "vocab_rows": (v[8], v[9])}
 
     def close(self) -> None:
         if self.h:

@@ -186,6 +186,22 @@ __device__ __forceinline__ void set_status(int* status, int code) {
 
 // Round to nearest, ties to even, through the 1.5*2^23 bias — the integer
 // rounding of ggml-quants.c:559-563, evaluated with a correctly rounded add.
+// System-scope release store / reduction and acquire load (flags and
+// counters that another GPU writes or reads over NVLink).
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ int round_biased(float v) {
     const float b = __fadd_rn(v, 12582912.f);
     return (__float_as_int(b) & 0x007fffff) - 0x00400000;

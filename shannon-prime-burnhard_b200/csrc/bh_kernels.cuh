@@ -7,6 +7,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "bh_common.cuh"
+
 namespace bh {
 
 // Function attributes (dynamic shared-memory limit, carveout) are per device:
@@ -44,6 +46,56 @@ enum Epilogue : int {
     // values of row i: y[b*ldy + i] = silu(gate_i) * up_i, i < n_ff.
     EPI_SWIGLU = 3,
 };
+
+// Row-split (tensor-parallel) decode over the GPUs of one node: a launch's
+// output rows are also stored into every peer's copy of the output vector
+// (plain stores over NVLink to IPC-mapped memory), and each CTA, once its
+// stores are visible system-wide, adds one to this rank's arrival counter of
+// that exchange in every peer's memory (release). The launch that reads the
+// whole vector waits, bounded, until every peer's counter shows all of that
+// peer's CTAs of the current step (acquire); a wait that runs out sets
+// ST_TIMEOUT and goes on.
+constexpr int TP_MAX_WORLD = 8;
+struct TpOut {
+    float* peer_y[TP_MAX_WORLD];       // peer i's copy of y, same offset (i < npeer)
+    uint32_t* peer_sig[TP_MAX_WORLD];  // peer i's arrival counter of this exchange for this rank
+    int npeer;                          // 0: no exchange
+};
+struct TpIn {
+    const uint32_t* sig;   // own arrival counters of the exchange, one per source rank (null: none)
+    const uint32_t* step;  // completed steps: each source's counter reaches (step + 1) * inc
+    uint32_t inc;          // CTAs of a source's producing launch
+    int world, rank;
+};
+
+// Thread 0 waits for the peers' arrivals of the exchange, then the CTA syncs.
+__device__ __forceinline__ void tp_wait_inputs(const TpIn& in, int* status) {
+    if (threadIdx.x == 0) {
+        const uint32_t want = (*reinterpret_cast<const volatile uint32_t*>(in.step) + 1u) * in.inc;
+        const long long t0 = clock64();
+        bool ok = true;
+        for (int s = 0; s < in.world && ok; ++s) {
+            if (s == in.rank) continue;
+            while ((int32_t)(ld_acquire_sys(in.sig + s) - want) < 0) {
+                if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+                    set_status(status, ST_TIMEOUT);
+                    ok = false;
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// Every thread of the CTA calls this after its last output store.
+__device__ __forceinline__ void tp_signal(const TpOut& o) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int i = 0; i < o.npeer; ++i) red_release_sys_add(o.peer_sig[i], 1u);
+    }
+}
 
 struct MatvecParams {
     // one 2-D tensor map per weight segment: 8-byte elements, rows of
@@ -83,6 +135,10 @@ struct MatvecParams {
     int stages;
     int prefill;           // stages per warp issued before the programmatic wait (0 = the whole ring, -1 = none)
     int act_off, ring_off, bar_off, smem_bytes;
+    // row-split decode: wait for the peers' rows of the input (tp_in.sig) and
+    // store this launch's rows into the peers' copies (tp_out.npeer)
+    TpIn tp_in;
+    TpOut tp_out;
 };
 
 struct LaunchOpts {
@@ -188,6 +244,12 @@ int launch_q4k_quantize(const float* w, int64_t N, int64_t K, uint8_t* out, cuda
 int launch_q4k_dequantize(const uint8_t* w, int64_t N, int64_t K, float* out, cudaStream_t s);
 // status (may be null): when the word is nonzero as the finisher runs (an
 // earlier bounded wait ran out), every token is written as -1.
+// The row-split LM head's pick merged across ranks through peer mailboxes
+// (peer_xchg.cu); epoch_dev, when set, replaces epoch by *epoch_dev + 1 and
+// step_out receives the epoch at the end (the decode stack's step counter).
+int launch_xchg_argmax(const float* cv, const int32_t* ci, int ncand, int B, int64_t row_offset, int rank, int world,
+                       void* const* boxes, uint32_t epoch, int32_t* tok, float* val, int* status, cudaStream_t s,
+                       const uint32_t* epoch_dev = nullptr, uint32_t* step_out = nullptr);
 int launch_argmax_finish(const float* cand_val, const int32_t* cand_idx, int ncand, int B,
                          int32_t* tok_out, float* val_out, cudaStream_t s, bool pdl, const int* status = nullptr);
 

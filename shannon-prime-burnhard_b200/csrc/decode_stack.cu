@@ -82,6 +82,7 @@ struct AttnParams {
     const uint8_t* pf_ptr;   // L2 prefetch of the weights streamed next (null: none)
     int64_t pf_bytes;
     int* status;             // device status word (a bounded copy wait that ran out)
+    TpOut tp_out;            // row-split decode: the peers' copies of out
 };
 
 #ifdef BH_TRACE
@@ -428,7 +429,11 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParam
             }
         }
     }
-    if (d < HD) a.out[(int64_t)h * HD + d] = sumf;
+    if (d < HD) {
+        a.out[(int64_t)h * HD + d] = sumf;
+        for (int i = 0; i < a.tp_out.npeer; ++i) a.tp_out.peer_y[i][(int64_t)h * HD + d] = sumf;
+    }
+    if (a.tp_out.npeer) tp_signal(a.tp_out);
     ATTN_TRACE_AT(6);
 }
 
@@ -461,13 +466,31 @@ struct bh_stack {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     int lm_grid = 0;
-    int64_t step_bytes = 0;         // algorithmic bytes of one decode step
+    int64_t step_bytes = 0;         // algorithmic bytes of one decode step (this GPU's rows)
     int64_t launches = 0;           // kernel launches in one step
+    // Row split over tp_world GPUs (1: the whole model here). This rank owns
+    // query heads [qh0, qh0 + n_head_l), KV heads [kh0, kh0 + n_head_kv_l),
+    // rows [e0, e0 + n_embd_l) of O and down, [f0, f0 + n_ff_l) of gate and
+    // up, [v0, v0 + n_vocab_l) of the LM head.
+    int tp_rank = 0, tp_world = 1;
+    int qh0 = 0, kh0 = 0, n_head_l = 0, n_head_kv_l = 0;
+    int64_t e0 = 0, f0 = 0, v0 = 0, n_embd_l = 0, n_ff_l = 0, n_vocab_l = 0;
+    // exchange region (one allocation, exported to the peers through CUDA
+    // IPC): the full h, attention output and SwiGLU output vectors, the
+    // arrival counters, the step counter and the LM head's pick mailbox
+    uint8_t* xbuf = nullptr;
+    size_t xbytes = 0, x_h = 0, x_attn = 0, x_gu = 0, x_sig = 0, x_step = 0, x_box = 0;
+    uint8_t* peer_x[bh::TP_MAX_WORLD] = {};  // every rank's exchange region as mapped here (own at [tp_rank])
+    bool tp_connected = false;
 };
 
 namespace {
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Exchanges of one layer in the row-split step: the attention output, h
+// after O, the SwiGLU output, h after down.
+constexpr int XG_ATTN = 0, XG_H_O = 1, XG_GU = 2, XG_H_DOWN = 3, XG_PER_LAYER = 4;
 
 int check_cfg(const bh_stack_config* c) {
     if (!c) return BH_EINVAL;
@@ -478,18 +501,51 @@ int check_cfg(const bh_stack_config* c) {
     return BH_OK;
 }
 
-void mat_dims(const bh_stack_config& c, int which, int64_t* rows, int64_t* cols) {
-    const int64_t qd = (int64_t)c.n_head * c.head_dim, kvd = (int64_t)c.n_head_kv * c.head_dim;
+// Rows of matrix `which` (-1: the LM head) this rank holds, the model row
+// the first of them is, and the columns.
+void mat_dims(const bh_stack* st, int which, int64_t* rows, int64_t* cols, int64_t* row0 = nullptr) {
+    const bh_stack_config& c = st->cfg;
+    const int64_t hd = c.head_dim, qd = (int64_t)c.n_head * hd;
+    int64_t r0 = 0;
     switch (which) {
-        case BH_W_Q: *rows = qd; *cols = c.n_embd; break;
-        case BH_W_K: *rows = kvd; *cols = c.n_embd; break;
-        case BH_W_V: *rows = kvd; *cols = c.n_embd; break;
-        case BH_W_O: *rows = c.n_embd; *cols = qd; break;
-        case BH_W_GATE: *rows = c.n_ff; *cols = c.n_embd; break;
-        case BH_W_UP: *rows = c.n_ff; *cols = c.n_embd; break;
-        case BH_W_DOWN: *rows = c.n_embd; *cols = c.n_ff; break;
-        default: *rows = c.n_vocab; *cols = c.n_embd; break;  // LM head
+        case BH_W_Q: *rows = st->n_head_l * hd; r0 = st->qh0 * hd; *cols = c.n_embd; break;
+        case BH_W_K:
+        case BH_W_V: *rows = st->n_head_kv_l * hd; r0 = st->kh0 * hd; *cols = c.n_embd; break;
+        case BH_W_O: *rows = st->n_embd_l; r0 = st->e0; *cols = qd; break;
+        case BH_W_GATE:
+        case BH_W_UP: *rows = st->n_ff_l; r0 = st->f0; *cols = c.n_embd; break;
+        case BH_W_DOWN: *rows = st->n_embd_l; r0 = st->e0; *cols = c.n_ff; break;
+        default: *rows = st->n_vocab_l; r0 = st->v0; *cols = c.n_embd; break;  // LM head
     }
+    if (row0) *row0 = r0;
+}
+
+// Peer stores and arrival counters of exchange xg of layer l, for a launch
+// whose output element 0 sits `off` bytes into the exchange region.
+bh::TpOut tp_out(const bh_stack* st, int l, int xg, size_t off) {
+    bh::TpOut o{};
+    if (st->tp_world < 2) return o;
+    for (int q = 0; q < st->tp_world; ++q) {
+        if (q == st->tp_rank) continue;
+        o.peer_y[o.npeer] = reinterpret_cast<float*>(st->peer_x[q] + off);
+        o.peer_sig[o.npeer] = reinterpret_cast<uint32_t*>(st->peer_x[q] + st->x_sig) +
+                              ((size_t)l * XG_PER_LAYER + xg) * bh::TP_MAX_WORLD + st->tp_rank;
+        ++o.npeer;
+    }
+    return o;
+}
+
+// The wait of a launch that reads the whole vector of exchange xg of layer l
+// (each peer's producing launch has `ctas` CTAs).
+bh::TpIn tp_in(const bh_stack* st, int l, int xg, int ctas) {
+    bh::TpIn in{};
+    if (st->tp_world < 2) return in;
+    in.sig = reinterpret_cast<const uint32_t*>(st->xbuf + st->x_sig) + ((size_t)l * XG_PER_LAYER + xg) * bh::TP_MAX_WORLD;
+    in.step = reinterpret_cast<const uint32_t*>(st->xbuf + st->x_step);
+    in.inc = (uint32_t)ctas;
+    in.world = st->tp_world;
+    in.rank = st->tp_rank;
+    return in;
 }
 
 uint64_t tensor_seed(uint64_t seed, int layer, int which) {
@@ -503,10 +559,11 @@ uint64_t tensor_seed(uint64_t seed, int layer, int which) {
 bh::MatvecParams gate_up_params(bh_stack* st, int l) {
     const bh_stack_config& c = st->cfg;
     const uint8_t* const* W = st->wq + (size_t)l * BH_W_PER_LAYER;
-    bh::MatvecParams p = bh::base_params(st->ctx, W[BH_W_GATE], 2 * (int64_t)c.n_ff, c.n_embd, 1, st->gu);
+    const int64_t nf = st->n_ff_l;  // this rank's rows of gate and of up (all of them on one GPU)
+    bh::MatvecParams p = bh::base_params(st->ctx, W[BH_W_GATE], 2 * nf, c.n_embd, 1, st->gu + st->f0);
     p.w[1] = p.w[2] = W[BH_W_UP];
-    p.seg_end[0] = c.n_ff;
-    p.seg_end[1] = p.seg_end[2] = 2 * (int64_t)c.n_ff;
+    p.seg_end[0] = nf;
+    p.seg_end[1] = p.seg_end[2] = 2 * nf;
     p.ldy = c.n_ff;
     p.xf = st->h;
     p.gamma = st->ffn_norm + (size_t)l * c.n_embd;
@@ -534,7 +591,7 @@ void set_prefetch(const bh_stack* st, const uint8_t* end, const uint8_t** ptr, i
 const uint8_t* mat_end(const bh_stack* st, int i) {
     const bh_stack_config& c = st->cfg;
     int64_t r, k;
-    mat_dims(c, i < c.n_layer * BH_W_PER_LAYER ? i % BH_W_PER_LAYER : -1, &r, &k);
+    mat_dims(st, i < c.n_layer * BH_W_PER_LAYER ? i % BH_W_PER_LAYER : -1, &r, &k);
     return st->wq[i] + r * (k / bh::QK) * bh::Q4K_BYTES;
 }
 
@@ -546,10 +603,12 @@ int stack_matvec(bh_stack* st, bh::MatvecParams& p, int src, int epi, bool pdl) 
 }
 
 // Attention of layer l over positions 0..pos (one CTA per query head).
+// (Row split: this rank's query heads and their KV heads, the output at the
+// heads' place in the full vector, also stored into the peers' copies.)
 int launch_attn(bh_stack* st, int l, bool pdl) {
     const bh_stack_config& c = st->cfg;
-    const int64_t kvd = (int64_t)c.n_head_kv * c.head_dim;
-    bh::AttnParams a;
+    const int64_t kvd = (int64_t)st->n_head_kv_l * c.head_dim;
+    bh::AttnParams a{};
     a.qkv = st->qkv;
     a.kc = st->kc + (size_t)l * c.n_ctx * kvd;
     a.vc = st->vc + (size_t)l * c.n_ctx * kvd;
@@ -557,9 +616,10 @@ int launch_attn(bh_stack* st, int l, bool pdl) {
     a.k_norm = st->k_norm + (size_t)l * c.head_dim;
     a.pos = st->pos;
     a.rope = st->rope;
-    a.out = st->attn;
-    a.n_head = c.n_head;
-    a.n_head_kv = c.n_head_kv;
+    a.out = st->attn + (size_t)st->qh0 * c.head_dim;
+    a.tp_out = tp_out(st, l, XG_ATTN, st->x_attn + sizeof(float) * (size_t)st->qh0 * c.head_dim);
+    a.n_head = st->n_head_l;
+    a.n_head_kv = st->n_head_kv_l;
     a.head_dim = c.head_dim;
     a.n_ctx = c.n_ctx;
     a.eps = c.rms_eps;
@@ -571,7 +631,7 @@ int launch_attn(bh_stack* st, int l, bool pdl) {
     if (st->ctx->trace) a.trace = st->ctx->trace + st->launches * bh::TRACE_LAUNCH;
 #endif
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)c.n_head);
+    cfg.gridDim = dim3((unsigned)st->n_head_l);
     cfg.blockDim = dim3((unsigned)bh::ATTN_THREADS);
     cfg.dynamicSmemBytes = sizeof(float) * ((size_t)2 * bh::ATTN_TILE * bh::ATTN_KROW + (size_t)c.n_ctx);
     cfg.stream = st->stream;
@@ -592,11 +652,23 @@ int launch_attn(bh_stack* st, int l, bool pdl) {
     return cudaLaunchKernelEx(&cfg, bh::attn_head_kernel, a) == cudaSuccess ? BH_OK : BH_EIO;
 }
 
-// Enqueue one decode step on st->stream (captured into the graph).
+// Grid of a matvec launch as the stack plans it.
+int planned_grid(bh_stack* st, const bh::MatvecParams& p) {
+    bh::MatvecParams q = p;
+    return bh::plan_for(&st->plan, q, 0, BH_FOLD_X86);
+}
+
+// Enqueue one decode step on st->stream (captured into the graph). On a row
+// split every launch works this rank's rows; the vectors the next launch
+// reads whole (attention output, h, SwiGLU output) are completed through the
+// peer stores of the launch that produces them and the wait at the start of
+// the one that reads them.
 int enqueue_step(bh_stack* st) {
     const bh_stack_config& c = st->cfg;
     bh_ctx* ctx = st->ctx;
-    const int64_t qd = (int64_t)c.n_head * c.head_dim, kvd = (int64_t)c.n_head_kv * c.head_dim;
+    const int64_t hd = c.head_dim, qd = (int64_t)c.n_head * hd;
+    const int64_t qd_l = (int64_t)st->n_head_l * hd, kvd_l = (int64_t)st->n_head_kv_l * hd;
+    const bool tp = st->tp_world > 1;
     int rc;
     if (cudaMemcpyAsync(st->h, st->x_in, sizeof(float) * c.n_embd, cudaMemcpyDeviceToDevice, st->stream) != cudaSuccess)
         return BH_EIO;
@@ -606,53 +678,66 @@ int enqueue_step(bh_stack* st) {
         st->step_bytes += p.N * (int64_t)p.nb * bh::Q4K_BYTES + b_in_bytes + out_rows * 4;
         st->launches += 1;
     };
+    int prev_grid = 0;  // CTAs of the launch that produced the last exchanged vector
     for (int l = 0; l < c.n_layer; ++l) {
         const uint8_t* const* W = st->wq + (size_t)l * BH_W_PER_LAYER;
-        // 1. QKV
-        bh::MatvecParams p = bh::base_params(ctx, W[BH_W_Q], qd + 2 * kvd, c.n_embd, 1, st->qkv);
+        const bool last = l == c.n_layer - 1;
+        // 1. QKV (this rank's heads; h is whole here)
+        bh::MatvecParams p = bh::base_params(ctx, W[BH_W_Q], qd_l + 2 * kvd_l, c.n_embd, 1, st->qkv);
         p.w[1] = W[BH_W_K];
         p.w[2] = W[BH_W_V];
-        p.seg_end[0] = qd;
-        p.seg_end[1] = qd + kvd;
-        p.seg_end[2] = qd + 2 * kvd;
+        p.seg_end[0] = qd_l;
+        p.seg_end[1] = qd_l + kvd_l;
+        p.seg_end[2] = qd_l + 2 * kvd_l;
         p.xf = st->h;
         p.gamma = st->attn_norm + (size_t)l * c.n_embd;
         p.eps = c.rms_eps;
+        if (l > 0) p.tp_in = tp_in(st, l - 1, XG_H_DOWN, prev_grid);
         set_prefetch(st, mat_end(st, l * BH_W_PER_LAYER + BH_W_V), &p.pf_ptr, &p.pf_bytes);
         if ((rc = stack_matvec(st, p, bh::ACT_F32_RMSNORM, bh::EPI_STORE, l > 0)) != BH_OK) return rc;
         account(p, c.n_embd * 4, p.N);
         // 2. attention
         if ((rc = launch_attn(st, l, true)) != BH_OK) return rc;
         st->launches += 1;
-        // 3. O projection, residual add
-        const bool last = l == c.n_layer - 1;
-        p = bh::base_params(ctx, W[BH_W_O], c.n_embd, qd, 1, st->h);
+        // 3. O projection, residual add on this rank's rows of h
+        p = bh::base_params(ctx, W[BH_W_O], st->n_embd_l, qd, 1, st->h + st->e0);
         p.xf = st->attn;
-        if (last) p.capture = st->cap_h_attn;
+        if (last && !tp) p.capture = st->cap_h_attn;
+        p.tp_in = tp_in(st, l, XG_ATTN, st->n_head_l);
+        p.tp_out = tp_out(st, l, XG_H_O, st->x_h + sizeof(float) * (size_t)st->e0);
         set_prefetch(st, mat_end(st, l * BH_W_PER_LAYER + BH_W_O), &p.pf_ptr, &p.pf_bytes);
+        if ((prev_grid = planned_grid(st, p)) < 0) return prev_grid;
         if ((rc = stack_matvec(st, p, bh::ACT_F32, bh::EPI_ADD, true)) != BH_OK) return rc;
         account(p, (int)qd * 4, p.N);
         // 4. gate / up in row pairs, silu(gate) * up in the epilogue
         p = gate_up_params(st, l);
-        if (last) p.capture = st->cap_gate_up;
+        if (last && !tp) p.capture = st->cap_gate_up;
+        p.tp_in = tp_in(st, l, XG_H_O, prev_grid);
+        p.tp_out = tp_out(st, l, XG_GU, st->x_gu + sizeof(float) * (size_t)st->f0);
         set_prefetch(st, mat_end(st, l * BH_W_PER_LAYER + BH_W_UP), &p.pf_ptr, &p.pf_bytes);
+        if ((prev_grid = planned_grid(st, p)) < 0) return prev_grid;
         if ((rc = stack_matvec(st, p, bh::ACT_F32_RMSNORM, bh::EPI_SWIGLU, true)) != BH_OK) return rc;
-        account(p, c.n_embd * 4, c.n_ff);
-        // 5. down, residual add
-        p = bh::base_params(ctx, W[BH_W_DOWN], c.n_embd, c.n_ff, 1, st->h);
+        account(p, c.n_embd * 4, st->n_ff_l);
+        // 5. down, residual add on this rank's rows of h
+        p = bh::base_params(ctx, W[BH_W_DOWN], st->n_embd_l, c.n_ff, 1, st->h + st->e0);
         p.xf = st->gu;
+        p.tp_in = tp_in(st, l, XG_GU, prev_grid);
+        p.tp_out = tp_out(st, l, XG_H_DOWN, st->x_h + sizeof(float) * (size_t)st->e0);
         set_prefetch(st, mat_end(st, l * BH_W_PER_LAYER + BH_W_DOWN), &p.pf_ptr, &p.pf_bytes);
+        if ((prev_grid = planned_grid(st, p)) < 0) return prev_grid;
         if ((rc = stack_matvec(st, p, bh::ACT_F32, bh::EPI_ADD, true)) != BH_OK) return rc;
         account(p, c.n_ff * 4, p.N);
     }
-    // LM head + argmax
-    bh::MatvecParams p = bh::base_params(ctx, st->wq[(size_t)c.n_layer * BH_W_PER_LAYER], c.n_vocab, c.n_embd, 1,
+    // LM head + argmax (row split: this rank's vocabulary rows, then the pick
+    // merged across ranks through the mailboxes)
+    bh::MatvecParams p = bh::base_params(ctx, st->wq[(size_t)c.n_layer * BH_W_PER_LAYER], st->n_vocab_l, c.n_embd, 1,
                                          st->logits);
     p.xf = st->h;
     p.gamma = st->out_norm;
     p.eps = c.rms_eps;
     p.cand_val = st->cand_val;
     p.cand_idx = st->cand_idx;
+    p.tp_in = tp_in(st, c.n_layer - 1, XG_H_DOWN, prev_grid);
     set_prefetch(st, mat_end(st, c.n_layer * BH_W_PER_LAYER), &p.pf_ptr, &p.pf_bytes);
 #ifdef BH_TRACE
     if (ctx->trace) p.trace = ctx->trace + st->launches * bh::TRACE_LAUNCH;
@@ -666,9 +751,16 @@ int enqueue_step(bh_stack* st) {
     o.pdl = true;
     if ((rc = bh::launch_matvec(p, BH_FOLD_X86, bh::ACT_F32_RMSNORM, bh::EPI_ARGMAX, o)) != BH_OK) return rc;
     account(p, c.n_embd * 4, p.N);
-    if ((rc = bh::launch_argmax_finish(st->cand_val, st->cand_idx, grid, 1, st->tok, nullptr, st->stream, true)) !=
-        BH_OK)
-        return rc;
+    if (tp) {
+        void* boxes[bh::TP_MAX_WORLD];
+        for (int q = 0; q < st->tp_world; ++q) boxes[q] = st->peer_x[q] + st->x_box;
+        uint32_t* step = reinterpret_cast<uint32_t*>(st->xbuf + st->x_step);
+        rc = bh::launch_xchg_argmax(st->cand_val, st->cand_idx, grid, 1, st->v0, st->tp_rank, st->tp_world, boxes, 0,
+                                    st->tok, nullptr, ctx->d_status, st->stream, step, step);
+    } else {
+        rc = bh::launch_argmax_finish(st->cand_val, st->cand_idx, grid, 1, st->tok, nullptr, st->stream, true);
+    }
+    if (rc != BH_OK) return rc;
     st->launches += 1;
     return BH_OK;
 }
@@ -738,6 +830,7 @@ int enqueue_op(bh_stack* st, int op) {
 
 int ensure_graph(bh_stack* st) {
     if (st->exec) return BH_OK;
+    if (st->tp_world > 1 && !st->tp_connected) return BH_EINVAL;  // bh_stack_tp_connect first
     if (cudaStreamBeginCapture(st->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return BH_EIO;
     const int rc = enqueue_step(st);
     cudaGraph_t g = nullptr;
@@ -775,14 +868,35 @@ void bh_stack_default_config(bh_stack_config* c) {
 }
 
 int bh_stack_create(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, bh_stack** out) {
+    return bh_stack_create_tp(ctx, cfg, seed, 0, 1, out);
+}
+
+int bh_stack_create_tp(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, int rank, int world, bh_stack** out) {
     if (!ctx || !out) return BH_EINVAL;
     *out = nullptr;
     int rc = check_cfg(cfg);
     if (rc != BH_OK) return rc;
+    // a row split keeps whole KV groups (and so whole query heads) on one
+    // rank, and 8-row multiples of every split matrix
+    if (world < 1 || world > bh::TP_MAX_WORLD || rank < 0 || rank >= world || cfg->n_head_kv % world ||
+        cfg->n_embd % (8 * world) || cfg->n_ff % (8 * world) || cfg->n_vocab < world)
+        return BH_EINVAL;
     if (cudaSetDevice(ctx->device) != cudaSuccess) return BH_ENODEV;
     bh_stack* st = new (std::nothrow) bh_stack();
     if (!st) return BH_ENOMEM;
     st->ctx = ctx;
+    st->tp_rank = rank;
+    st->tp_world = world;
+    st->n_head_l = cfg->n_head / world;
+    st->qh0 = st->n_head_l * rank;
+    st->n_head_kv_l = cfg->n_head_kv / world;
+    st->kh0 = st->n_head_kv_l * rank;
+    st->n_embd_l = cfg->n_embd / world;
+    st->e0 = st->n_embd_l * rank;
+    st->n_ff_l = cfg->n_ff / world;
+    st->f0 = st->n_ff_l * rank;
+    st->v0 = (int64_t)cfg->n_vocab * rank / world;  // the LM head's rows: an even split, the last shards may differ by one
+    st->n_vocab_l = (int64_t)cfg->n_vocab * (rank + 1) / world - st->v0;
     // Launch plan of the layer matvecs, unless the caller tuned a per-SM
     // budget on ctx: at most 168 KiB of shared memory per SM, 1440-byte row
     // slices per stage (one 16-warp CTA per SM; the planner picks the threads
@@ -814,7 +928,7 @@ int bh_stack_create(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, bh_s
     size_t total = 0, max_mat = 0;
     for (int i = 0; i < nmat; ++i) {
         int64_t r, k;
-        mat_dims(c, i < c.n_layer * BH_W_PER_LAYER ? i % BH_W_PER_LAYER : -1, &r, &k);
+        mat_dims(st, i < c.n_layer * BH_W_PER_LAYER ? i % BH_W_PER_LAYER : -1, &r, &k);
         off[i] = total;
         const size_t b = (size_t)r * (k / bh::QK) * bh::Q4K_BYTES;
         total = align_up(total + b, 256);
@@ -827,8 +941,9 @@ int bh_stack_create(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, bh_s
         return BH_ENOMEM;
     }
     for (int i = 0; i < nmat; ++i) st->wq[i] = st->wbuf + off[i];
-    // fp32 side buffers
-    const int64_t qd = (int64_t)c.n_head * c.head_dim, kvd = (int64_t)c.n_head_kv * c.head_dim;
+    // fp32 side buffers (this rank's heads and rows)
+    const int64_t qd = (int64_t)c.n_head * c.head_dim;
+    const int64_t qd_l = (int64_t)st->n_head_l * c.head_dim, kvd = (int64_t)st->n_head_kv_l * c.head_dim;
     const int cand_max = ctx->num_sms * 4;
     size_t fl = 0;
     auto take = [&](int64_t n) { const size_t o = fl; fl = align_up(fl + (size_t)n, 64); return o; };
@@ -836,12 +951,24 @@ int bh_stack_create(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, bh_s
     const size_t o_qn = take((int64_t)c.n_layer * c.head_dim), o_kn = take((int64_t)c.n_layer * c.head_dim);
     const size_t o_on = take(c.n_embd);
     const size_t o_kc = take((int64_t)c.n_layer * c.n_ctx * kvd), o_vc = take((int64_t)c.n_layer * c.n_ctx * kvd);
-    const size_t o_x = take(c.n_embd), o_h = take(c.n_embd), o_qkv = take(qd + 2 * kvd), o_at = take(qd);
-    const size_t o_gu = take(2 * (int64_t)c.n_ff), o_lg = take(c.n_vocab), o_cv = take(cand_max);
+    const size_t o_x = take(c.n_embd), o_qkv = take(qd_l + 2 * kvd);
+    const size_t o_lg = take(st->n_vocab_l), o_cv = take(cand_max);
     const size_t o_ci = take(cand_max), o_tk = take(1), o_ps = take(1);
     const size_t o_rf = take((int64_t)c.n_ctx * c.head_dim);  // (cos, sin) per position and pair
     const size_t o_ch = take(c.n_embd), o_cg = take(2 * (int64_t)c.n_ff);
-    if (cudaMalloc(&st->fbuf, fl * sizeof(float)) != cudaSuccess ||
+    // the exchange region: h, attention output, SwiGLU output (whole
+    // vectors), then per layer and exchange one arrival counter per source
+    // rank, the step counter, the pick mailbox
+    size_t xl = 0;
+    auto xtake = [&](size_t bytes) { const size_t o = xl; xl = align_up(xl + bytes, 256); return o; };
+    st->x_h = xtake(sizeof(float) * (size_t)c.n_embd);
+    st->x_attn = xtake(sizeof(float) * (size_t)qd);
+    st->x_gu = xtake(sizeof(float) * (size_t)c.n_ff);
+    st->x_sig = xtake(sizeof(uint32_t) * (size_t)c.n_layer * XG_PER_LAYER * bh::TP_MAX_WORLD);
+    st->x_step = xtake(sizeof(uint32_t));
+    st->x_box = xtake(bh_xchg_mailbox_bytes());
+    st->xbytes = xl;
+    if (cudaMalloc(&st->fbuf, fl * sizeof(float)) != cudaSuccess || cudaMalloc(&st->xbuf, st->xbytes) != cudaSuccess ||
         cudaMallocHost(&st->host_tok, sizeof(int32_t)) != cudaSuccess ||
         cudaMallocHost(&st->host_x, sizeof(float) * c.n_embd) != cudaSuccess) {
         cudaGetLastError();
@@ -849,10 +976,15 @@ int bh_stack_create(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, bh_s
         return BH_ENOMEM;
     }
     cudaMemsetAsync(st->fbuf, 0, fl * sizeof(float), st->stream);
+    cudaMemsetAsync(st->xbuf, 0, st->xbytes, st->stream);
+    st->peer_x[rank] = st->xbuf;
     float* F = st->fbuf;
     st->attn_norm = F + o_an; st->ffn_norm = F + o_fn; st->q_norm = F + o_qn; st->k_norm = F + o_kn;
-    st->out_norm = F + o_on; st->kc = F + o_kc; st->vc = F + o_vc; st->x_in = F + o_x; st->h = F + o_h;
-    st->qkv = F + o_qkv; st->attn = F + o_at; st->gu = F + o_gu; st->logits = F + o_lg; st->cand_val = F + o_cv;
+    st->out_norm = F + o_on; st->kc = F + o_kc; st->vc = F + o_vc; st->x_in = F + o_x;
+    st->h = reinterpret_cast<float*>(st->xbuf + st->x_h);
+    st->attn = reinterpret_cast<float*>(st->xbuf + st->x_attn);
+    st->gu = reinterpret_cast<float*>(st->xbuf + st->x_gu);
+    st->qkv = F + o_qkv; st->logits = F + o_lg; st->cand_val = F + o_cv;
     st->cand_idx = reinterpret_cast<int32_t*>(F + o_ci);
     st->tok = reinterpret_cast<int32_t*>(F + o_tk);
     st->pos = reinterpret_cast<int*>(F + o_ps);
@@ -905,13 +1037,15 @@ int bh_stack_create(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, bh_s
     for (int i = 0; i < nmat && rc == BH_OK; ++i) {
         const int layer = i < c.n_layer * BH_W_PER_LAYER ? i / BH_W_PER_LAYER : c.n_layer;
         const int which = i < c.n_layer * BH_W_PER_LAYER ? i % BH_W_PER_LAYER : BH_W_PER_LAYER;
-        int64_t r, k;
-        mat_dims(c, i < c.n_layer * BH_W_PER_LAYER ? which : -1, &r, &k);
+        int64_t r, k, row0;
+        mat_dims(st, i < c.n_layer * BH_W_PER_LAYER ? which : -1, &r, &k, &row0);
         const int64_t rows_per_chunk = (int64_t)(chunk_floats / (size_t)k);
         const uint64_t ts = tensor_seed(seed, layer, which);
+        // (the values of model rows row0 .. row0 + r - 1: on a row split each
+        // rank holds exactly the bytes one GPU holds for those rows)
         for (int64_t r0 = 0; r0 < r && rc == BH_OK; r0 += rows_per_chunk) {
             const int64_t nr = r - r0 < rows_per_chunk ? r - r0 : rows_per_chunk;
-            rc = bh::fill_normal(tmp, nr * k, r0 * k, ts, 0.0, 0.02, st->stream);
+            rc = bh::fill_normal(tmp, nr * k, (row0 + r0) * k, ts, 0.0, 0.02, st->stream);
             if (rc == BH_OK)
                 rc = bh::launch_q4k_quantize(tmp, nr, k,
                                              const_cast<uint8_t*>(st->wq[i]) + (size_t)r0 * (k / bh::QK) * bh::Q4K_BYTES,
@@ -930,11 +1064,15 @@ int bh_stack_create(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, bh_s
 
 int bh_stack_free(bh_stack* st) {
     if (!st) return BH_EINVAL;
+    if (st->ctx) cudaSetDevice(st->ctx->device);
     if (st->stream) cudaStreamSynchronize(st->stream);
     if (st->exec) cudaGraphExecDestroy(st->exec);
     if (st->graph) cudaGraphDestroy(st->graph);
+    for (int q = 0; q < st->tp_world; ++q)
+        if (q != st->tp_rank && st->peer_x[q]) cudaIpcCloseMemHandle(st->peer_x[q]);
     if (st->wbuf) cudaFree(st->wbuf);
     if (st->fbuf) cudaFree(st->fbuf);
+    if (st->xbuf) cudaFree(st->xbuf);
     if (st->host_tok) cudaFreeHost(st->host_tok);
     if (st->host_x) cudaFreeHost(st->host_x);
     if (st->stream) cudaStreamDestroy(st->stream);
@@ -954,15 +1092,85 @@ int bh_stack_set_pos(bh_stack* st, int pos) {
 int bh_stack_fill_kv(bh_stack* st, int n_pos, uint64_t seed) {
     if (!st || n_pos < 0 || n_pos > st->cfg.n_ctx) return BH_EINVAL;
     const bh_stack_config& c = st->cfg;
-    const int64_t kvd = (int64_t)c.n_head_kv * c.head_dim;
+    const int64_t kvd = (int64_t)c.n_head_kv * c.head_dim;         // the model's KV width
+    const int64_t kvd_l = (int64_t)st->n_head_kv_l * c.head_dim;   // this rank's KV heads
+    if (cudaSetDevice(st->ctx->device) != cudaSuccess) return BH_ENODEV;
+    // on a row split: the model's rows generated whole, this rank's KV heads
+    // copied out (the values one GPU holds for them)
+    float* tmp = nullptr;
+    if (st->tp_world > 1 && n_pos > 0 && cudaMalloc(&tmp, sizeof(float) * (size_t)n_pos * kvd) != cudaSuccess) {
+        cudaGetLastError();
+        return BH_ENOMEM;
+    }
     int rc = BH_OK;
     for (int l = 0; l < c.n_layer && rc == BH_OK; ++l) {
-        rc = bh::fill_normal(st->kc + (size_t)l * c.n_ctx * kvd, n_pos * kvd, 0, tensor_seed(seed, l, 100), 0.0, 1.0, st->stream);
-        if (rc == BH_OK)
-            rc = bh::fill_normal(st->vc + (size_t)l * c.n_ctx * kvd, n_pos * kvd, 0, tensor_seed(seed, l, 101), 0.0, 1.0, st->stream);
+        for (int v = 0; v < 2 && rc == BH_OK; ++v) {
+            float* dst = (v ? st->vc : st->kc) + (size_t)l * c.n_ctx * kvd_l;
+            const uint64_t ts = tensor_seed(seed, l, 100 + v);
+            if (!tmp) {
+                rc = bh::fill_normal(dst, n_pos * kvd, 0, ts, 0.0, 1.0, st->stream);
+                continue;
+            }
+            rc = bh::fill_normal(tmp, n_pos * kvd, 0, ts, 0.0, 1.0, st->stream);
+            if (rc == BH_OK &&
+                cudaMemcpy2DAsync(dst, sizeof(float) * kvd_l, tmp + (size_t)st->kh0 * c.head_dim, sizeof(float) * kvd,
+                                  sizeof(float) * kvd_l, (size_t)n_pos, cudaMemcpyDeviceToDevice, st->stream) != cudaSuccess)
+                rc = BH_EIO;
+        }
     }
-    if (cudaStreamSynchronize(st->stream) != cudaSuccess) return BH_EIO;
+    if (cudaStreamSynchronize(st->stream) != cudaSuccess) rc = BH_EIO;
+    if (tmp) cudaFree(tmp);
     return rc;
+}
+
+int bh_stack_tp_handle(bh_stack* st, void* handle_out) {
+    if (!st || !handle_out) return BH_EINVAL;
+    if (cudaSetDevice(st->ctx->device) != cudaSuccess) return BH_ENODEV;
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, st->xbuf) != cudaSuccess) {
+        cudaGetLastError();
+        return BH_EIO;
+    }
+    static_assert(sizeof(h) == 64, "IPC handle size");
+    std::memcpy(handle_out, &h, sizeof(h));
+    return BH_OK;
+}
+
+int bh_stack_tp_connect(bh_stack* st, const void* handles) {
+    if (!st || !handles || st->tp_connected) return BH_EINVAL;
+    if (cudaSetDevice(st->ctx->device) != cudaSuccess) return BH_ENODEV;
+    const uint8_t* hb = static_cast<const uint8_t*>(handles);
+    for (int q = 0; q < st->tp_world; ++q) {
+        if (q == st->tp_rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, hb + 64 * (size_t)q, sizeof(h));
+        void* ptr = nullptr;
+        if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            for (int r = 0; r < q; ++r)
+                if (r != st->tp_rank && st->peer_x[r]) {
+                    cudaIpcCloseMemHandle(st->peer_x[r]);
+                    st->peer_x[r] = nullptr;
+                }
+            return BH_EIO;
+        }
+        st->peer_x[q] = static_cast<uint8_t*>(ptr);
+    }
+    st->tp_connected = true;
+    return BH_OK;
+}
+
+int bh_stack_tp_info(bh_stack* st, int* rank, int* world, int64_t* row_ranges) {
+    if (!st) return BH_EINVAL;
+    if (rank) *rank = st->tp_rank;
+    if (world) *world = st->tp_world;
+    if (row_ranges) {
+        // query heads, KV heads, O / down rows, gate / up rows, LM head rows: (first, count)
+        const int64_t v[10] = {st->qh0, st->n_head_l, st->kh0, st->n_head_kv_l, st->e0,
+                               st->n_embd_l, st->f0, st->n_ff_l, st->v0, st->n_vocab_l};
+        std::memcpy(row_ranges, v, sizeof(v));
+    }
+    return BH_OK;
 }
 
 int bh_stack_decode(bh_stack* st, const float* x, int32_t* tok_out, void* stream) {
@@ -1003,6 +1211,7 @@ int bh_stack_info(bh_stack* st, int64_t* weight_bytes, int64_t* step_bytes, int6
 
 int bh_stack_time_op(bh_stack* st, int op, int reps, float* avg_ms, int64_t* bytes_per_launch) {
     if (!st || !avg_ms || reps < 1 || op < BH_OP_QKV || op > BH_OP_ATTN) return BH_EINVAL;
+    if (st->tp_world > 1) return BH_EINVAL;  // one GPU's step only (a row split's launches wait on each other)
     const bh_stack_config& c = st->cfg;
     const int64_t qd = (int64_t)c.n_head * c.head_dim, kvd = (int64_t)c.n_head_kv * c.head_dim;
     int64_t rows = 0, k = 0, xin = 0;
@@ -1043,16 +1252,16 @@ int bh_stack_tensor(bh_stack* st, int layer, int which, void** ptr, int64_t* row
     int64_t r = 0, k = 0;
     if (which >= 0 && which < BH_W_PER_LAYER) {
         if (layer < 0 || layer >= c.n_layer) return BH_EINVAL;
-        mat_dims(c, which, &r, &k);
+        mat_dims(st, which, &r, &k);
         *ptr = const_cast<uint8_t*>(st->wq[(size_t)layer * BH_W_PER_LAYER + which]);
     } else if (which == BH_W_OUTPUT) {
-        mat_dims(c, -1, &r, &k);
+        mat_dims(st, -1, &r, &k);
         *ptr = const_cast<uint8_t*>(st->wq[(size_t)c.n_layer * BH_W_PER_LAYER]);
     } else {
         const bool per_layer = which == BH_T_ATTN_NORM || which == BH_T_FFN_NORM || which == BH_T_Q_NORM ||
                                which == BH_T_K_NORM || which == BH_T_K_CACHE || which == BH_T_V_CACHE;
         if (per_layer && (layer < 0 || layer >= c.n_layer)) return BH_EINVAL;
-        const int64_t kvd = (int64_t)c.n_head_kv * c.head_dim;
+        const int64_t kvd = (int64_t)st->n_head_kv_l * c.head_dim;
         switch (which) {
             case BH_T_ATTN_NORM: *ptr = st->attn_norm + (size_t)layer * c.n_embd; r = 1; k = c.n_embd; break;
             case BH_T_FFN_NORM: *ptr = st->ffn_norm + (size_t)layer * c.n_embd; r = 1; k = c.n_embd; break;
@@ -1061,9 +1270,9 @@ int bh_stack_tensor(bh_stack* st, int layer, int which, void** ptr, int64_t* row
             case BH_T_OUT_NORM: *ptr = st->out_norm; r = 1; k = c.n_embd; break;
             case BH_T_K_CACHE: *ptr = st->kc + (size_t)layer * c.n_ctx * kvd; r = c.n_ctx; k = kvd; break;
             case BH_T_V_CACHE: *ptr = st->vc + (size_t)layer * c.n_ctx * kvd; r = c.n_ctx; k = kvd; break;
-            case BH_T_LOGITS: *ptr = st->logits; r = 1; k = c.n_vocab; break;
+            case BH_T_LOGITS: *ptr = st->logits; r = 1; k = st->n_vocab_l; break;
             case BH_T_HIDDEN: *ptr = st->h; r = 1; k = c.n_embd; break;
-            case BH_T_QKV: *ptr = st->qkv; r = 1; k = (int64_t)(c.n_head + 2 * c.n_head_kv) * c.head_dim; break;
+            case BH_T_QKV: *ptr = st->qkv; r = 1; k = (int64_t)(st->n_head_l + 2 * st->n_head_kv_l) * c.head_dim; break;
             case BH_T_ATTN: *ptr = st->attn; r = 1; k = (int64_t)c.n_head * c.head_dim; break;
             case BH_T_H_ATTN: *ptr = st->cap_h_attn; r = 1; k = c.n_embd; break;
             case BH_T_GATE_UP: *ptr = st->cap_gate_up; r = 1; k = 2 * (int64_t)c.n_ff; break;

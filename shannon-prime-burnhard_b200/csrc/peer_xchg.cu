@@ -47,23 +47,16 @@ struct XchgParams {
     int rank, world;
     uint8_t* box[XCHG_MAX_WORLD];  // every rank's mailbox as seen from this process (own at [rank])
     uint32_t epoch;
+    const uint32_t* epoch_dev;  // non-null: the epoch is *epoch_dev + 1 (read after the programmatic wait)
+    uint32_t* step_out;         // non-null: receives the epoch once the pick is merged
     int32_t* tok;
     float* val;
     int* status;
 };
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 __global__ void __launch_bounds__(256) xchg_argmax_kernel(const XchgParams a) {
     pdl_wait();
+    const uint32_t epoch = a.epoch_dev ? *reinterpret_cast<const volatile uint32_t*>(a.epoch_dev) + 1u : a.epoch;
     __shared__ float sv[8], bestv[BH_MAX_BATCH];
     __shared__ int si[8], besti[BH_MAX_BATCH];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -94,7 +87,7 @@ __global__ void __launch_bounds__(256) xchg_argmax_kernel(const XchgParams a) {
         __syncthreads();
     }
     if (threadIdx.x != 0) return;
-    const size_t bank = (a.epoch & 1u) * XCHG_BANK;
+    const size_t bank = (epoch & 1u) * XCHG_BANK;
     // publish: the pair into slot `rank` of every mailbox, then the flags
     for (int q = 0; q < a.world; ++q) {
         XchgSlot* s = reinterpret_cast<XchgSlot*>(a.box[q] + bank) + a.rank;
@@ -105,13 +98,13 @@ __global__ void __launch_bounds__(256) xchg_argmax_kernel(const XchgParams a) {
     }
     __threadfence_system();
     for (int q = 0; q < a.world; ++q)
-        st_release_sys(reinterpret_cast<uint32_t*>(a.box[q] + bank + XCHG_FLAGS_OFF) + a.rank, a.epoch);
+        st_release_sys(reinterpret_cast<uint32_t*>(a.box[q] + bank + XCHG_FLAGS_OFF) + a.rank, epoch);
     // collect every rank's slot from this GPU's own mailbox (bounded waits)
     const uint32_t* flags = reinterpret_cast<const uint32_t*>(a.box[a.rank] + bank + XCHG_FLAGS_OFF);
     const long long t0 = clock64();
     bool ok = true;
     for (int r = 0; r < a.world && ok; ++r) {
-        while (ld_acquire_sys(flags + r) != a.epoch) {
+        while (ld_acquire_sys(flags + r) != epoch) {
             if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
                 ok = false;
                 set_status(a.status, ST_TIMEOUT);
@@ -136,10 +129,12 @@ __global__ void __launch_bounds__(256) xchg_argmax_kernel(const XchgParams a) {
         a.tok[b] = ok ? bi : -1;
         if (a.val) a.val[b] = bv;
     }
+    if (a.step_out) *a.step_out = epoch;
 }
 
 int launch_xchg_argmax(const float* cv, const int32_t* ci, int ncand, int B, int64_t row_offset, int rank, int world,
-                       void* const* boxes, uint32_t epoch, int32_t* tok, float* val, int* status, cudaStream_t s) {
+                       void* const* boxes, uint32_t epoch, int32_t* tok, float* val, int* status, cudaStream_t s,
+                       const uint32_t* epoch_dev, uint32_t* step_out) {
     XchgParams a;
     a.cv = cv;
     a.ci = ci;
@@ -150,6 +145,8 @@ int launch_xchg_argmax(const float* cv, const int32_t* ci, int ncand, int B, int
     a.world = world;
     for (int q = 0; q < XCHG_MAX_WORLD; ++q) a.box[q] = q < world ? static_cast<uint8_t*>(boxes[q]) : nullptr;
     a.epoch = epoch;
+    a.epoch_dev = epoch_dev;
+    a.step_out = step_out;
     a.tok = tok;
     a.val = val;
     a.status = status;

@@ -284,8 +284,10 @@ __device__ __forceinline__ void finish_row(const MatvecParams& p, const float (&
             const float hv = __fadd_rn(*yp, v);  // ggml_add(x, W.a)
             *yp = hv;
             if (p.capture) p.capture[(int64_t)b * p.ldy + row] = hv;
+            for (int i = 0; i < p.tp_out.npeer; ++i) p.tp_out.peer_y[i][(int64_t)b * p.ldy + row] = hv;
         } else if (EPI != EPI_ARGMAX || p.y) {
             *yp = v;
+            for (int i = 0; i < p.tp_out.npeer; ++i) p.tp_out.peer_y[i][(int64_t)b * p.ldy + row] = v;
         }
         if (EPI == EPI_ARGMAX && v > best_v) { best_v = v; best_i = (int)row; }
     }
@@ -374,6 +376,7 @@ __global__ void __launch_bounds__(dense_warps(NB) * 32, dense_min_blocks(NB)) q4
     pdl_trigger();
     pdl_wait();
     BH_TRACE_AT(5);
+    if (p.tp_in.sig) tp_wait_inputs(p.tp_in, p.status);  // row-split decode: the peers' rows of the input
     // this warp's share of the L2 prefetch of a later launch's weights: now
     // when it has no copies of its own, else right after its last copy
     const int64_t wg = (int64_t)blockIdx.x * W + warp, nwg = (int64_t)gridDim.x * W;
@@ -455,7 +458,9 @@ BH_UNROLL(BH_KB_UNROLL)
                 const float u = __shfl_down_sync(FULLM, v, 16);
                 if (live && t == 0 && rgrp < R / 2) {
                     const int64_t i = (r_begin + (int64_t)(warp + j * W) * R) / 2 + rgrp;
-                    p.y[(int64_t)b * p.ldy + i] = __fmul_rn(silu_ggml(v), u);  // ggml_silu then ggml_mul
+                    const float a = __fmul_rn(silu_ggml(v), u);  // ggml_silu then ggml_mul
+                    p.y[(int64_t)b * p.ldy + i] = a;
+                    for (int q = 0; q < p.tp_out.npeer; ++q) p.tp_out.peer_y[q][(int64_t)b * p.ldy + i] = a;
                     if (p.capture) {  // the gate and up rows before the SwiGLU
                         p.capture[(int64_t)b * 2 * p.ldy + i] = v;
                         p.capture[(int64_t)b * 2 * p.ldy + p.ldy + i] = u;
@@ -502,6 +507,7 @@ BH_UNROLL(BH_KB_UNROLL)
             __syncthreads();
         }
     }
+    if (p.tp_out.npeer) tp_signal(p.tp_out);
 }
 
 // ---------------------------------------------------------------------------
