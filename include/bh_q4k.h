@@ -327,11 +327,11 @@ int bh_stack_tensor(bh_stack *st, int layer, int which, void **ptr, int64_t *row
  * on one rank, so tokens and hidden states equal one GPU's bit for bit.
  * world in 1..8 dividing n_head_kv, n_embd / 8 and n_ff / 8; world 1 is
  * bh_stack_create. The launches that produce a vector the next launch reads
- * whole (attention output, h after O and after down, the SwiGLU output) also
- * store their rows into the peers' copies over NVLink and signal per CTA;
- * the reading launch waits for the peers' signals (bounded, about a second:
- * then BH_ETIMEDOUT through bh_device_status and the stack must be
- * recreated). The LM head's pick is merged through peer mailboxes. Replaces
+ * whole (attention output, h after O and after down, the SwiGLU output)
+ * store each row as a 64-bit (value, generation) pair into every rank's copy
+ * (over NVLink for the peers); the reading launch polls for the
+ * generation it expects (bounded, about a second: then BH_ETIMEDOUT through
+ * bh_device_status and the stack must be recreated). The LM head's pick is merged through peer mailboxes. Replaces
  * the reference's single-device path through forward.cpp:2706-2854 and the
  * NCCL all-gather of ggml-cuda.cu:1216. */
 int bh_stack_create_tp(bh_ctx *ctx, const bh_stack_config *cfg, uint64_t seed, int rank, int world,
@@ -346,7 +346,9 @@ int bh_stack_tp_connect(bh_stack *st, const void *handles);
 int bh_stack_tp_info(bh_stack *st, int *rank, int *world, int64_t *row_ranges);
 /* On a row split: bh_stack_free after every rank's last decode has
  * completed (a host barrier), since the peers store into this rank's
- * exchange region; bh_stack_time_op is for one GPU only (BH_EINVAL). */
+ * exchange region; bh_stack_time_op is for one GPU only (BH_EINVAL); the
+ * exchanged vectors (BH_T_HIDDEN, BH_T_ATTN, BH_T_FFN_ACT) are 64-bit
+ * (fp32 value, generation) pairs, value in the low word (cols = 2 x n). */
 
 /* ------------------------------------------------------------------------
  * NCCL communicators from C (tp_comm.cu). A communicator is a void*

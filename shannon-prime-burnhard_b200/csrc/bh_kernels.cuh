@@ -47,54 +47,74 @@ enum Epilogue : int {
     EPI_SWIGLU = 3,
 };
 
-// Row-split (tensor-parallel) decode over the GPUs of one node: a launch's
-// output rows are also stored into every peer's copy of the output vector
-// (plain stores over NVLink to IPC-mapped memory), and each CTA, once its
-// stores are visible system-wide, adds one to this rank's arrival counter of
-// that exchange in every peer's memory (release). The launch that reads the
-// whole vector waits, bounded, until every peer's counter shows all of that
-// peer's CTAs of the current step (acquire); a wait that runs out sets
-// ST_TIMEOUT and goes on.
+// Row-split (tensor-parallel) decode over the GPUs of one node. The vectors
+// that one launch produces in row slices and the next reads whole (attention
+// output, h, SwiGLU output) are arrays of 64-bit (value, generation) pairs
+// with a copy on every rank: the producing launch stores each of its rows as
+// one pair into every rank's copy (its own and, over NVLink, the peers'),
+// and the reading launch takes a pair once its generation is the one it
+// expects (bounded polling, then ST_TIMEOUT). A 64-bit aligned store is
+// single-copy atomic, so a matching generation carries its value: no fence,
+// flag or counter, and the producer ends as soon as its stores are issued.
+// generation = completed steps * gen_mul + the exchange's offset (>= 1); a
+// buffer is rewritten only after every rank has read the previous
+// generation (each rank's next producer of it depends on data every reader
+// publishes after reading).
 constexpr int TP_MAX_WORLD = 8;
-struct TpOut {
-    float* peer_y[TP_MAX_WORLD];       // peer i's copy of y, same offset (i < npeer)
-    uint32_t* peer_sig[TP_MAX_WORLD];  // peer i's arrival counter of this exchange for this rank
-    int npeer;                          // 0: no exchange
-};
-struct TpIn {
-    const uint32_t* sig;   // own arrival counters of the exchange, one per source rank (null: none)
-    const uint32_t* step;  // completed steps: each source's counter reaches (step + 1) * inc
-    uint32_t inc;          // CTAs of a source's producing launch
-    int world, rank;
+struct TpLL {
+    const uint64_t* x;                 // input pairs (null: the plain fp32 input)
+    uint64_t* y_self;                  // this rank's output pairs (null: the plain fp32 output)
+    uint64_t* y_peer[TP_MAX_WORLD];    // the peers' copies (same offsets), npeer of them
+    int npeer;
+    const uint32_t* step;              // completed steps of the stack
+    uint32_t gen_mul, gen_in, gen_out;
 };
 
-// Thread 0 waits for the peers' arrivals of the exchange, then the CTA syncs.
-__device__ __forceinline__ void tp_wait_inputs(const TpIn& in, int* status) {
-    if (threadIdx.x == 0) {
-        const uint32_t want = (*reinterpret_cast<const volatile uint32_t*>(in.step) + 1u) * in.inc;
-        const long long t0 = clock64();
-        bool ok = true;
-        for (int s = 0; s < in.world && ok; ++s) {
-            if (s == in.rank) continue;
-            while ((int32_t)(ld_acquire_sys(in.sig + s) - want) < 0) {
+__device__ __forceinline__ uint32_t tp_gen(const TpLL& ll, uint32_t off) {
+    return *reinterpret_cast<const volatile uint32_t*>(ll.step) * ll.gen_mul + off;
+}
+
+__device__ __forceinline__ void st_pair(uint64_t* p, float v, uint32_t gen) {
+    const uint64_t w = (uint64_t)__float_as_uint(v) | ((uint64_t)gen << 32);
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+// Store one output value as a pair into this rank's and every peer's copy.
+__device__ __forceinline__ void tp_store(const TpLL& ll, int64_t i, float v, uint32_t gen) {
+    st_pair(ll.y_self + i, v, gen);
+    for (int q = 0; q < ll.npeer; ++q) st_pair(ll.y_peer[q] + i, v, gen);
+}
+
+__device__ __forceinline__ void ld_pairs2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// Eight consecutive values (16-byte aligned pairs) once all carry generation
+// gen; false when the bound ran out (the values are then whatever was read).
+__device__ __forceinline__ bool tp_load8(const uint64_t* src, uint32_t gen, float (&v)[8]) {
+    uint64_t w[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) ld_pairs2(src + 2 * k, w[2 * k], w[2 * k + 1]);
+    bool ok = true;
+    long long t0 = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        if ((uint32_t)(w[k] >> 32) != gen) {
+            if (t0 == 0) t0 = clock64();
+            for (;;) {
+                uint64_t a, b;
+                ld_pairs2(src + (k & ~1), a, b);
+                w[k] = (k & 1) ? b : a;
+                if ((uint32_t)(w[k] >> 32) == gen) break;
                 if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
-                    set_status(status, ST_TIMEOUT);
                     ok = false;
                     break;
                 }
             }
         }
+        v[k] = __uint_as_float((uint32_t)w[k]);
     }
-    __syncthreads();
-}
-
-// Every thread of the CTA calls this after its last output store.
-__device__ __forceinline__ void tp_signal(const TpOut& o) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();
-        for (int i = 0; i < o.npeer; ++i) red_release_sys_add(o.peer_sig[i], 1u);
-    }
+    return ok;
 }
 
 struct MatvecParams {
@@ -135,10 +155,8 @@ struct MatvecParams {
     int stages;
     int prefill;           // stages per warp issued before the programmatic wait (0 = the whole ring, -1 = none)
     int act_off, ring_off, bar_off, smem_bytes;
-    // row-split decode: wait for the peers' rows of the input (tp_in.sig) and
-    // store this launch's rows into the peers' copies (tp_out.npeer)
-    TpIn tp_in;
-    TpOut tp_out;
+    // row-split decode: input and output vectors as exchanged pairs
+    TpLL ll;
 };
 
 struct LaunchOpts {

@@ -82,7 +82,7 @@ struct AttnParams {
     const uint8_t* pf_ptr;   // L2 prefetch of the weights streamed next (null: none)
     int64_t pf_bytes;
     int* status;             // device status word (a bounded copy wait that ran out)
-    TpOut tp_out;            // row-split decode: the peers' copies of out
+    TpLL ll;                 // row-split decode: out as exchanged pairs (ll.y_self set)
 };
 
 #ifdef BH_TRACE
@@ -247,6 +247,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParam
     pdl_trigger();
     pdl_wait();
     ATTN_TRACE_AT(5);
+    const uint32_t gen_out = a.ll.y_self ? tp_gen(a.ll, a.ll.gen_out) : 0u;
 
     // this head's q, the group's k and v of this token: norm, rotation
     if (w == 0) {
@@ -430,10 +431,11 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParam
         }
     }
     if (d < HD) {
-        a.out[(int64_t)h * HD + d] = sumf;
-        for (int i = 0; i < a.tp_out.npeer; ++i) a.tp_out.peer_y[i][(int64_t)h * HD + d] = sumf;
+        if (a.ll.y_self)
+            tp_store(a.ll, (int64_t)h * HD + d, sumf, gen_out);
+        else
+            a.out[(int64_t)h * HD + d] = sumf;
     }
-    if (a.tp_out.npeer) tp_signal(a.tp_out);
     ATTN_TRACE_AT(6);
 }
 
@@ -476,10 +478,10 @@ struct bh_stack {
     int qh0 = 0, kh0 = 0, n_head_l = 0, n_head_kv_l = 0;
     int64_t e0 = 0, f0 = 0, v0 = 0, n_embd_l = 0, n_ff_l = 0, n_vocab_l = 0;
     // exchange region (one allocation, exported to the peers through CUDA
-    // IPC): the full h, attention output and SwiGLU output vectors, the
-    // arrival counters, the step counter and the LM head's pick mailbox
+    // IPC): the full h, attention output and SwiGLU output vectors, the step
+    // counter and the LM head's pick mailbox
     uint8_t* xbuf = nullptr;
-    size_t xbytes = 0, x_h = 0, x_attn = 0, x_gu = 0, x_sig = 0, x_step = 0, x_box = 0;
+    size_t xbytes = 0, x_h = 0, x_attn = 0, x_gu = 0, x_step = 0, x_box = 0;
     uint8_t* peer_x[bh::TP_MAX_WORLD] = {};  // every rank's exchange region as mapped here (own at [tp_rank])
     bool tp_connected = false;
 };
@@ -488,8 +490,8 @@ namespace {
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Exchanges of one layer in the row-split step: the attention output, h
-// after O, the SwiGLU output, h after down.
+// Exchanges of one layer in the row-split step (generation offsets): the
+// attention output, h after O, the SwiGLU output, h after down.
 constexpr int XG_ATTN = 0, XG_H_O = 1, XG_GU = 2, XG_H_DOWN = 3, XG_PER_LAYER = 4;
 
 int check_cfg(const bh_stack_config* c) {
@@ -520,32 +522,27 @@ void mat_dims(const bh_stack* st, int which, int64_t* rows, int64_t* cols, int64
     if (row0) *row0 = r0;
 }
 
-// Peer stores and arrival counters of exchange xg of layer l, for a launch
-// whose output element 0 sits `off` bytes into the exchange region.
-bh::TpOut tp_out(const bh_stack* st, int l, int xg, size_t off) {
-    bh::TpOut o{};
-    if (st->tp_world < 2) return o;
-    for (int q = 0; q < st->tp_world; ++q) {
-        if (q == st->tp_rank) continue;
-        o.peer_y[o.npeer] = reinterpret_cast<float*>(st->peer_x[q] + off);
-        o.peer_sig[o.npeer] = reinterpret_cast<uint32_t*>(st->peer_x[q] + st->x_sig) +
-                              ((size_t)l * XG_PER_LAYER + xg) * bh::TP_MAX_WORLD + st->tp_rank;
-        ++o.npeer;
+// Exchanged-pair parameters of a launch on a row split (world 1: none):
+// input = the pairs of exchange (l_in, xg_in) at byte offset in_off of the
+// exchange region (xg_in < 0: the plain fp32 input), output = exchange
+// (l_out, xg_out) into the pairs at byte offset out_off of every rank's
+// region (xg_out < 0: the plain output).
+bh::TpLL tp_ll(const bh_stack* st, size_t in_off, int l_in, int xg_in, size_t out_off, int l_out, int xg_out) {
+    bh::TpLL ll{};
+    if (st->tp_world < 2) return ll;
+    ll.step = reinterpret_cast<const uint32_t*>(st->xbuf + st->x_step);
+    ll.gen_mul = (uint32_t)(st->cfg.n_layer * XG_PER_LAYER);
+    if (xg_in >= 0) {
+        ll.x = reinterpret_cast<const uint64_t*>(st->xbuf + in_off);
+        ll.gen_in = (uint32_t)(l_in * XG_PER_LAYER + xg_in + 1);
     }
-    return o;
-}
-
-// The wait of a launch that reads the whole vector of exchange xg of layer l
-// (each peer's producing launch has `ctas` CTAs).
-bh::TpIn tp_in(const bh_stack* st, int l, int xg, int ctas) {
-    bh::TpIn in{};
-    if (st->tp_world < 2) return in;
-    in.sig = reinterpret_cast<const uint32_t*>(st->xbuf + st->x_sig) + ((size_t)l * XG_PER_LAYER + xg) * bh::TP_MAX_WORLD;
-    in.step = reinterpret_cast<const uint32_t*>(st->xbuf + st->x_step);
-    in.inc = (uint32_t)ctas;
-    in.world = st->tp_world;
-    in.rank = st->tp_rank;
-    return in;
+    if (xg_out >= 0) {
+        ll.y_self = reinterpret_cast<uint64_t*>(st->xbuf + out_off);
+        for (int q = 0; q < st->tp_world; ++q)
+            if (q != st->tp_rank) ll.y_peer[ll.npeer++] = reinterpret_cast<uint64_t*>(st->peer_x[q] + out_off);
+        ll.gen_out = (uint32_t)(l_out * XG_PER_LAYER + xg_out + 1);
+    }
+    return ll;
 }
 
 uint64_t tensor_seed(uint64_t seed, int layer, int which) {
@@ -617,7 +614,7 @@ int launch_attn(bh_stack* st, int l, bool pdl) {
     a.pos = st->pos;
     a.rope = st->rope;
     a.out = st->attn + (size_t)st->qh0 * c.head_dim;
-    a.tp_out = tp_out(st, l, XG_ATTN, st->x_attn + sizeof(float) * (size_t)st->qh0 * c.head_dim);
+    a.ll = tp_ll(st, 0, 0, -1, st->x_attn + 8 * (size_t)st->qh0 * c.head_dim, l, XG_ATTN);
     a.n_head = st->n_head_l;
     a.n_head_kv = st->n_head_kv_l;
     a.head_dim = c.head_dim;
@@ -652,17 +649,11 @@ int launch_attn(bh_stack* st, int l, bool pdl) {
     return cudaLaunchKernelEx(&cfg, bh::attn_head_kernel, a) == cudaSuccess ? BH_OK : BH_EIO;
 }
 
-// Grid of a matvec launch as the stack plans it.
-int planned_grid(bh_stack* st, const bh::MatvecParams& p) {
-    bh::MatvecParams q = p;
-    return bh::plan_for(&st->plan, q, 0, BH_FOLD_X86);
-}
-
 // Enqueue one decode step on st->stream (captured into the graph). On a row
 // split every launch works this rank's rows; the vectors the next launch
-// reads whole (attention output, h, SwiGLU output) are completed through the
-// peer stores of the launch that produces them and the wait at the start of
-// the one that reads them.
+// reads whole (attention output, h, SwiGLU output) are exchanged as
+// generation-tagged pairs that the producing launch stores into every rank's
+// copy and the reading launch polls for.
 int enqueue_step(bh_stack* st) {
     const bh_stack_config& c = st->cfg;
     bh_ctx* ctx = st->ctx;
@@ -670,29 +661,32 @@ int enqueue_step(bh_stack* st) {
     const int64_t qd_l = (int64_t)st->n_head_l * hd, kvd_l = (int64_t)st->n_head_kv_l * hd;
     const bool tp = st->tp_world > 1;
     int rc;
-    if (cudaMemcpyAsync(st->h, st->x_in, sizeof(float) * c.n_embd, cudaMemcpyDeviceToDevice, st->stream) != cudaSuccess)
-        return BH_EIO;
+    const cudaError_t ce =
+        tp ? cudaMemcpy2DAsync(st->xbuf + st->x_h, 8, st->x_in, 4, 4, (size_t)c.n_embd, cudaMemcpyDeviceToDevice,
+                               st->stream)  // the values of h's pairs (the first QKV reads x_in itself)
+           : cudaMemcpyAsync(st->h, st->x_in, sizeof(float) * c.n_embd, cudaMemcpyDeviceToDevice, st->stream);
+    if (ce != cudaSuccess) return BH_EIO;
     st->step_bytes = 0;
     st->launches = 0;
     auto account = [&](const bh::MatvecParams& p, int b_in_bytes, int64_t out_rows) {
         st->step_bytes += p.N * (int64_t)p.nb * bh::Q4K_BYTES + b_in_bytes + out_rows * 4;
         st->launches += 1;
     };
-    int prev_grid = 0;  // CTAs of the launch that produced the last exchanged vector
+    const size_t h_e0 = st->x_h + 8 * (size_t)st->e0, gu_f0 = st->x_gu + 8 * (size_t)st->f0;
     for (int l = 0; l < c.n_layer; ++l) {
         const uint8_t* const* W = st->wq + (size_t)l * BH_W_PER_LAYER;
         const bool last = l == c.n_layer - 1;
-        // 1. QKV (this rank's heads; h is whole here)
+        // 1. QKV (this rank's heads of the whole h)
         bh::MatvecParams p = bh::base_params(ctx, W[BH_W_Q], qd_l + 2 * kvd_l, c.n_embd, 1, st->qkv);
         p.w[1] = W[BH_W_K];
         p.w[2] = W[BH_W_V];
         p.seg_end[0] = qd_l;
         p.seg_end[1] = qd_l + kvd_l;
         p.seg_end[2] = qd_l + 2 * kvd_l;
-        p.xf = st->h;
+        p.xf = tp && l == 0 ? st->x_in : st->h;
         p.gamma = st->attn_norm + (size_t)l * c.n_embd;
         p.eps = c.rms_eps;
-        if (l > 0) p.tp_in = tp_in(st, l - 1, XG_H_DOWN, prev_grid);
+        p.ll = tp_ll(st, st->x_h, l - 1, l > 0 ? XG_H_DOWN : -1, 0, 0, -1);
         set_prefetch(st, mat_end(st, l * BH_W_PER_LAYER + BH_W_V), &p.pf_ptr, &p.pf_bytes);
         if ((rc = stack_matvec(st, p, bh::ACT_F32_RMSNORM, bh::EPI_STORE, l > 0)) != BH_OK) return rc;
         account(p, c.n_embd * 4, p.N);
@@ -703,28 +697,22 @@ int enqueue_step(bh_stack* st) {
         p = bh::base_params(ctx, W[BH_W_O], st->n_embd_l, qd, 1, st->h + st->e0);
         p.xf = st->attn;
         if (last && !tp) p.capture = st->cap_h_attn;
-        p.tp_in = tp_in(st, l, XG_ATTN, st->n_head_l);
-        p.tp_out = tp_out(st, l, XG_H_O, st->x_h + sizeof(float) * (size_t)st->e0);
+        p.ll = tp_ll(st, st->x_attn, l, XG_ATTN, h_e0, l, XG_H_O);
         set_prefetch(st, mat_end(st, l * BH_W_PER_LAYER + BH_W_O), &p.pf_ptr, &p.pf_bytes);
-        if ((prev_grid = planned_grid(st, p)) < 0) return prev_grid;
         if ((rc = stack_matvec(st, p, bh::ACT_F32, bh::EPI_ADD, true)) != BH_OK) return rc;
         account(p, (int)qd * 4, p.N);
         // 4. gate / up in row pairs, silu(gate) * up in the epilogue
         p = gate_up_params(st, l);
         if (last && !tp) p.capture = st->cap_gate_up;
-        p.tp_in = tp_in(st, l, XG_H_O, prev_grid);
-        p.tp_out = tp_out(st, l, XG_GU, st->x_gu + sizeof(float) * (size_t)st->f0);
+        p.ll = tp_ll(st, st->x_h, l, XG_H_O, gu_f0, l, XG_GU);
         set_prefetch(st, mat_end(st, l * BH_W_PER_LAYER + BH_W_UP), &p.pf_ptr, &p.pf_bytes);
-        if ((prev_grid = planned_grid(st, p)) < 0) return prev_grid;
         if ((rc = stack_matvec(st, p, bh::ACT_F32_RMSNORM, bh::EPI_SWIGLU, true)) != BH_OK) return rc;
         account(p, c.n_embd * 4, st->n_ff_l);
         // 5. down, residual add on this rank's rows of h
         p = bh::base_params(ctx, W[BH_W_DOWN], st->n_embd_l, c.n_ff, 1, st->h + st->e0);
         p.xf = st->gu;
-        p.tp_in = tp_in(st, l, XG_GU, prev_grid);
-        p.tp_out = tp_out(st, l, XG_H_DOWN, st->x_h + sizeof(float) * (size_t)st->e0);
+        p.ll = tp_ll(st, st->x_gu, l, XG_GU, h_e0, l, XG_H_DOWN);
         set_prefetch(st, mat_end(st, l * BH_W_PER_LAYER + BH_W_DOWN), &p.pf_ptr, &p.pf_bytes);
-        if ((prev_grid = planned_grid(st, p)) < 0) return prev_grid;
         if ((rc = stack_matvec(st, p, bh::ACT_F32, bh::EPI_ADD, true)) != BH_OK) return rc;
         account(p, c.n_ff * 4, p.N);
     }
@@ -737,7 +725,7 @@ int enqueue_step(bh_stack* st) {
     p.eps = c.rms_eps;
     p.cand_val = st->cand_val;
     p.cand_idx = st->cand_idx;
-    p.tp_in = tp_in(st, c.n_layer - 1, XG_H_DOWN, prev_grid);
+    p.ll = tp_ll(st, st->x_h, c.n_layer - 1, XG_H_DOWN, 0, 0, -1);
     set_prefetch(st, mat_end(st, c.n_layer * BH_W_PER_LAYER), &p.pf_ptr, &p.pf_bytes);
 #ifdef BH_TRACE
     if (ctx->trace) p.trace = ctx->trace + st->launches * bh::TRACE_LAUNCH;
@@ -881,6 +869,11 @@ int bh_stack_create_tp(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, i
     if (world < 1 || world > bh::TP_MAX_WORLD || rank < 0 || rank >= world || cfg->n_head_kv % world ||
         cfg->n_embd % (8 * world) || cfg->n_ff % (8 * world) || cfg->n_vocab < world)
         return BH_EINVAL;
+    // (a split's launches read the exchanged vectors in their one-round
+    // staging: at most 32 blocks through RMSNorm, 48 plain)
+    if (world > 1 && (cfg->n_embd > 32 * bh::QK || (int64_t)cfg->n_head * cfg->head_dim > 48 * bh::QK ||
+                      cfg->n_ff > 48 * bh::QK))
+        return BH_EINVAL;
     if (cudaSetDevice(ctx->device) != cudaSuccess) return BH_ENODEV;
     bh_stack* st = new (std::nothrow) bh_stack();
     if (!st) return BH_ENOMEM;
@@ -957,14 +950,12 @@ int bh_stack_create_tp(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, i
     const size_t o_rf = take((int64_t)c.n_ctx * c.head_dim);  // (cos, sin) per position and pair
     const size_t o_ch = take(c.n_embd), o_cg = take(2 * (int64_t)c.n_ff);
     // the exchange region: h, attention output, SwiGLU output (whole
-    // vectors), then per layer and exchange one arrival counter per source
-    // rank, the step counter, the pick mailbox
+    // vectors), the step counter, the pick mailbox
     size_t xl = 0;
     auto xtake = [&](size_t bytes) { const size_t o = xl; xl = align_up(xl + bytes, 256); return o; };
-    st->x_h = xtake(sizeof(float) * (size_t)c.n_embd);
-    st->x_attn = xtake(sizeof(float) * (size_t)qd);
-    st->x_gu = xtake(sizeof(float) * (size_t)c.n_ff);
-    st->x_sig = xtake(sizeof(uint32_t) * (size_t)c.n_layer * XG_PER_LAYER * bh::TP_MAX_WORLD);
+    st->x_h = xtake(sizeof(uint64_t) * (size_t)c.n_embd);  // fp32 values on one GPU, (value, generation) pairs on a split
+    st->x_attn = xtake(sizeof(uint64_t) * (size_t)qd);
+    st->x_gu = xtake(sizeof(uint64_t) * (size_t)c.n_ff);
     st->x_step = xtake(sizeof(uint32_t));
     st->x_box = xtake(bh_xchg_mailbox_bytes());
     st->xbytes = xl;
@@ -1271,12 +1262,12 @@ int bh_stack_tensor(bh_stack* st, int layer, int which, void** ptr, int64_t* row
             case BH_T_K_CACHE: *ptr = st->kc + (size_t)layer * c.n_ctx * kvd; r = c.n_ctx; k = kvd; break;
             case BH_T_V_CACHE: *ptr = st->vc + (size_t)layer * c.n_ctx * kvd; r = c.n_ctx; k = kvd; break;
             case BH_T_LOGITS: *ptr = st->logits; r = 1; k = st->n_vocab_l; break;
-            case BH_T_HIDDEN: *ptr = st->h; r = 1; k = c.n_embd; break;
+            case BH_T_HIDDEN: *ptr = st->h; r = 1; k = c.n_embd * (st->tp_world > 1 ? 2 : 1); break;
             case BH_T_QKV: *ptr = st->qkv; r = 1; k = (int64_t)(st->n_head_l + 2 * st->n_head_kv_l) * c.head_dim; break;
-            case BH_T_ATTN: *ptr = st->attn; r = 1; k = (int64_t)c.n_head * c.head_dim; break;
+            case BH_T_ATTN: *ptr = st->attn; r = 1; k = (int64_t)c.n_head * c.head_dim * (st->tp_world > 1 ? 2 : 1); break;
             case BH_T_H_ATTN: *ptr = st->cap_h_attn; r = 1; k = c.n_embd; break;
             case BH_T_GATE_UP: *ptr = st->cap_gate_up; r = 1; k = 2 * (int64_t)c.n_ff; break;
-            case BH_T_FFN_ACT: *ptr = st->gu; r = 1; k = c.n_ff; break;
+            case BH_T_FFN_ACT: *ptr = st->gu; r = 1; k = (int64_t)c.n_ff * (st->tp_world > 1 ? 2 : 1); break;
             default: return BH_EINVAL;
         }
     }

@@ -91,7 +91,7 @@ __device__ __forceinline__ void preload_gamma(const MatvecParams& p, float (&gp)
 // is issued (the warp's remaining weight copies go out behind them).
 template <int FOLD, int SRC, int W, class TopUp>
 __device__ void stage_activations(const MatvecParams& p, uint8_t* act, double* red, int ctid,
-                                  const float (&gp)[STAGE_UF][8], TopUp&& top_up) {
+                                  const float (&gp)[STAGE_UF][8], uint32_t gen_in, TopUp&& top_up) {
     const int warp = ctid >> 5, lane = ctid & 31;
     const int nblk = p.B * p.nb;
     // Each warp stages blocks warp, warp+W, ...; U blocks at a time with all
@@ -196,10 +196,15 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, double* r
 #pragma unroll
             for (int t = 0; t < 8; ++t) { v[u][t] = 0.f; aux[u][t] = 0.f; }
             if (blk < nblk) {
-                const float* x = p.xf + (int64_t)b * p.K + e0;
-                const float4 a0 = *reinterpret_cast<const float4*>(x), a1 = *reinterpret_cast<const float4*>(x + 4);
-                v[u][0] = a0.x; v[u][1] = a0.y; v[u][2] = a0.z; v[u][3] = a0.w;
-                v[u][4] = a1.x; v[u][5] = a1.y; v[u][6] = a1.z; v[u][7] = a1.w;
+                if (p.ll.x) {
+                    // row split: the exchanged pairs of this generation
+                    if (!tp_load8(p.ll.x + (int64_t)b * p.K + e0, gen_in, v[u])) set_status(p.status, ST_TIMEOUT);
+                } else {
+                    const float* x = p.xf + (int64_t)b * p.K + e0;
+                    const float4 a0 = *reinterpret_cast<const float4*>(x), a1 = *reinterpret_cast<const float4*>(x + 4);
+                    v[u][0] = a0.x; v[u][1] = a0.y; v[u][2] = a0.z; v[u][3] = a0.w;
+                    v[u][4] = a1.x; v[u][5] = a1.y; v[u][6] = a1.z; v[u][7] = a1.w;
+                }
                 if constexpr (SRC == ACT_F32_RMSNORM) {
                     if (one_round) {
 #pragma unroll
@@ -276,18 +281,23 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, double* r
 // Per-row epilogue of the dense kernel.
 template <int FOLD, int EPI, int TPR>
 __device__ __forceinline__ void finish_row(const MatvecParams& p, const float (&acc)[RowBlk<TPR>::L], float accm, int rgrp,
-                                           int t, int b, bool has_row, int64_t row, float& best_v, int& best_i) {
+                                           int t, int b, bool has_row, int64_t row, float& best_v, int& best_i,
+                                           uint32_t gen_out) {
     const float v = row_value<FOLD, TPR>(acc, accm, rgrp);
     if (has_row && t == 0) {
-        float* yp = p.y + (int64_t)b * p.ldy + row;
-        if (EPI == EPI_ADD) {
+        const int64_t yi = (int64_t)b * p.ldy + row;
+        if (p.ll.y_self && EPI != EPI_ARGMAX) {
+            // row split: the pair into every rank's copy (the residual is
+            // this rank's own row of the previous generation)
+            const float hv = EPI == EPI_ADD ? __fadd_rn(__uint_as_float((uint32_t)p.ll.y_self[yi]), v) : v;
+            tp_store(p.ll, yi, hv, gen_out);
+        } else if (EPI == EPI_ADD) {
+            float* yp = p.y + yi;
             const float hv = __fadd_rn(*yp, v);  // ggml_add(x, W.a)
             *yp = hv;
-            if (p.capture) p.capture[(int64_t)b * p.ldy + row] = hv;
-            for (int i = 0; i < p.tp_out.npeer; ++i) p.tp_out.peer_y[i][(int64_t)b * p.ldy + row] = hv;
+            if (p.capture) p.capture[yi] = hv;
         } else if (EPI != EPI_ARGMAX || p.y) {
-            *yp = v;
-            for (int i = 0; i < p.tp_out.npeer; ++i) p.tp_out.peer_y[i][(int64_t)b * p.ldy + row] = v;
+            p.y[yi] = v;
         }
         if (EPI == EPI_ARGMAX && v > best_v) { best_v = v; best_i = (int)row; }
     }
@@ -376,7 +386,10 @@ __global__ void __launch_bounds__(dense_warps(NB) * 32, dense_min_blocks(NB)) q4
     pdl_trigger();
     pdl_wait();
     BH_TRACE_AT(5);
-    if (p.tp_in.sig) tp_wait_inputs(p.tp_in, p.status);  // row-split decode: the peers' rows of the input
+    // row split: generations of the exchanged input and output (the step
+    // counter is final once the previous kernel has completed)
+    const uint32_t gen_in = p.ll.x ? tp_gen(p.ll, p.ll.gen_in) : 0u;
+    const uint32_t gen_out = p.ll.y_self ? tp_gen(p.ll, p.ll.gen_out) : 0u;
     // this warp's share of the L2 prefetch of a later launch's weights: now
     // when it has no copies of its own, else right after its last copy
     const int64_t wg = (int64_t)blockIdx.x * W + warp, nwg = (int64_t)gridDim.x * W;
@@ -385,7 +398,7 @@ __global__ void __launch_bounds__(dense_warps(NB) * 32, dense_min_blocks(NB)) q4
         prefetch_share(p.pf_ptr, p.pf_bytes, wg, nwg, lane);
         prefetched = true;
     }
-    stage_activations<FOLD, SRC, W>(p, act, s_ssq, threadIdx.x, gpre, [&]() {
+    stage_activations<FOLD, SRC, W>(p, act, s_ssq, threadIdx.x, gpre, gen_in, [&]() {
         while (issued < ring_fill) issue_next();
     });
     __syncthreads();
@@ -459,15 +472,18 @@ BH_UNROLL(BH_KB_UNROLL)
                 if (live && t == 0 && rgrp < R / 2) {
                     const int64_t i = (r_begin + (int64_t)(warp + j * W) * R) / 2 + rgrp;
                     const float a = __fmul_rn(silu_ggml(v), u);  // ggml_silu then ggml_mul
-                    p.y[(int64_t)b * p.ldy + i] = a;
-                    for (int q = 0; q < p.tp_out.npeer; ++q) p.tp_out.peer_y[q][(int64_t)b * p.ldy + i] = a;
+                    if (p.ll.y_self)
+                        tp_store(p.ll, (int64_t)b * p.ldy + i, a, gen_out);
+                    else
+                        p.y[(int64_t)b * p.ldy + i] = a;
                     if (p.capture) {  // the gate and up rows before the SwiGLU
                         p.capture[(int64_t)b * 2 * p.ldy + i] = v;
                         p.capture[(int64_t)b * 2 * p.ldy + p.ldy + i] = u;
                     }
                 }
             } else {
-                finish_row<FOLD, EPI, TPR>(p, acc[b], accm[b], rgrp, t, b, live, r_begin + rin, best_v[b], best_i[b]);
+                finish_row<FOLD, EPI, TPR>(p, acc[b], accm[b], rgrp, t, b, live, r_begin + rin, best_v[b], best_i[b],
+                                           gen_out);
             }
         }
     }
@@ -507,7 +523,6 @@ BH_UNROLL(BH_KB_UNROLL)
             __syncthreads();
         }
     }
-    if (p.tp_out.npeer) tp_signal(p.tp_out);
 }
 
 // ---------------------------------------------------------------------------

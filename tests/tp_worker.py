@@ -44,8 +44,9 @@ def run(bh, ctx, rank, world, comm, cfg_kw, steps, seed, fails):
             break
         if int(tok1.item()) != int(tok2.item()):
             fails.append(f"{cfg_kw} step {s}: token {tok2.item()} vs one GPU {tok1.item()}")
-        if not torch.equal(h_one.view(torch.int32), h_tp.view(torch.int32)):
-            d = (h_one - h_tp).abs().max().item()
+        h_vals = h_tp.reshape(-1)[0::2]  # (value, generation) pairs on a split
+        if not torch.equal(h_one.reshape(-1).view(torch.int32), h_vals.contiguous().view(torch.int32)):
+            d = (h_one.reshape(-1) - h_vals).abs().max().item()
             fails.append(f"{cfg_kw} step {s}: hidden differs (max {d})")
     # this rank's K cache rows equal the one-GPU cache's columns of its KV heads
     kv0, kvn = info["kv_heads"]
