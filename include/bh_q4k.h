@@ -64,6 +64,8 @@ const char *bh_strerror(int code);
  * 73-76: one context per engine, created at init, freed at shutdown). */
 int bh_init(int device, bh_ctx **out);
 int bh_free(bh_ctx *ctx);
+/* The CUDA device ordinal of a context (or BH_EINVAL). */
+int bh_ctx_device(bh_ctx *ctx);
 /* Synchronize the context's device and report (and optionally clear) the
  * device-side status word that kernels set when a bounded wait runs out:
  * 0, or BH_ETIMEDOUT / BH_EINVAL. A routed-expert launch whose grid-barrier
@@ -440,6 +442,12 @@ int bh_q4k_moe_ep(bh_ctx *ctx, const float *cur, int n_tok, const int32_t *selec
  * the result is added to out instead. */
 int bh_moe_combine(bh_ctx *ctx, const float *dout, const float *weights, int n_tok, int k, int n_embd, float *out,
                    int residual, void *stream);
+/* bh_moe_combine over two expert-parallel shares computed on one device
+ * (BURN_MOE's pivot split: bh_q4k_moe_ep on the experts [0, pivot) bank into
+ * dout_a and on the [pivot, n_expert) bank into dout_b): each pair's row is
+ * dout_a + dout_b, exact since one of them is -0.0. */
+int bh_moe_combine_split(bh_ctx *ctx, const float *dout_a, const float *dout_b, const float *weights, int n_tok,
+                         int k, int n_embd, float *out, int residual, void *stream);
 
 /* The MoE layer stack of the 30B-A3B shape: per layer h += moe(RMSNorm(h) *
  * ffn_norm) with router logits seeded N(0, 1) per (layer, token), expert

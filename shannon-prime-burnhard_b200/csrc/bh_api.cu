@@ -288,6 +288,8 @@ int bh_tune(bh_ctx* ctx, int key, int value) {
     }
 }
 
+int bh_ctx_device(bh_ctx* ctx) { return ctx ? ctx->device : BH_EINVAL; }
+
 int bh_device_status(bh_ctx* ctx, int clear) {
     if (!ctx) return BH_EINVAL;
     DeviceGuard g(ctx->device);

@@ -243,9 +243,10 @@ int moe_plan(MoeParams& p, int smem_cap, int stage_target);
 int launch_moe(const MoeParams& p, int fold, const LaunchOpts& o);
 // Routing alone (one CTA): logits -> ids_out / w_out.
 int launch_moe_route(const MoeParams& p, const LaunchOpts& o);
-// out[t][i] (+)= (float) sum_s (double)(dout[t*k+s][i] * w[t][s])
+// out[t][i] (+)= (float) sum_s (double)(dout[t*k+s][i] * w[t][s]); with dout2
+// the pair rows are dout + dout2 (disjoint owners, -0.0 elsewhere)
 int launch_moe_combine(const float* dout, const float* w, int B, int k, int n_embd, float* out, bool residual,
-                       const LaunchOpts& o);
+                       const LaunchOpts& o, const float* dout2 = nullptr);
 int encode_q4k_map(CUtensorMap* map, const void* base, int64_t rows, int nb, int row_stride, int box_rows);
 int encode_q4k_pair_map(CUtensorMap* map, const void* gate, int64_t rows, int nb, int64_t dist, int row_stride,
                         int box_rows);

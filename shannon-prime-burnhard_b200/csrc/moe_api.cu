@@ -229,6 +229,19 @@ int bh_moe_combine(bh_ctx* ctx, const float* dout, const float* weights, int n_t
     return bh::launch_moe_combine(dout, weights, n_tok, k, n_embd, out, residual != 0, o);
 }
 
+int bh_moe_combine_split(bh_ctx* ctx, const float* dout_a, const float* dout_b, const float* weights, int n_tok, int k,
+                         int n_embd, float* out, int residual, void* stream) {
+    if (!ctx || !dout_a || !dout_b || !weights || !out || n_tok < 1 || n_tok > bh::MOE_MAX_TOK || k < 1 ||
+        k > bh::MOE_MAX_K || n_embd < 1)
+        return BH_EINVAL;
+    if (!aligned(dout_a, 4) || !aligned(dout_b, 4) || !aligned(weights, 4) || !aligned(out, 4)) return BH_EINVAL;
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return BH_ENODEV;
+    bh::LaunchOpts o;
+    o.stream = static_cast<cudaStream_t>(stream);
+    return bh::launch_moe_combine(dout_a, weights, n_tok, k, n_embd, out, residual != 0, o, dout_b);
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------

@@ -711,8 +711,11 @@ __global__ void __launch_bounds__(MV_THREADS, 1) moe_route_kernel(const __grid_c
     }
 }
 
-__global__ void __launch_bounds__(256) moe_combine_kernel(const float* __restrict__ dout, const float* __restrict__ w,
-                                                          int B, int k, int n_embd, float* out, int residual) {
+// (dout2, when set: a pair's row is dout + dout2, one of them holding the
+// expert output and the other -0.0, which makes the sum that value exactly)
+__global__ void __launch_bounds__(256) moe_combine_kernel(const float* __restrict__ dout, const float* __restrict__ dout2,
+                                                          const float* __restrict__ w, int B, int k, int n_embd,
+                                                          float* out, int residual) {
     pdl_wait();
     pdl_trigger();
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;
@@ -720,8 +723,11 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const float* __restric
     const int t = idx / n_embd, i = idx - t * n_embd;
     // ggml_mul (fp32 product) then ggml_sum_rows over the slots (double, in order)
     double a = 0.0;
-    for (int s = 0; s < k; ++s)
-        a = __dadd_rn(a, (double)__fmul_rn(__ldcg(dout + ((int64_t)t * k + s) * n_embd + i), __ldcg(w + t * k + s)));
+    for (int s = 0; s < k; ++s) {
+        const int64_t o = ((int64_t)t * k + s) * n_embd + i;
+        const float e = dout2 ? __fadd_rn(__ldcg(dout + o), __ldcg(dout2 + o)) : __ldcg(dout + o);
+        a = __dadd_rn(a, (double)__fmul_rn(e, __ldcg(w + t * k + s)));
+    }
     const float r = __double2float_rn(a);
     out[idx] = residual ? __fadd_rn(out[idx], r) : r;
 }
@@ -833,7 +839,7 @@ int launch_moe(const MoeParams& pin, int fold, const LaunchOpts& o) {
 }
 
 int launch_moe_combine(const float* dout, const float* w, int B, int k, int n_embd, float* out, bool residual,
-                       const LaunchOpts& o) {
+                       const LaunchOpts& o, const float* dout2) {
     const int n = B * n_embd;
     if (n < 1 || k < 1 || !dout || !w || !out) return BH_EINVAL;
     cudaLaunchConfig_t cfg = {};
@@ -845,7 +851,8 @@ int launch_moe_combine(const float* dout, const float* w, int B, int k, int n_em
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = o.pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, moe_combine_kernel, dout, w, B, k, n_embd, out, residual ? 1 : 0) == cudaSuccess
+    return cudaLaunchKernelEx(&cfg, moe_combine_kernel, dout, dout2, w, B, k, n_embd, out, residual ? 1 : 0) ==
+                   cudaSuccess
                ? BH_OK
                : BH_EIO;
 }
