@@ -199,6 +199,7 @@ __device__ __forceinline__ void load_kv_tile(float* s_kt, float* s_vt, const flo
     if (want_v) issue_kv_rows(s_vt, vbase, row_stride, t0, nh, bar_v, w, lane, pol);
 }
 
+template <bool LL>
 __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParams a) {
     extern __shared__ __align__(128) float smem_f[];
     float* s_kt = smem_f;                              // [ATTN_TILE][ATTN_KROW] K rows of the current tile
@@ -247,7 +248,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParam
     pdl_trigger();
     pdl_wait();
     ATTN_TRACE_AT(5);
-    const uint32_t gen_out = a.ll.y_self ? tp_gen(a.ll, a.ll.gen_out) : 0u;
+    const uint32_t gen_out = LL ? tp_gen(a.ll, a.ll.gen_out) : 0u;
 
     // this head's q, the group's k and v of this token: norm, rotation
     if (w == 0) {
@@ -431,7 +432,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParam
         }
     }
     if (d < HD) {
-        if (a.ll.y_self)
+        if (LL)
             tp_store(a.ll, (int64_t)h * HD + d, sumf, gen_out);
         else
             a.out[(int64_t)h * HD + d] = sumf;
@@ -637,16 +638,18 @@ int launch_attn(bh_stack* st, int l, bool pdl) {
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl ? 1 : 0;
-    static std::atomic<uint64_t> attr_devices{0};
+    // (the row split's variant stores the output as exchanged pairs)
+    auto kern = a.ll.y_self ? bh::attn_head_kernel<true> : bh::attn_head_kernel<false>;
+    static std::atomic<uint64_t> attr_devices[2];
     // the same shared-memory carveout as the matvecs around it
-    if (!bh::attrs_on_device(attr_devices, [] {
-            return cudaFuncSetAttribute(bh::attn_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        200 * 1024) == cudaSuccess &&
-                   cudaFuncSetAttribute(bh::attn_head_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+    if (!bh::attrs_on_device(attr_devices[a.ll.y_self ? 1 : 0], [&] {
+            return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) ==
+                       cudaSuccess &&
+                   cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                                         cudaSharedmemCarveoutMaxShared) == cudaSuccess;
         }))
         return BH_EIO;
-    return cudaLaunchKernelEx(&cfg, bh::attn_head_kernel, a) == cudaSuccess ? BH_OK : BH_EIO;
+    return cudaLaunchKernelEx(&cfg, kern, a) == cudaSuccess ? BH_OK : BH_EIO;
 }
 
 // Enqueue one decode step on st->stream (captured into the graph). On a row

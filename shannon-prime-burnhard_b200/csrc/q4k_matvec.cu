@@ -89,7 +89,7 @@ __device__ __forceinline__ void preload_gamma(const MatvecParams& p, float (&gp)
 
 // top_up(): called once by every warp after its first round of global loads
 // is issued (the warp's remaining weight copies go out behind them).
-template <int FOLD, int SRC, int W, class TopUp>
+template <int FOLD, int SRC, int W, bool LL, class TopUp>
 __device__ void stage_activations(const MatvecParams& p, uint8_t* act, double* red, int ctid,
                                   const float (&gp)[STAGE_UF][8], uint32_t gen_in, TopUp&& top_up) {
     const int warp = ctid >> 5, lane = ctid & 31;
@@ -196,9 +196,18 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, double* r
 #pragma unroll
             for (int t = 0; t < 8; ++t) { v[u][t] = 0.f; aux[u][t] = 0.f; }
             if (blk < nblk) {
-                if (p.ll.x) {
-                    // row split: the exchanged pairs of this generation
-                    if (!tp_load8(p.ll.x + (int64_t)b * p.K + e0, gen_in, v[u])) set_status(p.status, ST_TIMEOUT);
+                if constexpr (LL) {
+                    // row split: the exchanged pairs of this generation (LL
+                    // kernels read their fp32 input from p.xf only when
+                    // ll.x is null: the first layer's embedding)
+                    if (p.ll.x) {
+                        if (!tp_load8(p.ll.x + (int64_t)b * p.K + e0, gen_in, v[u])) set_status(p.status, ST_TIMEOUT);
+                    } else {
+                        const float* x = p.xf + (int64_t)b * p.K + e0;
+                        const float4 a0 = *reinterpret_cast<const float4*>(x), a1 = *reinterpret_cast<const float4*>(x + 4);
+                        v[u][0] = a0.x; v[u][1] = a0.y; v[u][2] = a0.z; v[u][3] = a0.w;
+                        v[u][4] = a1.x; v[u][5] = a1.y; v[u][6] = a1.z; v[u][7] = a1.w;
+                    }
                 } else {
                     const float* x = p.xf + (int64_t)b * p.K + e0;
                     const float4 a0 = *reinterpret_cast<const float4*>(x), a1 = *reinterpret_cast<const float4*>(x + 4);
@@ -279,14 +288,14 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, double* r
 }
 
 // Per-row epilogue of the dense kernel.
-template <int FOLD, int EPI, int TPR>
+template <int FOLD, int EPI, int TPR, bool LL>
 __device__ __forceinline__ void finish_row(const MatvecParams& p, const float (&acc)[RowBlk<TPR>::L], float accm, int rgrp,
                                            int t, int b, bool has_row, int64_t row, float& best_v, int& best_i,
                                            uint32_t gen_out) {
     const float v = row_value<FOLD, TPR>(acc, accm, rgrp);
     if (has_row && t == 0) {
         const int64_t yi = (int64_t)b * p.ldy + row;
-        if (p.ll.y_self && EPI != EPI_ARGMAX) {
+        if (LL && p.ll.y_self && EPI != EPI_ARGMAX) {
             // row split: the pair into every rank's copy (the residual is
             // this rank's own row of the previous generation)
             const float hv = EPI == EPI_ADD ? __fadd_rn(__uint_as_float((uint32_t)p.ll.y_self[yi]), v) : v;
@@ -314,7 +323,7 @@ __device__ __forceinline__ void finish_row(const MatvecParams& p, const float (&
 // on the stage's mbarrier; the warp both fills and drains its ring (no
 // cross-warp handshake). Thread (r, t) works row r of the tile; its fp32
 // fold runs in registers as the blocks stream by.
-template <int FOLD, int NB, int SRC, int EPI, bool PART, int TPR>
+template <int FOLD, int NB, int SRC, int EPI, bool PART, int TPR, bool LL>
 __global__ void __launch_bounds__(dense_warps(NB) * 32, dense_min_blocks(NB)) q4k_matvec_kernel(const __grid_constant__ MatvecParams p) {
     constexpr int W = dense_warps(NB);
     constexpr int R = 32 / TPR;
@@ -388,8 +397,8 @@ __global__ void __launch_bounds__(dense_warps(NB) * 32, dense_min_blocks(NB)) q4
     BH_TRACE_AT(5);
     // row split: generations of the exchanged input and output (the step
     // counter is final once the previous kernel has completed)
-    const uint32_t gen_in = p.ll.x ? tp_gen(p.ll, p.ll.gen_in) : 0u;
-    const uint32_t gen_out = p.ll.y_self ? tp_gen(p.ll, p.ll.gen_out) : 0u;
+    const uint32_t gen_in = LL && p.ll.x ? tp_gen(p.ll, p.ll.gen_in) : 0u;
+    const uint32_t gen_out = LL && p.ll.y_self ? tp_gen(p.ll, p.ll.gen_out) : 0u;
     // this warp's share of the L2 prefetch of a later launch's weights: now
     // when it has no copies of its own, else right after its last copy
     const int64_t wg = (int64_t)blockIdx.x * W + warp, nwg = (int64_t)gridDim.x * W;
@@ -398,7 +407,7 @@ __global__ void __launch_bounds__(dense_warps(NB) * 32, dense_min_blocks(NB)) q4
         prefetch_share(p.pf_ptr, p.pf_bytes, wg, nwg, lane);
         prefetched = true;
     }
-    stage_activations<FOLD, SRC, W>(p, act, s_ssq, threadIdx.x, gpre, gen_in, [&]() {
+    stage_activations<FOLD, SRC, W, LL>(p, act, s_ssq, threadIdx.x, gpre, gen_in, [&]() {
         while (issued < ring_fill) issue_next();
     });
     __syncthreads();
@@ -472,7 +481,7 @@ BH_UNROLL(BH_KB_UNROLL)
                 if (live && t == 0 && rgrp < R / 2) {
                     const int64_t i = (r_begin + (int64_t)(warp + j * W) * R) / 2 + rgrp;
                     const float a = __fmul_rn(silu_ggml(v), u);  // ggml_silu then ggml_mul
-                    if (p.ll.y_self)
+                    if (LL && p.ll.y_self)
                         tp_store(p.ll, (int64_t)b * p.ldy + i, a, gen_out);
                     else
                         p.y[(int64_t)b * p.ldy + i] = a;
@@ -482,7 +491,7 @@ BH_UNROLL(BH_KB_UNROLL)
                     }
                 }
             } else {
-                finish_row<FOLD, EPI, TPR>(p, acc[b], accm[b], rgrp, t, b, live, r_begin + rin, best_v[b], best_i[b],
+                finish_row<FOLD, EPI, TPR, LL>(p, acc[b], accm[b], rgrp, t, b, live, r_begin + rin, best_v[b], best_i[b],
                                            gen_out);
             }
         }
@@ -574,9 +583,9 @@ int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int t
     return BH_EINVAL;  // activations too large for shared memory
 }
 
-template <int FOLD, int NB, int SRC, int EPI, bool PART, int TPR>
+template <int FOLD, int NB, int SRC, int EPI, bool PART, int TPR, bool LL = false>
 static int launch_t(const MatvecParams& p, const LaunchOpts& o, int grid) {
-    auto kern = q4k_matvec_kernel<FOLD, NB, SRC, EPI, PART, TPR>;
+    auto kern = q4k_matvec_kernel<FOLD, NB, SRC, EPI, PART, TPR, LL>;
     static std::atomic<uint64_t> attr_devices{0};
     // all kernels of a step ask for the same (largest) shared-memory
     // carveout, so consecutive launches can share an SM without the SM
@@ -631,6 +640,27 @@ static int launch_nb(const MatvecParams& p, const LaunchOpts& o, int grid) {
         case 6: return launch_t<FOLD, 6, SRC, EPI, PART, 4>(p, o, grid);
         case 7: return launch_t<FOLD, 7, SRC, EPI, PART, 4>(p, o, grid);
         case 8: return launch_t<FOLD, 8, SRC, EPI, PART, 4>(p, o, grid);
+        default: return BH_EINVAL;
+    }
+}
+
+// Row-split launches (exchanged pairs in or out): batch 1, the x86 fold, no
+// partials; their own instantiations, so that one GPU's kernels carry none of
+// the pair code (measured: it cost the one-GPU step 1.667 -> 1.746 ms).
+template <int SRC, int EPI>
+static int launch_ll_tpr(const MatvecParams& p, const LaunchOpts& o, int grid) {
+    if (p.tpr == 8) return launch_t<BH_FOLD_X86, 1, SRC, EPI, false, 8, true>(p, o, grid);
+    if (p.tpr == 4) return launch_t<BH_FOLD_X86, 1, SRC, EPI, false, 4, true>(p, o, grid);
+    return BH_EINVAL;
+}
+
+static int launch_ll(const MatvecParams& p, int src, int epi, const LaunchOpts& o, int grid) {
+    if (p.B != 1 || p.partials) return BH_EINVAL;
+    switch (src * 4 + epi) {
+        case ACT_F32 * 4 + EPI_ADD: return launch_ll_tpr<ACT_F32, EPI_ADD>(p, o, grid);
+        case ACT_F32_RMSNORM * 4 + EPI_STORE: return launch_ll_tpr<ACT_F32_RMSNORM, EPI_STORE>(p, o, grid);
+        case ACT_F32_RMSNORM * 4 + EPI_SWIGLU: return launch_ll_tpr<ACT_F32_RMSNORM, EPI_SWIGLU>(p, o, grid);
+        case ACT_F32_RMSNORM * 4 + EPI_ARGMAX: return launch_ll_tpr<ACT_F32_RMSNORM, EPI_ARGMAX>(p, o, grid);
         default: return BH_EINVAL;
     }
 }
@@ -741,6 +771,7 @@ int launch_matvec(const MatvecParams& pin, int fold, int act_src, int epi, const
     const int rc = encode_maps(p, epi == EPI_SWIGLU);
     if (rc != BH_OK) return rc;
     const int grid = o.grid;
+    if (p.ll.x || p.ll.y_self) return fold == BH_FOLD_X86 ? launch_ll(p, act_src, epi, o, grid) : BH_EINVAL;
     if (fold == BH_FOLD_X86) return launch_fold<BH_FOLD_X86>(p, act_src, epi, o, grid);
     if (fold == BH_FOLD_GENERIC) return launch_fold<BH_FOLD_GENERIC>(p, act_src, epi, o, grid);
     return BH_EINVAL;
