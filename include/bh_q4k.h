@@ -353,6 +353,25 @@ int bh_stack_tp_info(bh_stack *st, int *rank, int *world, int64_t *row_ranges);
  * (fp32 value, generation) pairs, value in the low word (cols = 2 x n). */
 
 /* ------------------------------------------------------------------------
+ * The native engine's dense-matmul hook (forward_native.h:115-119,
+ * mm_dispatch_fn_t; called by weight_matmul, forward_native.cpp:102-118).
+ * The hook receives the fp16 copy of a weight, used here only as a key: the
+ * engine registers at bind time the device Q4_K bytes (N rows x K, the GGUF
+ * layout) of the same weight under that key. bh_mm_dispatch then computes
+ * out[m][n] = W_q4k[n] . lhs[m] for host lhs [M][K] / out [M][N] with lhs
+ * quantized to Q8_K and the x86 fold (ggml's own Q4_K matmul, bit for bit),
+ * M in chunks of 8. It returns non-zero for a key that was not registered
+ * or a shape that differs from the registration, and the engine falls
+ * through to its CPU matmul as without a hook. Pass bh_mm_dispatch as
+ * mm_dispatch and the registry as mm_dispatch_userdata.
+ * ------------------------------------------------------------------------ */
+typedef struct bh_mm_registry bh_mm_registry;
+int bh_mm_registry_create(bh_ctx *ctx, bh_mm_registry **out);
+int bh_mm_registry_add(bh_mm_registry *reg, const void *W_fp16_key, const void *W_q4k, int N, int K);
+int bh_mm_registry_free(bh_mm_registry *reg);
+int bh_mm_dispatch(void *userdata, const float *lhs, const uint16_t *W_fp16, int M, int K, int N, float *out);
+
+/* ------------------------------------------------------------------------
  * NCCL communicators from C (tp_comm.cu). A communicator is a void*
  * (ncclComm_t). Creation is non-blocking (ncclCommInitRankConfig with
  * blocking = 0) and every wait is polled against timeout_ms of wall clock

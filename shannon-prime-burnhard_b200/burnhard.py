@@ -152,6 +152,12 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.bh_stack_tp_connect.argtypes = [_vp, _vp]
     L.bh_stack_tp_info.argtypes = [_vp, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(_i64)]
     L.bh_stack_tp_connect_comm.argtypes = [_vp, _vp, C.c_int]
+    L.bh_mm_registry_create.argtypes = [_vp, C.POINTER(_vp)]
+    L.bh_mm_registry_add.argtypes = [_vp, _vp, _vp, C.c_int, C.c_int]
+    L.bh_mm_registry_free.argtypes = [_vp]
+    L.bh_mm_dispatch.argtypes = [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp]
+    L.bh_ctx_device.argtypes = [_vp]
+    L.bh_moe_combine_split.argtypes = [_vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp, C.c_int, _vp]
     L.bh_tp_unique_id.argtypes = [_vp]
     L.bh_tp_comm_init.argtypes = [C.c_int, _vp, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]
     L.bh_tp_comm_abort.argtypes = [_vp]
