@@ -238,6 +238,15 @@ def bench_batch_sweep(bh, ctx, peak: float) -> dict:
             by = wbytes + b * k * 4 + b * n * 4
             us = graph_us(lambda i, s: ctx.matvec_f32(ws[i], n, k, x, y=y, stream=s), ncopy)
             e = {"us": round(us, 2), "GBps": round(by / us / 1e3, 1), "frac_of_peak": round(by / us / 1e3 / peak, 4)}
+            # the same sequence with programmatic dependent launch: each matvec
+            # streams its (different) weights while the one before finishes
+            ctx.tune(bh.TUNE_PDL, 1)
+            try:
+                pus = graph_us(lambda i, s: ctx.matvec_f32(ws[i], n, k, x, y=y, stream=s), ncopy)
+            finally:
+                ctx.tune(bh.TUNE_PDL, 0)
+            e.update({"pdl_us": round(pus, 2), "pdl_GBps": round(by / pus / 1e3, 1),
+                      "pdl_frac_of_peak": round(by / pus / 1e3 / peak, 4)})
             if ref is not None:
                 xq = torch.empty(ref.xq_bytes(k, b), dtype=torch.uint8, device="cuda")
                 yr = torch.empty((b, n), device="cuda")

@@ -109,6 +109,14 @@ int bh_device_status(bh_ctx *ctx, int clear);
  * the L2, from each launch, this many MiB of the weights the step streams
  * next (0 = off, -1 = the stack's default, at most 120). */
 #define BH_TUNE_PREFETCH_MB 10
+/* BH_TUNE_PDL: 1 launches the context's matvecs (bh_q4k_matvec,
+ * bh_q4k_matvec_f32, bh_q4k_mul_mat_host, bh_q4k_lmhead_argmax) with the
+ * programmatic-dependent-launch attribute: a matvec that follows another
+ * kernel on the stream starts streaming its weights (and RMSNorm weights)
+ * before that kernel ends, and reads its activations and writes its output
+ * only after it. Only for sequences in which the kernel just before does not
+ * write those weights. 0 (default): plain launches. */
+#define BH_TUNE_PDL 11
 int bh_tune(bh_ctx *ctx, int key, int value);
 
 /* fp32 activations [B][K] -> B columns of Q8_K, byte-identical to

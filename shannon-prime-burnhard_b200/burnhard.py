@@ -33,6 +33,7 @@ TUNE_SMALL_ACT = 7
 TUNE_PREFILL = 8
 TUNE_BARRIER_WAIT = 9
 TUNE_PREFETCH_MB = 10
+TUNE_PDL = 11
 BH_EIO = -5
 BH_ENOMEM = -12
 BH_ENODEV = -19

@@ -170,7 +170,7 @@ using bh::plan_for;
 using bh::ACT_BLOCK_BYTES;
 using bh::MV_ROWS;
 inline int run_matvec(bh_ctx* ctx, bh::MatvecParams& p, int fold, int src, int epi, cudaStream_t s) {
-    return bh::run_matvec(ctx, p, fold, src, epi, s, false);
+    return bh::run_matvec(ctx, p, fold, src, epi, s, ctx->api_pdl);
 }
 }  // namespace
 
@@ -262,6 +262,10 @@ int bh_tune(bh_ctx* ctx, int key, int value) {
         case BH_TUNE_SMEM_CAP:
             if (value < 32 * 1024 || value > 200 * 1024) return BH_EINVAL;
             ctx->smem_cap_small = value;
+            return BH_OK;
+        case BH_TUNE_PDL:
+            if (value != 0 && value != 1) return BH_EINVAL;
+            ctx->api_pdl = value != 0;
             return BH_OK;
         case BH_TUNE_PREFILL:
             if (value < -1 || value > 8) return BH_EINVAL;
@@ -380,6 +384,7 @@ int bh_q4k_lmhead_argmax(bh_ctx* ctx, const void* W_q4k, int64_t N, int64_t K, c
     bh::LaunchOpts o;
     o.stream = s;
     o.grid = grid;
+    o.pdl = ctx->api_pdl;
     if ((rc = bh::launch_matvec(p, fold, bh::ACT_F32, bh::EPI_ARGMAX, o)) != BH_OK) return rc;
     return bh::launch_argmax_finish(ctx->cand_val, ctx->cand_idx, grid, B, tok_out, max_opt, s, false);
 }

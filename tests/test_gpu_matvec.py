@@ -260,3 +260,33 @@ def torch_zeros_int(shape):
     import torch
 
     return torch.zeros(shape, dtype=torch.int32, device="cuda")
+
+
+def test_pdl_sequence_bit_exact(ctx, bh, oracle):
+    """Back-to-back matvecs launched with programmatic dependent launch
+    (BH_TUNE_PDL): each result equals the plain launch's bits, including
+    launches whose input is computed from the output of the one before."""
+    import torch
+
+    n, k = 4096, 4096
+    w = oracle.normal((n, k), 4242, 0.0, 0.02)
+    wq = dev(oracle.quantize_q4k(w))
+    x = dev(oracle.normal((1, k), 4343, 0.0, 1.0))
+    want = [host(ctx.matvec_f32(wq, n, k, x))]
+    for i in range(3):
+        want.append(host(ctx.matvec_f32(wq, n, k, dev(want[-1] * np.float32(0.05)))))
+    ys = [torch.empty((1, n), device="cuda") for _ in range(4)]
+    xs = [torch.empty((1, n), device="cuda") for _ in range(3)]
+    ctx.tune(bh.TUNE_PDL, 1)
+    try:
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            ctx.matvec_f32(wq, n, k, x, y=ys[0], stream=s)
+            for i in range(3):
+                torch.mul(ys[i], 0.05, out=xs[i])
+                ctx.matvec_f32(wq, n, k, xs[i], y=ys[i + 1], stream=s)
+        s.synchronize()
+    finally:
+        ctx.tune(bh.TUNE_PDL, 0)
+    for i in range(4):
+        assert_bits_equal(host(ys[i]), want[i], f"pdl step {i}")
