@@ -50,4 +50,15 @@ __device__ __forceinline__ float silu_ggml(float x) {
     return __fdiv_rn(x, __fadd_rn(1.f, exp_ggml(__fsub_rn(0.f, x))));
 }
 
+// sum / n in double, as rms_norm_f32's mean: when n is a power of two the
+// quotient is an exact scaling, so a multiply by 2^-log2(n) gives the same
+// bits without the division's latency.
+__device__ __forceinline__ double div_by_count(double sum, int n) {
+    if ((n & (n - 1)) == 0) {
+        const int sh = __ffs(n) - 1;
+        return __dmul_rn(sum, __longlong_as_double((long long)(1023 - sh) << 52));
+    }
+    return __ddiv_rn(sum, (double)n);
+}
+
 }  // namespace bh

@@ -161,7 +161,7 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, double* r
     __shared__ float s_scale[BH_MAX_BATCH];
     const bool one_round = nblk <= W * UF;
     auto rms_scale = [&](double sum) {
-        const float mean = __double2float_rn(__ddiv_rn(sum, (double)p.K));
+        const float mean = __double2float_rn(div_by_count(sum, p.K));
         return __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
     };
     if (SRC == ACT_F32_RMSNORM && !one_round) {

@@ -261,7 +261,7 @@ __device__ void stage_tokens(const MoeParams& p, const float* gamma, uint8_t* ac
         if (threadIdx.x < p.B) {
             double ss = 0.0;
             for (int i = 0; i < nb; ++i) ss = __dadd_rn(ss, s_bss[threadIdx.x * nb + i]);
-            const float mean = __double2float_rn(__ddiv_rn(ss, (double)K));
+            const float mean = __double2float_rn(div_by_count(ss, K));
             s_scale[threadIdx.x] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
         }
         __syncthreads();
