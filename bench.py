@@ -485,6 +485,10 @@ def main() -> None:
             for _ in range(warmup):
                 stk.decode(x_dev, tok, stream)
             stream.synchronize()
+            # a broken exchange (a bounded wait that ran out on any rank) ends
+            # the run on every rank before the timed region
+            if max_over_ranks(float(ctx.status(clear=False) != 0), world) > 0:
+                raise RuntimeError("device status set during warm-up (a bounded wait ran out)")
             time.sleep(0.3)
             barrier(world)
             torch.cuda.synchronize()

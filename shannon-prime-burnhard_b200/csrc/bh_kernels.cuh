@@ -90,8 +90,11 @@ __device__ __forceinline__ void ld_pairs2(const uint64_t* p, uint64_t& a, uint64
 }
 
 // Eight consecutive values (16-byte aligned pairs) once all carry generation
-// gen; false when the bound ran out (the values are then whatever was read).
-__device__ __forceinline__ bool tp_load8(const uint64_t* src, uint32_t gen, float (&v)[8]) {
+// gen; false when the bound ran out, or when the status word already holds
+// an error (an earlier wait of the stack ran out: the exchange is broken and
+// later waits give up at once instead of each spending the bound); the
+// values are then whatever was read.
+__device__ __forceinline__ bool tp_load8(const uint64_t* src, uint32_t gen, float (&v)[8], const int* status) {
     uint64_t w[8];
 #pragma unroll
     for (int k = 0; k < 4; ++k) ld_pairs2(src + 2 * k, w[2 * k], w[2 * k + 1]);
@@ -99,14 +102,15 @@ __device__ __forceinline__ bool tp_load8(const uint64_t* src, uint32_t gen, floa
     long long t0 = 0;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-        if ((uint32_t)(w[k] >> 32) != gen) {
+        if (ok && (uint32_t)(w[k] >> 32) != gen) {
             if (t0 == 0) t0 = clock64();
-            for (;;) {
+            for (uint32_t n = 1;; ++n) {
                 uint64_t a, b;
                 ld_pairs2(src + (k & ~1), a, b);
                 w[k] = (k & 1) ? b : a;
                 if ((uint32_t)(w[k] >> 32) == gen) break;
-                if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+                if ((n & 63u) == 0 &&
+                    (clock64() - t0 > WAIT_LIMIT_CYCLES || (status && *reinterpret_cast<const volatile int*>(status)))) {
                     ok = false;
                     break;
                 }

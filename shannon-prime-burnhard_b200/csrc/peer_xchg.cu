@@ -105,7 +105,8 @@ __global__ void __launch_bounds__(256) xchg_argmax_kernel(const XchgParams a) {
     bool ok = true;
     for (int r = 0; r < a.world && ok; ++r) {
         while (ld_acquire_sys(flags + r) != epoch) {
-            if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+            // (gives up at once when an earlier wait of the context ran out)
+            if (clock64() - t0 > WAIT_LIMIT_CYCLES || (a.epoch_dev && *reinterpret_cast<const volatile int*>(a.status))) {
                 ok = false;
                 set_status(a.status, ST_TIMEOUT);
                 break;

@@ -201,7 +201,8 @@ __device__ void stage_activations(const MatvecParams& p, uint8_t* act, double* r
                     // kernels read their fp32 input from p.xf only when
                     // ll.x is null: the first layer's embedding)
                     if (p.ll.x) {
-                        if (!tp_load8(p.ll.x + (int64_t)b * p.K + e0, gen_in, v[u])) set_status(p.status, ST_TIMEOUT);
+                        if (!tp_load8(p.ll.x + (int64_t)b * p.K + e0, gen_in, v[u], p.status))
+                            set_status(p.status, ST_TIMEOUT);
                     } else {
                         const float* x = p.xf + (int64_t)b * p.K + e0;
                         const float4 a0 = *reinterpret_cast<const float4*>(x), a1 = *reinterpret_cast<const float4*>(x + 4);

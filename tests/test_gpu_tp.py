@@ -66,3 +66,59 @@ def test_row_split_stack_matches_one_gpu():
     assert r.returncode == 0, out[-4000:]
     for q in range(world):
         assert f"rank {q} TP OK" in out, out[-4000:]
+
+
+_HOLDER = r"""
+import sys
+sys.path.insert(0, %r)
+import burnhard as bh
+ctx = bh.Context(0)
+cfg = bh.default_stack_config(n_layer=2, n_embd=1024, n_head=16, n_head_kv=8, n_ff=2048, n_vocab=5000)
+st = bh.Stack(ctx, cfg, 11, rank=1, world=2)
+print(st.tp_handle().hex(), flush=True)
+sys.stdin.readline()      # holds its exchange region until told; launches no kernel that waits
+st.close()
+"""
+
+
+def test_row_split_wait_runs_out_when_a_peer_never_decodes(bh, ctx):
+    """Rank 0 of a two-rank split decodes while rank 1 (another process on
+    the same GPU) only holds its exchange region and never decodes: the pairs
+    rank 0 waits for never arrive, its bounded waits run out (the first after
+    about a second, the rest at once since the status already holds the
+    error), the step ends, the token is -1 and bh_device_status reports
+    BH_ETIMEDOUT; the context stays usable."""
+    import time
+
+    import numpy as np
+    import torch
+
+    holder = subprocess.Popen([sys.executable, "-c", _HOLDER % os.path.join(ROOT, "shannon-prime-burnhard_b200")],
+                              stdin=subprocess.PIPE, stdout=subprocess.PIPE, text=True)
+    try:
+        peer = bytes.fromhex(holder.stdout.readline().strip())
+        cfg = bh.default_stack_config(n_layer=2, n_embd=1024, n_head=16, n_head_kv=8, n_ff=2048, n_vocab=5000)
+        st = bh.Stack(ctx, cfg, 11, rank=0, world=2)
+        st.tp_connect([st.tp_handle(), peer])
+        st.fill_kv(5, 13)
+        st.set_pos(5)
+        x = torch.from_numpy(np.random.default_rng(3).standard_normal(1024).astype(np.float32)).cuda()
+        tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+        ctx.status()
+        t0 = time.monotonic()
+        st.decode(x, tok)
+        torch.cuda.synchronize()
+        dt = time.monotonic() - t0
+        assert ctx.status() == bh.BH_ETIMEDOUT
+        assert int(tok.item()) == -1
+        assert dt < 30, dt
+        st.close()
+        # the context still works
+        y = ctx.matvec_f32(ctx.q4k_quantize(torch.randn((256, 256), device="cuda") * 0.02), 256, 256,
+                           torch.randn((1, 256), device="cuda"))
+        torch.cuda.synchronize()
+        assert torch.isfinite(y).all() and ctx.status() == 0
+    finally:
+        holder.stdin.write("done\n")
+        holder.stdin.flush()
+        holder.wait(timeout=60)
