@@ -69,8 +69,11 @@ namespace bh {
 // launch.
 //  - Batch 1-2 (16-warp CTAs, whose registers fill an SM): one CTA per SM.
 //    Matrices with fewer than 32 eight-row tiles per CTA (everything but the
-//    LM-head-sized ones) run 8 threads per row, i.e. 4-row tiles: twice the
-//    working warps, each with half the arithmetic per block. (16 threads per
+//    LM-head-sized ones) run ctx->tpr_narrow threads per row: 4 for
+//    standalone launches (measured on B200 with back-to-back launches:
+//    12288x4096 10.4 against 12.5 us at 8, 4096x4096 6.45 against 6.77 us),
+//    8 in the decode stack's plan, where twice the working warps, each with
+//    half the arithmetic per block, measured faster inside the step. (16 threads per
 //    row, 2-row tiles, is available through BH_TUNE_TPR: for the 4096-row
 //    matrices of the decode step it puts 14 of 16 warps to work instead of 7,
 //    but measured slower there, 1.76 against 1.68 ms per token.)
@@ -91,7 +94,7 @@ int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override, int fold) {
         grid = ctx->num_sms;
         cap = 200 * 1024;
         const int64_t tiles8 = ((p.N + MV_ROWS - 1) / MV_ROWS + grid - 1) / grid;
-        if (tiles8 < 2 * W) tpr = 8;
+        if (tiles8 < 2 * W) tpr = ctx->tpr_narrow;
     } else {
         const int64_t cps_grid = (int64_t)ctx->num_sms * ctx->ctas_per_sm;
         const int64_t tiles_wide = ((p.N + cps_grid - 1) / cps_grid + MV_ROWS - 1) / MV_ROWS;

@@ -33,6 +33,10 @@ struct bh_ctx {
     int smem_cap_small = 100 * 1024;
     int small_act_bytes = 24 * 1024;
     int tpr_force = 0;  // threads per matvec row: 0 = planner's choice, else 4, 8 or 16
+    // threads per row the planner takes at batch 1-2 for matrices with fewer
+    // than two 8-row tiles per warp (4 for standalone launches; the decode
+    // stack's plan sets 8)
+    int tpr_narrow = 4;
     bool api_pdl = false;  // the C-ABI matvecs launch with programmatic dependent launch
     int sm_budget = 0;  // shared memory one matvec launch may hold per SM (0 = no limit)
     int prefill_stages = 0;  // ring stages per warp a matvec issues before its programmatic wait (0 = all, -1 = none)
