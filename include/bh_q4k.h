@@ -79,15 +79,16 @@ int bh_device_status(bh_ctx *ctx, int clear);
  *   small (batch x K/256 x 304 bytes <= 24 KiB), 1..4 (default 2);
  * BH_TUNE_STAGE_BYTES: bytes of one row's slice in a weight pipeline stage
  *   (rounded down to whole 144-byte blocks, shrunk until 2 stages fit),
- *   144..65536 (default 576); BH_TUNE_SMEM_CAP: shared-memory budget of a matvec CTA
+ *   144..65536 (default 1440 for the dense matvecs, 576 for the routed
+ *   experts; the key sets both); BH_TUNE_SMEM_CAP: shared-memory budget of a matvec CTA
  *   whose staged activations are small, 32768..204800 (default 102400). */
 #define BH_TUNE_CTAS_PER_SM 1
 #define BH_TUNE_STAGE_BYTES 2
 #define BH_TUNE_SMEM_CAP 3
 /* BH_TUNE_TPR: threads working one matvec row, 0 = the planner's choice
- * (8 for narrow matrices at batch <= 2, else 4), or 4 / 8 / 16 to force it
- * (16: batch <= 2 with BH_FOLD_X86 and no partials, else 8); results are
- * identical either way. */
+ * (4; in the decode stack's plan 8 for the layer matrices), or 4 / 8 / 16
+ * to force it (8 and 16: batch <= 2; 16 also needs BH_FOLD_X86 and no
+ * partials, else 8); results are identical either way. */
 #define BH_TUNE_TPR 4
 /* BH_TUNE_SM_BUDGET: shared memory (bytes) one matvec launch may occupy per
  * SM, 0 = no limit (default) or 48 KiB..228 KiB; below the SM's capacity the
@@ -98,7 +99,7 @@ int bh_device_status(bh_ctx *ctx, int clear);
  * default 24 KiB) for which a matvec may run several CTAs per SM. */
 #define BH_TUNE_SMALL_ACT 7
 /* BH_TUNE_PREFILL: ring stages per warp a matvec issues before its
- * programmatic-launch wait, -1..8 (0, the default: the whole ring; -1: none);
+ * programmatic-launch wait, -1..8 (default 1; 0: the whole ring; -1: none);
  * the rest go out right after the activation loads that follow the wait. */
 #define BH_TUNE_PREFILL 8
 /* BH_TUNE_BARRIER_WAIT: log2 of the SM cycles a routed-expert grid barrier

@@ -257,6 +257,7 @@ int bh_tune(bh_ctx* ctx, int key, int value) {
         case BH_TUNE_STAGE_BYTES:
             if (value < bh::Q4K_BYTES || value > 65536) return BH_EINVAL;
             ctx->stage_bytes = value;
+            ctx->moe_stage_bytes = value;
             return BH_OK;
         case BH_TUNE_TPR:
             if (value != 0 && value != 4 && value != 8 && value != 16) return BH_EINVAL;

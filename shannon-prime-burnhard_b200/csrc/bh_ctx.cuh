@@ -29,7 +29,13 @@ struct bh_ctx {
     size_t scratch_bytes = 0;
     // launch-shape tuning (bh_tune)
     int ctas_per_sm = 2;
-    int stage_bytes = 576;
+    // bytes of one row's slice in a dense matvec stage, and in a routed-expert
+    // one (BH_TUNE_STAGE_BYTES sets both); measured on B200, back-to-back
+    // standalone launches: 1440 with one stage before the programmatic wait
+    // beat 576 with the whole ring before it at every shape and batch of
+    // configs 1 and 3 (4096x12288 batch 1: 11.0 against 13.6 us)
+    int stage_bytes = 1440;
+    int moe_stage_bytes = 576;
     int smem_cap_small = 100 * 1024;
     int small_act_bytes = 24 * 1024;
     int tpr_force = 0;  // threads per matvec row: 0 = planner's choice, else 4, 8 or 16
@@ -39,7 +45,7 @@ struct bh_ctx {
     int tpr_narrow = 4;
     bool api_pdl = false;  // the C-ABI matvecs launch with programmatic dependent launch
     int sm_budget = 0;  // shared memory one matvec launch may hold per SM (0 = no limit)
-    int prefill_stages = 0;  // ring stages per warp a matvec issues before its programmatic wait (0 = all, -1 = none)
+    int prefill_stages = 1;  // ring stages per warp a matvec issues before its programmatic wait (0 = all, -1 = none)
     // decode stacks: bytes of the weights after a launch's own that it
     // prefetches into the L2 (-1: the stack's default)
     int64_t prefetch_bytes = -1;

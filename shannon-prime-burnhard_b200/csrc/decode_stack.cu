@@ -906,7 +906,7 @@ int bh_stack_create_tp(bh_ctx* ctx, const bh_stack_config* cfg, uint64_t seed, i
         st->plan.sm_budget = 168 * 1024;
         st->plan.stage_bytes = 1440;
         st->plan.tpr_narrow = 8;
-        if (ctx->prefill_stages == 0) st->plan.prefill_stages = 1;
+        st->plan.prefill_stages = 1;
     }
     // L2 prefetch of the weights ahead measured no faster on B200 (16 MiB:
     // -2%; 48-96 MiB: +9% to +39% per token): off unless tuned

@@ -88,7 +88,7 @@ namespace bh {
 // slots that at batch 1 every warp's gate|up and down rows are in flight at
 // once.
 int run_moe(bh_ctx* ctx, MoeParams& p, int fold, cudaStream_t s, bool pdl) {
-    int rc = moe_plan(p, 200 * 1024, ctx->stage_bytes);
+    int rc = moe_plan(p, 200 * 1024, ctx->moe_stage_bytes);
     if (rc != BH_OK) return rc;
     LaunchOpts o;
     o.stream = s;

@@ -237,11 +237,11 @@ def test_threads_per_row_argmax(ctx, bh, oracle, tpr, n, k, b):
         ctx.tune(bh.TUNE_TPR, 0)
 
 
-@pytest.mark.parametrize("prefill", [1, 2])
+@pytest.mark.parametrize("prefill", [0, 1, 2, -1])
 @pytest.mark.parametrize("n,k,b", [(4096, 4096, 1), (4096, 12288, 2), (33, 2048, 1), (12288, 4096, 4)])
 def test_split_prefill_bit_exact(ctx, bh, oracle, prefill, n, k, b):
-    """Issuing only part of each warp's ring before the programmatic wait (the
-    rest after the activation loads) gives the same bits."""
+    """Issuing all, part or none of each warp's ring before the programmatic
+    wait (the rest after the activation loads) gives the same bits."""
     w = oracle.normal((n, k), 7 + n + k, 0.0, 0.02)
     wq = oracle.quantize_q4k(w)
     x = oracle.normal((b, k), 5 + k, 0.0, 1.0)
@@ -253,7 +253,7 @@ def test_split_prefill_bit_exact(ctx, bh, oracle, prefill, n, k, b):
             assert_bits_equal(host(ctx.matvec(dev(wq), n, k, dev(xq), b, fold=fold)), want, f"q8k prefill{prefill}")
             assert_bits_equal(host(ctx.matvec_f32(dev(wq), n, k, dev(x), fold=fold)), want, f"f32 prefill{prefill}")
     finally:
-        ctx.tune(bh.TUNE_PREFILL, 0)
+        ctx.tune(bh.TUNE_PREFILL, 1)  # the default
 
 
 def torch_zeros_int(shape):
