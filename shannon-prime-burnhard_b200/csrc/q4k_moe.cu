@@ -237,11 +237,40 @@ __device__ __forceinline__ void moe_route(const MoeParams& p, const float* logit
     __syncthreads();
 }
 
+// The token values (and norm weights) of this warp's block, loaded before the
+// routing when every warp has at most one block (one token): their L2 round
+// trip then overlaps the router instead of following it.
+struct TokPre {
+    float v[8], g[8];
+    bool have;
+};
+
+__device__ __forceinline__ void preload_tokens(const MoeParams& p, const float* gamma, TokPre& t) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nb = p.n_embd / QK, nblk = p.B * nb;
+    t.have = nblk <= MV_WARPS;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { t.v[j] = 0.f; t.g[j] = 0.f; }
+    if (!t.have || warp >= nblk) return;
+    const int b = warp / nb, i = warp - b * nb;
+    const int e0 = i * QK + 8 * lane;
+    const float4* x = reinterpret_cast<const float4*>(p.h + (int64_t)b * p.n_embd + e0);
+    const float4 a0 = __ldcg(x), a1 = __ldcg(x + 1);
+    t.v[0] = a0.x; t.v[1] = a0.y; t.v[2] = a0.z; t.v[3] = a0.w;
+    t.v[4] = a1.x; t.v[5] = a1.y; t.v[6] = a1.z; t.v[7] = a1.w;
+    if (gamma) {
+        const uint64_t keep = policy_evict_last();
+        const float4 g0 = ldg_f4_keep(gamma + e0, keep), g1 = ldg_f4_keep(gamma + e0 + 4, keep);
+        t.g[0] = g0.x; t.g[1] = g0.y; t.g[2] = g0.z; t.g[3] = g0.w;
+        t.g[4] = g1.x; t.g[5] = g1.y; t.g[6] = g1.z; t.g[7] = g1.w;
+    }
+}
+
 // Gate|up prologue: the B input columns, RMSNorm'd when a weight is given
 // (ggml rms_norm: fp32 squares summed in double, mean = (float)(sum / n),
 // scale = 1 / sqrt(mean + eps), y = (x * scale) * gamma), quantized to Q8_K.
 template <int FOLD>
-__device__ void stage_tokens(const MoeParams& p, const float* gamma, uint8_t* act, float* s_scale) {
+__device__ void stage_tokens(const MoeParams& p, const float* gamma, uint8_t* act, float* s_scale, const TokPre& pre) {
     __shared__ double s_bss[MOE_MAX_TOK * MOE_MAX_EMBD_BLOCKS];  // per-block sums of squares
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int K = p.n_embd, nb = K / QK;
@@ -281,7 +310,15 @@ __device__ void stage_tokens(const MoeParams& p, const float* gamma, uint8_t* ac
             const int b = blk / nb, i = blk - b * nb;
             const int e0 = i * QK + 8 * lane;
             float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0, g0 = a0, g1 = a0;
-            if (blk < nblk) {
+            if (pre.have) {
+                // (one block per warp, loaded before the routing)
+                if (u == 0) {
+                    a0 = make_float4(pre.v[0], pre.v[1], pre.v[2], pre.v[3]);
+                    a1 = make_float4(pre.v[4], pre.v[5], pre.v[6], pre.v[7]);
+                    g0 = make_float4(pre.g[0], pre.g[1], pre.g[2], pre.g[3]);
+                    g1 = make_float4(pre.g[4], pre.g[5], pre.g[6], pre.g[7]);
+                }
+            } else if (blk < nblk) {
                 const float4* x = reinterpret_cast<const float4*>(p.h + (int64_t)b * K + e0);
                 a0 = __ldcg(x);
                 a1 = __ldcg(x + 1);
@@ -505,6 +542,9 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_moe_kernel(const __grid_con
 
     for (int l = 0; l < p.n_layer; ++l) {
         MOE_TRACE_AT(0);
+        const float* gamma_l = p.gamma ? p.gamma + l * p.gamma_ls : nullptr;
+        TokPre pre;
+        preload_tokens(p, gamma_l, pre);
         moe_route(p, p.logits ? p.logits + l * p.logits_ls : nullptr, tb, rs);
         MOE_TRACE_AT(1);
         if (tb.bad) {
@@ -578,7 +618,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_moe_kernel(const __grid_con
         for (int q = 0; q < min(2, ring_fill); ++q) issue_next();
         MOE_TRACE_AT(2);
 
-        stage_tokens<FOLD>(p, p.gamma ? p.gamma + l * p.gamma_ls : nullptr, act, s_scale);
+        stage_tokens<FOLD>(p, gamma_l, act, s_scale, pre);
         while (issued < ring_fill) issue_next();
         __syncthreads();
         MOE_TRACE_AT(3);
