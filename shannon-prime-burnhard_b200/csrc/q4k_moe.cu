@@ -615,7 +615,11 @@ __global__ void __launch_bounds__(MV_THREADS, 1) q4k_moe_kernel(const __grid_con
         // activations are staged (their loads then do not queue behind a full
         // ring of weight copies)
         const int ring_fill = min(p.stages, total);
-        for (int q = 0; q < min(2, ring_fill); ++q) issue_next();
+        MOE_TRACE_R(6);
+        for (int q = 0; q < min(2, ring_fill); ++q) {
+            issue_next();
+            if (q == 0) MOE_TRACE_R(7);
+        }
         MOE_TRACE_AT(2);
 
         stage_tokens<FOLD>(p, gamma_l, act, s_scale, pre);
