@@ -434,6 +434,37 @@ def run_reference_arm(args, cfg: dict, workload: dict) -> None:
 
 
 # ---------------------------------------------------------------- main
+def run_matvec_only(args) -> None:
+    """One standalone Q4_K matvec shape, launched args.steps times back to back
+    on one GPU (seeded weights, fp32 activations quantized in the prologue);
+    prints the mean device time per launch."""
+    import torch
+
+    import burnhard as bh
+
+    n, k, b = (int(v) for v in args.matvec.lower().split("x"))
+    ctx = bh.Context(0)
+    g = torch.Generator(device="cuda").manual_seed(SEED + 9)
+    w = ctx.q4k_quantize(torch.randn((n, k), generator=g, device="cuda") * 0.02)
+    x = torch.randn((b, k), generator=g, device="cuda")
+    y = torch.empty((b, n), device="cuda")
+    for _ in range(args.warmup):
+        ctx.matvec_f32(w, n, k, x, y=y)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        ctx.matvec_f32(w, n, k, x, y=y)
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    by = n * (k // 256) * 144 + b * k * 4 + b * n * 4
+    print(json.dumps({"matvec": [n, k, b], "us": round(us, 2), "GBps": round(by / us / 1e3, 1),
+                      "status": ctx.status()}), flush=True)
+    ctx.close()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -443,6 +474,9 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=0, help="override n_layer (testing only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the config 4 / config 5 measurements")
+    ap.add_argument("--matvec", default="", metavar="NxKxB",
+                    help="only run one standalone matvec shape (fp32 input, batch B) --steps times and print its "
+                         "time (a small case for a profiler)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -456,6 +490,9 @@ def main() -> None:
                 "l2": "no flush needed: 4.26 GB of weights streamed per step >> 126 MB L2",
                 "parallelism": (f"row-split tensor parallel x{world_env} (peer-memory exchange in the epilogues)"
                                 if world_env > 1 else "single GPU")}
+    if args.matvec:
+        run_matvec_only(args)
+        return
     if args.impl == "reference":
         run_reference_arm(args, cfg_d, workload)
         return
