@@ -86,9 +86,9 @@ int bh_device_status(bh_ctx *ctx, int clear);
 #define BH_TUNE_STAGE_BYTES 2
 #define BH_TUNE_SMEM_CAP 3
 /* BH_TUNE_TPR: threads working one matvec row, 0 = the planner's choice
- * (4; in the decode stack's plan 8 for the layer matrices), or 4 / 8 / 16
- * to force it (8 and 16: batch <= 2; 16 also needs BH_FOLD_X86 and no
- * partials, else 8); results are identical either way. */
+ * (4, and 8 for narrow matrices at batch 3-8; in the decode stack's plan 8
+ * for the layer matrices), or 4 / 8 / 16 to force it (16: batch <= 2 with
+ * BH_FOLD_X86 and no partials, else 8); results are identical either way. */
 #define BH_TUNE_TPR 4
 /* BH_TUNE_SM_BUDGET: shared memory (bytes) one matvec launch may occupy per
  * SM, 0 = no limit (default) or 48 KiB..228 KiB; below the SM's capacity the

@@ -77,9 +77,11 @@ namespace bh {
 //    row, 2-row tiles, is available through BH_TUNE_TPR: for the 4096-row
 //    matrices of the decode step it puts 14 of 16 warps to work instead of 7,
 //    but measured slower there, 1.76 against 1.68 ms per token.)
-//  - Larger batches (8-warp CTAs): wide matrices (at least one 8-row tile per
-//    warp with ctas_per_sm CTAs per SM) run that many CTAs per SM, each with
-//    smem_cap_small bytes; narrow ones one CTA per SM.
+//  - Larger batches: narrow matrices (fewer than 32 eight-row tiles per SM)
+//    run 16-warp CTAs at 8 threads per row, one per SM; the others 8-warp
+//    CTAs at 4 threads per row, wide ones (at least one 8-row tile per warp
+//    with ctas_per_sm CTAs per SM) that many CTAs per SM, each with
+//    smem_cap_small bytes.
 // A non-zero sm_budget caps the shared memory one launch holds per SM, so the
 // next programmatic launch finds room to start its weight copies early.
 int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override, int fold) {
@@ -95,6 +97,16 @@ int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override, int fold) {
         cap = 200 * 1024;
         const int64_t tiles8 = ((p.N + MV_ROWS - 1) / MV_ROWS + grid - 1) / grid;
         if (tiles8 < 2 * W) tpr = ctx->tpr_narrow;
+    } else if (ctx->tpr_force == 8 ||
+               (ctx->tpr_force == 0 &&
+                ((p.N + MV_ROWS - 1) / MV_ROWS + ctx->num_sms - 1) / ctx->num_sms < 2 * DENSE_MAX_WARPS)) {
+        // narrow matrices at batch 3-8: 16-warp CTAs, one per SM, 8 threads
+        // per row (measured on B200, back-to-back launches at batch 8:
+        // 4096x12288 42.5 against 53.2 us, 4096x4096 16.8 against 20.7 us
+        // with 8-warp CTAs at 4 threads per row)
+        grid = ctx->num_sms;
+        cap = 200 * 1024;
+        tpr = 8;
     } else {
         const int64_t cps_grid = (int64_t)ctx->num_sms * ctx->ctas_per_sm;
         const int64_t tiles_wide = ((p.N + cps_grid - 1) / cps_grid + MV_ROWS - 1) / MV_ROWS;
@@ -112,10 +124,10 @@ int plan_for(bh_ctx* ctx, MatvecParams& p, int grid_override, int fold) {
         const int per = grid > ctx->num_sms ? per_sm : 1;
         if (cap * per > ctx->sm_budget) cap = ctx->sm_budget / per;
     }
-    if (ctx->tpr_force) {
+    if (ctx->tpr_force && p.B <= 2) {
         tpr = 4;
-        if (ctx->tpr_force == 8 && p.B <= 2) tpr = 8;
-        if (ctx->tpr_force == 16 && p.B <= 2) tpr = (fold == BH_FOLD_X86 && !p.partials) ? 16 : 8;
+        if (ctx->tpr_force == 8) tpr = 8;
+        if (ctx->tpr_force == 16) tpr = (fold == BH_FOLD_X86 && !p.partials) ? 16 : 8;
     }
     const int64_t ntile = (p.N + 32 / tpr - 1) / (32 / tpr);  // CTAs own whole tiles
     if ((int64_t)grid > ntile) grid = (int)ntile;

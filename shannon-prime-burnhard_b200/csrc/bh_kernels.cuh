@@ -177,16 +177,21 @@ constexpr int MV_THREADS = MV_WARPS * 32;
 // Dense matvec: warps per CTA for a batch of B columns. Batch 1-2 runs one
 // CTA of 16 warps per SM (twice the warps to hide each warp's dependent
 // per-block chain; ~100 registers a thread); larger batches hold more
-// accumulators per thread and run 8-warp CTAs.
+// accumulators per thread and run 8-warp CTAs at 4 threads per row, or
+// 16-warp CTAs at 8 threads per row for narrow matrices.
 constexpr int DENSE_MAX_WARPS = 16;
 #ifndef BH_DENSE_W12
 #define BH_DENSE_W12 16
 #endif
-__host__ __device__ constexpr int dense_warps(int B) { return B <= 2 ? BH_DENSE_W12 : 8; }
+// At 8 or 16 threads per row a thread holds one reference lane, which leaves
+// room for 16 warps at any batch (narrow matrices at batch 3-8 run so).
+__host__ __device__ constexpr int dense_warps(int B, int tpr = 4) { return (B <= 2 || tpr >= 8) ? BH_DENSE_W12 : 8; }
 // CTAs per SM a dense matvec kernel is compiled for: 8-warp CTAs at batch 1-2
 // are kept within half the register file, so the next launch of a step can be
 // resident beside them (and start its weight copies) while they finish.
-__host__ __device__ constexpr int dense_min_blocks(int B) { return (B <= 2 && dense_warps(B) == 8) ? 2 : 1; }
+__host__ __device__ constexpr int dense_min_blocks(int B, int tpr = 4) {
+    return (B <= 2 && dense_warps(B, tpr) == 8) ? 2 : 1;
+}
 constexpr int MV_ROWS = 8;                  // largest tile (rows of one warp stage); segment boundaries align to it
 constexpr int ACT_BLOCK_BYTES = 304;   // staged Q8_K block: 272 (q8, lane-padded) + 16 (d) + 16 (S)
 

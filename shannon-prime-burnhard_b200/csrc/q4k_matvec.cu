@@ -1,7 +1,8 @@
 // q4k_matvec.cu — the sm_100a Q4_K x Q8_K matvec (batch 1..8).
 //
-// Structure (16 warps per CTA at batch 1-2, else 8; 1 or 2 CTAs per SM, each
-// CTA persistent over a contiguous range of rows):
+// Structure (16 warps per CTA at batch 1-2 and for narrow matrices at batch
+// 3-8, else 8; 1 or 2 CTAs per SM, each CTA persistent over a contiguous
+// range of rows):
 //  - every warp owns tiles of 32/TPR consecutive rows and streams them
 //    through its own ring of shared-memory stages: one 2-D tensor copy
 //    (cp.async.bulk.tensor, the TMA engine) per stage, issued by lane 0 and
@@ -325,8 +326,8 @@ __device__ __forceinline__ void finish_row(const MatvecParams& p, const float (&
 // cross-warp handshake). Thread (r, t) works row r of the tile; its fp32
 // fold runs in registers as the blocks stream by.
 template <int FOLD, int NB, int SRC, int EPI, bool PART, int TPR, bool LL>
-__global__ void __launch_bounds__(dense_warps(NB) * 32, dense_min_blocks(NB)) q4k_matvec_kernel(const __grid_constant__ MatvecParams p) {
-    constexpr int W = dense_warps(NB);
+__global__ void __launch_bounds__(dense_warps(NB, TPR) * 32, dense_min_blocks(NB, TPR)) q4k_matvec_kernel(const __grid_constant__ MatvecParams p) {
+    constexpr int W = dense_warps(NB, TPR);
     constexpr int R = 32 / TPR;
     constexpr int L = RowBlk<TPR>::L;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -547,7 +548,7 @@ BH_UNROLL(BH_KB_UNROLL)
 int matvec_plan(MatvecParams& p, int grid, int smem_cap, int stage_target, int tpr) {
     if (grid < 1 || (tpr != 4 && tpr != 8 && tpr != 16)) return BH_EINVAL;
     const int R = 32 / tpr;
-    const int W = dense_warps(p.B);
+    const int W = dense_warps(p.B, tpr);
     const int64_t tiles_cta = ((p.N + R - 1) / R + grid - 1) / grid;
     const int wbusy = tiles_cta < W ? (int)(tiles_cta > 0 ? tiles_cta : 1) : W;
     const int act_bytes = p.B * p.nb * ACT_BLOCK_BYTES;
@@ -600,7 +601,7 @@ static int launch_t(const MatvecParams& p, const LaunchOpts& o, int grid) {
         return BH_EIO;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(dense_warps(NB) * 32);
+    cfg.blockDim = dim3(dense_warps(NB, TPR) * 32);
     cfg.dynamicSmemBytes = (size_t)p.smem_bytes;
     cfg.stream = o.stream;
     cudaLaunchAttribute at[1];
@@ -625,10 +626,16 @@ static int launch_nb(const MatvecParams& p, const LaunchOpts& o, int grid) {
         return BH_EINVAL;
     }
     if (p.tpr == 8) {
-        // eight threads per row: narrow matrices, batch <= 2
+        // eight threads per row, 16-warp CTAs: narrow matrices
         switch (p.B) {
             case 1: return launch_t<FOLD, 1, SRC, EPI, PART, 8>(p, o, grid);
             case 2: return launch_t<FOLD, 2, SRC, EPI, PART, 8>(p, o, grid);
+            case 3: return launch_t<FOLD, 3, SRC, EPI, PART, 8>(p, o, grid);
+            case 4: return launch_t<FOLD, 4, SRC, EPI, PART, 8>(p, o, grid);
+            case 5: return launch_t<FOLD, 5, SRC, EPI, PART, 8>(p, o, grid);
+            case 6: return launch_t<FOLD, 6, SRC, EPI, PART, 8>(p, o, grid);
+            case 7: return launch_t<FOLD, 7, SRC, EPI, PART, 8>(p, o, grid);
+            case 8: return launch_t<FOLD, 8, SRC, EPI, PART, 8>(p, o, grid);
             default: return BH_EINVAL;
         }
     }

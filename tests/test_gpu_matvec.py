@@ -114,7 +114,7 @@ def seeded_q4k(ctx, oracle, n, k, seed, check_rows=48):
 
 
 @pytest.mark.parametrize("n,k", [(4096, 4096), (12288, 4096), (4096, 12288), (6144, 4096), (768, 2048), (2048, 768)])
-@pytest.mark.parametrize("b", [1, 2, 4, 8])
+@pytest.mark.parametrize("b", [1, 2, 3, 4, 8])
 def test_config_shapes_bit_exact(ctx, oracle, n, k, b):
     wq = seeded_q4k(ctx, oracle, n, k, seed=1000 + n + k)
     x = oracle.normal((b, k), 2000 + b, 0.0, 1.0)
