@@ -4,12 +4,13 @@ control path.
 - One GPU: a communicator of two ranks of which only rank 0 ever joins:
   bh_tp_comm_init returns BH_ETIMEDOUT within its limit (the non-blocking
   init is polled and then aborted) instead of hanging.
-- Two or more GPUs (tests/tp_worker.py under torchrun, one rank per GPU):
+- Two, four and eight GPUs, as many as there are (tests/tp_worker.py under
+  torchrun, one rank per GPU):
   the row-split stack at a small shape and at the full config-2 shape
   (36 layers, 4096 / 12288, 151936-row LM head) gives the one-GPU stack's
   tokens and hidden states bit for bit, step after step; the library's
-  all-gather and all-reduce over the same communicator. Skipped with fewer
-  than two GPUs."""
+  all-gather and all-reduce over the same communicator. A world size is
+  skipped when there are fewer GPUs than ranks."""
 from __future__ import annotations
 
 import os
@@ -50,13 +51,13 @@ def test_nccl_rank_that_never_joins_times_out():
     assert r.returncode == 0, (r.stdout + r.stderr)[-3000:]
 
 
-def test_row_split_stack_matches_one_gpu():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_row_split_stack_matches_one_gpu(world):
     import torch
 
     n = torch.cuda.device_count()
-    if n < 2:
-        pytest.skip("needs two GPUs")
-    world = 2
+    if n < world:
+        pytest.skip(f"needs {world} GPUs")
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes", "1",
            "--nproc-per-node", str(world), "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(HERE, "tp_worker.py")]
