@@ -220,18 +220,20 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParam
     const float* vbase = a.vc + (int64_t)g * HD;
     ATTN_TRACE_AT(0);
 
-    // before the wait, nothing that depends on the previous kernel: the norm
-    // weights, the rotation table row of pos (pos is set before the step),
-    // and the copies of the first tile of the K / V history
+    // before the wait, nothing that depends on the previous kernel: the
+    // copies of the first tile of the K / V history, then the norm weights
+    // and the rotation table row of pos (pos is set before the step), whose
+    // loads are left in flight over the wait
     const uint64_t keep = policy_evict_last();
-    const int pos = *a.pos;
-    const int n = pos + 1;
     if (tid == 0) {
         mbar_init(&bar_k, 1);
         mbar_init(&bar_v, 1);
         fence_mbar_init();
         s_ok = 1;
     }
+    const int pos = *a.pos;
+    load_kv_tile(s_kt, s_vt, kbase, vbase, row_stride, 0, min(pos, ATTN_TILE), &bar_k, &bar_v, true, true, tid, keep);
+    const int n = pos + 1;
     float4 qn = f4_zero(), kn = f4_zero();
     float2 cs[4];
     if (w == 0) {
@@ -242,10 +244,11 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_head_kernel(const AttnParam
         cs[0] = make_float2(r01.x, r01.y); cs[1] = make_float2(r01.z, r01.w);
         cs[2] = make_float2(r23.x, r23.y); cs[3] = make_float2(r23.z, r23.w);
     }
-    load_kv_tile(s_kt, s_vt, kbase, vbase, row_stride, 0, min(pos, ATTN_TILE), &bar_k, &bar_v, true, true, tid, keep);
+    ATTN_TRACE_AT(4);
     uint32_t ph_k = 0, ph_v = 0;
     prefetch_share(a.pf_ptr, a.pf_bytes, (int64_t)blockIdx.x * ATTN_WARPS + w, (int64_t)gridDim.x * ATTN_WARPS, lane);
     pdl_trigger();
+    ATTN_TRACE_AT(7);
     pdl_wait();
     ATTN_TRACE_AT(5);
     const uint32_t gen_out = LL ? tp_gen(a.ll, a.ll.gen_out) : 0u;
