@@ -315,8 +315,9 @@ int bh_stack_decode_host(bh_stack *st, const float *host_x, int32_t *host_tok);
  * per step (on a row split: this rank's). */
 int bh_stack_info(bh_stack *st, int64_t *weight_bytes, int64_t *step_bytes, int64_t *launches);
 /* Average device time of one op of the step (CUDA events around reps
- * eager repetitions over all layers on the stack's stream, the same launch
- * parameters as inside the step), and its algorithmic bytes per launch.
+ * eager repetitions over all layers on the stack's stream, launched as
+ * inside the step: the same launch parameters, programmatic dependent
+ * launch), and its algorithmic bytes per launch.
  * The state it leaves (hidden, caches) is scratch: reset x / pos after it. */
 #define BH_OP_QKV 0
 #define BH_OP_O 1

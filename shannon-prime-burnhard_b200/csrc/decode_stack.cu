@@ -762,7 +762,8 @@ int enqueue_step(bh_stack* st) {
 }
 
 // Launch one op of the step for every layer (or the LM head once), eagerly,
-// with the same parameters the step uses.
+// with the same parameters the step uses, the layer launches programmatic as
+// in the step.
 int enqueue_op(bh_stack* st, int op) {
     const bh_stack_config& c = st->cfg;
     bh_ctx* ctx = st->ctx;
@@ -784,7 +785,7 @@ int enqueue_op(bh_stack* st, int op) {
         return bh::launch_matvec(p, BH_FOLD_X86, bh::ACT_F32_RMSNORM, bh::EPI_ARGMAX, o);
     }
     if (op == BH_OP_ATTN) {
-        for (int l = 0; l < c.n_layer && rc == BH_OK; ++l) rc = launch_attn(st, l, false);
+        for (int l = 0; l < c.n_layer && rc == BH_OK; ++l) rc = launch_attn(st, l, true);
         return rc;
     }
     for (int l = 0; l < c.n_layer && rc == BH_OK; ++l) {
@@ -801,21 +802,21 @@ int enqueue_op(bh_stack* st, int op) {
                 p.xf = st->h;
                 p.gamma = st->attn_norm + (size_t)l * c.n_embd;
                 p.eps = c.rms_eps;
-                rc = stack_matvec(st, p, bh::ACT_F32_RMSNORM, bh::EPI_STORE, false);
+                rc = stack_matvec(st, p, bh::ACT_F32_RMSNORM, bh::EPI_STORE, true);
                 break;
             case BH_OP_O:
                 p = bh::base_params(ctx, W[BH_W_O], c.n_embd, qd, 1, st->h);
                 p.xf = st->attn;
-                rc = stack_matvec(st, p, bh::ACT_F32, bh::EPI_ADD, false);
+                rc = stack_matvec(st, p, bh::ACT_F32, bh::EPI_ADD, true);
                 break;
             case BH_OP_GATE_UP:
                 p = gate_up_params(st, l);
-                rc = stack_matvec(st, p, bh::ACT_F32_RMSNORM, bh::EPI_SWIGLU, false);
+                rc = stack_matvec(st, p, bh::ACT_F32_RMSNORM, bh::EPI_SWIGLU, true);
                 break;
             case BH_OP_DOWN:
                 p = bh::base_params(ctx, W[BH_W_DOWN], c.n_embd, c.n_ff, 1, st->h);
                 p.xf = st->gu;
-                rc = stack_matvec(st, p, bh::ACT_F32, bh::EPI_ADD, false);
+                rc = stack_matvec(st, p, bh::ACT_F32, bh::EPI_ADD, true);
                 break;
             default:
                 return BH_EINVAL;
